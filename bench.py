@@ -1,0 +1,381 @@
+#!/usr/bin/env python
+"""Benchmark of the DSA lightning-indexer path on B200.
+
+Default workload (the decode indexer the metric is quoted on):
+64 requests x next_n=2 rows, contexts U[4096, 65536], 64 index heads x 128 dim fp8,
+shared shuffled pool of 64-token pages.  One step = one CUDA-graph replay of the
+sglang decode call pair: hcu_ops.mqa_logits (tcgen05 fp8 paged logits + mask) ->
+hcu_ops.sparse_mask_topk_transform (exact top-2048 + page-table transform).
+
+metric: G-scores/s = (sum over rows of visible KV tokens) / step time.
+Multi-GPU (torchrun): the decode indexer does not shard, so every rank runs its
+own replica of the workload ("scaling": "weak"); value = all ranks' scores / the
+slowest rank's time.  --impl reference times the CPU restatement of the same
+pipeline (the reference's kernels are HIP-only) on the host cores, rank 0 only.
+
+Other workloads (--workload): prefill (config 2), dequant (config 3), mla_dequant.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PKG_ROOT = os.path.join(REPO, "sglang0.5.18-opt_b200")
+for _p in (REPO, PKG_ROOT):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+L2_BYTES = 126 * 1024 * 1024
+
+
+def _peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:  # noqa: BLE001
+        return 6650.0, 1590.0, "fallback"
+
+
+def _profile_traffic(name):
+    """Per-launch DRAM bytes of a kernel from a committed ncu summary, or None."""
+    path = os.path.join(REPO, "profiles", name + ".json")
+    try:
+        with open(path) as f:
+            return json.load(f).get("dram_bytes_per_launch")
+    except Exception:  # noqa: BLE001
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:  # noqa: BLE001
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.out = ""
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except Exception:  # noqa: BLE001
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        for line in (self.out or "").strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) >= 9:
+                rows.append(f)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": float(rows[0][2]),
+                "reasons": reasons, "samples": len(rows)}
+
+
+def _dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+# ------------------------------------------------------------------------------------------------
+# decode (config 1) -- the headline
+# ------------------------------------------------------------------------------------------------
+def decode_inputs(device, seed):
+    from hcu_ops.workloads import config1
+
+    return config1(device=device, seed=seed)
+
+
+def decode_alg_bytes(w):
+    """Algorithmic HBM bytes of one logits launch: each group's K pages read once (128 fp8 + 4 B
+    scale per token), q + weights, block-table entries, logits written at every visible token,
+    mask words written for every processed tile, and the mask memset of the full width."""
+    import torch
+
+    lens = w["context_lens"].long().cpu()
+    G, H = w["group_size"], w["heads"]
+    B = lens.numel()
+    glen = lens.view(-1, G).max(1).values
+    k_bytes = int((glen * 132).sum())
+    bt_bytes = int(((glen + 63) // 64).sum() * 4)
+    q_bytes = B * H * 128 + B * H * 4
+    logits_bytes = int(lens.sum() * 4)
+    mask_bytes = B * (w["max_context_len"] // 16) * 2 + int(((glen + 127) // 128).sum() * G * 16)
+    del torch
+    return k_bytes + bt_bytes + q_bytes + logits_bytes + mask_bytes
+
+
+def run_decode(args, world, rank, local):
+    import torch
+
+    import hcu_ops
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    w = decode_inputs(dev, seed=rank)
+    pairs = int(w["context_lens"].long().sum())
+    lens, pt, cu = w["context_lens"], w["page_table_size_1"], w["cu_seqlens_q"]
+
+    def step():
+        lg, mk = hcu_ops.mqa_logits(w["q"], w["kv_cache"], w["weights"], lens, w["block_table"],
+                                    w["max_context_len"], w["group_size"], hist_lens=lens)
+        return hcu_ops.sparse_mask_topk_transform(lg, mk, lens, pt, cu, 2048)
+
+    def logits_only():
+        return hcu_ops._C.mqa_logits_hist(w["q"], w["kv_cache"], w["weights"], lens, w["block_table"],
+                                          w["max_context_len"], w["group_size"], 0, 0, None)
+
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(max(args.warmup, 3)):
+            step()
+            logits_only()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        out = step()
+    g_lg = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_lg):
+        logits_only()
+    for _ in range(max(args.warmup, 3)):
+        g.replay()
+        g_lg.replay()
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    stream = torch.cuda.current_stream()
+    # ---- headline: K graph replays of the pipeline (inputs resident in HBM; K pool > L2)
+    with ClockSampler(local) as clk:
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            g.replay()
+        e1.record(stream)
+        barrier()
+    ms = e0.elapsed_time(e1) / args.steps
+    # ---- dominant kernel alone (the logits op) for the roofline
+    barrier()
+    l0, l1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    l0.record(stream)
+    for _ in range(args.steps):
+        g_lg.replay()
+    l1.record(stream)
+    barrier()
+    ms_logits = l0.elapsed_time(l1) / args.steps
+    # ---- e2e through the public API with host buffers
+    host = {k: w[k].cpu().pin_memory() for k in ("q", "weights", "context_lens", "block_table", "page_table_size_1")}
+    dev_in = {k: torch.empty_like(w[k]) for k in host}
+    res_host = torch.empty((lens.numel(), 2048), dtype=torch.int32).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = res_host.numel() * 4
+
+    def e2e_step():
+        for k, t in host.items():
+            dev_in[k].copy_(t, non_blocking=True)
+        lg, mk = hcu_ops.mqa_logits(dev_in["q"], w["kv_cache"], dev_in["weights"], dev_in["context_lens"],
+                                    dev_in["block_table"], w["max_context_len"], w["group_size"],
+                                    hist_lens=dev_in["context_lens"])
+        o = hcu_ops.sparse_mask_topk_transform(lg, mk, dev_in["context_lens"], dev_in["page_table_size_1"], cu, 2048)
+        res_host.copy_(o, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    barrier()
+    x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    x0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    x1.record(stream)
+    barrier()
+    ms_e2e = x0.elapsed_time(x1) / args.steps
+    st = hcu_ops.read_device_status(clear=True)
+    ok = torch.equal(res_host, out.cpu())
+
+    t = torch.tensor([ms, ms_logits, ms_e2e, float(pairs)], dtype=torch.float64, device=dev)
+    if world > 1:
+        mx = t.clone()
+        torch.distributed.all_reduce(mx, op=torch.distributed.ReduceOp.MAX)
+        sm_ = t.clone()
+        torch.distributed.all_reduce(sm_, op=torch.distributed.ReduceOp.SUM)
+        ms, ms_logits, ms_e2e = mx[0].item(), mx[1].item(), mx[2].item()
+        total_pairs = sm_[3].item()
+    else:
+        total_pairs = float(pairs)
+    if rank != 0:
+        return None
+    hbm, _, src = _peaks()
+    alg = decode_alg_bytes(w)
+    achieved = alg / (ms_logits * 1e-3) / 1e9
+    traffic = _profile_traffic("mqa_logits_paged_config1")
+    rec = {
+        "metric": "indexer G-scores/s (rows x visible KV tokens / s), decode logits + top-2048",
+        "value": total_pairs / (ms * 1e-3) / 1e9,
+        "unit": "G-scores/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "fp8e4m3 x fp8e4m3 -> fp32",
+        "data": "synthetic (seeded; q,K ~ N(0,1) per-row/per-token amax/448 fp8; w ~ N(0,1)/8)",
+        "config": {"workload": "config1: decode 64 req x next_n 2 (128 rows), ctx U[4096,65536], "
+                               "64 heads x 128, 64-token pages, shuffled pool; CUDA-graph replay",
+                   "rows": int(lens.numel()), "heads": w["heads"], "width": w["max_context_len"],
+                   "pairs_per_gpu": pairs, "kv_pool_bytes": int(w["kv_cache"].numel()),
+                   "l2": "no flush: K pool > 126 MB L2", "parallelism": f"replicas x{world}"},
+        "top_k_rows_per_s": lens.numel() * world / (ms * 1e-3),
+        "logits_op_ms": ms_logits,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "traffic": traffic, "kernel": "mqa_logits_paged_kernel<64> (+ mask memset)",
+                     "alg_bytes_per_launch": alg, "peak_source": src},
+        "e2e": {"value": total_pairs / (ms_e2e * 1e-3) / 1e9, "unit": "G-scores/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e, "result_matches_graph": bool(ok)},
+        "gpu_launches": args.steps * 2,
+        "clocks": clk.summary(),
+        "device_status": st,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        rec["cpu_baseline"] = cpu_decode_sample(w)
+    return rec
+
+
+def cpu_decode_sample(w, n_req=8):
+    """Oracle (CPU restatement) on the first n_req requests of the same workload."""
+    import numpy as np
+    import torch
+
+    from oracle import indexer as O
+
+    G = w["group_size"]
+    rows = n_req * G
+    q = w["q"][:rows].cpu().view(torch.uint8).numpy().reshape(rows, w["heads"], 128)
+    kv = w["kv_cache"].cpu().numpy().reshape(w["kv_cache"].shape[0], -1)
+    wt = w["weights"][:rows].cpu().numpy()
+    lens = w["context_lens"][:rows].cpu().numpy()
+    bt = w["block_table"][:rows].cpu().numpy()
+    pt = w["page_table_size_1"][:rows].cpu().numpy()
+    t0 = time.perf_counter()
+    lg, m, _ = O.mqa_logits_paged(q, kv, wt, lens, bt, w["max_context_len"], G)
+    O.topk_transform(lg, m, lens, pt)
+    dt = time.perf_counter() - t0
+    pairs = float(np.asarray(lens, np.int64).sum())
+    return {"value": pairs / dt / 1e9, "unit": "G-scores/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"first {n_req} requests ({rows} rows, {int(pairs)} scores) of the same workload, "
+                      f"oracle logits + top-k, {dt:.2f} s"}
+
+
+def run_reference(args):
+    """CPU restatement of the reference pipeline on the same config, all host threads."""
+    import numpy as np
+    import torch
+
+    from hcu_ops.workloads import config1
+    from oracle import indexer as O
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    w = config1(device="cpu", seed=0)
+    G = w["group_size"]
+    q = w["q"].view(torch.uint8).numpy().reshape(w["q"].shape[0], w["heads"], 128)
+    kv = w["kv_cache"].numpy().reshape(w["kv_cache"].shape[0], -1)
+    lens = w["context_lens"].numpy()
+    pairs = float(lens.astype(np.int64).sum())
+
+    def step():
+        lg, m, _ = O.mqa_logits_paged(q, kv, w["weights"].numpy(), lens, w["block_table"].numpy(),
+                                      w["max_context_len"], G)
+        O.topk_transform(lg, m, lens, w["page_table_size_1"].numpy())
+
+    for _ in range(min(args.warmup, 1)):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = (time.perf_counter() - t0) / args.steps
+    v = pairs / dt / 1e9
+    return {
+        "impl": "reference",
+        "metric": "indexer G-scores/s (rows x visible KV tokens / s), decode logits + top-2048",
+        "value": v, "unit": "G-scores/s", "n_gpus": 0, "steps": args.steps, "warmup": min(args.warmup, 1),
+        "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp8e4m3 x fp8e4m3 -> fp32", "data": "synthetic (seeded, same generator as the GPU arm)",
+        "config": {"workload": "config1: decode 64 req x next_n 2 (128 rows), ctx U[4096,65536], 64 heads x 128",
+                   "pairs": int(pairs)},
+        "cpu_baseline": {"value": v, "unit": "G-scores/s", "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": "whole config 1 per step (oracle restatement: the reference's kernels are "
+                                   "HIP for gfx938 and lightop is closed)"},
+        "e2e": {"value": v, "unit": "G-scores/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="decode")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    world, rank, local = _dist()
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps(run_reference(args)), flush=True)
+        return
+    import torch
+
+    if world > 1:
+        import datetime
+
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local))
+    try:
+        if args.workload != "decode":
+            raise SystemExit(f"unknown workload {args.workload}")
+        rec = run_decode(args, world, rank, local)
+        if rec is not None:
+            print(json.dumps(rec), flush=True)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,194 @@
+/*
+ * hcu_indexer.h -- C ABI of the B200 (sm_100a) DSA lightning-indexer library
+ * (libhcu_indexer.so).
+ *
+ * Plain pointers, sizes and a CUDA stream; no torch types.  Every entry point
+ * only enqueues work on `stream` (no host synchronisation, no allocation), so
+ * every call is CUDA-graph capturable.  Outputs and workspaces are owned by the
+ * caller; `*_workspace_bytes` queries size them.  Launch configuration depends
+ * only on the static shapes passed here and the device's SM count.
+ *
+ * Return value: HCU_OK or an error code; nothing throws across this ABI.
+ * HCU_ERR_ARG          an argument violates the contract (nothing launched)
+ * HCU_ERR_UNSUPPORTED  a shape/option this build does not implement
+ * HCU_ERR_LAUNCH       the CUDA launch failed (cudaGetLastError != success)
+ * Device-side faults that must not hang the GPU (a bounded wait that expired)
+ * are recorded in a sticky device status word read by hcu_read_device_status().
+ *
+ * Reference interface: the pybind11 module `hcu_ops._C`
+ * (hcu_ops/csrc/bind.cpp:3-10,36-44,47-51,76-80 of charliedhw/sglang0.5.18-opt)
+ * and the Triton dequant of prefill/patches/patch_fast_dequant.py:80-98.
+ */
+#ifndef HCU_INDEXER_H_
+#define HCU_INDEXER_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* hcu_stream_t; /* == cudaStream_t */
+
+enum {
+  HCU_OK = 0,
+  HCU_ERR_ARG = 1,
+  HCU_ERR_LAUNCH = 2,
+  HCU_ERR_TIMEOUT = 3,
+  HCU_ERR_UNSUPPORTED = 4,
+};
+
+/* Device status bits (sticky until cleared). */
+enum {
+  HCU_STATUS_WAIT_TIMEOUT = 1u << 0, /* an mbarrier / flag wait hit its bound */
+  HCU_STATUS_BAD_INPUT = 1u << 1,    /* a kernel saw an out-of-range index and skipped it */
+};
+
+/* Library version string and the compile target ("sm_100a"). */
+const char* hcu_version(void);
+
+/* Reads (and with clear != 0 resets) the device status word of the current
+ * device; synchronises the device.  Returns HCU_OK or HCU_ERR_LAUNCH. */
+int hcu_read_device_status(uint32_t* status, int clear);
+
+/* Last CUDA error string seen by this library on this thread ("" if none). */
+const char* hcu_last_error_string(void);
+
+/* ------------------------------------------------------------------------
+ * Stage 1: paged K-cache dequant
+ * ------------------------------------------------------------------------ */
+
+/* MLA latent slot dequant, drop-in for sglang's dequantize_k_cache_paged with
+ * the 656-byte slot (replaces prefill/patches/patch_fast_dequant.py:80-98 and
+ * its kernel :45-70).
+ *   quant_k_cache  uint8 [pool_slots, slot_stride] ; slot = 512 fp8 e4m3 |
+ *                  4 fp32 group scales | 64 bf16 rope; slot_stride % 16 == 0
+ *   page_table_1   int32 [n_tokens] slot index per output token
+ *   out            bf16 [n_tokens, 576] (row stride 576 elements)
+ * out[t, 128g+j] = bf16_rne(f32(fp8[s,128g+j]) * scale[s,g]); out[t,512:] = rope[s].
+ * Slot indices outside [0, pool_slots) are skipped (output row untouched) and
+ * flagged HCU_STATUS_BAD_INPUT. */
+int hcu_dequant_k_cache_paged(const uint8_t* quant_k_cache, int64_t pool_slots, int64_t slot_stride,
+                              const int32_t* page_table_1, int64_t n_tokens, uint16_t* out,
+                              hcu_stream_t stream);
+
+/* Indexer-K dequant (new in this build; the page layout of the logits op,
+ * hcu_ops/csrc/mqa_hist.cu:77-91): page = 64 x 128 fp8 then 64 fp32 scales.
+ *   kv_cache   uint8 [n_pages, page_stride] (page_stride >= 8448, % 16 == 0)
+ *   token_loc  int32 [n_tokens] = page * 64 + offset
+ *   out        bf16 [n_tokens, 128] */
+int hcu_dequant_index_k_paged(const uint8_t* kv_cache, int64_t n_pages, int64_t page_stride,
+                              const int32_t* token_loc, int64_t n_tokens, uint16_t* out,
+                              hcu_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Stage 2: MQA index logits  s = (sum_h w[h] * relu(q_h . k)) * k_scale
+ * ------------------------------------------------------------------------ */
+
+/* Workspace (int32 elements) of the fused pass-1 histogram: rows * (2*4096+2). */
+int64_t hcu_topk_hist_ws_elems(int64_t rows);
+
+/* Paged decode logits; replaces _C.mqa_logits_hist (hcu_ops/csrc/mqa_hist.cu:324-405,
+ * bind.cpp:41-44,78-80).
+ *   q            fp8 e4m3 [batch, heads, 128] contiguous (heads 32 or 64)
+ *   kv_cache     uint8 pages [n_pages, page_stride]
+ *   weights      fp32 [batch, heads] (q scale folded in)
+ *   context_lens int32 [batch]; clamped to [0, max_context_len]
+ *   block_table  int32 [batch, bt_stride]; rows of a group of `group_size`
+ *                share the table of the group's first row
+ *   max_context_len == (block-table capacity) * 64 = logits row width
+ *   logits       fp32 [batch, max_context_len]; written only where the mask bit is set
+ *   mask         int16 [batch, max_context_len/16]; bit j of word i = token 16i+j
+ *   hist_lens    optional int32 [batch]; when non-null also builds the top-k
+ *                pass-1 workspace `zws` (int32 [hcu_topk_hist_ws_elems(batch)])
+ *                for rows with min(hist_len, width) > 2048
+ *   persistent_ctas / rows_per_cta: tuning hints of the reference API; <= 0 = auto */
+int hcu_mqa_logits_hist(const uint8_t* q, int64_t batch, int64_t heads, const uint8_t* kv_cache,
+                        int64_t n_pages, int64_t page_stride, const float* weights,
+                        const int32_t* context_lens, const int32_t* block_table, int64_t bt_stride,
+                        int64_t max_context_len, int64_t group_size, int64_t persistent_ctas,
+                        int64_t rows_per_cta, const int32_t* hist_lens, float* logits, int16_t* mask,
+                        int32_t* zws, hcu_stream_t stream);
+
+/* Ragged prefill logits (new; the prefill indexer of the reference is closed
+ * lightop _mqa_logits).  Query row r sees tokens [row_start[r], row_end[r]) of a
+ * contiguous fp8 K; same logits + mask contract as hcu_mqa_logits_hist with the
+ * row width = n_tokens.
+ *   q        fp8 [rows, heads, 128]; weights fp32 [rows, heads]
+ *   k_fp8    fp8 [n_tokens, 128]; k_scale fp32 [n_tokens]
+ *   logits   fp32 [rows, logits_stride] (logits_stride >= n_tokens, % 4 == 0)
+ *   mask     int16 [rows, logits_stride/16] */
+int hcu_mqa_logits_ragged(const uint8_t* q, int64_t rows, int64_t heads, const uint8_t* k_fp8,
+                          const float* k_scale, int64_t n_tokens, const float* weights,
+                          const int32_t* row_start, const int32_t* row_end, float* logits,
+                          int64_t logits_stride, int16_t* mask, hcu_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Stage 3: exact top-2048 + page-table transform
+ * ------------------------------------------------------------------------ */
+
+/* Bytes of workspace the split variants need for [rows, width] scores. */
+int64_t hcu_topk_workspace_bytes(int64_t rows, int64_t width, int64_t max_splits);
+
+/* Exact top-k (topk must be 2048) of the masked scores of every row, written
+ * through the page table.  Replaces _C.sparse_mask_topk_transform
+ * (hcu_ops/csrc/sparse_mask_topk.cu:896-908, bind.cpp:3-6,47-48).
+ *   score   fp32 [rows, width] row stride score_stride (elements)
+ *   mask    int16 [rows, ceil(width/16)] row stride mask_stride
+ *   lengths int32 [rows]; len = min(lengths[r], width)
+ *   page_table int32 [rows, >= width] row stride pt_stride
+ *   dst     int32 [rows, 2048]
+ * Tokens whose mask bit is clear count as +0.  Ties break toward the lower
+ * token index.  Output: tokens above the threshold key in ascending token
+ * order, then the threshold ties in ascending order; len <= 2048 gives
+ * pt[i] for i < len and -1 after. */
+int hcu_sparse_mask_topk_transform(const float* score, int64_t rows, int64_t width, int64_t score_stride,
+                                   const int16_t* mask, int64_t mask_stride, const int32_t* lengths,
+                                   const int32_t* page_table, int64_t pt_stride, int64_t topk,
+                                   int32_t* dst, hcu_stream_t stream);
+
+/* Same result; a row is spread over up to max_splits CTAs when rows are few
+ * (replaces _C.sparse_mask_topk_transform_split, sparse_mask_topk.cu:910-981). */
+int hcu_sparse_mask_topk_transform_split(const float* score, int64_t rows, int64_t width,
+                                         int64_t score_stride, const int16_t* mask, int64_t mask_stride,
+                                         const int32_t* lengths, const int32_t* page_table,
+                                         int64_t pt_stride, int64_t topk, int64_t max_splits,
+                                         void* workspace, int64_t workspace_bytes, int32_t* dst,
+                                         hcu_stream_t stream);
+
+/* Split variant whose pass 1 was built by hcu_mqa_logits_hist(hist_lens=lengths)
+ * into zws (replaces _C.sparse_mask_topk_transform_split_pre, sparse_mask_topk.cu:986-1051). */
+int hcu_sparse_mask_topk_transform_split_pre(const float* score, int64_t rows, int64_t width,
+                                             int64_t score_stride, const int16_t* mask,
+                                             int64_t mask_stride, const int32_t* lengths,
+                                             const int32_t* page_table, int64_t pt_stride,
+                                             int64_t topk, int64_t max_splits, int32_t* zws,
+                                             void* workspace, int64_t workspace_bytes, int32_t* dst,
+                                             hcu_stream_t stream);
+
+/* Top-k that also returns the selected keys (the monotone uint32 image of the
+ * fp32 score; +0 = 0x80000000 for unset mask bits; 0 for -1 pads).  Used by the
+ * context-parallel path; same selection and order as hcu_sparse_mask_topk_transform. */
+int hcu_topk_keys(const float* score, int64_t rows, int64_t width, int64_t score_stride,
+                  const int16_t* mask, int64_t mask_stride, const int32_t* lengths,
+                  const int32_t* page_table, int64_t pt_stride, int32_t* dst, uint32_t* dst_keys,
+                  hcu_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Context-parallel merge (new): P per-range (key, global index) lists per row
+ * -> the global top-2048, in the single-GPU canonical order.
+ *   keys    uint32 [P, rows, 2048]; gidx int32 [P, rows, 2048] (-1 pads); part p
+ *           lists its candidates in ascending global index and parts cover
+ *           ascending contiguous ranges
+ *   lengths int32 [rows] total visible tokens of each row (<= 2048: keep all in
+ *           index order; else the canonical top-k order)
+ *   dst     int32 [rows, 2048] global token indices (-1 pads)
+ * ------------------------------------------------------------------------ */
+int hcu_cp_topk_merge(const uint32_t* keys, const int32_t* gidx, int64_t n_parts, int64_t rows,
+                      const int32_t* lengths, int32_t* dst, hcu_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* HCU_INDEXER_H_ */

@@ -1,0 +1,293 @@
+// hcu_ops._C: torch-tensor wrappers over the C ABI of libhcu_indexer.so.
+//
+// Op names, argument order and meaning, output allocation (torch::empty on the
+// input's device and current stream) and TORCH_CHECK messages follow the
+// reference binding hcu_ops/csrc/bind.cpp:3-10,36-44,47-51,76-80 and the host
+// checks of hcu_ops/csrc/mqa_hist.cu:329-357 / sparse_mask_topk.cu:846-870.
+// The additional ops (dequant, ragged logits, keys, CP merge) keep the same
+// conventions.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "../../include/hcu_indexer.h"
+
+namespace {
+
+constexpr int64_t kTopK = 2048;
+constexpr int64_t kBins = 4096;
+
+hcu_stream_t cur_stream() { return reinterpret_cast<hcu_stream_t>(at::cuda::getCurrentCUDAStream().stream()); }
+
+void check_status(int st, const char* op) {
+  TORCH_CHECK(st == HCU_OK, op, " failed: status ", st,
+              st == HCU_ERR_ARG           ? " (invalid argument)"
+              : st == HCU_ERR_UNSUPPORTED ? " (unsupported shape/option)"
+              : st == HCU_ERR_LAUNCH      ? " (launch error)"
+                                          : "",
+              " ", hcu_last_error_string());
+}
+
+template <typename T>
+T* ptr(const torch::Tensor& t) {
+  return reinterpret_cast<T*>(t.data_ptr());
+}
+
+void check_topk_inputs(const torch::Tensor& score, const torch::Tensor& nonzero_mask, const torch::Tensor& lengths,
+                       const torch::Tensor& page_table_size_1, const torch::Tensor& cu_seqlens_q, int64_t topk) {
+  TORCH_CHECK(topk == kTopK, "sparse-mask TopK requires topk=2048");
+  TORCH_CHECK(score.is_cuda() && score.scalar_type() == at::kFloat && score.dim() == 2 && score.stride(1) == 1,
+              "score must be row-contiguous float32 [rows, width]");
+  const int64_t rows = score.size(0);
+  TORCH_CHECK(nonzero_mask.scalar_type() == at::kShort && nonzero_mask.dim() == 2 && nonzero_mask.stride(1) == 1 &&
+                  nonzero_mask.size(0) == rows && nonzero_mask.size(1) == (score.size(1) + 15) / 16,
+              "nonzero_mask must be row-contiguous int16 [rows, ceil(width/16)]");
+  TORCH_CHECK(lengths.scalar_type() == at::kInt && lengths.dim() == 1 && lengths.is_contiguous() &&
+                  lengths.size(0) == rows,
+              "lengths must be contiguous int32 [rows]");
+  TORCH_CHECK(page_table_size_1.scalar_type() == at::kInt && page_table_size_1.dim() == 2 &&
+                  page_table_size_1.stride(1) == 1 && page_table_size_1.size(0) == rows,
+              "page_table_size_1 must be row-contiguous int32 [rows, *]");
+  TORCH_CHECK(cu_seqlens_q.size(0) == rows + 1,
+              "only the decode layout (one page-table row per score row) is supported");
+  TORCH_CHECK(rows == 0 || page_table_size_1.size(1) >= std::min<int64_t>(score.size(1), 1),
+              "page_table_size_1 must cover the score width");
+  TORCH_CHECK(nonzero_mask.device() == score.device() && lengths.device() == score.device() &&
+                  page_table_size_1.device() == score.device(),
+              "all tensors must be on the score's device");
+}
+
+torch::Tensor sparse_mask_topk_transform(const torch::Tensor& score, const torch::Tensor& nonzero_mask,
+                                         const torch::Tensor& lengths, const torch::Tensor& page_table_size_1,
+                                         const torch::Tensor& cu_seqlens_q, int64_t topk) {
+  check_topk_inputs(score, nonzero_mask, lengths, page_table_size_1, cu_seqlens_q, topk);
+  const c10::cuda::CUDAGuard guard(score.device());
+  const int64_t rows = score.size(0);
+  auto dst = torch::empty({rows, kTopK}, score.options().dtype(at::kInt));
+  if (rows == 0) return dst;
+  check_status(hcu_sparse_mask_topk_transform(ptr<const float>(score), rows, score.size(1), score.stride(0),
+                                              ptr<const int16_t>(nonzero_mask), nonzero_mask.stride(0),
+                                              ptr<const int32_t>(lengths), ptr<const int32_t>(page_table_size_1),
+                                              page_table_size_1.stride(0), topk, ptr<int32_t>(dst), cur_stream()),
+               "sparse_mask_topk_transform");
+  return dst;
+}
+
+torch::Tensor sparse_mask_topk_transform_split(const torch::Tensor& score, const torch::Tensor& nonzero_mask,
+                                               const torch::Tensor& lengths, const torch::Tensor& page_table_size_1,
+                                               const torch::Tensor& cu_seqlens_q, int64_t topk, int64_t max_splits) {
+  check_topk_inputs(score, nonzero_mask, lengths, page_table_size_1, cu_seqlens_q, topk);
+  const c10::cuda::CUDAGuard guard(score.device());
+  const int64_t rows = score.size(0);
+  auto dst = torch::empty({rows, kTopK}, score.options().dtype(at::kInt));
+  if (rows == 0) return dst;
+  const int64_t wsb = hcu_topk_workspace_bytes(rows, score.size(1), max_splits);
+  auto ws = torch::empty({std::max<int64_t>(wsb, 1)}, score.options().dtype(at::kByte));
+  check_status(hcu_sparse_mask_topk_transform_split(
+                   ptr<const float>(score), rows, score.size(1), score.stride(0), ptr<const int16_t>(nonzero_mask),
+                   nonzero_mask.stride(0), ptr<const int32_t>(lengths), ptr<const int32_t>(page_table_size_1),
+                   page_table_size_1.stride(0), topk, max_splits, ws.data_ptr(), wsb, ptr<int32_t>(dst),
+                   cur_stream()),
+               "sparse_mask_topk_transform_split");
+  return dst;
+}
+
+torch::Tensor sparse_mask_topk_transform_split_pre(const torch::Tensor& score, const torch::Tensor& nonzero_mask,
+                                                   const torch::Tensor& lengths,
+                                                   const torch::Tensor& page_table_size_1,
+                                                   const torch::Tensor& cu_seqlens_q, int64_t topk,
+                                                   int64_t max_splits, const torch::Tensor& zws) {
+  check_topk_inputs(score, nonzero_mask, lengths, page_table_size_1, cu_seqlens_q, topk);
+  const c10::cuda::CUDAGuard guard(score.device());
+  const int64_t rows = score.size(0);
+  auto dst = torch::empty({rows, kTopK}, score.options().dtype(at::kInt));
+  if (rows == 0) return dst;
+  TORCH_CHECK(zws.scalar_type() == at::kInt && zws.is_contiguous() && zws.numel() == rows * (2 * kBins + 2),
+              "zws must be the int32 [rows * (2 * 4096 + 2)] pass-1 workspace");
+  const int64_t wsb = hcu_topk_workspace_bytes(rows, score.size(1), max_splits);
+  auto ws = torch::empty({std::max<int64_t>(wsb, 1)}, score.options().dtype(at::kByte));
+  check_status(hcu_sparse_mask_topk_transform_split_pre(
+                   ptr<const float>(score), rows, score.size(1), score.stride(0), ptr<const int16_t>(nonzero_mask),
+                   nonzero_mask.stride(0), ptr<const int32_t>(lengths), ptr<const int32_t>(page_table_size_1),
+                   page_table_size_1.stride(0), topk, max_splits, ptr<int32_t>(zws), ws.data_ptr(), wsb,
+                   ptr<int32_t>(dst), cur_stream()),
+               "sparse_mask_topk_transform_split_pre");
+  return dst;
+}
+
+std::vector<torch::Tensor> topk_keys(const torch::Tensor& score, const torch::Tensor& nonzero_mask,
+                                     const torch::Tensor& lengths, const torch::Tensor& page_table) {
+  check_topk_inputs(score, nonzero_mask, lengths, page_table,
+                    torch::empty({score.size(0) + 1}, lengths.options()), kTopK);
+  const c10::cuda::CUDAGuard guard(score.device());
+  const int64_t rows = score.size(0);
+  auto dst = torch::empty({rows, kTopK}, score.options().dtype(at::kInt));
+  auto keys = torch::empty({rows, kTopK}, score.options().dtype(at::kInt));
+  if (rows == 0) return {dst, keys};
+  check_status(hcu_topk_keys(ptr<const float>(score), rows, score.size(1), score.stride(0),
+                             ptr<const int16_t>(nonzero_mask), nonzero_mask.stride(0), ptr<const int32_t>(lengths),
+                             ptr<const int32_t>(page_table), page_table.stride(0), ptr<int32_t>(dst),
+                             ptr<uint32_t>(keys), cur_stream()),
+               "topk_keys");
+  return {dst, keys};
+}
+
+std::vector<torch::Tensor> mqa_logits_hist(const torch::Tensor& q, const torch::Tensor& kv_cache,
+                                           const torch::Tensor& weights, const torch::Tensor& context_lens,
+                                           const torch::Tensor& block_table, int64_t max_context_len,
+                                           int64_t group_size, int64_t persistent_ctas, int64_t rows_per_cta,
+                                           const c10::optional<torch::Tensor>& hist_lens) {
+  TORCH_CHECK(q.is_cuda() && q.scalar_type() == at::kFloat8_e4m3fn && q.dim() == 4 && q.size(1) == 1 &&
+                  (q.size(2) == 32 || q.size(2) == 64) && q.size(3) == 128 && q.is_contiguous(),
+              "q must be contiguous fp8 e4m3fn [B, 1, 32|64, 128]");
+  const int64_t B = q.size(0);
+  const int64_t H = q.size(2);
+  TORCH_CHECK(kv_cache.scalar_type() == at::kByte && kv_cache.dim() == 4 && kv_cache.size(1) == 64 &&
+                  kv_cache.size(2) == 1 && kv_cache.size(3) == 132 && kv_cache.stride(1) == 132 &&
+                  kv_cache.stride(3) == 1 && kv_cache.stride(0) % 16 == 0,
+              "kv_cache must be packed fp8+scale uint8 [blocks, 64, 1, 132]");
+  TORCH_CHECK(weights.scalar_type() == at::kFloat && weights.dim() == 2 && weights.size(0) == B &&
+                  weights.size(1) == H && weights.is_contiguous(),
+              "weights must be contiguous float32 [B, heads]");
+  TORCH_CHECK(context_lens.scalar_type() == at::kInt && context_lens.dim() == 1 && context_lens.size(0) == B &&
+                  context_lens.is_contiguous(),
+              "context_lens must be contiguous int32 [B]");
+  TORCH_CHECK(block_table.scalar_type() == at::kInt && block_table.dim() == 2 && block_table.size(0) == B &&
+                  block_table.stride(1) == 1,
+              "block_table must be row-contiguous int32 [B, pages]");
+  TORCH_CHECK(max_context_len > 0 && max_context_len == block_table.size(1) * 64,
+              "max_context_len must equal block_table capacity");
+  TORCH_CHECK(B > 0 && group_size > 0 && B % group_size == 0, "batch must be a positive multiple of group_size");
+  const bool hist = hist_lens.has_value();
+  if (hist) {
+    TORCH_CHECK(hist_lens->scalar_type() == at::kInt && hist_lens->dim() == 1 && hist_lens->size(0) == B &&
+                    hist_lens->is_contiguous(),
+                "hist_lens must be contiguous int32 [B]");
+  }
+  const c10::cuda::CUDAGuard guard(q.device());
+  auto logits = torch::empty({B, max_context_len}, q.options().dtype(at::kFloat));
+  const int64_t mask_stride = (max_context_len + 15) / 16;
+  auto mask = torch::empty({B, mask_stride}, q.options().dtype(at::kShort));
+  torch::Tensor zws = hist ? torch::empty({B * (2 * kBins + 2)}, q.options().dtype(at::kInt))
+                           : torch::empty({0}, q.options().dtype(at::kInt));
+  check_status(hcu_mqa_logits_hist(ptr<const uint8_t>(q), B, H, ptr<const uint8_t>(kv_cache), kv_cache.size(0),
+                                   kv_cache.stride(0), ptr<const float>(weights), ptr<const int32_t>(context_lens),
+                                   ptr<const int32_t>(block_table), block_table.stride(0), max_context_len,
+                                   group_size, persistent_ctas, rows_per_cta,
+                                   hist ? ptr<const int32_t>(*hist_lens) : nullptr, ptr<float>(logits),
+                                   ptr<int16_t>(mask), hist ? ptr<int32_t>(zws) : nullptr, cur_stream()),
+               "mqa_logits_hist");
+  return {logits, mask, zws};
+}
+
+std::vector<torch::Tensor> mqa_logits_ragged(const torch::Tensor& q, const torch::Tensor& k_fp8,
+                                             const torch::Tensor& k_scale, const torch::Tensor& weights,
+                                             const torch::Tensor& row_start, const torch::Tensor& row_end) {
+  TORCH_CHECK(q.is_cuda() && q.scalar_type() == at::kFloat8_e4m3fn && q.dim() == 3 &&
+                  (q.size(1) == 32 || q.size(1) == 64) && q.size(2) == 128 && q.is_contiguous(),
+              "q must be contiguous fp8 e4m3fn [rows, 32|64, 128]");
+  const int64_t R = q.size(0);
+  const int64_t H = q.size(1);
+  TORCH_CHECK(k_fp8.scalar_type() == at::kFloat8_e4m3fn && k_fp8.dim() == 2 && k_fp8.size(1) == 128 &&
+                  k_fp8.is_contiguous(),
+              "k_fp8 must be contiguous fp8 e4m3fn [tokens, 128]");
+  const int64_t N = k_fp8.size(0);
+  TORCH_CHECK(k_scale.scalar_type() == at::kFloat && k_scale.numel() == N && k_scale.is_contiguous(),
+              "k_scale must be contiguous float32 [tokens]");
+  TORCH_CHECK(weights.scalar_type() == at::kFloat && weights.dim() == 2 && weights.size(0) == R &&
+                  weights.size(1) == H && weights.is_contiguous(),
+              "weights must be contiguous float32 [rows, heads]");
+  TORCH_CHECK(row_start.scalar_type() == at::kInt && row_start.numel() == R && row_start.is_contiguous() &&
+                  row_end.scalar_type() == at::kInt && row_end.numel() == R && row_end.is_contiguous(),
+              "row_start / row_end must be contiguous int32 [rows]");
+  const c10::cuda::CUDAGuard guard(q.device());
+  const int64_t stride = (N + 63) / 64 * 64;
+  auto logits = torch::empty({R, stride}, q.options().dtype(at::kFloat));
+  auto mask = torch::empty({R, stride / 16}, q.options().dtype(at::kShort));
+  if (R > 0)
+    check_status(hcu_mqa_logits_ragged(ptr<const uint8_t>(q), R, H, ptr<const uint8_t>(k_fp8),
+                                       ptr<const float>(k_scale), N, ptr<const float>(weights),
+                                       ptr<const int32_t>(row_start), ptr<const int32_t>(row_end),
+                                       ptr<float>(logits), stride, ptr<int16_t>(mask), cur_stream()),
+                 "mqa_logits_ragged");
+  return {logits.narrow(1, 0, N), mask.narrow(1, 0, (N + 15) / 16)};
+}
+
+torch::Tensor dequantize_k_cache_paged(const torch::Tensor& quant_k_cache, const torch::Tensor& page_table_1) {
+  TORCH_CHECK(quant_k_cache.is_cuda() && quant_k_cache.element_size() == 1 && quant_k_cache.size(-1) == 656 &&
+                  quant_k_cache.stride(-1) == 1,
+              "quant_k_cache must be a byte tensor [..., 656] with unit last stride");
+  TORCH_CHECK(page_table_1.scalar_type() == at::kInt && page_table_1.dim() == 1 && page_table_1.is_contiguous(),
+              "page_table_1_flattened must be contiguous int32 [n]");
+  const c10::cuda::CUDAGuard guard(quant_k_cache.device());
+  auto qk = quant_k_cache.view({-1, 656});
+  const int64_t n = page_table_1.size(0);
+  auto out = torch::empty({n, 1, 576}, quant_k_cache.options().dtype(at::kBFloat16));
+  check_status(hcu_dequant_k_cache_paged(ptr<const uint8_t>(qk), qk.size(0), qk.stride(0),
+                                         ptr<const int32_t>(page_table_1), n, ptr<uint16_t>(out), cur_stream()),
+               "dequantize_k_cache_paged");
+  return out;
+}
+
+torch::Tensor dequant_index_k_paged(const torch::Tensor& kv_cache, const torch::Tensor& token_loc) {
+  TORCH_CHECK(kv_cache.is_cuda() && kv_cache.scalar_type() == at::kByte && kv_cache.dim() == 4 &&
+                  kv_cache.size(1) == 64 && kv_cache.size(2) == 1 && kv_cache.size(3) == 132 &&
+                  kv_cache.stride(1) == 132 && kv_cache.stride(3) == 1 && kv_cache.stride(0) % 16 == 0,
+              "kv_cache must be packed fp8+scale uint8 [blocks, 64, 1, 132]");
+  TORCH_CHECK(token_loc.scalar_type() == at::kInt && token_loc.dim() == 1 && token_loc.is_contiguous(),
+              "token_loc must be contiguous int32 [n]");
+  const c10::cuda::CUDAGuard guard(kv_cache.device());
+  const int64_t n = token_loc.size(0);
+  auto out = torch::empty({n, 128}, kv_cache.options().dtype(at::kBFloat16));
+  check_status(hcu_dequant_index_k_paged(ptr<const uint8_t>(kv_cache), kv_cache.size(0), kv_cache.stride(0),
+                                         ptr<const int32_t>(token_loc), n, ptr<uint16_t>(out), cur_stream()),
+               "dequant_index_k_paged");
+  return out;
+}
+
+torch::Tensor cp_topk_merge(const torch::Tensor& keys, const torch::Tensor& gidx, const torch::Tensor& lengths) {
+  TORCH_CHECK(keys.is_cuda() && keys.scalar_type() == at::kInt && keys.dim() == 3 && keys.size(2) == kTopK &&
+                  keys.is_contiguous(),
+              "keys must be contiguous int32 (uint32 bits) [parts, rows, 2048]");
+  TORCH_CHECK(gidx.scalar_type() == at::kInt && gidx.sizes() == keys.sizes() && gidx.is_contiguous(),
+              "gidx must be contiguous int32 [parts, rows, 2048]");
+  TORCH_CHECK(lengths.scalar_type() == at::kInt && lengths.dim() == 1 && lengths.size(0) == keys.size(1) &&
+                  lengths.is_contiguous(),
+              "lengths must be contiguous int32 [rows]");
+  const c10::cuda::CUDAGuard guard(keys.device());
+  const int64_t rows = keys.size(1);
+  auto dst = torch::empty({rows, kTopK}, keys.options());
+  if (rows == 0) return dst;
+  check_status(hcu_cp_topk_merge(ptr<const uint32_t>(keys), ptr<const int32_t>(gidx), keys.size(0), rows,
+                                 ptr<const int32_t>(lengths), ptr<int32_t>(dst), cur_stream()),
+               "cp_topk_merge");
+  return dst;
+}
+
+int64_t read_device_status(bool clear) {
+  uint32_t s = 0;
+  check_status(hcu_read_device_status(&s, clear ? 1 : 0), "read_device_status");
+  return static_cast<int64_t>(s);
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("sparse_mask_topk_transform", &sparse_mask_topk_transform,
+        "Exact top-2048 + page-table transform over sparse-mask MQA logits");
+  m.def("sparse_mask_topk_transform_split", &sparse_mask_topk_transform_split,
+        "Same as sparse_mask_topk_transform; few rows may be split over several CTAs");
+  m.def("sparse_mask_topk_transform_split_pre", &sparse_mask_topk_transform_split_pre,
+        "sparse_mask_topk_transform_split with pass 1 (histogram) taken from mqa_logits_hist's workspace");
+  m.def("mqa_logits_hist", &mqa_logits_hist,
+        "paged fp8 indexer logits -> {logits, mask, zws}; with hist_lens also top-k pass 1 into zws");
+  m.def("mqa_logits_ragged", &mqa_logits_ragged,
+        "prefill fp8 indexer logits over a contiguous K with per-row [start, end) -> {logits, mask}");
+  m.def("topk_keys", &topk_keys, "top-2048 indices through a page table plus the selected uint32 keys");
+  m.def("dequantize_k_cache_paged", &dequantize_k_cache_paged,
+        "MLA 656-byte slot paged dequant -> bf16 [n, 1, 576] (sglang dequantize_k_cache_paged drop-in)");
+  m.def("dequant_index_k_paged", &dequant_index_k_paged, "indexer-K page dequant -> bf16 [n, 128]");
+  m.def("cp_topk_merge", &cp_topk_merge, "merge per-range (key, global index) top-2048 lists");
+  m.def("read_device_status", &read_device_status, "sticky device status bits of the library (synchronises)");
+  m.def("version", []() { return std::string(hcu_version()); });
+}

@@ -1,0 +1,179 @@
+// Stage 1: paged fp8 K-cache dequant (HBM streams).
+//
+// dequant_mla_kernel: the 656-byte MLA slot of sglang's DSA backend
+//   (512 fp8 e4m3 | 4 fp32 group scales | 64 bf16 rope) -> 576 bf16, one warp
+//   per token: lane l converts bytes [16l, 16l+16) with the scale of group l/8
+//   and stores 32 contiguous output bytes; lanes 0-7 copy the rope.  Semantics
+//   of prefill/patches/patch_fast_dequant.py:53-71 (fp32 multiply, one
+//   round-to-nearest-even to bf16, rope copied bit for bit).
+// dequant_index_k_kernel: the indexer-K page (64 x 128 fp8, then 64 fp32
+//   scales) -> bf16 [n, 128]; 8 lanes per token, 4 tokens per warp access.
+//
+// Both issue every load of kUnroll tokens before the first store so that each
+// warp keeps several KB in flight (HBM latency x bandwidth per SM is ~40 KB).
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+
+#include "common.cuh"
+
+HCU_DEFINE_STATUS(status_dequant)
+
+namespace hcu {
+namespace {
+
+constexpr int kMlaSlot = 656;
+constexpr int kMlaOut = 576;
+constexpr int kDqThreads = 256;
+constexpr int kMlaUnroll = 4;
+constexpr int kIdxUnroll = 4;
+
+__device__ __forceinline__ uint4 ld_stream(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ void st_v4(void* p, uint4 v) {
+  asm volatile("st.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+// Two fp8 e4m3 (low byte first) -> two bf16 of fp32(fp8) * s, packed.
+__device__ __forceinline__ uint32_t cvt2(uint16_t two, float s) {
+  const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(two), __NV_E4M3);
+  const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h));
+  const float a = __fmul_rn(f.x, s);
+  const float b = __fmul_rn(f.y, s);
+  const __nv_bfloat162 r = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&r);
+}
+
+// 16 fp8 bytes -> 32 output bytes.
+__device__ __forceinline__ void cvt16(const uint4& in, float s, uint4& o0, uint4& o1) {
+  const uint32_t w[4] = {in.x, in.y, in.z, in.w};
+  uint32_t r[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    r[2 * i] = cvt2(static_cast<uint16_t>(w[i] & 0xFFFFu), s);
+    r[2 * i + 1] = cvt2(static_cast<uint16_t>(w[i] >> 16), s);
+  }
+  o0 = make_uint4(r[0], r[1], r[2], r[3]);
+  o1 = make_uint4(r[4], r[5], r[6], r[7]);
+}
+
+__global__ __launch_bounds__(kDqThreads) void dequant_mla_kernel(const uint8_t* __restrict__ cache, int64_t pool,
+                                                                 int64_t slot_stride,
+                                                                 const int32_t* __restrict__ slots, int64_t n,
+                                                                 uint16_t* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * kDqThreads + threadIdx.x) >> 5;
+  const int64_t n_warps = (static_cast<int64_t>(gridDim.x) * kDqThreads) >> 5;
+  for (int64_t t0 = warp * kMlaUnroll; t0 < n; t0 += n_warps * kMlaUnroll) {
+    uint4 q[kMlaUnroll], rope[kMlaUnroll];
+    float s[kMlaUnroll];
+    bool ok[kMlaUnroll];
+#pragma unroll
+    for (int u = 0; u < kMlaUnroll; ++u) {
+      const int64_t t = t0 + u;
+      int64_t src = t < n ? static_cast<int64_t>(__ldg(slots + t)) : -1;
+      ok[u] = t < n && src >= 0 && src < pool;
+      if (t < n && !ok[u] && lane == 0) atomicOr(&g_hcu_status, HCU_STATUS_BAD_INPUT);
+      src = ok[u] ? src : 0;
+      const uint8_t* row = cache + src * slot_stride;
+      q[u] = ok[u] ? ld_stream(row + 16 * lane) : make_uint4(0, 0, 0, 0);
+      s[u] = ok[u] ? __ldg(reinterpret_cast<const float*>(row + 512) + (lane >> 3)) : 0.f;
+      rope[u] = (ok[u] && lane < 8) ? ld_stream(row + 528 + 16 * lane) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < kMlaUnroll; ++u) {
+      if (!ok[u]) continue;
+      uint8_t* dst = reinterpret_cast<uint8_t*>(out + (t0 + u) * kMlaOut);
+      uint4 o0, o1;
+      cvt16(q[u], s[u], o0, o1);
+      st_v4(dst + 32 * lane, o0);
+      st_v4(dst + 32 * lane + 16, o1);
+      if (lane < 8) st_v4(dst + 1024 + 16 * lane, rope[u]);
+    }
+  }
+}
+
+__global__ __launch_bounds__(kDqThreads) void dequant_index_k_kernel(const uint8_t* __restrict__ kv,
+                                                                     int64_t n_pages, int64_t page_stride,
+                                                                     const int32_t* __restrict__ loc, int64_t n,
+                                                                     uint16_t* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int sub = lane >> 3;   // token within the 4-token group
+  const int part = lane & 7;   // 16-byte chunk of the token
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * kDqThreads + threadIdx.x) >> 5;
+  const int64_t n_warps = (static_cast<int64_t>(gridDim.x) * kDqThreads) >> 5;
+  const int64_t n_slots = n_pages * kPage;
+  for (int64_t t0 = warp * 4 * kIdxUnroll; t0 < n; t0 += n_warps * 4 * kIdxUnroll) {
+    uint4 q[kIdxUnroll];
+    float s[kIdxUnroll];
+    bool ok[kIdxUnroll];
+#pragma unroll
+    for (int u = 0; u < kIdxUnroll; ++u) {
+      const int64_t t = t0 + 4 * u + sub;
+      int64_t l = t < n ? static_cast<int64_t>(__ldg(loc + t)) : -1;
+      ok[u] = t < n && l >= 0 && l < n_slots;
+      if (t < n && !ok[u] && part == 0) atomicOr(&g_hcu_status, HCU_STATUS_BAD_INPUT);
+      l = ok[u] ? l : 0;
+      const uint8_t* page = kv + (l >> 6) * page_stride;
+      q[u] = ok[u] ? ld_stream(page + (l & 63) * kHeadDim + 16 * part) : make_uint4(0, 0, 0, 0);
+      s[u] = ok[u] ? __ldg(reinterpret_cast<const float*>(page + kPageFp8Bytes) + (l & 63)) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < kIdxUnroll; ++u) {
+      if (!ok[u]) continue;
+      const int64_t t = t0 + 4 * u + sub;
+      uint8_t* dst = reinterpret_cast<uint8_t*>(out + t * kHeadDim);
+      uint4 o0, o1;
+      cvt16(q[u], s[u], o0, o1);
+      st_v4(dst + 32 * part, o0);
+      st_v4(dst + 32 * part + 16, o1);
+    }
+  }
+}
+
+int grid_for(int64_t warps_needed) {
+  const int64_t per_block = kDqThreads / 32;
+  int64_t blocks = (warps_needed + per_block - 1) / per_block;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * 8;  // 8 x 256 threads resident per SM
+  if (blocks > cap) blocks = cap;
+  return static_cast<int>(blocks < 1 ? 1 : blocks);
+}
+
+}  // namespace
+}  // namespace hcu
+
+extern "C" int hcu_dequant_k_cache_paged(const uint8_t* quant_k_cache, int64_t pool_slots, int64_t slot_stride,
+                                         const int32_t* page_table_1, int64_t n_tokens, uint16_t* out,
+                                         hcu_stream_t stream) {
+  using namespace hcu;
+  if (n_tokens < 0 || pool_slots < 0 || slot_stride < kMlaSlot || slot_stride % 16 != 0) return HCU_ERR_ARG;
+  if (n_tokens == 0) return HCU_OK;
+  if (!quant_k_cache || !page_table_1 || !out) return HCU_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(quant_k_cache) | reinterpret_cast<uintptr_t>(out)) % 16 != 0)
+    return HCU_ERR_ARG;
+  const int grid = grid_for((n_tokens + kMlaUnroll - 1) / kMlaUnroll);
+  dequant_mla_kernel<<<grid, kDqThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      quant_k_cache, pool_slots, slot_stride, page_table_1, n_tokens, out);
+  return launch_status();
+}
+
+extern "C" int hcu_dequant_index_k_paged(const uint8_t* kv_cache, int64_t n_pages, int64_t page_stride,
+                                         const int32_t* token_loc, int64_t n_tokens, uint16_t* out,
+                                         hcu_stream_t stream) {
+  using namespace hcu;
+  if (n_tokens < 0 || n_pages < 0 || page_stride < kPage * (kHeadDim + 4) || page_stride % 16 != 0)
+    return HCU_ERR_ARG;
+  if (n_tokens == 0) return HCU_OK;
+  if (!kv_cache || !token_loc || !out) return HCU_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(kv_cache) | reinterpret_cast<uintptr_t>(out)) % 16 != 0) return HCU_ERR_ARG;
+  const int grid = grid_for((n_tokens + 4 * kIdxUnroll - 1) / (4 * kIdxUnroll));
+  dequant_index_k_kernel<<<grid, kDqThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      kv_cache, n_pages, page_stride, token_loc, n_tokens, out);
+  return launch_status();
+}

@@ -1,0 +1,610 @@
+// Stage 3: exact top-2048 over masked scores + page-table transform.
+//
+// topk_row_kernel: one 1024-thread CTA (32 warps) per row.  Warp w owns the
+// contiguous token segment [w*seg, (w+1)*seg) of the row (seg a multiple of
+// 128 = 32 lanes x 4 tokens), so the final compaction only needs per-warp
+// counts and an in-warp prefix -- no block-wide scan per chunk.  Passes over
+// the row (the row stays L2-resident between passes):
+//   A  12-bit histogram of key[31:20] + per-warp positive / zero counts
+//      (skipped when the logits kernel already built it: the "pre" path);
+//      positives <= 2048 <= positives + zeros -> the threshold is +0 (fast path)
+//   B  12-bit histogram of key[19:8] inside the threshold bin
+//   C  per-warp 8-bit histograms of key[7:0] inside the 24-bit prefix, per-warp
+//      count of keys above the prefix and of exact zeros
+//   D  compaction: keys > thr in token order, then the first `remaining`
+//      threshold ties in token order, then one coalesced page-table gather.
+// Unset mask bits are an implicit +0 (key 0x80000000) whatever the score
+// storage holds.  The selection and output order are those of
+// hcu_ops/csrc/sparse_mask_topk.cu:1-7,141-349 of the reference.
+#include "common.cuh"
+
+HCU_DEFINE_STATUS(status_topk)
+
+namespace hcu {
+namespace {
+
+constexpr int kTkThreads = 1024;
+constexpr int kTkWarps = kTkThreads / 32;
+constexpr int kStep = 128;  // tokens per warp step (32 lanes x 4)
+constexpr int kTkUnroll = 4;
+constexpr int kHistTrash = kTkWarps * 256;  // trash slots follow the per-warp histograms
+
+struct __align__(16) TopkSmem {
+  int hist[kTkWarps * 256 + 32 + 256];  // A/B: [0,4096) + trash; C: 32 x 256 + trash + merged[256]
+  int out_idx[kTopK + 32];
+  uint32_t out_key[kTopK + 32];
+  int above[kTkWarps];
+  int ties[kTkWarps];
+  int zeros[kTkWarps];
+  int pos[kTkWarps];
+  int wtot[kTkWarps];
+  int res[4];
+};
+
+__device__ __forceinline__ int warp_sum(int x) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  return x;
+}
+
+// Loads tokens [i0, i0+4) (i0 a multiple of 4) and their 16-bit mask word.
+// Positions at or past `lim` read token 0 (always valid here) so the loads of
+// an unrolled group are branch-free.
+template <bool kVec>
+__device__ __forceinline__ void load4(const float* __restrict__ vals, const int16_t* __restrict__ mask, int i0,
+                                      int lim, float (&v)[4], uint32_t& mw) {
+  const int safe = i0 < lim ? i0 : 0;
+  mw = static_cast<uint16_t>(__ldg(mask + (safe >> 4)));
+  if constexpr (kVec) {
+    const float4 f = __ldg(reinterpret_cast<const float4*>(vals + safe));
+    v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = __ldg(vals + (safe + j < lim ? safe + j : lim - 1));
+  }
+}
+
+// Keys of tokens [i0, i0+4); returns the bitmask of tokens below `lim`.
+__device__ __forceinline__ uint32_t keys4(int i0, int lim, const float (&v)[4], uint32_t mw, uint32_t (&k)[4]) {
+  const uint32_t m = (mw >> (i0 & 15)) & 0xFu;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) k[j] = ((m >> j) & 1u) ? to_key(v[j]) : kZeroKey;
+  const int rem = lim - i0;
+  const int nv = rem <= 0 ? 0 : (rem < 4 ? rem : 4);
+  return (1u << nv) - 1u;
+}
+
+// Bin b of an NB-bin histogram with suffix(b) >= need > suffix(b+1):
+// res[0] = b, res[1] = suffix(b+1).  Requires sum(hist) >= need >= 1.
+template <int NB>
+__device__ __forceinline__ void find_threshold(const int* hist, int need, int* wtot, int* res) {
+  constexpr int BPT = NB >= kTkThreads ? NB / kTkThreads : 1;
+  constexpr int ACTIVE = NB / BPT;
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int w = tid >> 5;
+  int h[BPT];
+  int s = 0;
+#pragma unroll
+  for (int j = 0; j < BPT; ++j) {
+    h[j] = tid < ACTIVE ? hist[tid * BPT + j] : 0;
+    s += h[j];
+  }
+  int x = s;  // inclusive suffix over lanes >= lane
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_down_sync(0xffffffffu, x, o);
+    if (lane + o < 32) x += y;
+  }
+  if (lane == 0) wtot[w] = x;
+  __syncthreads();
+  int after = 0;
+  for (int v = w + 1; v < kTkWarps; ++v) after += wtot[v];
+  const int suf = x + after;
+  const int suf_next = suf - s;
+  if (tid < ACTIVE && suf >= need && suf_next < need) {
+    int acc = suf_next;
+#pragma unroll
+    for (int j = BPT - 1; j >= 0; --j) {
+      if (acc + h[j] >= need) {
+        res[0] = tid * BPT + j;
+        res[1] = acc;
+        break;
+      }
+      acc += h[j];
+    }
+  }
+  __syncthreads();
+}
+
+// Visits every token slot of this warp's segment as (valid, key, index i0+j).
+#define TK_FOR_EACH(BODY)                                                             \
+  for (int c = seg_begin; c < seg_end; c += kStep * kTkUnroll) {                      \
+    float rv[kTkUnroll][4];                                                           \
+    uint32_t rm[kTkUnroll];                                                           \
+    _Pragma("unroll") for (int u = 0; u < kTkUnroll; ++u)                             \
+        load4<kVec>(vals, mrow, c + u * kStep + lane * 4, seg_end, rv[u], rm[u]);     \
+    _Pragma("unroll") for (int u = 0; u < kTkUnroll; ++u) {                           \
+      const int i0 = c + u * kStep + lane * 4;                                        \
+      uint32_t kk[4];                                                                 \
+      const uint32_t vv = keys4(i0, seg_end, rv[u], rm[u], kk);                       \
+      _Pragma("unroll") for (int j = 0; j < 4; ++j) {                                 \
+        const bool valid = (vv >> j) & 1u;                                            \
+        const uint32_t key = kk[j];                                                   \
+        BODY                                                                          \
+      }                                                                               \
+    }                                                                                 \
+  }
+
+template <bool kVec, bool kSorted>
+__global__ __launch_bounds__(kTkThreads, 1) void topk_row_kernel(
+    const float* __restrict__ score, int64_t score_stride, int width, const int16_t* __restrict__ mask,
+    int64_t mask_stride, const int32_t* __restrict__ lengths, const int32_t* __restrict__ pt, int64_t pt_stride,
+    int32_t* __restrict__ dst, uint32_t* __restrict__ dst_keys, const int32_t* __restrict__ pre_ws, int rows) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  TopkSmem& sm = *reinterpret_cast<TopkSmem*>(smem_raw);
+  const int row = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int w = tid >> 5;
+  int len = lengths[row];
+  len = len < width ? len : width;
+  len = len < 0 ? 0 : len;
+  const int32_t* src = pt + static_cast<int64_t>(row) * pt_stride;
+  int32_t* out = dst + static_cast<int64_t>(row) * kTopK;
+  const float* vals = score + static_cast<int64_t>(row) * score_stride;
+  const int16_t* mrow = mask + static_cast<int64_t>(row) * mask_stride;
+
+  if (len <= kTopK) {
+    for (int i = tid; i < kTopK; i += kTkThreads) {
+      out[i] = i < len ? src[i] : -1;
+      if (dst_keys) {
+        uint32_t k = 0;
+        if (i < len) {
+          const bool set = (static_cast<uint16_t>(mrow[i >> 4]) >> (i & 15)) & 1u;
+          k = set ? to_key(vals[i]) : kZeroKey;
+        }
+        dst_keys[static_cast<int64_t>(row) * kTopK + i] = k;
+      }
+    }
+    return;
+  }
+
+  const int seg = (len + kTkWarps * kStep - 1) / (kTkWarps * kStep) * kStep;
+  const int seg_begin = min(w * seg, len);
+  const int seg_end = min(seg_begin + seg, len);
+  const int trash = kBins + lane;
+
+  // ---- pass A: key[31:20] histogram, positives and zeros ----
+  int positives = 0, zeros = 0;
+  const int* hist1 = sm.hist;
+  bool have_warp_counts = false;
+  if (pre_ws != nullptr) {
+    hist1 = pre_ws + static_cast<int64_t>(row) * kBins;
+    const int* cnt = pre_ws + 2 * static_cast<int64_t>(rows) * kBins + 2 * row;
+    positives = cnt[0];
+    zeros = cnt[1];
+  } else {
+    for (int i = tid; i < kBins + 32; i += kTkThreads) sm.hist[i] = 0;
+    __syncthreads();
+    int zc = 0, pc = 0;
+    TK_FOR_EACH({
+      const bool nz = key != kZeroKey;
+      zc += valid & !nz;
+      pc += valid & (key > kZeroKey);
+      atomicAdd(&sm.hist[(valid & nz) ? static_cast<int>(key >> 20) : trash], 1);
+    })
+    zc = warp_sum(zc);
+    pc = warp_sum(pc);
+    if (lane == 0) {
+      if (zc) atomicAdd(&sm.hist[kZeroBin], zc);
+      sm.pos[w] = pc;
+      sm.zeros[w] = zc;
+    }
+    __syncthreads();
+    for (int v = 0; v < kTkWarps; ++v) {
+      positives += sm.pos[v];
+      zeros += sm.zeros[v];
+    }
+    have_warp_counts = true;
+  }
+
+  uint32_t thr;
+  int remaining;
+  if (positives <= kTopK && positives + zeros >= kTopK) {
+    // Sparse fast path: every positive plus the lowest-index zeros.
+    thr = kZeroKey;
+    remaining = kTopK - positives;
+    if (!have_warp_counts) {
+      int zc = 0, pc = 0;
+      TK_FOR_EACH({
+        zc += valid & (key == kZeroKey);
+        pc += valid & (key > kZeroKey);
+      })
+      zc = warp_sum(zc);
+      pc = warp_sum(pc);
+      if (lane == 0) {
+        sm.pos[w] = pc;
+        sm.zeros[w] = zc;
+      }
+    }
+    if (lane == 0) {
+      sm.above[w] = sm.pos[w];
+      sm.ties[w] = sm.zeros[w];
+    }
+    __syncthreads();
+  } else {
+    find_threshold<kBins>(hist1, kTopK, sm.wtot, sm.res);
+    const uint32_t t1 = static_cast<uint32_t>(sm.res[0]);
+    const int need1 = kTopK - sm.res[1];
+
+    // ---- pass B: key[19:8] inside bin t1 ----
+    for (int i = tid; i < kBins + 32; i += kTkThreads) sm.hist[i] = 0;
+    __syncthreads();
+    if (tid == 0 && t1 == (kZeroKey >> 20) && zeros) atomicAdd(&sm.hist[(kZeroKey >> 8) & 0xFFFu], zeros);
+    TK_FOR_EACH({
+      const bool cand = valid & ((key >> 20) == t1) & (key != kZeroKey);
+      atomicAdd(&sm.hist[cand ? static_cast<int>((key >> 8) & 0xFFFu) : trash], 1);
+    })
+    __syncthreads();
+    find_threshold<kBins>(sm.hist, need1, sm.wtot, sm.res);
+    const uint32_t prefix24 = (t1 << 12) | static_cast<uint32_t>(sm.res[0]);
+    const int need2 = need1 - sm.res[1];
+
+    // ---- pass C: per-warp key[7:0] inside prefix24 + per-warp above / zeros ----
+    for (int i = tid; i < kTkWarps * 256 + 32; i += kTkThreads) sm.hist[i] = 0;
+    __syncthreads();
+    {
+      int above = 0, zc = 0;
+      int* wh = sm.hist + w * 256;
+      TK_FOR_EACH({
+        const uint32_t hi = key >> 8;
+        above += valid & (hi > prefix24);
+        zc += valid & (key == kZeroKey);
+        const bool cand = valid & (hi == prefix24) & (key != kZeroKey);
+        atomicAdd(cand ? &wh[key & 0xFFu] : &sm.hist[kHistTrash + lane], 1);
+      })
+      above = warp_sum(above);
+      zc = warp_sum(zc);
+      if (lane == 0) {
+        if (zc && prefix24 == (kZeroKey >> 8)) atomicAdd(&wh[kZeroKey & 0xFFu], zc);
+        sm.above[w] = above;
+      }
+    }
+    __syncthreads();
+    int* merged = sm.hist + kTkWarps * 256 + 32;
+    if (tid < 256) {
+      int s = 0;
+      for (int v = 0; v < kTkWarps; ++v) s += sm.hist[v * 256 + tid];
+      merged[tid] = s;
+    }
+    __syncthreads();
+    find_threshold<256>(merged, need2, sm.wtot, sm.res);
+    const uint32_t t3 = static_cast<uint32_t>(sm.res[0]);
+    thr = (prefix24 << 8) | t3;
+    remaining = need2 - sm.res[1];
+    {
+      const int* wh = sm.hist + w * 256;
+      int a = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const uint32_t d = lane * 8 + j;
+        if (d > t3) a += wh[d];
+      }
+      a = warp_sum(a);
+      if (lane == 0) {
+        sm.above[w] += a;
+        sm.ties[w] = wh[t3];
+      }
+    }
+    __syncthreads();
+  }
+  const int tie_base = kTopK - remaining;
+
+  // ---- pass D: ordered compaction into shared memory ----
+  // Canonical order: keys > thr in token order, then the first `remaining`
+  // threshold ties in token order.  kSorted: the same set in token order.
+  int above_pos = 0, tie_pos = 0, sel_pos = 0;
+  for (int v = 0; v < w; ++v) {
+    above_pos += sm.above[v];
+    const int tv = sm.ties[v];
+    const int take = min(max(remaining - tie_pos, 0), tv);
+    sel_pos += sm.above[v] + take;
+    tie_pos += tv;
+  }
+  for (int c = seg_begin; c < seg_end; c += kStep * kTkUnroll) {
+    float rv[kTkUnroll][4];
+    uint32_t rm[kTkUnroll];
+#pragma unroll
+    for (int u = 0; u < kTkUnroll; ++u) load4<kVec>(vals, mrow, c + u * kStep + lane * 4, seg_end, rv[u], rm[u]);
+#pragma unroll
+    for (int u = 0; u < kTkUnroll; ++u) {
+      const int i0 = c + u * kStep + lane * 4;
+      uint32_t kk[4];
+      const uint32_t vv = keys4(i0, seg_end, rv[u], rm[u], kk);
+      int na = 0, nt = 0;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const bool valid = (vv >> j) & 1u;
+        na += valid & (kk[j] > thr);
+        nt += valid & (kk[j] == thr);
+      }
+      // inclusive warp scan of (na | nt << 16)
+      const int packed = na | (nt << 16);
+      int inc = packed;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += y;
+      }
+      const int total = __shfl_sync(0xffffffffu, inc, 31);
+      const int ex = inc - packed;
+      if constexpr (!kSorted) {
+        int pa = above_pos + (ex & 0xFFFF);
+        int pq = tie_pos + (ex >> 16);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const bool valid = (vv >> j) & 1u;
+          if (valid & (kk[j] > thr)) {
+            sm.out_idx[pa] = i0 + j;
+            sm.out_key[pa] = kk[j];
+            ++pa;
+          } else if (valid & (kk[j] == thr)) {
+            if (pq < remaining) {
+              sm.out_idx[tie_base + pq] = i0 + j;
+              sm.out_key[tie_base + pq] = kk[j];
+            }
+            ++pq;
+          }
+        }
+      } else {
+        int pq = tie_pos + (ex >> 16);
+        uint32_t sel = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const bool valid = (vv >> j) & 1u;
+          const bool a = valid & (kk[j] > thr);
+          const bool t = valid & (kk[j] == thr);
+          if (a | (t & (pq < remaining))) sel |= 1u << j;
+          pq += t;
+        }
+        const int ns = __popc(sel);
+        int sinc = ns;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int y = __shfl_up_sync(0xffffffffu, sinc, o);
+          if (lane >= o) sinc += y;
+        }
+        const int stot = __shfl_sync(0xffffffffu, sinc, 31);
+        int ps = sel_pos + sinc - ns;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if ((sel >> j) & 1u) {
+            sm.out_idx[ps] = i0 + j;
+            sm.out_key[ps] = kk[j];
+            ++ps;
+          }
+        }
+        sel_pos += stot;
+      }
+      above_pos += total & 0xFFFF;
+      tie_pos += total >> 16;
+    }
+  }
+  __syncthreads();
+  for (int i = tid; i < kTopK; i += kTkThreads) {
+    out[i] = src[sm.out_idx[i]];
+    if (dst_keys) dst_keys[static_cast<int64_t>(row) * kTopK + i] = sm.out_key[i];
+  }
+}
+#undef TK_FOR_EACH
+
+// ---------------------------------------------------------------------------
+// Pass 1 as its own kernels (used by hcu_mqa_logits_hist when hist_lens is
+// given): workspace zws = [ghist1 rows*4096 | ghist2 rows*4096 | cnt rows*2],
+// the contract of hcu_ops/csrc/mqa_hist.cu:219-226,253-303 of the reference.
+// ---------------------------------------------------------------------------
+constexpr int kHistThreads = 512;
+constexpr int kHistChunk = 16384;
+
+__global__ __launch_bounds__(256) void hist_init_kernel(int32_t* __restrict__ zws, const int32_t* __restrict__ hist_lens,
+                                                       int width, int rows) {
+  const int row = blockIdx.x;
+  int h = hist_lens[row];
+  h = h < width ? h : width;
+  const int zeros = h > kTopK ? h : 0;
+  int4* g1 = reinterpret_cast<int4*>(zws + static_cast<int64_t>(row) * kBins);
+  int4* g2 = reinterpret_cast<int4*>(zws + static_cast<int64_t>(rows + row) * kBins);
+  for (int i = threadIdx.x; i < kBins / 4; i += blockDim.x) {
+    g1[i] = make_int4(i == kZeroBin / 4 ? zeros : 0, 0, 0, 0);
+    g2[i] = make_int4(0, 0, 0, 0);
+  }
+  if (threadIdx.x == 0) {
+    int32_t* cnt = zws + 2 * static_cast<int64_t>(rows) * kBins + 2 * row;
+    cnt[0] = 0;
+    cnt[1] = zeros;
+  }
+}
+
+__global__ __launch_bounds__(kHistThreads) void pass1_hist_kernel(const float* __restrict__ score,
+                                                                  int64_t score_stride, int width,
+                                                                  const int16_t* __restrict__ mask,
+                                                                  int64_t mask_stride,
+                                                                  const int32_t* __restrict__ hist_lens,
+                                                                  int32_t* __restrict__ zws, int rows) {
+  __shared__ int sh[kBins];
+  __shared__ int s_cnt[2];
+  const int row = blockIdx.y;
+  int h = hist_lens[row];
+  h = h < width ? h : width;
+  if (h <= kTopK) return;
+  const int begin = blockIdx.x * kHistChunk;
+  if (begin >= h) return;
+  const int end = min(begin + kHistChunk, h);
+  for (int i = threadIdx.x; i < kBins; i += kHistThreads) sh[i] = 0;
+  if (threadIdx.x < 2) s_cnt[threadIdx.x] = 0;
+  __syncthreads();
+  const float* vals = score + static_cast<int64_t>(row) * score_stride;
+  const int16_t* mrow = mask + static_cast<int64_t>(row) * mask_stride;
+  int nz = 0, pos = 0;
+  for (int i = begin + threadIdx.x; i < end; i += kHistThreads) {
+    const bool set = (static_cast<uint16_t>(__ldg(mrow + (i >> 4))) >> (i & 15)) & 1u;
+    if (set) {
+      const uint32_t key = to_key(__ldg(vals + i));
+      atomicAdd(&sh[key >> 20], 1);
+      ++nz;
+      pos += key > kZeroKey;
+    }
+  }
+  nz = warp_sum(nz);
+  pos = warp_sum(pos);
+  if ((threadIdx.x & 31) == 0) {
+    if (nz) atomicAdd(&s_cnt[0], nz);
+    if (pos) atomicAdd(&s_cnt[1], pos);
+  }
+  __syncthreads();
+  int32_t* g1 = zws + static_cast<int64_t>(row) * kBins;
+  for (int i = threadIdx.x; i < kBins; i += kHistThreads)
+    if (sh[i]) atomicAdd(&g1[i], sh[i]);
+  if (threadIdx.x == 0) {
+    int32_t* cnt = zws + 2 * static_cast<int64_t>(rows) * kBins + 2 * row;
+    if (s_cnt[0]) {
+      atomicSub(&g1[kZeroBin], s_cnt[0]);
+      atomicSub(&cnt[1], s_cnt[0]);
+    }
+    if (s_cnt[1]) atomicAdd(&cnt[0], s_cnt[1]);
+  }
+}
+
+bool use_vec(const float* score, int64_t width, int64_t stride) {
+  return width % 4 == 0 && stride % 4 == 0 && reinterpret_cast<uintptr_t>(score) % 16 == 0;
+}
+
+int check_common(const float* score, int64_t rows, int64_t width, int64_t score_stride, const int16_t* mask,
+                 int64_t mask_stride, const int32_t* lengths, const int32_t* pt, int64_t pt_stride, int64_t topk,
+                 const int32_t* dst) {
+  if (topk != kTopK) return HCU_ERR_ARG;
+  if (rows < 0 || width < 0 || width > INT32_MAX / 2 || rows > INT32_MAX) return HCU_ERR_ARG;
+  if (rows == 0) return HCU_OK;
+  if (!score || !mask || !lengths || !pt || !dst) return HCU_ERR_ARG;
+  if (score_stride < width || mask_stride < (width + 15) / 16 || pt_stride < 1) return HCU_ERR_ARG;
+  return HCU_OK;
+}
+
+template <bool kVec, bool kSorted>
+void launch_rows_t(const float* score, int rows, int width, int64_t score_stride, const int16_t* mask,
+                   int64_t mask_stride, const int32_t* lengths, const int32_t* pt, int64_t pt_stride, int32_t* dst,
+                   uint32_t* dst_keys, const int32_t* pre_ws, cudaStream_t stream) {
+  const size_t smem = sizeof(TopkSmem);
+  cudaFuncSetAttribute(topk_row_kernel<kVec, kSorted>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       static_cast<int>(smem));
+  topk_row_kernel<kVec, kSorted><<<rows, kTkThreads, smem, stream>>>(score, score_stride, width, mask, mask_stride,
+                                                                    lengths, pt, pt_stride, dst, dst_keys, pre_ws,
+                                                                    rows);
+}
+
+int launch_rows(const float* score, int64_t rows, int64_t width, int64_t score_stride, const int16_t* mask,
+                int64_t mask_stride, const int32_t* lengths, const int32_t* pt, int64_t pt_stride, int32_t* dst,
+                uint32_t* dst_keys, const int32_t* pre_ws, cudaStream_t stream, bool sorted = false) {
+  const int w = static_cast<int>(width);
+  const int r = static_cast<int>(rows);
+  const bool vec = use_vec(score, width, score_stride);
+  if (vec && !sorted)
+    launch_rows_t<true, false>(score, r, w, score_stride, mask, mask_stride, lengths, pt, pt_stride, dst, dst_keys,
+                               pre_ws, stream);
+  else if (vec)
+    launch_rows_t<true, true>(score, r, w, score_stride, mask, mask_stride, lengths, pt, pt_stride, dst, dst_keys,
+                              pre_ws, stream);
+  else if (!sorted)
+    launch_rows_t<false, false>(score, r, w, score_stride, mask, mask_stride, lengths, pt, pt_stride, dst, dst_keys,
+                                pre_ws, stream);
+  else
+    launch_rows_t<false, true>(score, r, w, score_stride, mask, mask_stride, lengths, pt, pt_stride, dst, dst_keys,
+                               pre_ws, stream);
+  return launch_status();
+}
+
+}  // namespace
+
+// Used by the logits translation unit for the hist_lens path.
+int launch_pass1_hist(const float* logits, int64_t rows, int64_t width, const int16_t* mask, int64_t mask_stride,
+                      const int32_t* hist_lens, int32_t* zws, cudaStream_t stream) {
+  if (rows == 0) return HCU_OK;
+  hist_init_kernel<<<static_cast<int>(rows), 256, 0, stream>>>(zws, hist_lens, static_cast<int>(width),
+                                                              static_cast<int>(rows));
+  const dim3 grid(static_cast<unsigned>((width + kHistChunk - 1) / kHistChunk), static_cast<unsigned>(rows));
+  pass1_hist_kernel<<<grid, kHistThreads, 0, stream>>>(logits, width, static_cast<int>(width), mask, mask_stride,
+                                                      hist_lens, zws, static_cast<int>(rows));
+  return launch_status();
+}
+
+}  // namespace hcu
+
+extern "C" int64_t hcu_topk_hist_ws_elems(int64_t rows) { return rows * (2 * hcu::kBins + 2); }
+
+extern "C" int64_t hcu_topk_workspace_bytes(int64_t rows, int64_t width, int64_t max_splits) {
+  (void)rows;
+  (void)width;
+  (void)max_splits;
+  return 0;  // the single-CTA-per-row kernel keeps all state in shared memory
+}
+
+extern "C" int hcu_sparse_mask_topk_transform(const float* score, int64_t rows, int64_t width, int64_t score_stride,
+                                              const int16_t* mask, int64_t mask_stride, const int32_t* lengths,
+                                              const int32_t* page_table, int64_t pt_stride, int64_t topk,
+                                              int32_t* dst, hcu_stream_t stream) {
+  using namespace hcu;
+  int st = check_common(score, rows, width, score_stride, mask, mask_stride, lengths, page_table, pt_stride, topk,
+                        dst);
+  if (st != HCU_OK || rows == 0) return st;
+  return launch_rows(score, rows, width, score_stride, mask, mask_stride, lengths, page_table, pt_stride, dst,
+                     nullptr, nullptr, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int hcu_sparse_mask_topk_transform_split(const float* score, int64_t rows, int64_t width,
+                                                    int64_t score_stride, const int16_t* mask, int64_t mask_stride,
+                                                    const int32_t* lengths, const int32_t* page_table,
+                                                    int64_t pt_stride, int64_t topk, int64_t max_splits,
+                                                    void* workspace, int64_t workspace_bytes, int32_t* dst,
+                                                    hcu_stream_t stream) {
+  using namespace hcu;
+  (void)workspace;
+  (void)workspace_bytes;
+  if (max_splits < 1) return HCU_ERR_ARG;
+  int st = check_common(score, rows, width, score_stride, mask, mask_stride, lengths, page_table, pt_stride, topk,
+                        dst);
+  if (st != HCU_OK || rows == 0) return st;
+  return launch_rows(score, rows, width, score_stride, mask, mask_stride, lengths, page_table, pt_stride, dst,
+                     nullptr, nullptr, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int hcu_sparse_mask_topk_transform_split_pre(const float* score, int64_t rows, int64_t width,
+                                                        int64_t score_stride, const int16_t* mask,
+                                                        int64_t mask_stride, const int32_t* lengths,
+                                                        const int32_t* page_table, int64_t pt_stride, int64_t topk,
+                                                        int64_t max_splits, int32_t* zws, void* workspace,
+                                                        int64_t workspace_bytes, int32_t* dst,
+                                                        hcu_stream_t stream) {
+  using namespace hcu;
+  (void)workspace;
+  (void)workspace_bytes;
+  if (max_splits < 1 || zws == nullptr) return HCU_ERR_ARG;
+  int st = check_common(score, rows, width, score_stride, mask, mask_stride, lengths, page_table, pt_stride, topk,
+                        dst);
+  if (st != HCU_OK || rows == 0) return st;
+  return launch_rows(score, rows, width, score_stride, mask, mask_stride, lengths, page_table, pt_stride, dst,
+                     nullptr, zws, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int hcu_topk_keys(const float* score, int64_t rows, int64_t width, int64_t score_stride,
+                             const int16_t* mask, int64_t mask_stride, const int32_t* lengths,
+                             const int32_t* page_table, int64_t pt_stride, int32_t* dst, uint32_t* dst_keys,
+                             hcu_stream_t stream) {
+  using namespace hcu;
+  int st = check_common(score, rows, width, score_stride, mask, mask_stride, lengths, page_table, pt_stride, kTopK,
+                        dst);
+  if (st != HCU_OK || rows == 0) return st;
+  if (!dst_keys) return HCU_ERR_ARG;
+  return launch_rows(score, rows, width, score_stride, mask, mask_stride, lengths, page_table, pt_stride, dst,
+                     dst_keys, nullptr, reinterpret_cast<cudaStream_t>(stream), /*sorted=*/true);
+}

@@ -1,0 +1,189 @@
+"""B200 (sm_100a) DSA lightning-indexer ops for sglang's dsa_indexer / dsa_indexer_metadata.
+
+Drop-in for the indexer part of the reference package ``hcu_ops``
+(``hcu_ops/hcu_ops/__init__.py:1-105`` of charliedhw/sglang0.5.18-opt): the same
+public functions (``sparse_mask_topk_transform``, ``mqa_logits_supported``,
+``mqa_logits``), the same ``_C`` op names and layouts, the same environment
+switches read once at import, and the same hand-off of the fused pass-1
+histogram from ``mqa_logits`` to the next ``sparse_mask_topk_transform``.
+Added: the paged K-cache dequant drop-in, the indexer-K dequant, ragged
+(prefill) logits, top-k with keys and the context-parallel merge.
+
+All compute runs in ``libhcu_indexer.so`` (hand-written CUDA for sm_100a)
+behind ``_C``.  There is no fallback: importing this package fails if the
+extension has not been built (``python build.py`` next to this package).
+"""
+import os
+
+import torch  # noqa: F401  (loads libtorch before the extension)
+
+from . import _C  # noqa: E402  -- ImportError here means the CUDA library is not built
+
+# --------------------------------------------------------------------------- switches
+# Call-site switches of the reference's sglang hooks (read by the integration
+# layer; kept with the reference's names and defaults).
+SGLANG_HCU_MQA_LOGITS = os.environ.get("SGLANG_HCU_MQA_LOGITS", "0") == "1"
+SGLANG_HCU_MQA_HIST = os.environ.get("SGLANG_HCU_MQA_HIST", "0") == "1"
+SGLANG_HCU_FAST_MASK_TOPK = os.environ.get("SGLANG_HCU_FAST_MASK_TOPK", "1") == "1"
+SGLANG_DSA_FAST_DEQUANT_PAGED = os.environ.get("SGLANG_DSA_FAST_DEQUANT_PAGED", "0") == "1"
+SGLANG_DSA_FAST_DEQUANT_TOKENS = int(os.environ.get("SGLANG_DSA_FAST_DEQUANT_TOKENS", "8"))
+SGLANG_DSA_FAST_DEQUANT_WARPS = int(os.environ.get("SGLANG_DSA_FAST_DEQUANT_WARPS", "4"))
+
+# split: few rows are spread over up to HCU_TOPK_SPLITS CTAs each; single: 1 CTA per row
+_TOPK_IMPL = os.environ.get("HCU_TOPK_IMPL", "split")
+_TOPK_SPLITS = int(os.environ.get("HCU_TOPK_SPLITS", "8"))
+
+# Logits tuning knobs of the reference API.  The B200 kernel schedules its
+# persistent CTAs from the SM count and the lengths on the device, so
+# persistent_ctas / rows_per_cta are accepted as hints only.
+_MQA_PCTAS = int(os.environ.get("HCU_MQA_PCTAS", "-1"))
+_MQA_PCTAS_G1 = int(os.environ.get("HCU_MQA_PCTAS_G1", str(_MQA_PCTAS)))
+_MQA_RPC = int(os.environ.get("HCU_MQA_RPC", "3"))
+_MQA_HIST_MAX_ROWS = int(os.environ.get("HCU_MQA_HIST_MAX_ROWS", "8"))
+_MQA_HIST_MAX_ROWS_G6 = int(os.environ.get("HCU_MQA_HIST_MAX_ROWS_G6", "0"))
+_MQA_HIST = None  # (logits, hist_lens, zws) of the last mqa_logits with a fused histogram
+_N_CU = None
+
+SUPPORTED_HEADS = (32, 64)
+
+
+def _topk_splits(rows, width):
+    """Splits sparse_mask_topk_transform_split uses for [rows, width] scores
+    (``hcu_ops/hcu_ops/__init__.py:52-57`` of the reference)."""
+    global _N_CU
+    if _N_CU is None:
+        _N_CU = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    return min(max((width + 8191) // 8192, 1), _N_CU // max(rows, 1), min(_TOPK_SPLITS, 64))
+
+
+def sparse_mask_topk_transform(score, nonzero_mask, lengths, page_table_size_1, cu_seqlens_q, topk=2048):
+    """Exact top-2048 + page-table transform (drop-in for lightop
+    fast_topk_transform_sparse_mask_fused; ``__init__.py:15-32`` of the reference).
+
+    Consumes the pass-1 histogram of the preceding ``mqa_logits(..., hist_lens=lengths)``
+    when it was built for this very ``score`` and ``lengths``."""
+    global _MQA_HIST
+    st = _MQA_HIST
+    if st is not None:
+        _MQA_HIST = None
+        if st[0] is score and st[1].data_ptr() == lengths.data_ptr() and st[1].shape == lengths.shape:
+            return _C.sparse_mask_topk_transform_split_pre(score, nonzero_mask, lengths, page_table_size_1,
+                                                           cu_seqlens_q, topk, _TOPK_SPLITS, st[2])
+    if _TOPK_IMPL == "single":
+        return _C.sparse_mask_topk_transform(score, nonzero_mask, lengths, page_table_size_1, cu_seqlens_q, topk)
+    return _C.sparse_mask_topk_transform_split(score, nonzero_mask, lengths, page_table_size_1, cu_seqlens_q,
+                                               topk, _TOPK_SPLITS)
+
+
+def mqa_logits_supported(q, kv_cache, weights, group_size, context_lens=None, block_table=None,
+                         max_context_len=None):
+    """Whether mqa_logits takes these operands (else the caller keeps its other path).
+
+    Same contract as ``__init__.py:60-79`` of the reference, widened to 32 or 64
+    index heads and any group size that divides the batch."""
+    b = q.shape[0] if q.dim() == 4 else 0
+    h = q.shape[2] if q.dim() == 4 else 0
+    ok = (q.dtype == torch.float8_e4m3fn and q.dim() == 4 and h in SUPPORTED_HEADS
+          and tuple(q.shape[1:]) == (1, h, 128) and b > 0 and q.is_contiguous()
+          and weights.dtype == torch.float32 and tuple(weights.shape) == (b, h) and weights.is_contiguous()
+          and kv_cache.dtype == torch.uint8 and kv_cache.dim() == 4
+          and tuple(kv_cache.shape[1:]) == (64, 1, 132) and kv_cache.stride(1) == 132
+          and kv_cache.stride(3) == 1 and kv_cache.stride(0) % 16 == 0
+          and group_size >= 1 and b % group_size == 0)
+    if ok and context_lens is not None:
+        ok = (context_lens.dtype == torch.int32 and context_lens.numel() == b and context_lens.is_contiguous())
+    if ok and block_table is not None:
+        ok = (block_table.dtype == torch.int32 and block_table.dim() == 2 and block_table.shape[0] == b
+              and block_table.stride(1) == 1
+              and (max_context_len is None or max_context_len == block_table.shape[1] * 64))
+    return ok
+
+
+def mqa_logits(q, kv_cache, weights, context_lens, block_table, max_context_len, group_size,
+               hist_lens=None, persistent_ctas=None, rows_per_cta=None):
+    """Indexer logits ``(logits [B, max_ctx] f32, mask [B, max_ctx/16] i16)``
+    (``__init__.py:82-105`` of the reference).
+
+    Logits hold ``(sum_h w[h] relu(q_h . k)) * k_scale`` where the mask bit is
+    set (token < length and the value is not +0) and are unwritten elsewhere.
+    hist_lens: lengths of the paired sparse_mask_topk_transform; when that call
+    will split rows, its pass-1 histogram is built here and consumed by it."""
+    global _MQA_HIST
+    rows = q.shape[0]
+    if persistent_ctas is None:
+        persistent_ctas = _MQA_PCTAS_G1 if group_size == 1 else _MQA_PCTAS
+    if rows_per_cta is None:
+        rows_per_cta = 1 if group_size == 1 else _MQA_RPC
+    if rows_per_cta <= 0 or group_size % rows_per_cta:
+        rows_per_cta = 0
+    hist_max_rows = _MQA_HIST_MAX_ROWS if group_size == 1 else _MQA_HIST_MAX_ROWS_G6
+    use_hist = (hist_lens is not None and _TOPK_IMPL == "split" and rows <= hist_max_rows
+                and hist_lens.dtype == torch.int32 and hist_lens.dim() == 1
+                and hist_lens.shape[0] == rows and hist_lens.is_contiguous()
+                and _topk_splits(rows, max_context_len) > 1)
+    logits, mask, zws = _C.mqa_logits_hist(q, kv_cache, weights, context_lens.view(-1), block_table,
+                                           max_context_len, group_size, persistent_ctas, rows_per_cta,
+                                           hist_lens if use_hist else None)
+    _MQA_HIST = (logits, hist_lens, zws) if use_hist else None
+    return logits, mask
+
+
+# --------------------------------------------------------------------------- dequant
+def dequantize_k_cache_paged(quant_k_cache, page_table_1_flattened, group_size: int = 128):
+    """MLA 656-byte slot paged dequant -> bf16 ``[n, 1, 576]``.
+
+    The arithmetic of ``prefill/patches/patch_fast_dequant.py:45-98`` (fp32
+    multiply by the group scale, one round-to-nearest-even to bf16, rope copied
+    raw).  Only the 656-byte / group-128 layout exists here; for anything else
+    use ``make_dequantize_k_cache_paged`` with sglang's original as fallback."""
+    if group_size != 128 or quant_k_cache.shape[-1] != 656:
+        raise NotImplementedError("hcu_ops dequant supports the 656-byte slot with group_size=128 only")
+    return _C.dequantize_k_cache_paged(quant_k_cache, page_table_1_flattened)
+
+
+def make_dequantize_k_cache_paged(original):
+    """The patched sglang ``dequantize_k_cache_paged``: ours when
+    SGLANG_DSA_FAST_DEQUANT_PAGED=1 and the layout is the 656-byte slot, else
+    ``original`` (the switch and fallback rule of ``patch_fast_dequant.py:74-84``)."""
+
+    def dequantize_k_cache_paged_hcu(quant_k_cache, page_table_1_flattened, group_size: int = 128):
+        if not SGLANG_DSA_FAST_DEQUANT_PAGED or group_size != 128 or quant_k_cache.shape[-1] != 656:
+            return original(quant_k_cache, page_table_1_flattened, group_size)
+        return _C.dequantize_k_cache_paged(quant_k_cache, page_table_1_flattened)
+
+    return dequantize_k_cache_paged_hcu
+
+
+def dequant_index_k_paged(kv_cache, token_loc):
+    """Indexer-K pages ``[blocks, 64, 1, 132]`` gathered at ``token_loc`` -> bf16 ``[n, 128]``."""
+    return _C.dequant_index_k_paged(kv_cache, token_loc)
+
+
+# --------------------------------------------------------------------------- prefill / CP
+def mqa_logits_ragged(q, k_fp8, k_scale, weights, row_start, row_end):
+    """Prefill logits: row r over tokens ``[row_start[r], row_end[r])`` of a contiguous fp8 K.
+
+    Returns ``(logits [rows, n_tokens] f32, mask [rows, ceil(n_tokens/16)] i16)``
+    with the ``mqa_logits`` contract (logits valid only at set mask bits)."""
+    return _C.mqa_logits_ragged(q, k_fp8, k_scale, weights, row_start, row_end)
+
+
+def topk_keys(score, nonzero_mask, lengths, page_table):
+    """Top-2048 through ``page_table`` plus the selected uint32 keys, in ascending token order."""
+    return _C.topk_keys(score, nonzero_mask, lengths, page_table)
+
+
+def cp_topk_merge(keys, gidx, lengths):
+    """Merge per-range (key, global index) lists ``[P, rows, 2048]`` into the global top-2048.
+
+    ``lengths``: total visible tokens per row (selects index order for rows of at most 2048)."""
+    return _C.cp_topk_merge(keys, gidx, lengths)
+
+
+def read_device_status(clear=True):
+    """Sticky device status bits (1: a bounded wait expired, 2: an out-of-range index was skipped)."""
+    return _C.read_device_status(clear)
+
+
+def library_path():
+    return os.path.join(os.path.dirname(os.path.abspath(__file__)), "libhcu_indexer.so")

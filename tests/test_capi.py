@@ -1,0 +1,92 @@
+"""CPU checks of the C ABI: the library loads, exports every symbol the header declares, and
+rejects bad arguments before launching anything (no GPU needed)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(REPO, "include", "hcu_indexer.h")
+LIB = os.path.join(REPO, "sglang0.5.18-opt_b200", "hcu_ops", "libhcu_indexer.so")
+
+HCU_OK, HCU_ERR_ARG, HCU_ERR_UNSUPPORTED = 0, 1, 4
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return re.findall(r"^(?:const char\*|int64_t|int)\s+(hcu_\w+)\(", text, re.M)
+
+
+@pytest.fixture(scope="module")
+def lib():
+    return ctypes.CDLL(LIB)
+
+
+def test_every_declared_symbol_is_exported(lib):
+    names = declared_symbols()
+    assert len(names) >= 14
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_version(lib):
+    lib.hcu_version.restype = ctypes.c_char_p
+    assert b"sm_100a" in lib.hcu_version()
+
+
+def test_workspace_queries(lib):
+    lib.hcu_topk_hist_ws_elems.restype = ctypes.c_int64
+    lib.hcu_topk_hist_ws_elems.argtypes = [ctypes.c_int64]
+    assert lib.hcu_topk_hist_ws_elems(3) == 3 * (2 * 4096 + 2)
+    lib.hcu_topk_workspace_bytes.restype = ctypes.c_int64
+    lib.hcu_topk_workspace_bytes.argtypes = [ctypes.c_int64] * 3
+    assert lib.hcu_topk_workspace_bytes(4, 65536, 8) >= 0
+
+
+def _topk_args(topk=2048, rows=1, width=4096):
+    p = ctypes.c_void_p(16)  # never dereferenced: validation fails or rows == 0 first
+    return [p, ctypes.c_int64(rows), ctypes.c_int64(width), ctypes.c_int64(width), p,
+            ctypes.c_int64((width + 15) // 16), p, p, ctypes.c_int64(width), ctypes.c_int64(topk), p, None]
+
+
+def test_topk_rejects_bad_topk_and_accepts_empty(lib):
+    f = lib.hcu_sparse_mask_topk_transform
+    f.restype = ctypes.c_int
+    assert f(*_topk_args(topk=100)) == HCU_ERR_ARG
+    assert f(*_topk_args(rows=0)) == HCU_OK
+    a = _topk_args()
+    a[0] = None  # null score
+    assert f(*a) == HCU_ERR_ARG
+
+
+def test_logits_rejects_unsupported_heads_and_bad_shapes(lib):
+    f = lib.hcu_mqa_logits_hist
+    f.restype = ctypes.c_int
+    p = ctypes.c_void_p(16)
+    i64 = ctypes.c_int64
+
+    def call(heads=64, batch=2, G=1, maxctx=4096, page_stride=8448):
+        return f(p, i64(batch), i64(heads), p, i64(100), i64(page_stride), p, p, p, i64(maxctx // 64), i64(maxctx),
+                 i64(G), i64(0), i64(0), None, p, p, None, None)
+
+    assert call(heads=48) == HCU_ERR_UNSUPPORTED
+    assert call(batch=3, G=2) == HCU_ERR_ARG
+    assert call(maxctx=100) == HCU_ERR_ARG
+    assert call(page_stride=8440) == HCU_ERR_ARG
+
+
+def test_dequant_rejects_unaligned_stride(lib):
+    f = lib.hcu_dequant_k_cache_paged
+    f.restype = ctypes.c_int
+    p = ctypes.c_void_p(16)
+    assert f(p, ctypes.c_int64(10), ctypes.c_int64(650), p, ctypes.c_int64(4), p, None) == HCU_ERR_ARG
+    assert f(p, ctypes.c_int64(10), ctypes.c_int64(656), p, ctypes.c_int64(0), p, None) == HCU_OK
+
+
+def test_merge_rejects_too_many_parts(lib):
+    f = lib.hcu_cp_topk_merge
+    f.restype = ctypes.c_int
+    p = ctypes.c_void_p(16)
+    assert f(p, p, ctypes.c_int64(17), ctypes.c_int64(4), p, p, None) == HCU_ERR_ARG
+    assert f(p, p, ctypes.c_int64(2), ctypes.c_int64(0), p, p, None) == HCU_OK
