@@ -3,8 +3,16 @@
 // topk_row_kernel: one 1024-thread CTA (32 warps) per row.  Warp w owns the
 // contiguous token segment [w*seg, (w+1)*seg) of the row (seg a multiple of
 // 128 = 32 lanes x 4 tokens), so the final compaction only needs per-warp
-// counts and an in-warp prefix -- no block-wide scan per chunk.  Passes over
-// the row (the row stays L2-resident between passes):
+// counts and an in-warp prefix -- no block-wide scan per chunk.
+// Threshold search, normally two streaming passes in total:
+//   S  4096 strided samples; a radix select of two sample order statistics
+//      around the threshold's expected sample rank (+-4 sigma) gives [lo, hi]
+//   1  one pass counts keys > hi, == hi, == lo per warp and collects the keys
+//      strictly inside (lo, hi) (a few % of the row) in shared memory; the
+//      threshold is hi, lo, or an exact radix select among the collected keys
+//   D  the ordered compaction below.
+// When the bracket misses (it cannot change the result, only the cost), the
+// full radix passes run instead (the row stays L2-resident between passes):
 //   A  12-bit histogram of key[31:20] + per-warp positive / zero counts
 //      (skipped when the logits kernel already built it: the "pre" path);
 //      positives <= 2048 <= positives + zeros -> the threshold is +0 (fast path)
@@ -29,16 +37,28 @@ constexpr int kStep = 128;  // tokens per warp step (32 lanes x 4)
 constexpr int kTkUnroll = 4;
 constexpr int kHistTrash = kTkWarps * 256;  // trash slots follow the per-warp histograms
 
+constexpr int kSample = 4096;   // row samples used to bracket the threshold
+constexpr int kMidCap = 8192;   // keys collected strictly inside the bracket
+
 struct __align__(16) TopkSmem {
   int hist[kTkWarps * 256 + 32 + 256];  // A/B: [0,4096) + trash; C: 32 x 256 + trash + merged[256]
   int out_idx[kTopK + 32];
   uint32_t out_key[kTopK + 32];
+  uint32_t samp[kSample];
+  uint32_t mid_key[kMidCap];
+  uint8_t mid_warp[kMidCap];
   int above[kTkWarps];
   int ties[kTkWarps];
   int zeros[kTkWarps];
   int pos[kTkWarps];
+  int gt_w[kTkWarps];
+  int eh_w[kTkWarps];
+  int el_w[kTkWarps];
+  int mid_above_w[kTkWarps];
+  int mid_tie_w[kTkWarps];
   int wtot[kTkWarps];
   int res[4];
+  int mid_n;
 };
 
 __device__ __forceinline__ int warp_sum(int x) {
@@ -117,6 +137,46 @@ __device__ __forceinline__ void find_threshold(const int* hist, int need, int* w
   __syncthreads();
 }
 
+// Key of rank `rank` (1 = largest) among keys[0, n) in shared memory, by a
+// 12/12/8-bit radix select; *above = number of keys strictly greater than it.
+// Requires 1 <= rank <= n.  Block-wide; uses sm.hist / sm.wtot / sm.res.
+__device__ __forceinline__ uint32_t smem_select_rank(const uint32_t* keys, int n, int rank, TopkSmem& sm,
+                                                     int* above) {
+  const int tid = threadIdx.x;
+  int need = rank;
+  int abv = 0;
+  for (int i = tid; i < kBins; i += kTkThreads) sm.hist[i] = 0;
+  __syncthreads();
+  for (int i = tid; i < n; i += kTkThreads) atomicAdd(&sm.hist[keys[i] >> 20], 1);
+  __syncthreads();
+  find_threshold<kBins>(sm.hist, need, sm.wtot, sm.res);
+  const uint32_t b1 = static_cast<uint32_t>(sm.res[0]);
+  abv += sm.res[1];
+  need -= sm.res[1];
+  for (int i = tid; i < kBins; i += kTkThreads) sm.hist[i] = 0;
+  __syncthreads();
+  for (int i = tid; i < n; i += kTkThreads) {
+    const uint32_t k = keys[i];
+    if ((k >> 20) == b1) atomicAdd(&sm.hist[(k >> 8) & 0xFFFu], 1);
+  }
+  __syncthreads();
+  find_threshold<kBins>(sm.hist, need, sm.wtot, sm.res);
+  const uint32_t p24 = (b1 << 12) | static_cast<uint32_t>(sm.res[0]);
+  abv += sm.res[1];
+  need -= sm.res[1];
+  for (int i = tid; i < 256; i += kTkThreads) sm.hist[i] = 0;
+  __syncthreads();
+  for (int i = tid; i < n; i += kTkThreads) {
+    const uint32_t k = keys[i];
+    if ((k >> 8) == p24) atomicAdd(&sm.hist[k & 0xFFu], 1);
+  }
+  __syncthreads();
+  find_threshold<256>(sm.hist, need, sm.wtot, sm.res);
+  abv += sm.res[1];
+  *above = abv;
+  return (p24 << 8) | static_cast<uint32_t>(sm.res[0]);
+}
+
 // Visits every token slot of this warp's segment as (valid, key, index i0+j).
 #define TK_FOR_EACH(BODY)                                                             \
   for (int c = seg_begin; c < seg_end; c += kStep * kTkUnroll) {                      \
@@ -175,6 +235,107 @@ __global__ __launch_bounds__(kTkThreads, 1) void topk_row_kernel(
   const int seg_end = min(seg_begin + seg, len);
   const int trash = kBins + lane;
 
+  uint32_t thr = 0;
+  int remaining = 0;
+  bool resolved = false;
+  if (pre_ws == nullptr) {
+    // ---- bracket select: sample -> [lo, hi] -> one counting pass -> exact select inside ----
+    const int m = len < kSample ? len : kSample;
+    for (int k = tid; k < m; k += kTkThreads) {
+      const int i = static_cast<int>((static_cast<int64_t>(k) * len) / m);
+      const bool set = (static_cast<uint16_t>(__ldg(mrow + (i >> 4))) >> (i & 15)) & 1u;
+      sm.samp[k] = set ? to_key(__ldg(vals + i)) : kZeroKey;
+    }
+    if (tid == 0) sm.mid_n = 0;
+    __syncthreads();
+    int r_hi = kTopK, r_lo = kTopK;
+    if (m < len) {  // expected sample rank of the threshold +- 4 sigma
+      const float t = static_cast<float>(kTopK) * static_cast<float>(m) / static_cast<float>(len);
+      const float d = 4.f * sqrtf(t) + 4.f;
+      r_hi = max(1, static_cast<int>(floorf(t - d)));
+      r_lo = min(m, static_cast<int>(ceilf(t + d)));
+    }
+    int dummy;
+    const uint32_t hi = smem_select_rank(sm.samp, m, r_hi, sm, &dummy);
+    const uint32_t lo = r_lo == r_hi ? hi : smem_select_rank(sm.samp, m, r_lo, sm, &dummy);
+    {
+      int n_gt = 0, n_eh = 0, n_el = 0;
+      TK_FOR_EACH({
+        n_gt += valid & (key > hi);
+        n_eh += valid & (key == hi);
+        n_el += valid & (key == lo) & (lo != hi);
+        const bool mid = valid & (key > lo) & (key < hi);
+        const uint32_t mb = __ballot_sync(0xffffffffu, mid);
+        if (mb) {
+          int base = 0;
+          if (lane == 0) base = atomicAdd(&sm.mid_n, __popc(mb));
+          base = __shfl_sync(0xffffffffu, base, 0);
+          if (mid) {
+            const int pos = base + __popc(mb & ((1u << lane) - 1u));
+            if (pos < kMidCap) {
+              sm.mid_key[pos] = key;
+              sm.mid_warp[pos] = static_cast<uint8_t>(w);
+            }
+          }
+        }
+      })
+      n_gt = warp_sum(n_gt);
+      n_eh = warp_sum(n_eh);
+      n_el = warp_sum(n_el);
+      if (lane == 0) {
+        sm.gt_w[w] = n_gt;
+        sm.eh_w[w] = n_eh;
+        sm.el_w[w] = n_el;
+        sm.mid_above_w[w] = 0;
+        sm.mid_tie_w[w] = 0;
+      }
+    }
+    __syncthreads();
+    int G = 0, EH = 0, EL = 0;
+    for (int v = 0; v < kTkWarps; ++v) {
+      G += sm.gt_w[v];
+      EH += sm.eh_w[v];
+      EL += sm.el_w[v];
+    }
+    const int M = sm.mid_n;
+    int mode = 0;  // 0: bracket missed -> full radix below
+    if (G < kTopK) {
+      if (G + EH >= kTopK) {
+        mode = 1;
+        thr = hi;
+        remaining = kTopK - G;
+      } else if (M <= kMidCap && G + EH + M >= kTopK) {
+        mode = 2;
+      } else if (M <= kMidCap && G + EH + M + EL >= kTopK) {
+        mode = 3;
+        thr = lo;
+        remaining = kTopK - (G + EH + M);
+      }
+    }
+    if (mode == 2) {
+      const int need = kTopK - G - EH;
+      int abv = 0;
+      thr = smem_select_rank(sm.mid_key, M, need, sm, &abv);
+      remaining = need - abv;
+    }
+    if (mode != 0) {
+      const int mn = M < kMidCap ? M : kMidCap;
+      for (int i = tid; i < mn; i += kTkThreads) {
+        const uint32_t k = sm.mid_key[i];
+        if (k > thr) atomicAdd(&sm.mid_above_w[sm.mid_warp[i]], 1);
+        else if (k == thr) atomicAdd(&sm.mid_tie_w[sm.mid_warp[i]], 1);
+      }
+      __syncthreads();
+      if (lane == 0) {
+        sm.above[w] = sm.gt_w[w] + (thr < hi ? sm.eh_w[w] : 0) + sm.mid_above_w[w];
+        sm.ties[w] = (thr == hi ? sm.eh_w[w] : 0) + sm.mid_tie_w[w] + ((lo != hi && thr == lo) ? sm.el_w[w] : 0);
+      }
+      __syncthreads();
+      resolved = true;
+    }
+  }
+
+  if (!resolved) {
   // ---- pass A: key[31:20] histogram, positives and zeros ----
   int positives = 0, zeros = 0;
   const int* hist1 = sm.hist;
@@ -209,8 +370,6 @@ __global__ __launch_bounds__(kTkThreads, 1) void topk_row_kernel(
     have_warp_counts = true;
   }
 
-  uint32_t thr;
-  int remaining;
   if (positives <= kTopK && positives + zeros >= kTopK) {
     // Sparse fast path: every positive plus the lowest-index zeros.
     thr = kZeroKey;
@@ -299,6 +458,7 @@ __global__ __launch_bounds__(kTkThreads, 1) void topk_row_kernel(
     }
     __syncthreads();
   }
+  }  // !resolved
   const int tie_base = kTopK - remaining;
 
   // ---- pass D: ordered compaction into shared memory ----

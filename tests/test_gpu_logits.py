@@ -86,16 +86,17 @@ def test_hist_workspace_exact_on_device_logits(hcu, dev):
     assert np.array_equal(z[2 * B * 4096:].reshape(B, 2), cnt)
 
 
-@pytest.mark.parametrize("use_hist", [False, True])
-def test_decode_pipeline(hcu, dev, use_hist):
-    """mqa_logits -> sparse_mask_topk_transform as sglang calls them."""
-    w = _decode(3, 2, [40000, 9000, 3000], 64, seed=5)
+@pytest.mark.parametrize("next_n,use_hist", [(2, False), (2, True), (1, True)])
+def test_decode_pipeline(hcu, dev, next_n, use_hist):
+    """mqa_logits -> sparse_mask_topk_transform as sglang calls them.  The fused pass-1
+    histogram is taken for single rows up to HCU_MQA_HIST_MAX_ROWS (8) rows and, as in the
+    reference, not for grouped rows (HCU_MQA_HIST_MAX_ROWS_G6 = 0)."""
+    w = _decode(3, next_n, [40000, 9000, 3000], 64, seed=5)
     d = _device(w, dev)
     lens = d["context_lens"]
     logits, mask = hcu.mqa_logits(d["q"].contiguous(), d["kv_cache"], d["weights"], lens, d["block_table"],
                                   d["max_context_len"], d["group_size"], hist_lens=lens if use_hist else None)
-    if use_hist:
-        assert hcu._MQA_HIST is not None or hcu._topk_splits(6, d["max_context_len"]) <= 1
+    assert (hcu._MQA_HIST is not None) == (use_hist and next_n == 1)
     out = hcu.sparse_mask_topk_transform(logits, mask, lens, d["page_table_size_1"], d["cu_seqlens_q"], 2048)
     assert hcu._MQA_HIST is None
     got = out.cpu().numpy()
