@@ -15,6 +15,10 @@ void set_last_error(cudaError_t e) {
   std::snprintf(t_last_error, sizeof(t_last_error), "%s: %s", cudaGetErrorName(e), cudaGetErrorString(e));
 }
 
+void set_last_error_msg(const char* a, const char* b) {
+  std::snprintf(t_last_error, sizeof(t_last_error), "%s%s", a, b);
+}
+
 int launch_status() {
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {

@@ -69,14 +69,19 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                : "memory");
 }
 
+// Suspend-time hint of a waiting thread (ns): the hardware parks the warp until
+// the phase completes or the hint elapses, so waiting warps do not spin on the
+// issue slots that the working warps of the same SM sub-partition need.
+constexpr uint32_t kSuspendHintNs = 200000;
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred P;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2, %3;\n\t"
       "selp.b32 %0, 1, 0, P;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
       : "memory");
   return ok != 0;
 }
@@ -266,6 +271,7 @@ __host__ __device__ constexpr uint32_t idesc_e4m3_f32(int M, int N) {
 namespace hcu {
 // Internal host helpers shared by the translation units (capi.cu).
 void set_last_error(cudaError_t e);
+void set_last_error_msg(const char* a, const char* b);
 int launch_status();  // HCU_OK or HCU_ERR_LAUNCH from cudaGetLastError()
 int sm_count();       // SM count of the current device (cached per device)
 cudaError_t status_dequant(uint32_t* out, int clear);

@@ -39,7 +39,7 @@ int launch_pass1_hist(const float* logits, int64_t rows, int64_t width, const in
 
 namespace {
 
-constexpr int kLgThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
+constexpr int kLgThreads = 352;  // warps 0 + 10 TMA, warp 1 MMA, warps 2-9 epilogue
 constexpr int kEpiWarps = 8;
 constexpr int kMaxAcc = 4;     // TMEM accumulator buffers (4 when N <= 128, else 2)
 constexpr int kStages = 8;
@@ -48,7 +48,6 @@ constexpr int kATile = kTileTok * kHeadDim;  // 16 KB
 constexpr int kMaxN = 256;
 constexpr int kQTile = kMaxN * kHeadDim;  // 32 KB
 
-constexpr int kBtWin = 256;  // block-table entries staged in shared memory by the producer warp
 
 struct __align__(1024) LgSmem {
   uint8_t a[kStages][kATile];      // K tile: two 64-token pages, 128-byte swizzled rows
@@ -56,9 +55,11 @@ struct __align__(1024) LgSmem {
   float sc[kStages][2 * kPage];    // k_scale of the stage's two pages
   float w[kEpiWarps][kMaxN];       // head weights, one copy per epilogue warp
   int lens[kEpiWarps][8];          // row lengths of the current row block, per epilogue warp
-  int bt[kBtWin];                  // producer's window of the current group's block-table row
+  int bq_ph[2][32];                // producer batch: page id of page `half` of each item (-1: none)
+  int bq_key[2][32];               // producer batch: (group, row block) key of each item
+  int bq_qrow[2][32];              // producer batch: first Q row of each item's row block
   uint64_t full[kStages];
-  uint64_t empty[kStages];         // 1 MMA commit + 8 epilogue warps (they read sc[] after the MMA)
+  uint64_t empty[kStages];         // 1 MMA commit + the 4 epilogue warps of the tile's team (they read sc[])
   uint64_t qfull[2];
   uint64_t qempty[2];
   uint64_t tfull[kMaxAcc];
@@ -99,27 +100,46 @@ __device__ __forceinline__ int group_tiles(const PagedArgs& p, int g) {
   return (group_len(p, g) + kTileTok - 1) / kTileTok;
 }
 
-// Cursor over this CTA's contiguous range of (group, row block, tile) items.
+// Cursor over this CTA's contiguous range of (group, row block, tile) items,
+// advanced without divisions.  init() positions it just before the first item.
 struct Cursor {
-  int g, li, len, tiles, n_sub;
+  int g, sub, tile, len, tiles, n_sub, n_groups;
   __device__ void init(const PagedArgs& p, int g0, int l0) {
     g = g0;
-    li = l0;
     n_sub = (p.G + p.R - 1) / p.R;
+    n_groups = p.batch / p.G;
     len = group_len(p, g);
     tiles = (len + kTileTok - 1) / kTileTok;
+    sub = l0 / tiles;
+    tile = l0 - sub * tiles - 1;
   }
-  // Advances to the next item; returns (sub, tile) of the current one.
-  __device__ void next(const PagedArgs& p, int& sub, int& tile) {
-    while (li >= tiles * n_sub) {
-      ++g;
-      li = 0;
-      len = group_len(p, g);
-      tiles = (len + kTileTok - 1) / kTileTok;
+  __device__ void next(const PagedArgs& p) {
+    if (++tile >= tiles) {
+      tile = 0;
+      if (++sub >= n_sub) {
+        sub = 0;
+        do {
+          if (++g >= n_groups) {  // never reached by callers that stay within their item count
+            tiles = 1;
+            break;
+          }
+          len = group_len(p, g);
+          tiles = (len + kTileTok - 1) / kTileTok;
+        } while (tiles == 0);
+      }
     }
-    sub = li / tiles;
-    tile = li - sub * tiles;
-    ++li;
+  }
+};
+
+// Index + phase parity of a ring of n slots (consumers wait on `phase`,
+// producers of a "slot free" barrier wait on `phase ^ 1`).
+struct Ring {
+  int idx = 0, phase = 0;
+  __device__ __forceinline__ void adv(int n) {
+    if (++idx == n) {
+      idx = 0;
+      phase ^= 1;
+    }
   }
 };
 
@@ -189,8 +209,8 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_paged_kernel(const _
   while (ncols < static_cast<uint32_t>(NACC * NC)) ncols <<= 1;
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&sm.full[s], 1);
-      mbar_init(&sm.empty[s], 1 + kEpiWarps);
+      mbar_init(&sm.full[s], 2);  // one expect_tx arrival per producer warp
+      mbar_init(&sm.empty[s], 1 + kEpiWarps / 2);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&sm.qfull[i], 1);
@@ -198,7 +218,7 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_paged_kernel(const _
     }
     for (int i = 0; i < kMaxAcc; ++i) {
       mbar_init(&sm.tfull[i], 1);
-      mbar_init(&sm.tempty[i], kEpiWarps);
+      mbar_init(&sm.tempty[i], kEpiWarps / 2);
     }
     mbar_init(&sm.done, 1);
     sm.abort = 0;
@@ -217,67 +237,93 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_paged_kernel(const _
   const uint32_t tmem = sm.tmem_base;
   volatile int* abort = &sm.abort;
 
-  if (warp == 0) {
-    // ------------------------------------------------ TMA producer (whole warp; lane 0 issues)
-    Cursor cur;
+  if (warp == 0 || warp == 10) {
+    // ------------------------------------------------ TMA producers
+    // A single issuing thread sustains roughly one TMA op per ~200 cycles and
+    // is slow at dependent scalar code, so (a) the two pages of a tile are
+    // issued by two warps (warp 0: page 0 and the Q rows, warp 10: page 1),
+    // and (b) each warp first resolves the page ids of up to 32 upcoming items
+    // in parallel (one lane per item) into shared memory; lane 0 then only
+    // waits for a free stage and issues the page + scale boxes.
+    const int half = warp == 0 ? 0 : 1;
+    Cursor cur;  // every lane keeps an identical copy, positioned before item `it`
     cur.init(p, sm.start_group, sm.start_local);
-    int qkey = -1, qn = 0, issued = 0;
-    int win_g = -1, win_base = 0;
-    for (int it = 0; it < count; ++it) {
-      int sub, tile;
-      cur.next(p, sub, tile);
-      const int n_pg = (cur.len + kPage - 1) / kPage;
-      const int p0 = 2 * tile;
-      const bool two = p0 + 1 < n_pg;
-      if (cur.g != win_g || p0 < win_base || p0 + 1 >= win_base + kBtWin) {
-        // stage the next kBtWin block-table entries of this group with one coalesced warp load
-        __syncwarp();
-        win_g = cur.g;
-        win_base = p0;
-        const int32_t* btr = p.bt + static_cast<int64_t>(cur.g) * p.G * p.bt_stride;
-        for (int i = lane; i < kBtWin; i += 32) {
-          const int pg = win_base + i;
-          sm.bt[i] = pg < n_pg ? __ldg(btr + pg) : 0;
+    Ring st;
+    Ring qr;
+    int qkey = -1, issued = 0, qloads = 0, ok = 1;
+    for (int it = 0; it < count && ok; it += 32) {
+      const int nb = min(32, count - it);
+      {
+        Cursor c = cur;
+        int ph = -1, key = 0, qrow = 0;
+        if (lane < nb) {
+          for (int k = 0; k <= lane; ++k) c.next(p);
+          const int pg = 2 * c.tile + half;
+          const int n_pg = (c.len + kPage - 1) / kPage;
+          if (pg < n_pg) ph = __ldg(p.bt + static_cast<int64_t>(c.g) * p.G * p.bt_stride + pg);
+          key = c.g * n_sub + c.sub;
+          qrow = (c.g * p.G + c.sub * p.R) * H;
         }
         __syncwarp();
+        sm.bq_ph[half][lane] = ph;
+        sm.bq_key[half][lane] = key;
+        sm.bq_qrow[half][lane] = qrow;
+        // every lane advances its copy to the item after this batch
+        const Cursor last = c;
+        cur.g = __shfl_sync(0xffffffffu, last.g, nb - 1);
+        cur.sub = __shfl_sync(0xffffffffu, last.sub, nb - 1);
+        cur.tile = __shfl_sync(0xffffffffu, last.tile, nb - 1);
+        cur.len = __shfl_sync(0xffffffffu, last.len, nb - 1);
+        cur.tiles = __shfl_sync(0xffffffffu, last.tiles, nb - 1);
+        __syncwarp();
       }
-      const int ph0 = sm.bt[p0 - win_base];
-      const int ph1 = two ? sm.bt[p0 + 1 - win_base] : 0;
-      int ok = 1;
       if (lane == 0) {
-        const int key = cur.g * n_sub + sub;
-        if (key != qkey) {
-          const int j = qn;
-          ok = mbar_wait(&sm.qempty[j & 1], ((j >> 1) & 1) ^ 1, abort, &g_hcu_status);
-          if (ok) {
-            mbar_arrive_expect_tx(&sm.qfull[j & 1], static_cast<uint32_t>(NC * kHeadDim));
-            tma_load_2d(sm.q[j & 1], &tm_q, &sm.qfull[j & 1], 0, (cur.g * p.G + sub * p.R) * H);
-            ++qn;
-            qkey = key;
+        for (int j = 0; j < nb; ++j) {
+          if (half == 0) {
+            const int key = sm.bq_key[0][j];
+            if (key != qkey) {
+              if (!mbar_wait(&sm.qempty[qr.idx], qr.phase ^ 1, abort, &g_hcu_status)) {
+                ok = 0;
+                break;
+              }
+              mbar_arrive_expect_tx(&sm.qfull[qr.idx], static_cast<uint32_t>(NC * kHeadDim));
+              tma_load_2d(sm.q[qr.idx], &tm_q, &sm.qfull[qr.idx], 0, sm.bq_qrow[0][j]);
+              qr.adv(2);
+              ++qloads;
+              qkey = key;
+            }
           }
-        }
-        const int s = it % kStages;
-        if (ok) ok = mbar_wait(&sm.empty[s], ((it / kStages) & 1) ^ 1, abort, &g_hcu_status);
-        if (ok) {
-          const uint32_t bytes = (two ? 2u : 1u) * (kPageFp8Bytes + kPage * 4);
-          mbar_arrive_expect_tx(&sm.full[s], bytes);
-          tma_load_3d(sm.a[s], &tm_kv, &sm.full[s], 0, 0, ph0);
-          tma_load_2d(sm.sc[s], &tm_sc, &sm.full[s], 0, ph0);
-          if (two) {
-            tma_load_3d(sm.a[s] + kPageFp8Bytes, &tm_kv, &sm.full[s], 0, 0, ph1);
-            tma_load_2d(sm.sc[s] + kPage, &tm_sc, &sm.full[s], 0, ph1);
+          if (!mbar_wait(&sm.empty[st.idx], st.phase ^ 1, abort, &g_hcu_status)) {
+            ok = 0;
+            break;
           }
-          issued = it + 1;
+          const int ph = sm.bq_ph[half][j];
+          if (ph >= 0) {
+            mbar_arrive_expect_tx(&sm.full[st.idx], kPageFp8Bytes + kPage * 4);
+            tma_load_3d(sm.a[st.idx] + half * kPageFp8Bytes, &tm_kv, &sm.full[st.idx], 0, 0, ph);
+            tma_load_2d(sm.sc[st.idx] + half * kPage, &tm_sc, &sm.full[st.idx], 0, ph);
+          } else {
+            mbar_arrive(&sm.full[st.idx]);  // no such page in this tile
+          }
+          st.adv(kStages);
+          ++issued;
         }
       }
-      if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
     }
     if (lane == 0) {
       // Drain: every copy issued must land before the CTA may exit.
+      Ring d;
       const int first = issued > kStages ? issued - kStages : 0;
-      for (int it = first; it < issued; ++it)
-        mbar_wait_drain(&sm.full[it % kStages], (it / kStages) & 1, &g_hcu_status);
-      for (int j = qn > 2 ? qn - 2 : 0; j < qn; ++j) mbar_wait_drain(&sm.qfull[j & 1], (j >> 1) & 1, &g_hcu_status);
+      for (int i2 = 0; i2 < issued; ++i2) {
+        if (i2 >= first) mbar_wait_drain(&sm.full[d.idx], d.phase, &g_hcu_status);
+        d.adv(kStages);
+      }
+      Ring dq;
+      for (int j = 0; j < qloads; ++j) {
+        if (j >= qloads - 2) mbar_wait_drain(&sm.qfull[dq.idx], dq.phase, &g_hcu_status);
+        dq.adv(2);
+      }
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -285,60 +331,68 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_paged_kernel(const _
     if (elect_one()) {
       Cursor cur;
       cur.init(p, sm.start_group, sm.start_local);
-      int qkey = -1;
-      int qn = 0;
+      Ring st, acc, qr;
+      int qkey = -1, qn = 0;
       uint32_t idesc = 0;
+      int q_slot = 0;
       for (int it = 0; it < count; ++it) {
-        int sub, tile;
-        cur.next(p, sub, tile);
-        const int key = cur.g * n_sub + sub;
+        cur.next(p);
+        const int key = cur.g * n_sub + cur.sub;
         if (key != qkey) {
-          if (qn > 0) tc_commit(&sm.qempty[(qn - 1) & 1]);
-          const int j = qn;
-          if (!mbar_wait(&sm.qfull[j & 1], (j >> 1) & 1, abort, &g_hcu_status)) break;
+          if (qn > 0) tc_commit(&sm.qempty[q_slot]);
+          if (!mbar_wait(&sm.qfull[qr.idx], qr.phase, abort, &g_hcu_status)) break;
+          q_slot = qr.idx;
+          qr.adv(2);
           ++qn;
           qkey = key;
-          const int nr = min(p.R, p.G - sub * p.R);
+          const int nr = min(p.R, p.G - cur.sub * p.R);
           idesc = idesc_e4m3_f32(128, nr * H);
         }
-        const int s = it % kStages;
-        const int a = it % NACC;
-        if (!mbar_wait(&sm.full[s], (it / kStages) & 1, abort, &g_hcu_status)) break;
-        if (!mbar_wait(&sm.tempty[a], ((it / NACC) & 1) ^ 1, abort, &g_hcu_status)) break;
+        if (!mbar_wait(&sm.full[st.idx], st.phase, abort, &g_hcu_status)) break;
+        if (!mbar_wait(&sm.tempty[acc.idx], acc.phase ^ 1, abort, &g_hcu_status)) break;
         tc_fence_after();
-        const uint64_t adesc = sw128_kmajor_desc(smem_u32(sm.a[s]));
-        const uint64_t bdesc = sw128_kmajor_desc(smem_u32(sm.q[(qn - 1) & 1]));
-        const uint32_t d = tmem + static_cast<uint32_t>(a * NC);
+        const uint64_t adesc = sw128_kmajor_desc(smem_u32(sm.a[st.idx]));
+        const uint64_t bdesc = sw128_kmajor_desc(smem_u32(sm.q[q_slot]));
+        const uint32_t d = tmem + static_cast<uint32_t>(acc.idx * NC);
 #pragma unroll
         for (int k = 0; k < kHeadDim / 32; ++k)
           mma_f8f6f4(d, adesc + 2 * k, bdesc + 2 * k, idesc, k > 0 ? 1u : 0u);
-        tc_commit(&sm.empty[s]);
-        tc_commit(&sm.tfull[a]);
+        tc_commit(&sm.empty[st.idx]);
+        tc_commit(&sm.tfull[acc.idx]);
+        st.adv(kStages);
+        acc.adv(NACC);
       }
       tc_commit(&sm.done);
       mbar_wait_drain(&sm.done, 0, &g_hcu_status);
     }
-  } else {
+  } else if (warp >= 2 && warp < 2 + kEpiWarps) {
     // ------------------------------------------------ epilogue (warps 2..9)
-    // Two warps per TMEM lane quadrant: with >= 2 rows per block they split the
-    // rows (r % 2 == half); a single-row block alternates tiles between them.
+    // Two teams of four warps (one warp per TMEM lane quadrant) take alternate
+    // tiles, so two tiles' TMEM-load / math / store chains are in flight at once;
+    // each warp computes every row of its team's tiles for its 32 tokens.
     const int ew = warp - 2;
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
-    const int half = ew >> 2;
+    const int team = ew >> 2;
     float* wsm = sm.w[ew];
     int* lsm = sm.lens[ew];
     Cursor cur;
     cur.init(p, sm.start_group, sm.start_local);
+    Ring st, acc;
     int qkey = -1;
     int nr = 0;
     const int64_t mstride = p.width / 16;
     for (int it = 0; it < count; ++it) {
-      int sub, tile;
-      cur.next(p, sub, tile);
-      const int key = cur.g * n_sub + sub;
-      const int row0 = cur.g * p.G + sub * p.R;
+      cur.next(p);
+      const int s = st.idx;
+      const int a = acc.idx;
+      const int aph = acc.phase;
+      st.adv(kStages);
+      acc.adv(NACC);
+      if ((it & 1) != team) continue;
+      const int key = cur.g * n_sub + cur.sub;
+      const int row0 = cur.g * p.G + cur.sub * p.R;
       if (key != qkey) {
-        nr = min(p.R, p.G - sub * p.R);
+        nr = min(p.R, p.G - cur.sub * p.R);
         __syncwarp();
         for (int i = lane; i < nr * H; i += 32) wsm[i] = __ldg(p.weights + static_cast<int64_t>(row0) * H + i);
         if (lane < nr) lsm[lane] = clamp_len(__ldg(p.ctx_lens + row0 + lane), p.width);
@@ -346,19 +400,15 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_paged_kernel(const _
         qkey = key;
       }
       const int tok_in_tile = quad * 32 + lane;
-      const int tok_base = tile * kTileTok + quad * 32;
+      const int tok_base = cur.tile * kTileTok + quad * 32;
       const int token = tok_base + lane;
-      const int s = it % kStages;
-      const int a = it % NACC;
-      if (!mbar_wait(&sm.tfull[a], (it / NACC) & 1, abort, &g_hcu_status)) break;
+      if (!mbar_wait(&sm.tfull[a], aph, abort, &g_hcu_status)) break;
       tc_fence_after();
       const float ksc = sm.sc[s][tok_in_tile];
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.empty[s]);  // this warp is done with the stage's scales
       const uint32_t tbase = tmem + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(a * NC);
-      const int r_first = nr >= 2 ? half : ((it & 1) == half ? 0 : nr);
-      const int r_step = nr >= 2 ? 2 : 1;
-      for (int r = r_first; r < nr; r += r_step) {
+      for (int r = 0; r < nr; ++r) {
         uint32_t v[H / 32][32];
 #pragma unroll
         for (int c = 0; c < H / 32; ++c) tmem_ld_x32(tbase + r * H + c * 32, v[c]);
@@ -397,6 +447,347 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_paged_kernel(const _
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.tempty[a]);
+    }
+  }
+
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, ncols);
+  }
+}
+
+// ---------------------------------------------------------------- ragged (prefill) kernel
+//
+// mqa_logits_ragged_kernel: query row r sees tokens [rs[r], re[r]) of a
+// contiguous fp8 K.  Rows are grouped into super-blocks of kQB row blocks of
+// RB = 256 / H rows (16 rows at H = 64); a CTA keeps one super-block's Q (4 x
+// 32 KB) resident and streams the 128-token K tiles the super-block sees
+// through a 4-stage TMA ring.  Each K tile feeds kQB MMAs (M = 128 tokens,
+// N = 256 query heads) into two 256-column TMEM accumulators, i.e. 2 KFLOP per
+// K byte.  The work list is (super-block, tile), cut into one contiguous range
+// per CTA on the device.  Same logits / mask contract as the paged kernel.
+constexpr int kPfStages = 4;
+constexpr int kQB = 4;
+
+struct __align__(1024) PfSmem {
+  uint8_t q[kQB][kQTile];
+  uint8_t a[kPfStages][kATile];
+  float w[kEpiWarps][kQB * kMaxN / 2];  // weights of the rows this epilogue warp owns
+  int rs[kEpiWarps][16];
+  int re[kEpiWarps][16];
+  uint64_t full[kPfStages];
+  uint64_t empty[kPfStages];
+  uint64_t qfull;
+  uint64_t qempty;
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint64_t done;
+  uint32_t tmem_base;
+  int start_sb;
+  int start_local;
+  int count;
+  int abort;
+};
+
+struct RaggedArgs {
+  const float* k_scale;
+  const float* weights;
+  const int32_t* rs;
+  const int32_t* re;
+  float* logits;
+  int16_t* mask;
+  int64_t stride;  // logits row stride (elements), multiple of 64
+  int rows;
+  int n_tokens;
+};
+
+template <int H>
+__device__ __forceinline__ void sb_tiles(const RaggedArgs& p, int sb, int& t0, int& tiles) {
+  constexpr int RB = kMaxN / H;
+  constexpr int SBR = kQB * RB;
+  int lo = INT32_MAX, hi = 0;
+  const int r1 = min(p.rows, (sb + 1) * SBR);
+  for (int r = sb * SBR; r < r1; ++r) {
+    const int a = max(__ldg(p.rs + r), 0);
+    const int e = min(__ldg(p.re + r), p.n_tokens);
+    if (e > a) {
+      lo = min(lo, a);
+      hi = max(hi, e);
+    }
+  }
+  if (hi <= lo) {
+    t0 = 0;
+    tiles = 0;
+  } else {
+    t0 = lo / kTileTok;
+    tiles = (hi + kTileTok - 1) / kTileTok - t0;
+  }
+}
+
+template <int H>
+struct RCursor {
+  int sb, li, t0, tiles;
+  __device__ void init(const RaggedArgs& p, int sb0, int l0) {
+    sb = sb0;
+    li = l0;
+    sb_tiles<H>(p, sb, t0, tiles);
+  }
+  __device__ int next(const RaggedArgs& p) {  // returns the absolute tile index
+    while (li >= tiles) {
+      ++sb;
+      li = 0;
+      sb_tiles<H>(p, sb, t0, tiles);
+    }
+    return t0 + li++;
+  }
+};
+
+template <int H>
+__global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_ragged_kernel(const __grid_constant__ CUtensorMap tm_k,
+                                                                         const __grid_constant__ CUtensorMap tm_q,
+                                                                         const RaggedArgs p) {
+  constexpr int RB = kMaxN / H;  // rows per row block (N = 256)
+  constexpr int SBR = kQB * RB;  // rows per super-block
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  PfSmem& sm = *reinterpret_cast<PfSmem*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n_sb = (p.rows + SBR - 1) / SBR;
+
+  if (warp == 0) {
+    int64_t total = 0;
+    for (int base = 0; base < n_sb; base += 32) {
+      int t0, c = 0;
+      if (base + lane < n_sb) sb_tiles<H>(p, base + lane, t0, c);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+      total += c;
+    }
+    const int64_t begin = total * blockIdx.x / gridDim.x;
+    const int64_t end = total * (blockIdx.x + 1) / gridDim.x;
+    int sg = 0, sl = 0;
+    if (end > begin) {
+      int64_t run = 0;
+      for (int base = 0; base < n_sb; base += 32) {
+        int t0, c = 0;
+        if (base + lane < n_sb) sb_tiles<H>(p, base + lane, t0, c);
+        int inc = c;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int y = __shfl_up_sync(0xffffffffu, inc, o);
+          if (lane >= o) inc += y;
+        }
+        const bool hit = run + inc > begin && c > 0;
+        const uint32_t bal = __ballot_sync(0xffffffffu, hit);
+        if (bal) {
+          const int src = __ffs(bal) - 1;
+          const int inc_s = __shfl_sync(0xffffffffu, inc, src);
+          const int c_s = __shfl_sync(0xffffffffu, c, src);
+          sg = base + src;
+          sl = static_cast<int>(begin - (run + inc_s - c_s));
+          break;
+        }
+        run += __shfl_sync(0xffffffffu, inc, 31);
+      }
+    }
+    if (lane == 0) {
+      sm.start_sb = sg;
+      sm.start_local = sl;
+      sm.count = static_cast<int>(end - begin);
+    }
+  }
+  __syncthreads();
+  const int count = sm.count;
+  if (count <= 0) return;
+
+  constexpr uint32_t ncols = 512;  // two 256-column accumulators
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPfStages; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], 1 + kEpiWarps);
+    }
+    mbar_init(&sm.qfull, 1);
+    mbar_init(&sm.qempty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sm.tfull[i], 1);
+      mbar_init(&sm.tempty[i], kEpiWarps);
+    }
+    mbar_init(&sm.done, 1);
+    sm.abort = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_q);
+  }
+  if (warp == 0) {
+    tmem_alloc(&sm.tmem_base, ncols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+  volatile int* abort = &sm.abort;
+
+  if (warp == 0) {
+    // ------------------------------------------------ TMA producer
+    if (elect_one()) {
+      RCursor<H> cur;
+      cur.init(p, sm.start_sb, sm.start_local);
+      int qsb = -1, qn = 0, issued = 0;
+      for (int it = 0; it < count; ++it) {
+        const int tile = cur.next(p);
+        if (cur.sb != qsb) {
+          if (!mbar_wait(&sm.qempty, (qn & 1) ^ 1, abort, &g_hcu_status)) break;
+          const int row0 = cur.sb * SBR;
+          const int nrb = min(kQB, (p.rows - row0 + RB - 1) / RB);
+          mbar_arrive_expect_tx(&sm.qfull, static_cast<uint32_t>(nrb * kQTile));
+          for (int j = 0; j < nrb; ++j) tma_load_2d(sm.q[j], &tm_q, &sm.qfull, 0, (row0 + j * RB) * H);
+          ++qn;
+          qsb = cur.sb;
+        }
+        const int s = it % kPfStages;
+        if (!mbar_wait(&sm.empty[s], ((it / kPfStages) & 1) ^ 1, abort, &g_hcu_status)) break;
+        mbar_arrive_expect_tx(&sm.full[s], static_cast<uint32_t>(kATile));
+        tma_load_2d(sm.a[s], &tm_k, &sm.full[s], 0, tile * kTileTok);
+        issued = it + 1;
+      }
+      const int first = issued > kPfStages ? issued - kPfStages : 0;
+      for (int it = first; it < issued; ++it)
+        mbar_wait_drain(&sm.full[it % kPfStages], (it / kPfStages) & 1, &g_hcu_status);
+      if (qn > 0) mbar_wait_drain(&sm.qfull, (qn - 1) & 1, &g_hcu_status);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------ MMA issuer
+    if (elect_one()) {
+      RCursor<H> cur;
+      cur.init(p, sm.start_sb, sm.start_local);
+      int qsb = -1, qn = 0, nrb = 0, u = 0;
+      bool ok = true;
+      for (int it = 0; it < count && ok; ++it) {
+        cur.next(p);
+        if (cur.sb != qsb) {
+          if (qn > 0) tc_commit(&sm.qempty);
+          if (!mbar_wait(&sm.qfull, qn & 1, abort, &g_hcu_status)) break;
+          ++qn;
+          qsb = cur.sb;
+          nrb = min(kQB, (p.rows - cur.sb * SBR + RB - 1) / RB);
+        }
+        const int s = it % kPfStages;
+        if (!mbar_wait(&sm.full[s], (it / kPfStages) & 1, abort, &g_hcu_status)) break;
+        const uint64_t adesc = sw128_kmajor_desc(smem_u32(sm.a[s]));
+        for (int j = 0; j < nrb; ++j, ++u) {
+          const int a = u & 1;
+          if (!mbar_wait(&sm.tempty[a], ((u >> 1) & 1) ^ 1, abort, &g_hcu_status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const int nr = min(RB, p.rows - (cur.sb * SBR + j * RB));
+          const uint32_t idesc = idesc_e4m3_f32(128, nr * H);
+          const uint64_t bdesc = sw128_kmajor_desc(smem_u32(sm.q[j]));
+          const uint32_t d = tmem + static_cast<uint32_t>(a * kMaxN);
+#pragma unroll
+          for (int k = 0; k < kHeadDim / 32; ++k)
+            mma_f8f6f4(d, adesc + 2 * k, bdesc + 2 * k, idesc, k > 0 ? 1u : 0u);
+          tc_commit(&sm.tfull[a]);
+        }
+        if (ok) tc_commit(&sm.empty[s]);
+      }
+      tc_commit(&sm.done);
+      mbar_wait_drain(&sm.done, 0, &g_hcu_status);
+    }
+  } else if (warp >= 2 && warp < 2 + kEpiWarps) {
+    // ------------------------------------------------ epilogue (warps 2..9; warp 10 idles here)
+    const int ew = warp - 2;
+    const int quad = warp & 3;
+    const int half = ew >> 2;  // rows r % 2 == half of every row block
+    constexpr int RPW = RB / 2;  // rows per row block owned by this warp
+    float* wsm = sm.w[ew];
+    int* rs = sm.rs[ew];
+    int* re = sm.re[ew];
+    RCursor<H> cur;
+    cur.init(p, sm.start_sb, sm.start_local);
+    int qsb = -1, nrb = 0, u = 0;
+    bool ok = true;
+    for (int it = 0; it < count && ok; ++it) {
+      const int tile = cur.next(p);
+      const int row0 = cur.sb * SBR;
+      if (cur.sb != qsb) {
+        qsb = cur.sb;
+        nrb = min(kQB, (p.rows - row0 + RB - 1) / RB);
+        __syncwarp();
+        for (int lr = 0; lr < kQB * RPW; ++lr) {
+          const int row = row0 + (lr / RPW) * RB + (lr % RPW) * 2 + half;
+          const bool in = row < p.rows;
+          for (int h = lane; h < H; h += 32)
+            wsm[lr * H + h] = in ? __ldg(p.weights + static_cast<int64_t>(row) * H + h) : 0.f;
+          if (lane == 0) {
+            rs[lr] = in ? max(__ldg(p.rs + row), 0) : 0;
+            re[lr] = in ? min(__ldg(p.re + row), p.n_tokens) : 0;
+          }
+        }
+        __syncwarp();
+      }
+      const int s = it % kPfStages;
+      const int tok_base = tile * kTileTok + quad * 32;
+      const int token = tok_base + lane;
+      // k_scale of this thread's token: contiguous K, so a plain load issued before the wait
+      const float ksc = token < p.n_tokens ? __ldg(p.k_scale + token) : 0.f;
+      for (int j = 0; j < nrb; ++j, ++u) {
+        const int a = u & 1;
+        if (!mbar_wait(&sm.tfull[a], (u >> 1) & 1, abort, &g_hcu_status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (j == 0) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sm.empty[s]);  // the MMAs read the stage; nothing else does
+        }
+        const uint32_t tbase = tmem + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(a * kMaxN);
+        const int nr = min(RB, p.rows - (row0 + j * RB));
+        for (int r = half, lr = j * RPW; r < nr; r += 2, ++lr) {
+          uint32_t v[H / 32][32];
+#pragma unroll
+          for (int c = 0; c < H / 32; ++c) tmem_ld_x32(tbase + r * H + c * 32, v[c]);
+          tmem_ld_wait();
+#pragma unroll
+          for (int c = 0; c < H / 32; ++c) tmem_reg_fence(v[c]);
+          float2 acc0 = make_float2(0.f, 0.f), acc1 = acc0, acc2 = acc0, acc3 = acc0;
+#pragma unroll
+          for (int c = 0; c < H / 32; ++c) {
+            const float4* w4 = reinterpret_cast<const float4*>(wsm + lr * H + c * 32);
+#pragma unroll
+            for (int jj = 0; jj < 8; jj += 2) {
+              const float4 wa = w4[jj];
+              const float4 wb = w4[jj + 1];
+              const uint32_t* x = &v[c][4 * jj];
+              acc0 = fma2(make_float2(fmaxf(__uint_as_float(x[0]), 0.f), fmaxf(__uint_as_float(x[1]), 0.f)),
+                          make_float2(wa.x, wa.y), acc0);
+              acc1 = fma2(make_float2(fmaxf(__uint_as_float(x[2]), 0.f), fmaxf(__uint_as_float(x[3]), 0.f)),
+                          make_float2(wa.z, wa.w), acc1);
+              acc2 = fma2(make_float2(fmaxf(__uint_as_float(x[4]), 0.f), fmaxf(__uint_as_float(x[5]), 0.f)),
+                          make_float2(wb.x, wb.y), acc2);
+              acc3 = fma2(make_float2(fmaxf(__uint_as_float(x[6]), 0.f), fmaxf(__uint_as_float(x[7]), 0.f)),
+                          make_float2(wb.z, wb.w), acc3);
+            }
+          }
+          float s0 = ((acc0.x + acc0.y) + (acc1.x + acc1.y)) + ((acc2.x + acc2.y) + (acc3.x + acc3.y));
+          s0 *= ksc;
+          const int row = row0 + j * RB + r;
+          const bool keep = token >= rs[lr] && token < re[lr] && __float_as_uint(s0) != 0u;
+          const uint32_t bits = __ballot_sync(0xffffffffu, keep);
+          if (lane == 0 && tok_base < p.stride)
+            reinterpret_cast<uint32_t*>(p.mask)[(static_cast<int64_t>(row) * (p.stride / 16) + tok_base / 16) >> 1] =
+                bits;
+          if (keep) p.logits[static_cast<int64_t>(row) * p.stride + token] = s0;
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.tempty[a]);
+      }
     }
   }
 
@@ -459,6 +850,11 @@ bool make_map_page_scales(CUtensorMap* m, const uint8_t* kv, uint64_t n_pages, u
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+int map_error(const char* what) {
+  set_last_error_msg("cuTensorMapEncodeTiled rejected the tensor map of ", what);
+  return HCU_ERR_LAUNCH;
+}
+
 template <int H>
 int launch_paged(const CUtensorMap& tkv, const CUtensorMap& tsc, const CUtensorMap& tq, const PagedArgs& a,
                  cudaStream_t stream) {
@@ -498,12 +894,12 @@ extern "C" int hcu_mqa_logits_hist(const uint8_t* q, int64_t batch, int64_t head
     return launch_status();
   CUtensorMap tkv, tsc, tq;
   if (!make_map_pages(&tkv, kv_cache, static_cast<uint64_t>(n_pages), static_cast<uint64_t>(page_stride)))
-    return HCU_ERR_LAUNCH;
+    return map_error("kv_cache pages");
   if (!make_map_page_scales(&tsc, kv_cache, static_cast<uint64_t>(n_pages), static_cast<uint64_t>(page_stride)))
-    return HCU_ERR_LAUNCH;
+    return map_error("kv_cache scales");
   if (!make_map_2d(&tq, q, kHeadDim, static_cast<uint64_t>(batch * heads), kHeadDim, kHeadDim,
                    static_cast<uint32_t>(R * heads), CU_TENSOR_MAP_SWIZZLE_128B))
-    return HCU_ERR_LAUNCH;
+    return map_error("q");
   PagedArgs a;
   a.kv = kv_cache;
   a.page_stride = page_stride;
@@ -528,7 +924,46 @@ extern "C" int hcu_mqa_logits_ragged(const uint8_t* q, int64_t rows, int64_t hea
                                      const float* k_scale, int64_t n_tokens, const float* weights,
                                      const int32_t* row_start, const int32_t* row_end, float* logits,
                                      int64_t logits_stride, int16_t* mask, hcu_stream_t stream) {
-  (void)q; (void)rows; (void)heads; (void)k_fp8; (void)k_scale; (void)n_tokens; (void)weights;
-  (void)row_start; (void)row_end; (void)logits; (void)logits_stride; (void)mask; (void)stream;
-  return HCU_ERR_UNSUPPORTED;
+  using namespace hcu;
+  if (heads != 32 && heads != 64) return HCU_ERR_UNSUPPORTED;
+  if (rows < 0 || n_tokens < 0 || rows * heads > INT32_MAX || n_tokens > INT32_MAX) return HCU_ERR_ARG;
+  if (logits_stride < n_tokens || logits_stride % 64 != 0) return HCU_ERR_ARG;
+  if (rows == 0) return HCU_OK;
+  if (!q || !k_fp8 || !k_scale || !weights || !row_start || !row_end || !logits || !mask) return HCU_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k_fp8) | reinterpret_cast<uintptr_t>(k_scale) |
+       reinterpret_cast<uintptr_t>(mask) | reinterpret_cast<uintptr_t>(weights)) % 16 != 0)
+    return HCU_ERR_ARG;
+  const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(mask, 0, static_cast<size_t>(rows * (logits_stride / 16)) * sizeof(int16_t), st) != cudaSuccess)
+    return launch_status();
+  if (n_tokens == 0) return HCU_OK;
+  CUtensorMap tk, tq;
+  const int RB = static_cast<int>(kMaxN / heads);
+  if (!make_map_2d(&tk, k_fp8, kHeadDim, static_cast<uint64_t>(n_tokens), kHeadDim, kHeadDim, kTileTok,
+                   CU_TENSOR_MAP_SWIZZLE_128B))
+    return map_error("k_fp8");
+  if (!make_map_2d(&tq, q, kHeadDim, static_cast<uint64_t>(rows * heads), kHeadDim, kHeadDim,
+                   static_cast<uint32_t>(RB * heads), CU_TENSOR_MAP_SWIZZLE_128B))
+    return map_error("q");
+  RaggedArgs a;
+  a.k_scale = k_scale;
+  a.weights = weights;
+  a.rs = row_start;
+  a.re = row_end;
+  a.logits = logits;
+  a.mask = mask;
+  a.stride = logits_stride;
+  a.rows = static_cast<int>(rows);
+  a.n_tokens = static_cast<int>(n_tokens);
+  const size_t smem = sizeof(PfSmem) + 1024;
+  if (heads == 64) {
+    cudaFuncSetAttribute(mqa_logits_ragged_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(smem));
+    mqa_logits_ragged_kernel<64><<<sm_count(), kLgThreads, smem, st>>>(tk, tq, a);
+  } else {
+    cudaFuncSetAttribute(mqa_logits_ragged_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(smem));
+    mqa_logits_ragged_kernel<32><<<sm_count(), kLgThreads, smem, st>>>(tk, tq, a);
+  }
+  return launch_status();
 }

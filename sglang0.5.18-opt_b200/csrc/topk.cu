@@ -37,7 +37,8 @@ constexpr int kStep = 128;  // tokens per warp step (32 lanes x 4)
 constexpr int kTkUnroll = 4;
 constexpr int kHistTrash = kTkWarps * 256;  // trash slots follow the per-warp histograms
 
-constexpr int kSample = 4096;   // row samples used to bracket the threshold
+constexpr int kSmallSample = 2048;  // row samples used to bracket the threshold (rows <= 128K)
+constexpr int kSample = 8192;       // sample capacity (rows > 512K)
 constexpr int kMidCap = 8192;   // keys collected strictly inside the bracket
 
 struct __align__(16) TopkSmem {
@@ -118,8 +119,15 @@ __device__ __forceinline__ void find_threshold(const int* hist, int need, int* w
   }
   if (lane == 0) wtot[w] = x;
   __syncthreads();
-  int after = 0;
-  for (int v = w + 1; v < kTkWarps; ++v) after += wtot[v];
+  // suffix of the warp totals after warp w, by a shuffle scan (no serial loop)
+  int t = wtot[lane];
+  int sx = t;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_down_sync(0xffffffffu, sx, o);
+    if (lane + o < 32) sx += y;
+  }
+  const int after = __shfl_sync(0xffffffffu, sx - t, w);
   const int suf = x + after;
   const int suf_next = suf - s;
   if (tid < ACTIVE && suf >= need && suf_next < need) {
@@ -177,7 +185,56 @@ __device__ __forceinline__ uint32_t smem_select_rank(const uint32_t* keys, int n
   return (p24 << 8) | static_cast<uint32_t>(sm.res[0]);
 }
 
-// Visits every token slot of this warp's segment as (valid, key, index i0+j).
+// Branch-free monotone key.
+__device__ __forceinline__ uint32_t key_of(float x) {
+  const uint32_t b = __float_as_uint(x);
+  return b ^ (static_cast<uint32_t>(static_cast<int32_t>(b) >> 31) | 0x80000000u);
+}
+
+// Loads the 16 consecutive tokens [i0, i0 + 16) (i0 % 16 == 0) of this lane:
+// their keys (unset mask bit -> +0) and the mask of slots below `lim`.
+template <bool kVec>
+__device__ __forceinline__ uint32_t load16(const float* __restrict__ vals, const int16_t* __restrict__ mrow, int i0,
+                                           int lim, uint32_t (&k)[16]) {
+  if (i0 >= lim) {
+#pragma unroll
+    for (int t = 0; t < 16; ++t) k[t] = kZeroKey;
+    return 0u;
+  }
+  const uint32_t mw = static_cast<uint16_t>(__ldg(mrow + (i0 >> 4)));
+  float v[16];
+  if constexpr (kVec) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (i0 + 4 * q < lim) f = __ldg(reinterpret_cast<const float4*>(vals + i0 + 4 * q));
+      v[4 * q] = f.x;
+      v[4 * q + 1] = f.y;
+      v[4 * q + 2] = f.z;
+      v[4 * q + 3] = f.w;
+    }
+  } else {
+#pragma unroll
+    for (int t = 0; t < 16; ++t) v[t] = i0 + t < lim ? __ldg(vals + i0 + t) : 0.f;
+  }
+#pragma unroll
+  for (int t = 0; t < 16; ++t) k[t] = ((mw >> t) & 1u) ? key_of(v[t]) : kZeroKey;
+  const int nv = lim - i0;
+  return nv >= 16 ? 0xFFFFu : ((1u << nv) - 1u);
+}
+
+__device__ __forceinline__ int warp_incl_scan(int x) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  return x;
+}
+
+// Visits every token slot of this warp's segment as (valid, key, index i0+j);
+// lane l takes tokens c + 4l .. c + 4l + 3 of each 128-token step (fallback passes).
 #define TK_FOR_EACH(BODY)                                                             \
   for (int c = seg_begin; c < seg_end; c += kStep * kTkUnroll) {                      \
     float rv[kTkUnroll][4];                                                           \
@@ -240,17 +297,18 @@ __global__ __launch_bounds__(kTkThreads, 1) void topk_row_kernel(
   bool resolved = false;
   if (pre_ws == nullptr) {
     // ---- bracket select: sample -> [lo, hi] -> one counting pass -> exact select inside ----
-    const int m = len < kSample ? len : kSample;
+    const int m = len <= kSmallSample ? len : (len <= (1 << 17) ? kSmallSample : (len <= (1 << 19) ? 4096 : kSample));
+    const float stride_f = static_cast<float>(len) / static_cast<float>(m);
     for (int k = tid; k < m; k += kTkThreads) {
-      const int i = static_cast<int>((static_cast<int64_t>(k) * len) / m);
+      const int i = min(len - 1, static_cast<int>((static_cast<float>(k) + 0.5f) * stride_f));
       const bool set = (static_cast<uint16_t>(__ldg(mrow + (i >> 4))) >> (i & 15)) & 1u;
-      sm.samp[k] = set ? to_key(__ldg(vals + i)) : kZeroKey;
+      sm.samp[k] = set ? key_of(__ldg(vals + i)) : kZeroKey;
     }
     if (tid == 0) sm.mid_n = 0;
     __syncthreads();
     int r_hi = kTopK, r_lo = kTopK;
     if (m < len) {  // expected sample rank of the threshold +- 4 sigma
-      const float t = static_cast<float>(kTopK) * static_cast<float>(m) / static_cast<float>(len);
+      const float t = static_cast<float>(kTopK) / stride_f;
       const float d = 4.f * sqrtf(t) + 4.f;
       r_hi = max(1, static_cast<int>(floorf(t - d)));
       r_lo = min(m, static_cast<int>(ceilf(t + d)));
@@ -260,43 +318,55 @@ __global__ __launch_bounds__(kTkThreads, 1) void topk_row_kernel(
     const uint32_t lo = r_lo == r_hi ? hi : smem_select_rank(sm.samp, m, r_lo, sm, &dummy);
     {
       int n_gt = 0, n_eh = 0, n_el = 0;
-      TK_FOR_EACH({
-        n_gt += valid & (key > hi);
-        n_eh += valid & (key == hi);
-        n_el += valid & (key == lo) & (lo != hi);
-        const bool mid = valid & (key > lo) & (key < hi);
-        const uint32_t mb = __ballot_sync(0xffffffffu, mid);
-        if (mb) {
+      for (int c = seg_begin; c < seg_end; c += 32 * 16) {
+        const int i0 = c + 16 * lane;
+        uint32_t k[16];
+        const uint32_t vm = load16<kVec>(vals, mrow, i0, seg_end, k);
+        uint32_t midb = 0;
+#pragma unroll
+        for (int t = 0; t < 16; ++t) {
+          const uint32_t v = (vm >> t) & 1u;
+          n_gt += v & (k[t] > hi);
+          n_eh += v & (k[t] == hi);
+          n_el += v & (k[t] == lo);
+          midb |= (v & (k[t] > lo) & (k[t] < hi)) << t;
+        }
+        if (__any_sync(0xffffffffu, midb != 0u)) {
+          const int nm = __popc(midb);
+          const int inc = warp_incl_scan(nm);
           int base = 0;
-          if (lane == 0) base = atomicAdd(&sm.mid_n, __popc(mb));
-          base = __shfl_sync(0xffffffffu, base, 0);
-          if (mid) {
-            const int pos = base + __popc(mb & ((1u << lane) - 1u));
-            if (pos < kMidCap) {
-              sm.mid_key[pos] = key;
-              sm.mid_warp[pos] = static_cast<uint8_t>(w);
+          if (lane == 31) base = atomicAdd(&sm.mid_n, inc);
+          base = __shfl_sync(0xffffffffu, base, 31);
+          int pos = base + inc - nm;
+          if (midb) {
+#pragma unroll
+            for (int t = 0; t < 16; ++t) {
+              if ((midb >> t) & 1u) {
+                if (pos < kMidCap) {
+                  sm.mid_key[pos] = k[t];
+                  sm.mid_warp[pos] = static_cast<uint8_t>(w);
+                }
+                ++pos;
+              }
             }
           }
         }
-      })
+      }
       n_gt = warp_sum(n_gt);
       n_eh = warp_sum(n_eh);
       n_el = warp_sum(n_el);
       if (lane == 0) {
         sm.gt_w[w] = n_gt;
         sm.eh_w[w] = n_eh;
-        sm.el_w[w] = n_el;
+        sm.el_w[w] = lo != hi ? n_el : 0;
         sm.mid_above_w[w] = 0;
         sm.mid_tie_w[w] = 0;
       }
     }
     __syncthreads();
-    int G = 0, EH = 0, EL = 0;
-    for (int v = 0; v < kTkWarps; ++v) {
-      G += sm.gt_w[v];
-      EH += sm.eh_w[v];
-      EL += sm.el_w[v];
-    }
+    const int G = warp_sum(sm.gt_w[lane]);
+    const int EH = warp_sum(sm.eh_w[lane]);
+    const int EL = warp_sum(sm.el_w[lane]);
     const int M = sm.mid_n;
     int mode = 0;  // 0: bracket missed -> full radix below
     if (G < kTopK) {
@@ -328,7 +398,7 @@ __global__ __launch_bounds__(kTkThreads, 1) void topk_row_kernel(
       __syncthreads();
       if (lane == 0) {
         sm.above[w] = sm.gt_w[w] + (thr < hi ? sm.eh_w[w] : 0) + sm.mid_above_w[w];
-        sm.ties[w] = (thr == hi ? sm.eh_w[w] : 0) + sm.mid_tie_w[w] + ((lo != hi && thr == lo) ? sm.el_w[w] : 0);
+        sm.ties[w] = (thr == hi ? sm.eh_w[w] : 0) + sm.mid_tie_w[w] + (thr == lo ? sm.el_w[w] : 0);
       }
       __syncthreads();
       resolved = true;
@@ -336,220 +406,209 @@ __global__ __launch_bounds__(kTkThreads, 1) void topk_row_kernel(
   }
 
   if (!resolved) {
-  // ---- pass A: key[31:20] histogram, positives and zeros ----
-  int positives = 0, zeros = 0;
-  const int* hist1 = sm.hist;
-  bool have_warp_counts = false;
-  if (pre_ws != nullptr) {
-    hist1 = pre_ws + static_cast<int64_t>(row) * kBins;
-    const int* cnt = pre_ws + 2 * static_cast<int64_t>(rows) * kBins + 2 * row;
-    positives = cnt[0];
-    zeros = cnt[1];
-  } else {
-    for (int i = tid; i < kBins + 32; i += kTkThreads) sm.hist[i] = 0;
-    __syncthreads();
-    int zc = 0, pc = 0;
-    TK_FOR_EACH({
-      const bool nz = key != kZeroKey;
-      zc += valid & !nz;
-      pc += valid & (key > kZeroKey);
-      atomicAdd(&sm.hist[(valid & nz) ? static_cast<int>(key >> 20) : trash], 1);
-    })
-    zc = warp_sum(zc);
-    pc = warp_sum(pc);
-    if (lane == 0) {
-      if (zc) atomicAdd(&sm.hist[kZeroBin], zc);
-      sm.pos[w] = pc;
-      sm.zeros[w] = zc;
-    }
-    __syncthreads();
-    for (int v = 0; v < kTkWarps; ++v) {
-      positives += sm.pos[v];
-      zeros += sm.zeros[v];
-    }
-    have_warp_counts = true;
-  }
-
-  if (positives <= kTopK && positives + zeros >= kTopK) {
-    // Sparse fast path: every positive plus the lowest-index zeros.
-    thr = kZeroKey;
-    remaining = kTopK - positives;
-    if (!have_warp_counts) {
+    // ---- pass A: key[31:20] histogram, positives and zeros ----
+    int positives = 0, zeros = 0;
+    const int* hist1 = sm.hist;
+    bool have_warp_counts = false;
+    if (pre_ws != nullptr) {
+      hist1 = pre_ws + static_cast<int64_t>(row) * kBins;
+      const int* cnt = pre_ws + 2 * static_cast<int64_t>(rows) * kBins + 2 * row;
+      positives = cnt[0];
+      zeros = cnt[1];
+    } else {
+      for (int i = tid; i < kBins + 32; i += kTkThreads) sm.hist[i] = 0;
+      __syncthreads();
       int zc = 0, pc = 0;
       TK_FOR_EACH({
-        zc += valid & (key == kZeroKey);
+        const bool nz = key != kZeroKey;
+        zc += valid & !nz;
         pc += valid & (key > kZeroKey);
+        atomicAdd(&sm.hist[(valid & nz) ? static_cast<int>(key >> 20) : trash], 1);
       })
       zc = warp_sum(zc);
       pc = warp_sum(pc);
       if (lane == 0) {
+        if (zc) atomicAdd(&sm.hist[kZeroBin], zc);
         sm.pos[w] = pc;
         sm.zeros[w] = zc;
       }
+      __syncthreads();
+      positives = warp_sum(sm.pos[lane]);
+      zeros = warp_sum(sm.zeros[lane]);
+      have_warp_counts = true;
     }
-    if (lane == 0) {
-      sm.above[w] = sm.pos[w];
-      sm.ties[w] = sm.zeros[w];
-    }
-    __syncthreads();
-  } else {
-    find_threshold<kBins>(hist1, kTopK, sm.wtot, sm.res);
-    const uint32_t t1 = static_cast<uint32_t>(sm.res[0]);
-    const int need1 = kTopK - sm.res[1];
 
-    // ---- pass B: key[19:8] inside bin t1 ----
-    for (int i = tid; i < kBins + 32; i += kTkThreads) sm.hist[i] = 0;
-    __syncthreads();
-    if (tid == 0 && t1 == (kZeroKey >> 20) && zeros) atomicAdd(&sm.hist[(kZeroKey >> 8) & 0xFFFu], zeros);
-    TK_FOR_EACH({
-      const bool cand = valid & ((key >> 20) == t1) & (key != kZeroKey);
-      atomicAdd(&sm.hist[cand ? static_cast<int>((key >> 8) & 0xFFFu) : trash], 1);
-    })
-    __syncthreads();
-    find_threshold<kBins>(sm.hist, need1, sm.wtot, sm.res);
-    const uint32_t prefix24 = (t1 << 12) | static_cast<uint32_t>(sm.res[0]);
-    const int need2 = need1 - sm.res[1];
+    if (positives <= kTopK && positives + zeros >= kTopK) {
+      // Sparse fast path: every positive plus the lowest-index zeros.
+      thr = kZeroKey;
+      remaining = kTopK - positives;
+      if (!have_warp_counts) {
+        int zc = 0, pc = 0;
+        TK_FOR_EACH({
+          zc += valid & (key == kZeroKey);
+          pc += valid & (key > kZeroKey);
+        })
+        zc = warp_sum(zc);
+        pc = warp_sum(pc);
+        if (lane == 0) {
+          sm.pos[w] = pc;
+          sm.zeros[w] = zc;
+        }
+      }
+      if (lane == 0) {
+        sm.above[w] = sm.pos[w];
+        sm.ties[w] = sm.zeros[w];
+      }
+      __syncthreads();
+    } else {
+      find_threshold<kBins>(hist1, kTopK, sm.wtot, sm.res);
+      const uint32_t t1 = static_cast<uint32_t>(sm.res[0]);
+      const int need1 = kTopK - sm.res[1];
 
-    // ---- pass C: per-warp key[7:0] inside prefix24 + per-warp above / zeros ----
-    for (int i = tid; i < kTkWarps * 256 + 32; i += kTkThreads) sm.hist[i] = 0;
-    __syncthreads();
-    {
-      int above = 0, zc = 0;
-      int* wh = sm.hist + w * 256;
+      // ---- pass B: key[19:8] inside bin t1 ----
+      for (int i = tid; i < kBins + 32; i += kTkThreads) sm.hist[i] = 0;
+      __syncthreads();
+      if (tid == 0 && t1 == (kZeroKey >> 20) && zeros) atomicAdd(&sm.hist[(kZeroKey >> 8) & 0xFFFu], zeros);
       TK_FOR_EACH({
-        const uint32_t hi = key >> 8;
-        above += valid & (hi > prefix24);
-        zc += valid & (key == kZeroKey);
-        const bool cand = valid & (hi == prefix24) & (key != kZeroKey);
-        atomicAdd(cand ? &wh[key & 0xFFu] : &sm.hist[kHistTrash + lane], 1);
+        const bool cand = valid & ((key >> 20) == t1) & (key != kZeroKey);
+        atomicAdd(&sm.hist[cand ? static_cast<int>((key >> 8) & 0xFFFu) : trash], 1);
       })
-      above = warp_sum(above);
-      zc = warp_sum(zc);
-      if (lane == 0) {
-        if (zc && prefix24 == (kZeroKey >> 8)) atomicAdd(&wh[kZeroKey & 0xFFu], zc);
-        sm.above[w] = above;
+      __syncthreads();
+      find_threshold<kBins>(sm.hist, need1, sm.wtot, sm.res);
+      const uint32_t prefix24 = (t1 << 12) | static_cast<uint32_t>(sm.res[0]);
+      const int need2 = need1 - sm.res[1];
+
+      // ---- pass C: per-warp key[7:0] inside prefix24 + per-warp above / zeros ----
+      for (int i = tid; i < kTkWarps * 256 + 32; i += kTkThreads) sm.hist[i] = 0;
+      __syncthreads();
+      {
+        int above = 0, zc = 0;
+        int* wh = sm.hist + w * 256;
+        TK_FOR_EACH({
+          const uint32_t hk = key >> 8;
+          above += valid & (hk > prefix24);
+          zc += valid & (key == kZeroKey);
+          const bool cand = valid & (hk == prefix24) & (key != kZeroKey);
+          atomicAdd(cand ? &wh[key & 0xFFu] : &sm.hist[kHistTrash + lane], 1);
+        })
+        above = warp_sum(above);
+        zc = warp_sum(zc);
+        if (lane == 0) {
+          if (zc && prefix24 == (kZeroKey >> 8)) atomicAdd(&wh[kZeroKey & 0xFFu], zc);
+          sm.above[w] = above;
+        }
       }
-    }
-    __syncthreads();
-    int* merged = sm.hist + kTkWarps * 256 + 32;
-    if (tid < 256) {
-      int s = 0;
-      for (int v = 0; v < kTkWarps; ++v) s += sm.hist[v * 256 + tid];
-      merged[tid] = s;
-    }
-    __syncthreads();
-    find_threshold<256>(merged, need2, sm.wtot, sm.res);
-    const uint32_t t3 = static_cast<uint32_t>(sm.res[0]);
-    thr = (prefix24 << 8) | t3;
-    remaining = need2 - sm.res[1];
-    {
-      const int* wh = sm.hist + w * 256;
-      int a = 0;
+      __syncthreads();
+      int* merged = sm.hist + kTkWarps * 256 + 32;
+      if (tid < 256) {
+        int s = 0;
+        for (int v = 0; v < kTkWarps; ++v) s += sm.hist[v * 256 + tid];
+        merged[tid] = s;
+      }
+      __syncthreads();
+      find_threshold<256>(merged, need2, sm.wtot, sm.res);
+      const uint32_t t3 = static_cast<uint32_t>(sm.res[0]);
+      thr = (prefix24 << 8) | t3;
+      remaining = need2 - sm.res[1];
+      {
+        const int* wh = sm.hist + w * 256;
+        int a = 0;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const uint32_t d = lane * 8 + j;
-        if (d > t3) a += wh[d];
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t d = lane * 8 + j;
+          if (d > t3) a += wh[d];
+        }
+        a = warp_sum(a);
+        if (lane == 0) {
+          sm.above[w] += a;
+          sm.ties[w] = wh[t3];
+        }
       }
-      a = warp_sum(a);
-      if (lane == 0) {
-        sm.above[w] += a;
-        sm.ties[w] = wh[t3];
-      }
+      __syncthreads();
     }
-    __syncthreads();
   }
-  }  // !resolved
   const int tie_base = kTopK - remaining;
 
   // ---- pass D: ordered compaction into shared memory ----
   // Canonical order: keys > thr in token order, then the first `remaining`
   // threshold ties in token order.  kSorted: the same set in token order.
-  int above_pos = 0, tie_pos = 0, sel_pos = 0;
-  for (int v = 0; v < w; ++v) {
-    above_pos += sm.above[v];
-    const int tv = sm.ties[v];
-    const int take = min(max(remaining - tie_pos, 0), tv);
-    sel_pos += sm.above[v] + take;
-    tie_pos += tv;
+  int above_pos, tie_pos, sel_pos;
+  {
+    const int av = sm.above[lane];
+    const int tv = sm.ties[lane];
+    const int a_inc = warp_incl_scan(av);
+    const int t_inc = warp_incl_scan(tv);
+    const int t_exc = t_inc - tv;
+    const int take = min(max(remaining - t_exc, 0), tv);
+    const int s_inc = warp_incl_scan(av + take);
+    above_pos = __shfl_sync(0xffffffffu, a_inc - av, w);
+    tie_pos = __shfl_sync(0xffffffffu, t_exc, w);
+    sel_pos = __shfl_sync(0xffffffffu, s_inc - (av + take), w);
   }
-  for (int c = seg_begin; c < seg_end; c += kStep * kTkUnroll) {
-    float rv[kTkUnroll][4];
-    uint32_t rm[kTkUnroll];
+  for (int c = seg_begin; c < seg_end; c += 32 * 16) {
+    const int i0 = c + 16 * lane;
+    uint32_t k[16];
+    const uint32_t vm = load16<kVec>(vals, mrow, i0, seg_end, k);
+    uint32_t ab = 0, tb = 0;
 #pragma unroll
-    for (int u = 0; u < kTkUnroll; ++u) load4<kVec>(vals, mrow, c + u * kStep + lane * 4, seg_end, rv[u], rm[u]);
-#pragma unroll
-    for (int u = 0; u < kTkUnroll; ++u) {
-      const int i0 = c + u * kStep + lane * 4;
-      uint32_t kk[4];
-      const uint32_t vv = keys4(i0, seg_end, rv[u], rm[u], kk);
-      int na = 0, nt = 0;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const bool valid = (vv >> j) & 1u;
-        na += valid & (kk[j] > thr);
-        nt += valid & (kk[j] == thr);
-      }
-      // inclusive warp scan of (na | nt << 16)
-      const int packed = na | (nt << 16);
-      int inc = packed;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, inc, o);
-        if (lane >= o) inc += y;
-      }
-      const int total = __shfl_sync(0xffffffffu, inc, 31);
-      const int ex = inc - packed;
-      if constexpr (!kSorted) {
+    for (int t = 0; t < 16; ++t) {
+      const uint32_t v = (vm >> t) & 1u;
+      ab |= (v & (k[t] > thr)) << t;
+      tb |= (v & (k[t] == thr)) << t;
+    }
+    const int na = __popc(ab);
+    const int nt = __popc(tb);
+    const int packed = na | (nt << 16);
+    const int inc = warp_incl_scan(packed);
+    const int total = __shfl_sync(0xffffffffu, inc, 31);
+    const int ex = inc - packed;
+    if constexpr (!kSorted) {
+      if (ab | tb) {
         int pa = above_pos + (ex & 0xFFFF);
         int pq = tie_pos + (ex >> 16);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const bool valid = (vv >> j) & 1u;
-          if (valid & (kk[j] > thr)) {
-            sm.out_idx[pa] = i0 + j;
-            sm.out_key[pa] = kk[j];
+        for (int t = 0; t < 16; ++t) {
+          if ((ab >> t) & 1u) {
+            sm.out_idx[pa] = i0 + t;
+            sm.out_key[pa] = k[t];
             ++pa;
-          } else if (valid & (kk[j] == thr)) {
+          } else if ((tb >> t) & 1u) {
             if (pq < remaining) {
-              sm.out_idx[tie_base + pq] = i0 + j;
-              sm.out_key[tie_base + pq] = kk[j];
+              sm.out_idx[tie_base + pq] = i0 + t;
+              sm.out_key[tie_base + pq] = k[t];
             }
             ++pq;
           }
         }
-      } else {
-        int pq = tie_pos + (ex >> 16);
-        uint32_t sel = 0;
+      }
+    } else {
+      int pq = tie_pos + (ex >> 16);
+      uint32_t sel = ab;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const bool valid = (vv >> j) & 1u;
-          const bool a = valid & (kk[j] > thr);
-          const bool t = valid & (kk[j] == thr);
-          if (a | (t & (pq < remaining))) sel |= 1u << j;
-          pq += t;
+      for (int t = 0; t < 16; ++t) {
+        if ((tb >> t) & 1u) {
+          if (pq < remaining) sel |= 1u << t;
+          ++pq;
         }
-        const int ns = __popc(sel);
-        int sinc = ns;
+      }
+      const int ns = __popc(sel);
+      const int sinc = warp_incl_scan(ns);
+      const int stot = __shfl_sync(0xffffffffu, sinc, 31);
+      int ps = sel_pos + sinc - ns;
+      if (sel) {
 #pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const int y = __shfl_up_sync(0xffffffffu, sinc, o);
-          if (lane >= o) sinc += y;
-        }
-        const int stot = __shfl_sync(0xffffffffu, sinc, 31);
-        int ps = sel_pos + sinc - ns;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          if ((sel >> j) & 1u) {
-            sm.out_idx[ps] = i0 + j;
-            sm.out_key[ps] = kk[j];
+        for (int t = 0; t < 16; ++t) {
+          if ((sel >> t) & 1u) {
+            sm.out_idx[ps] = i0 + t;
+            sm.out_key[ps] = k[t];
             ++ps;
           }
         }
-        sel_pos += stot;
       }
-      above_pos += total & 0xFFFF;
-      tie_pos += total >> 16;
+      sel_pos += stot;
     }
+    above_pos += total & 0xFFFF;
+    tie_pos += total >> 16;
   }
   __syncthreads();
   for (int i = tid; i < kTopK; i += kTkThreads) {
