@@ -44,11 +44,14 @@ def _peaks():
 
 
 def _profile_traffic(name):
-    """Per-launch DRAM bytes of a kernel from a committed ncu summary, or None."""
-    path = os.path.join(REPO, "profiles", name + ".json")
+    """Per-launch DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of a kernel from the
+    committed ncu summary profiles/<name>.md (its `dram_bytes_per_launch` row), or None."""
+    import re
+
+    path = os.path.join(REPO, "profiles", name + ".md")
     try:
-        with open(path) as f:
-            return json.load(f).get("dram_bytes_per_launch")
+        m = re.search(r"dram_bytes_per_launch\s*\|\s*(\d+)", open(path).read())
+        return int(m.group(1)) if m else None
     except Exception:  # noqa: BLE001
         return None
 
@@ -216,13 +219,14 @@ def run_decode(args, world, rank, local):
     for _ in range(3):
         e2e_step()
     barrier()
+    e2e_steps = min(args.steps, 200)
     x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     x0.record(stream)
-    for _ in range(args.steps):
+    for _ in range(e2e_steps):
         e2e_step()
     x1.record(stream)
     barrier()
-    ms_e2e = x0.elapsed_time(x1) / args.steps
+    ms_e2e = x0.elapsed_time(x1) / e2e_steps
     st = hcu_ops.read_device_status(clear=True)
     ok = torch.equal(res_host, out.cpu())
 
@@ -266,7 +270,8 @@ def run_decode(args, world, rank, local):
                      "traffic": traffic, "kernel": "mqa_logits_paged_kernel<64> (+ mask memset)",
                      "alg_bytes_per_launch": alg, "peak_source": src},
         "e2e": {"value": total_pairs / (ms_e2e * 1e-3) / 1e9, "unit": "G-scores/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e, "result_matches_graph": bool(ok)},
+                "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e, "steps": e2e_steps,
+                "result_matches_graph": bool(ok)},
         "gpu_launches": args.steps * 2,
         "clocks": clk.summary(),
         "device_status": st,
@@ -322,17 +327,18 @@ def run_reference(args):
                                       w["max_context_len"], G)
         O.topk_transform(lg, m, lens, w["page_table_size_1"].numpy())
 
+    steps = min(args.steps, 20)  # each step is the whole config on the CPU (~1-2 s)
     for _ in range(min(args.warmup, 1)):
         step()
     t0 = time.perf_counter()
-    for _ in range(args.steps):
+    for _ in range(steps):
         step()
-    dt = (time.perf_counter() - t0) / args.steps
+    dt = (time.perf_counter() - t0) / steps
     v = pairs / dt / 1e9
     return {
         "impl": "reference",
         "metric": "indexer G-scores/s (rows x visible KV tokens / s), decode logits + top-2048",
-        "value": v, "unit": "G-scores/s", "n_gpus": 0, "steps": args.steps, "warmup": min(args.warmup, 1),
+        "value": v, "unit": "G-scores/s", "n_gpus": 0, "steps": steps, "warmup": min(args.warmup, 1),
         "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "fp8e4m3 x fp8e4m3 -> fp32", "data": "synthetic (seeded, same generator as the GPU arm)",
         "config": {"workload": "config1: decode 64 req x next_n 2 (128 rows), ctx U[4096,65536], 64 heads x 128",
@@ -344,11 +350,286 @@ def run_reference(args):
     }
 
 
+# ------------------------------------------------------------------------------------------------
+# secondary workloads: bench.py --workload decode0 | prefill | dequant | mla_dequant | cp_prefill
+# (2, 3, the 656-byte MLA dequant, and 4).  Inputs that fit in L2 are timed one
+# launch at a time with a 256 MB L2 flush between launches (events around the launch only).
+# ------------------------------------------------------------------------------------------------
+def _timed_iters(fn, iters, flush):
+    import torch
+
+    evs = []
+    for _ in range(iters):
+        if flush is not None:
+            flush()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        evs.append((a, b))
+    torch.cuda.synchronize()
+    return sum(a.elapsed_time(b) for a, b in evs) / iters  # ms
+
+
+def _flusher(dev):
+    import torch
+
+    buf = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    return lambda: buf.zero_()
+
+
+def _base_record(args, world, metric, value, unit, ms, workload, **cfg):
+    return {"metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp8e4m3 x fp8e4m3 -> fp32", "data": "synthetic (seeded)",
+            "config": dict(workload=workload, **cfg)}
+
+
+def run_decode0(args, world, rank, local):
+    import torch
+
+    import hcu_ops
+    from hcu_ops.workloads import config0
+
+    dev = torch.device("cuda", local)
+    w = config0(device=dev, seed=rank)
+    lens, pt, cu = w["context_lens"], w["page_table_size_1"], w["cu_seqlens_q"]
+
+    def step():
+        lg, mk = hcu_ops.mqa_logits(w["q"], w["kv_cache"], w["weights"], lens, w["block_table"],
+                                    w["max_context_len"], 1, hist_lens=lens)
+        return hcu_ops.sparse_mask_topk_transform(lg, mk, lens, pt, cu, 2048)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    flush = _flusher(dev)
+    iters = min(args.steps, 500)
+    ms = _timed_iters(step, iters, flush)
+    pairs = int(lens.long().sum())
+    hbm, _, src = _peaks()
+    alg = decode_alg_bytes(w)
+    rec = _base_record(args, world, "decode indexer latency, config 0 (1 row x 8192 tokens, 64 heads)",
+                       ms * 1e3, "us", ms, "config0: decode 1 x 8192, 64 heads, permuted pages; L2 flushed",
+                       pairs=pairs)
+    rec["higher_is_better"] = False
+    rec["g_scores_per_s"] = pairs / (ms * 1e-3) / 1e9
+    rec["roofline"] = {"bound": "latency", "achieved": alg / (ms * 1e-3) / 1e9, "peak": hbm, "unit": "GB/s",
+                       "frac": alg / (ms * 1e-3) / 1e9 / hbm, "traffic": None, "peak_source": src,
+                       "note": "1.1 MB of work: latency-bound, roofline not claimed"}
+    rec["gpu_launches"] = iters * 2
+    return rec
+
+
+def run_dequant(args, world, rank, local, mla=False):
+    import torch
+
+    import hcu_ops
+    from hcu_ops.workloads import make_index_k_dequant, make_mla_dequant
+
+    dev = torch.device("cuda", local)
+    if mla:
+        n = int(os.environ.get("HCU_BENCH_MLA_TOKENS", "392832"))
+        w = make_mla_dequant(n, 1 << 19, seed=rank, device=dev)
+        fn = lambda: hcu_ops.dequantize_k_cache_paged(w["quant_k_cache"], w["page_table_1_flattened"])  # noqa: E731
+        per_tok = 656 + 1152 + 4
+        name = f"MLA 656-byte paged dequant, {n} tokens (pool 2^19 slots)"
+    else:
+        n = 131072
+        w = make_index_k_dequant(n, 4096, seed=rank, device=dev)
+        fn = lambda: hcu_ops.dequant_index_k_paged(w["kv_cache"], w["token_loc"])  # noqa: E731
+        per_tok = 132 + 256 + 4
+        name = "config3: indexer-K paged dequant, 131072 tokens over permuted 64-token pages"
+    for _ in range(max(args.warmup, 3)):
+        fn()
+    iters = min(args.steps, 500)
+    ms = _timed_iters(fn, iters, _flusher(dev))
+    alg = per_tok * n
+    gbs = alg / (ms * 1e-3) / 1e9
+    hbm, _, src = _peaks()
+    rec = _base_record(args, world, "paged K-cache dequant throughput (algorithmic bytes / s)", gbs * world,
+                       "GB/s", ms, name + "; L2 flushed between launches", tokens=n, bytes_per_token=per_tok)
+    rec["dtype"] = "fp8e4m3 -> fp32 -> bf16"
+    rec["roofline"] = {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                       "traffic": None, "alg_bytes_per_launch": alg, "peak_source": src}
+    rec["gpu_launches"] = iters
+    return rec
+
+
+def _prefill_inputs(dev, rows, prefix, seed):
+    from hcu_ops.workloads import make_ragged
+
+    return make_ragged(rows, prefix, heads=64, seed=seed, device=dev)
+
+
+def run_prefill(args, world, rank, local):
+    import torch
+
+    import hcu_ops
+
+    dev = torch.device("cuda", local)
+    w = _prefill_inputs(dev, 8192, 65536, seed=rank)
+    N = w["k_fp8"].shape[0]
+    rows = w["q"].shape[0]
+    lens = w["row_end"]
+    ident = torch.arange(N, dtype=torch.int32, device=dev).expand(rows, N)
+    cu = torch.arange(rows + 1, dtype=torch.int32, device=dev)
+
+    def logits():
+        return hcu_ops.mqa_logits_ragged(w["q"], w["k_fp8"], w["k_scale"], w["weights"], w["row_start"], lens)
+
+    def step():
+        lg, mk = logits()
+        return hcu_ops._C.sparse_mask_topk_transform(lg, mk, lens, ident, cu, 2048)
+
+    for _ in range(max(min(args.warmup, 3), 1)):
+        step()
+    iters = min(args.steps, 10)
+    ms = _timed_iters(step, iters, None)
+    ms_lg = _timed_iters(logits, iters, None)
+    pairs = int((lens.long() - w["row_start"].long()).sum())
+    flops = 2.0 * 64 * 128 * pairs
+    _, bf16, src = _peaks()
+    fp8_peak = 2.0 * bf16
+    tflops = flops / (ms_lg * 1e-3) / 1e12
+    rec = _base_record(args, world, "prefill indexer G-scores/s (rows x visible KV tokens / s), logits + top-2048",
+                       pairs / (ms * 1e-3) / 1e9 * world, "G-scores/s", ms,
+                       "config2: prefill chunk 8192 rows x (65536 + i + 1) tokens, 64 heads; inputs 77 MB, "
+                       "logits 2.4 GB > L2", pairs=pairs)
+    rec["logits_op_ms"] = ms_lg
+    rec["top_k_rows_per_s"] = rows / ((ms - ms_lg) * 1e-3)
+    rec["roofline"] = {"bound": "tensor", "achieved": tflops, "peak": fp8_peak, "unit": "TFLOP/s",
+                       "frac": tflops / fp8_peak, "traffic": None, "kernel": "mqa_logits_ragged_kernel<64>",
+                       "flops_per_launch": flops, "peak_source": src + " (fp8 dense = 2 x measured bf16 burst)"}
+    rec["gpu_launches"] = iters * 2
+    return rec
+
+
+def run_cp_prefill(args, world, rank, local):
+    import torch
+
+    from hcu_ops.cp import cp_prefill_topk, kv_range
+
+    dev = torch.device("cuda", local)
+    rows, prefix = 16384, 131072 - 16384
+    w = _prefill_inputs(dev, rows, prefix, seed=0)  # identical on every rank (replicated q, full K generated)
+    N = w["k_fp8"].shape[0]
+    lo, hi = kv_range(rank, world, N)
+    kf = w["k_fp8"][lo:hi].contiguous()
+    ks = w["k_scale"][lo:hi].contiguous()
+    del w["k_fp8"], w["k_scale"]
+    torch.cuda.empty_cache()
+
+    def step():
+        return cp_prefill_topk(w["q"], kf, ks, w["weights"], w["row_end"], N)
+
+    for _ in range(max(min(args.warmup, 2), 1)):
+        out = step()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    iters = min(args.steps, 5)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        out = step()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / iters
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms = t.item()
+    pairs = int(w["row_end"].long().sum())
+    del out
+    if rank != 0:
+        return None
+    flops = 2.0 * 64 * 128 * pairs
+    _, bf16, src = _peaks()
+    rec = _base_record(args, world, "CP prefill indexer G-scores/s (rows x visible KV tokens / s), logits + local "
+                       "top-2048 + exchange + merge", pairs / (ms * 1e-3) / 1e9, "G-scores/s", ms,
+                       "config4: 16384 rows x (114688 + i + 1) tokens over a 131072-token context split into "
+                       f"{world} contiguous KV ranges, 64 heads; row-sharded NCCL exchange", pairs=pairs,
+                       parallelism=f"cp{world}")
+    rec["scaling"] = "strong"
+    achieved = flops / (ms * 1e-3) / 1e12
+    rec["roofline"] = {"bound": "tensor", "achieved": achieved, "peak": 2.0 * bf16 * world, "unit": "TFLOP/s",
+                       "frac": achieved / (2.0 * bf16 * world), "traffic": None,
+                       "peak_source": src + " (fp8 dense = 2 x measured bf16 burst, x n_gpus)"}
+    rec["gpu_launches"] = iters * 3
+    return rec
+
+
+WORKLOADS = {"decode0": run_decode0, "dequant": run_dequant,
+             "mla_dequant": lambda a, w, r, l: run_dequant(a, w, r, l, mla=True),
+             "prefill": run_prefill, "cp_prefill": run_cp_prefill}
+
+
+def run_reference_sample(args):
+    """CPU oracle on a bounded sample of a secondary workload (--impl reference)."""
+    import numpy as np
+    import torch
+
+    from oracle import indexer as O
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    wl = args.workload
+    t0 = time.perf_counter()
+    if wl == "decode0":
+        from hcu_ops.workloads import config0
+
+        w = config0()
+        lg, m, _ = O.mqa_logits_paged(w["q"].view(torch.uint8).numpy().reshape(1, 64, 128),
+                                      w["kv_cache"].numpy().reshape(w["kv_cache"].shape[0], -1),
+                                      w["weights"].numpy(), w["context_lens"].numpy(), w["block_table"].numpy(),
+                                      w["max_context_len"], 1)
+        O.topk_transform(lg, m, w["context_lens"].numpy(), w["page_table_size_1"].numpy())
+        dt = time.perf_counter() - t0
+        value, unit, sample = dt * 1e6, "us", "whole config 0"
+    elif wl in ("dequant", "mla_dequant"):
+        from hcu_ops.workloads import make_index_k_dequant, make_mla_dequant
+
+        if wl == "dequant":
+            w = make_index_k_dequant(131072, 4096)
+            t0 = time.perf_counter()
+            O.dequant_index_k(w["kv_cache"].numpy().reshape(4096, -1), w["token_loc"].numpy())
+            n, per = 131072, 392
+        else:
+            w = make_mla_dequant(32768, 1 << 19)
+            t0 = time.perf_counter()
+            O.dequant_mla_656(w["quant_k_cache"].view(torch.uint8).numpy().reshape(-1, 656),
+                              w["page_table_1_flattened"].numpy())
+            n, per = 32768, 1812
+        dt = time.perf_counter() - t0
+        value, unit, sample = n * per / dt / 1e9, "GB/s", f"{n} tokens"
+    else:
+        rows, prefix = (8192, 65536) if wl == "prefill" else (16384, 131072 - 16384)
+        from hcu_ops.workloads import make_ragged
+
+        w = make_ragged(rows, prefix, heads=64)
+        sel = np.linspace(0, rows - 1, 64).astype(int)  # stratified subset of rows
+        t0 = time.perf_counter()
+        lg, m, _ = O.mqa_logits_ragged(w["q"].view(torch.uint8).numpy(), w["k_fp8"].view(torch.uint8).numpy(),
+                                       w["k_scale"].numpy(), w["weights"].numpy(), w["row_start"].numpy(),
+                                       w["row_end"].numpy(), rows=list(sel))
+        N = lg.shape[1]
+        O.topk_transform(lg, m, w["row_end"].numpy()[sel], np.tile(np.arange(N, dtype=np.int32), (64, 1)))
+        dt = time.perf_counter() - t0
+        pairs_s = float(w["row_end"].numpy()[sel].astype(np.int64).sum())
+        value, unit = pairs_s / dt / 1e9, "G-scores/s"
+        sample = f"64 stratified rows of {rows} ({int(pairs_s)} scores), rate extrapolated by pair count"
+    return {"impl": "reference", "metric": f"{wl} (CPU oracle)", "value": value, "unit": unit, "n_gpus": 0,
+            "steps": 1, "warmup": 0, "ms_per_step": dt * 1e3, "higher_is_better": unit != "us",
+            "config": {"workload": wl},
+            "cpu_baseline": {"value": value, "unit": unit, "cores": torch.get_num_threads(), "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=3000)
+    ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="decode")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -356,7 +637,8 @@ def main():
     world, rank, local = _dist()
     if args.impl == "reference":
         if rank == 0:
-            print(json.dumps(run_reference(args)), flush=True)
+            rec = run_reference(args) if args.workload == "decode" else run_reference_sample(args)
+            print(json.dumps(rec), flush=True)
         return
     import torch
 
@@ -367,9 +649,14 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=torch.device("cuda", local))
     try:
-        if args.workload != "decode":
+        if args.workload == "decode":
+            rec = run_decode(args, world, rank, local)
+        elif args.workload in WORKLOADS:
+            rec = WORKLOADS[args.workload](args, world, rank, local)
+            if rec is not None and world > 1 and args.workload != "cp_prefill":
+                rec = rec if rank == 0 else None
+        else:
             raise SystemExit(f"unknown workload {args.workload}")
-        rec = run_decode(args, world, rank, local)
         if rec is not None:
             print(json.dumps(rec), flush=True)
     finally:

@@ -706,7 +706,7 @@ int check_common(const float* score, int64_t rows, int64_t width, int64_t score_
   if (rows < 0 || width < 0 || width > INT32_MAX / 2 || rows > INT32_MAX) return HCU_ERR_ARG;
   if (rows == 0) return HCU_OK;
   if (!score || !mask || !lengths || !pt || !dst) return HCU_ERR_ARG;
-  if (score_stride < width || mask_stride < (width + 15) / 16 || pt_stride < 1) return HCU_ERR_ARG;
+  if (score_stride < width || mask_stride < (width + 15) / 16 || pt_stride < 0) return HCU_ERR_ARG;
   return HCU_OK;
 }
 

@@ -1,0 +1,102 @@
+"""CPU multi-process test of the context-parallel driver (gloo, world size 2 and 3).
+
+The device ops are replaced by oracle-backed CPU stand-ins so the distributed plumbing (KV-range
+split, local selection in token order, row-sharded all-to-all / all-gather exchange, merge) is
+exercised without a GPU; the result must equal the single-range top-k exactly."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+
+class OracleOps:
+    def logits(self, q, k_fp8, k_scale, weights, rs, re):
+        from oracle import indexer as O
+
+        lg, m, _ = O.mqa_logits_ragged(q.view(torch.uint8).numpy(), k_fp8.view(torch.uint8).numpy(),
+                                       k_scale.numpy(), weights.numpy(), rs.numpy(), re.numpy())
+        return torch.from_numpy(lg), torch.from_numpy(m)
+
+    def local_topk(self, score, mask, lengths, pt):
+        from oracle import indexer as O
+
+        idx, keys = O.topk_transform(score.numpy(), mask.numpy(), lengths.numpy(),
+                                     np.ascontiguousarray(pt.numpy()), return_keys=True)
+        for r in range(idx.shape[0]):  # ascending token order, as the device op emits
+            v = idx[r] >= 0
+            o = np.argsort(idx[r][v], kind="stable")
+            idx[r][v] = idx[r][v][o]
+            keys[r][v] = keys[r][v][o]
+        return torch.from_numpy(idx), torch.from_numpy(keys.view(np.int32))
+
+    def merge(self, keys, gidx, lengths):
+        from oracle import indexer as O
+
+        return torch.from_numpy(O.cp_merge(keys.numpy().view(np.uint32), gidx.numpy(), lengths.numpy()))
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, mode, q):
+    import sys
+
+    here = os.path.dirname(os.path.abspath(__file__))
+    for p in (os.path.dirname(here), os.path.join(os.path.dirname(here), "sglang0.5.18-opt_b200"), here):
+        sys.path.insert(0, p)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        from hcu_ops.cp import cp_prefill_topk, kv_range
+        from hcu_ops.workloads import make_ragged
+
+        w = make_ragged(23, 5000, heads=32, seed=11)  # same seed on every rank: replicated q
+        N = w["k_fp8"].shape[0]
+        lo, hi = kv_range(rank, world, N)
+        out = cp_prefill_topk(w["q"], w["k_fp8"][lo:hi].contiguous(), w["k_scale"][lo:hi].contiguous(),
+                              w["weights"], w["row_end"], N, mode=mode, ops=OracleOps())
+        q.put((rank, out.numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,mode", [(2, "rowshard"), (2, "allgather"), (3, "rowshard")])
+def test_cp_driver_equals_single_range(world, mode):
+    from hcu_ops.workloads import make_ragged
+    from oracle import indexer as O
+
+    w = make_ragged(23, 5000, heads=32, seed=11)
+    lg, m, _ = O.mqa_logits_ragged(w["q"].view(torch.uint8).numpy(), w["k_fp8"].view(torch.uint8).numpy(),
+                                   w["k_scale"].numpy(), w["weights"].numpy(), w["row_start"].numpy(),
+                                   w["row_end"].numpy())
+    N = lg.shape[1]
+    ident = np.tile(np.arange(N, dtype=np.int32), (23, 1))
+    ref = O.topk_transform(lg, m, w["row_end"].numpy(), ident)
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, mode, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = {}
+    for _ in range(world):
+        r, out = q.get(timeout=240)
+        got[r] = out
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for r in range(world):
+        assert np.array_equal(got[r], ref), f"rank {r}"
