@@ -39,8 +39,10 @@ int launch_pass1_hist(const float* logits, int64_t rows, int64_t width, const in
 
 namespace {
 
-constexpr int kLgThreads = 352;  // warps 0 + 10 TMA, warp 1 MMA, warps 2-9 epilogue
-constexpr int kEpiWarps = 8;
+constexpr int kLgThreads = 480;  // warps 0 + 14 TMA, warp 1 MMA, warps 2-13 epilogue
+constexpr int kTeams = 3;        // epilogue teams of 4 warps (one per TMEM lane quadrant) on alternate tiles
+constexpr int kEpiWarps = 4 * kTeams;
+constexpr int kProducerB = 2 + kEpiWarps;  // second TMA producer warp
 constexpr int kMaxAcc = 4;     // TMEM accumulator buffers (4 when N <= 128, else 2)
 constexpr int kStages = 8;
 constexpr int kTileTok = 128;
@@ -210,7 +212,7 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_paged_kernel(const _
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&sm.full[s], 2);  // one expect_tx arrival per producer warp
-      mbar_init(&sm.empty[s], 1 + kEpiWarps / 2);
+      mbar_init(&sm.empty[s], 1 + 4);  // MMA commit + the 4 warps of the tile's team
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&sm.qfull[i], 1);
@@ -218,7 +220,7 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_paged_kernel(const _
     }
     for (int i = 0; i < kMaxAcc; ++i) {
       mbar_init(&sm.tfull[i], 1);
-      mbar_init(&sm.tempty[i], kEpiWarps / 2);
+      mbar_init(&sm.tempty[i], 4);
     }
     mbar_init(&sm.done, 1);
     sm.abort = 0;
@@ -237,11 +239,11 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_paged_kernel(const _
   const uint32_t tmem = sm.tmem_base;
   volatile int* abort = &sm.abort;
 
-  if (warp == 0 || warp == 10) {
+  if (warp == 0 || warp == kProducerB) {
     // ------------------------------------------------ TMA producers
     // A single issuing thread sustains roughly one TMA op per ~200 cycles and
     // is slow at dependent scalar code, so (a) the two pages of a tile are
-    // issued by two warps (warp 0: page 0 and the Q rows, warp 10: page 1),
+    // issued by two warps (warp 0: page 0 and the Q rows, warp kProducerB: page 1),
     // and (b) each warp first resolves the page ids of up to 32 upcoming items
     // in parallel (one lane per item) into shared memory; lane 0 then only
     // waits for a free stage and issues the page + scale boxes.
@@ -366,13 +368,14 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_paged_kernel(const _
       mbar_wait_drain(&sm.done, 0, &g_hcu_status);
     }
   } else if (warp >= 2 && warp < 2 + kEpiWarps) {
-    // ------------------------------------------------ epilogue (warps 2..9)
-    // Two teams of four warps (one warp per TMEM lane quadrant) take alternate
-    // tiles, so two tiles' TMEM-load / math / store chains are in flight at once;
-    // each warp computes every row of its team's tiles for its 32 tokens.
+    // ------------------------------------------------ epilogue (warps 2..13)
+    // kTeams teams of four warps (one warp per TMEM lane quadrant) take the tiles
+    // round robin, so kTeams tiles' TMEM-load / math / store chains are in flight
+    // at once; each warp computes every row of its team's tiles for its 32 tokens.
     const int ew = warp - 2;
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
     const int team = ew >> 2;
+    int turn = 0;  // it % kTeams
     float* wsm = sm.w[ew];
     int* lsm = sm.lens[ew];
     Cursor cur;
@@ -388,7 +391,9 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_paged_kernel(const _
       const int aph = acc.phase;
       st.adv(kStages);
       acc.adv(NACC);
-      if ((it & 1) != team) continue;
+      const bool mine = turn == team;
+      if (++turn == kTeams) turn = 0;
+      if (!mine) continue;
       const int key = cur.g * n_sub + cur.sub;
       const int row0 = cur.g * p.G + cur.sub * p.R;
       if (key != qkey) {
@@ -469,13 +474,14 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_paged_kernel(const _
 // per CTA on the device.  Same logits / mask contract as the paged kernel.
 constexpr int kPfStages = 4;
 constexpr int kQB = 4;
+constexpr int kPfEpiWarps = 8;  // warps 2..9; the kernel shares the block size of the paged kernel
 
 struct __align__(1024) PfSmem {
   uint8_t q[kQB][kQTile];
   uint8_t a[kPfStages][kATile];
-  float w[kEpiWarps][kQB * kMaxN / 2];  // weights of the rows this epilogue warp owns
-  int rs[kEpiWarps][16];
-  int re[kEpiWarps][16];
+  float w[kPfEpiWarps][kQB * kMaxN / 2];  // weights of the rows this epilogue warp owns
+  int rs[kPfEpiWarps][16];
+  int re[kPfEpiWarps][16];
   uint64_t full[kPfStages];
   uint64_t empty[kPfStages];
   uint64_t qfull;
@@ -606,13 +612,13 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_ragged_kernel(const 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kPfStages; ++s) {
       mbar_init(&sm.full[s], 1);
-      mbar_init(&sm.empty[s], 1 + kEpiWarps);
+      mbar_init(&sm.empty[s], 1 + kPfEpiWarps);
     }
     mbar_init(&sm.qfull, 1);
     mbar_init(&sm.qempty, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&sm.tfull[i], 1);
-      mbar_init(&sm.tempty[i], kEpiWarps);
+      mbar_init(&sm.tempty[i], kPfEpiWarps);
     }
     mbar_init(&sm.done, 1);
     sm.abort = 0;
@@ -698,8 +704,8 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_ragged_kernel(const 
       tc_commit(&sm.done);
       mbar_wait_drain(&sm.done, 0, &g_hcu_status);
     }
-  } else if (warp >= 2 && warp < 2 + kEpiWarps) {
-    // ------------------------------------------------ epilogue (warps 2..9; warp 10 idles here)
+  } else if (warp >= 2 && warp < 2 + kPfEpiWarps) {
+    // ------------------------------------------------ epilogue (warps 2..9; warps 10+ idle here)
     const int ew = warp - 2;
     const int quad = warp & 3;
     const int half = ew >> 2;  // rows r % 2 == half of every row block
