@@ -1,0 +1,90 @@
+"""Context-parallel prefill over NCCL on 2 GPUs: every rank's result equals the 1-GPU result.
+
+Each rank scores its own KV range with the ragged logits kernel, selects a local top-2048 in
+token order, and the ranks exchange and merge the lists (row-sharded all-to-all, then an
+all-gather of the final indices; the all-gather mode is checked too).  Skipped with fewer
+than two visible GPUs.  Ranks are spawned processes with NVLS off and a short process-group
+timeout, so a rank that fails ends the others' collectives with an error instead of a wait."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+ROWS, PREFIX = 300, 20000
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _rank(rank, world, port, mode, q):
+    import datetime
+    import sys
+
+    here = os.path.dirname(os.path.abspath(__file__))
+    for p in (os.path.dirname(here), os.path.join(os.path.dirname(here), "sglang0.5.18-opt_b200")):
+        sys.path.insert(0, p)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        from hcu_ops.cp import cp_prefill_topk, kv_range
+        from hcu_ops.workloads import make_ragged
+
+        w = make_ragged(ROWS, PREFIX, heads=64, seed=5)
+        N = w["k_fp8"].shape[0]
+        lo, hi = kv_range(rank, world, N)
+        out = cp_prefill_topk(w["q"].to(dev), w["k_fp8"][lo:hi].contiguous().to(dev),
+                              w["k_scale"][lo:hi].contiguous().to(dev), w["weights"].to(dev),
+                              w["row_end"].to(dev), N, mode=mode)
+        torch.cuda.synchronize()
+        q.put((rank, out.cpu().numpy()))
+    except Exception as e:  # reported to the parent; the process group timeout ends the peer
+        q.put((rank, repr(e)))
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("mode", ["rowshard", "allgather"])
+def test_cp_nccl_two_gpus_equals_one_gpu(hcu, dev, mode):
+    from hcu_ops.cp import cp_prefill_topk
+    from hcu_ops.workloads import make_ragged
+
+    w = make_ragged(ROWS, PREFIX, heads=64, seed=5)
+    N = w["k_fp8"].shape[0]
+    ref = cp_prefill_topk(w["q"].to(dev), w["k_fp8"].to(dev), w["k_scale"].to(dev), w["weights"].to(dev),
+                          w["row_end"].to(dev), N).cpu().numpy()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, mode, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = {}
+    try:
+        for _ in range(2):
+            r, out = q.get(timeout=300)
+            got[r] = out
+    finally:
+        for p in procs:
+            p.join(timeout=120)
+    for p in procs:
+        assert p.exitcode == 0
+    for r in range(2):
+        assert isinstance(got[r], np.ndarray), got[r]
+        assert np.array_equal(got[r], ref), f"rank {r}: {(got[r] != ref).sum()} differing entries"
