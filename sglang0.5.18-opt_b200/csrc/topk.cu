@@ -1,21 +1,25 @@
 // Stage 3: exact top-2048 over masked scores + page-table transform.
 //
-// topk_row_kernel: one 1024-thread CTA (32 warps) per row.  Warp w owns the
-// contiguous token segment [w*seg, (w+1)*seg) of the row (seg a multiple of
-// 128 = 32 lanes x 4 tokens), so the final compaction only needs per-warp
-// counts and an in-warp prefix -- no block-wide scan per chunk.
-// Threshold search, normally two streaming passes in total:
-//   S  4096 strided samples; a radix select of two sample order statistics
-//      around the threshold's expected sample rank (+-4 sigma) gives [lo, hi]
-//   1  one pass counts keys > hi, == hi, == lo per warp and collects the keys
-//      strictly inside (lo, hi) (a few % of the row) in shared memory; the
-//      threshold is hi, lo, or an exact radix select among the collected keys
-//   D  the ordered compaction below.
-// When the bracket misses (it cannot change the result, only the cost), the
-// full radix passes run instead (the row stays L2-resident between passes):
+// topk_row_kernel: one 1024-thread CTA (32 warps) per row.
+// Candidate path (the normal case, one streaming pass over the row):
+//   S  m strided samples (2048 for rows <= 128K tokens) go into a 12-bit and
+//      then an 8-bit histogram; the sample order statistic a few sigma below
+//      the threshold's expected sample rank gives a lower bound lo (20 key
+//      bits resolved).  With the logits kernel's exact pass-1 histogram (the
+//      "pre" path) lo is the threshold's 12-bit bin instead, with no sampling.
+//   P  rounds of 16384 tokens (lane: 16 consecutive tokens; warp: 512): every
+//      token with key >= lo is appended to a shared-memory candidate list at
+//      its block-wide prefix position, so the list is in token order.  For a
+//      positive lo the test is one signed compare of the raw float bits.
+//   Q  an 8-bit-digit radix select over the candidates (digits below the
+//      common prefix of lo and the largest candidate) gives the threshold key,
+//      the count above it and the number of ties to take.
+//   R  one block scan of (above, tie) flags over the list writes the output.
+// If the list holds fewer than 2048 tokens (the bound missed) or overflows,
+// the full radix passes run instead (the row stays L2-resident):
 //   A  12-bit histogram of key[31:20] + per-warp positive / zero counts
-//      (skipped when the logits kernel already built it: the "pre" path);
-//      positives <= 2048 <= positives + zeros -> the threshold is +0 (fast path)
+//      (skipped on the "pre" path); positives <= 2048 <= positives + zeros ->
+//      the threshold is +0 (sparse fast path)
 //   B  12-bit histogram of key[19:8] inside the threshold bin
 //   C  per-warp 8-bit histograms of key[7:0] inside the 24-bit prefix, per-warp
 //      count of keys above the prefix and of exact zeros
@@ -37,30 +41,36 @@ constexpr int kStep = 128;  // tokens per warp step (32 lanes x 4)
 constexpr int kTkUnroll = 4;
 constexpr int kHistTrash = kTkWarps * 256;  // trash slots follow the per-warp histograms
 
-constexpr int kSmallSample = 2048;  // row samples used to bracket the threshold (rows <= 128K)
-constexpr int kSample = 8192;       // sample capacity (rows > 512K)
-constexpr int kMidCap = 8192;   // keys collected strictly inside the bracket
+constexpr int kSmallSample = 2048;  // row samples used to bound the threshold (rows <= 128K)
+constexpr int kSample = 8192;       // sample count for rows > 512K
+constexpr int kCandCap = 8192;      // candidate list capacity (tokens with key >= lo)
+constexpr int kLaneTok = 16;        // consecutive tokens per lane in a streaming round
+constexpr int kRound = kTkThreads * kLaneTok;  // tokens per streaming round
 
 struct __align__(16) TopkSmem {
   int hist[kTkWarps * 256 + 32 + 256];  // A/B: [0,4096) + trash; C: 32 x 256 + trash + merged[256]
   int out_idx[kTopK + 32];
   uint32_t out_key[kTopK + 32];
-  uint32_t samp[kSample];
-  uint32_t mid_key[kMidCap];
-  uint8_t mid_warp[kMidCap];
+  uint32_t cand_key[kCandCap];
+  int32_t cand_idx[kCandCap];
+  int32_t cand_pid[kCandCap];  // page-table entry of each candidate (async copies)
+  uint4 scr[kLaneTok / 4][kTkThreads];  // this thread's current 16 score words (candidate pass)
+  int hb[2][512];  // digit histograms (sample refinement: 256 bins, candidate select: 512)
+  int wcnt[2][kTkWarps];
+  uint32_t wmax[kTkWarps];
   int above[kTkWarps];
   int ties[kTkWarps];
   int zeros[kTkWarps];
   int pos[kTkWarps];
-  int gt_w[kTkWarps];
-  int eh_w[kTkWarps];
-  int el_w[kTkWarps];
-  int mid_above_w[kTkWarps];
-  int mid_tie_w[kTkWarps];
   int wtot[kTkWarps];
   int res[4];
-  int mid_n;
 };
+
+// 4-byte global -> shared copy that does not hold a register (LDGSTS).
+__device__ __forceinline__ void cp_async4(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 __device__ __forceinline__ int warp_sum(int x) {
 #pragma unroll
@@ -145,46 +155,6 @@ __device__ __forceinline__ void find_threshold(const int* hist, int need, int* w
   __syncthreads();
 }
 
-// Key of rank `rank` (1 = largest) among keys[0, n) in shared memory, by a
-// 12/12/8-bit radix select; *above = number of keys strictly greater than it.
-// Requires 1 <= rank <= n.  Block-wide; uses sm.hist / sm.wtot / sm.res.
-__device__ __forceinline__ uint32_t smem_select_rank(const uint32_t* keys, int n, int rank, TopkSmem& sm,
-                                                     int* above) {
-  const int tid = threadIdx.x;
-  int need = rank;
-  int abv = 0;
-  for (int i = tid; i < kBins; i += kTkThreads) sm.hist[i] = 0;
-  __syncthreads();
-  for (int i = tid; i < n; i += kTkThreads) atomicAdd(&sm.hist[keys[i] >> 20], 1);
-  __syncthreads();
-  find_threshold<kBins>(sm.hist, need, sm.wtot, sm.res);
-  const uint32_t b1 = static_cast<uint32_t>(sm.res[0]);
-  abv += sm.res[1];
-  need -= sm.res[1];
-  for (int i = tid; i < kBins; i += kTkThreads) sm.hist[i] = 0;
-  __syncthreads();
-  for (int i = tid; i < n; i += kTkThreads) {
-    const uint32_t k = keys[i];
-    if ((k >> 20) == b1) atomicAdd(&sm.hist[(k >> 8) & 0xFFFu], 1);
-  }
-  __syncthreads();
-  find_threshold<kBins>(sm.hist, need, sm.wtot, sm.res);
-  const uint32_t p24 = (b1 << 12) | static_cast<uint32_t>(sm.res[0]);
-  abv += sm.res[1];
-  need -= sm.res[1];
-  for (int i = tid; i < 256; i += kTkThreads) sm.hist[i] = 0;
-  __syncthreads();
-  for (int i = tid; i < n; i += kTkThreads) {
-    const uint32_t k = keys[i];
-    if ((k >> 8) == p24) atomicAdd(&sm.hist[k & 0xFFu], 1);
-  }
-  __syncthreads();
-  find_threshold<256>(sm.hist, need, sm.wtot, sm.res);
-  abv += sm.res[1];
-  *above = abv;
-  return (p24 << 8) | static_cast<uint32_t>(sm.res[0]);
-}
-
 // Branch-free monotone key.
 __device__ __forceinline__ uint32_t key_of(float x) {
   const uint32_t b = __float_as_uint(x);
@@ -231,6 +201,271 @@ __device__ __forceinline__ int warp_incl_scan(int x) {
     if (lane >= o) x += y;
   }
   return x;
+}
+
+// Warp 0 of the block: bin b of the NB-bin histogram h with
+// suffix(b) >= need > suffix(b+1); res[0] = b, res[1] = suffix(b+1).
+// Requires sum(h) >= need >= 1.
+template <int NB>
+__device__ __forceinline__ void warp_find(const int* h, int need, int* res) {
+  constexpr int P = NB / 32;  // bins per lane
+  const int lane = threadIdx.x & 31;
+  int v[P];
+#pragma unroll
+  for (int q = 0; q < P / 4; ++q) {
+    const int4 a = reinterpret_cast<const int4*>(h)[lane * (P / 4) + q];
+    v[4 * q] = a.x;
+    v[4 * q + 1] = a.y;
+    v[4 * q + 2] = a.z;
+    v[4 * q + 3] = a.w;
+  }
+  int s = 0;
+#pragma unroll
+  for (int j = 0; j < P; ++j) s += v[j];
+  int x = s;  // inclusive suffix over lanes >= lane
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_down_sync(0xffffffffu, x, o);
+    if (lane + o < 32) x += y;
+  }
+  const int nxt = x - s;
+  if (x >= need && nxt < need) {
+    int acc = nxt;
+#pragma unroll
+    for (int j = P - 1; j >= 0; --j) {
+      if (acc + v[j] >= need) {
+        res[0] = lane * P + j;
+        res[1] = acc;
+        break;
+      }
+      acc += v[j];
+    }
+  }
+}
+
+// Exclusive block-wide prefix sum of x; *total = the block sum.  One barrier;
+// consecutive calls must be separated by a barrier (wtot is reused).
+__device__ __forceinline__ int block_excl_scan(int x, int* wtot, int* total) {
+  const int lane = threadIdx.x & 31;
+  const int w = threadIdx.x >> 5;
+  const int inc = warp_incl_scan(x);
+  if (lane == 31) wtot[w] = inc;
+  __syncthreads();
+  const int t = wtot[lane];
+  const int ti = warp_incl_scan(t);
+  *total = __shfl_sync(0xffffffffu, ti, 31);
+  return __shfl_sync(0xffffffffu, ti - t, w) + inc - x;
+}
+
+// Raw float bits of this lane's 16 consecutive tokens [i0, i0 + 16) (0 at and
+// past `lim`); `valid` = the slots below lim.  Returns their mask word.
+template <bool kVec>
+__device__ __forceinline__ uint32_t load16_raw(const float* __restrict__ vals, const int16_t* __restrict__ mrow,
+                                               int i0, int lim, uint32_t (&b)[16], uint32_t& valid) {
+  if (i0 >= lim) {
+#pragma unroll
+    for (int t = 0; t < 16; ++t) b[t] = 0u;
+    valid = 0u;
+    return 0u;
+  }
+  const uint32_t mw = static_cast<uint16_t>(__ldg(mrow + (i0 >> 4)));
+  if constexpr (kVec) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 f = make_uint4(0u, 0u, 0u, 0u);
+      if (i0 + 4 * q < lim) f = __ldg(reinterpret_cast<const uint4*>(vals + i0 + 4 * q));
+      b[4 * q] = f.x;
+      b[4 * q + 1] = f.y;
+      b[4 * q + 2] = f.z;
+      b[4 * q + 3] = f.w;
+    }
+  } else {
+#pragma unroll
+    for (int t = 0; t < 16; ++t) b[t] = i0 + t < lim ? __float_as_uint(__ldg(vals + i0 + t)) : 0u;
+  }
+  const int nv = lim - i0;
+  valid = nv >= 16 ? 0xFFFFu : ((1u << nv) - 1u);
+  return mw;
+}
+
+// One round of the candidate pass for the 16 tokens of this lane whose raw
+// bits are in X (round r).  The words go to this thread's scratch slot, X is
+// refilled with round r + 2, and after the round's barrier the candidates are
+// appended at their block-wide prefix position, visiting set bits only.
+template <bool kVec, bool kPos>
+__device__ __forceinline__ void candidate_round(const float* __restrict__ vals, const int16_t* __restrict__ mrow,
+                                                const int32_t* __restrict__ src, int len, uint32_t lo, int r, int nr,
+                                                TopkSmem& sm,
+                                                uint32_t (&X)[16], uint32_t& mX, uint32_t& vX, int& base,
+                                                uint32_t& kmax) {
+  const int lane = threadIdx.x & 31;
+  const int w = threadIdx.x >> 5;
+  const int i0 = r * kRound + w * (32 * kLaneTok) + lane * kLaneTok;
+  const int lim_pos = static_cast<int>(lo ^ kZeroKey);
+  uint32_t cb = 0u;
+#pragma unroll
+  for (int t = 0; t < 16; ++t) {
+    bool c;
+    if constexpr (kPos) {
+      c = static_cast<int>(X[t]) >= lim_pos;
+    } else {
+      c = (((mX >> t) & 1u) ? key_of(__uint_as_float(X[t])) : kZeroKey) >= lo;
+    }
+    cb |= static_cast<uint32_t>(c) << t;
+  }
+  cb &= kPos ? (mX & vX) : vX;
+  const uint32_t mcur = mX;
+  if (cb) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) sm.scr[q][threadIdx.x] = make_uint4(X[4 * q], X[4 * q + 1], X[4 * q + 2], X[4 * q + 3]);
+  }
+  const int nc = __popc(cb);
+  const int inc = warp_incl_scan(nc);
+  if (lane == 31) sm.wcnt[r & 1][w] = inc;
+  if (r + 2 < nr) mX = load16_raw<kVec>(vals, mrow, i0 + 2 * kRound, len, X, vX);
+  __syncthreads();
+  const int wc = sm.wcnt[r & 1][lane];
+  const int wi = warp_incl_scan(wc);
+  const int wbase = __shfl_sync(0xffffffffu, wi - wc, w);
+  const int rtot = __shfl_sync(0xffffffffu, wi, 31);
+  int pos = base + wbase + inc - nc;
+  const uint32_t* mine = reinterpret_cast<const uint32_t*>(&sm.scr[0][threadIdx.x]);
+  while (cb) {
+    const int t = __ffs(cb) - 1;
+    cb &= cb - 1u;
+    const uint32_t raw = mine[(t >> 2) * (4 * kTkThreads) + (t & 3)];
+    uint32_t key;
+    if constexpr (kPos) {
+      key = raw | kZeroKey;
+    } else {
+      key = ((mcur >> t) & 1u) ? key_of(__uint_as_float(raw)) : kZeroKey;
+    }
+    kmax = key > kmax ? key : kmax;
+    if (pos < kCandCap) {
+      sm.cand_key[pos] = key;
+      sm.cand_idx[pos] = i0 + t;
+      cp_async4(&sm.cand_pid[pos], src + i0 + t);
+    }
+    ++pos;
+  }
+  base += rtot;
+}
+
+// Candidate pass: appends every token of [0, len) whose key is >= lo to
+// sm.cand_key / sm.cand_idx in token order, in block-wide rounds of kRound
+// tokens (warp w takes tokens [w*512, w*512+512) of a round, lane l 16 of
+// them).  A / mA / vA hold round 0's loads on entry; two rounds of loads are
+// in flight at every barrier.  kPos (lo > +0): a token is a candidate iff its
+// mask bit is set and its float bits, as a signed integer, are >=
+// lo ^ 0x80000000.  Returns the candidate count (nothing past kCandCap is
+// stored); sm.wmax receives each warp's largest candidate key.  Each stored
+// candidate's page-table entry src[idx] is copied to sm.cand_pid
+// asynchronously (waited for in write_candidates).
+template <bool kVec, bool kPos>
+__device__ __forceinline__ int collect_candidates(const float* __restrict__ vals, const int16_t* __restrict__ mrow,
+                                                  const int32_t* __restrict__ src, int len, uint32_t lo, TopkSmem& sm,
+                                                  uint32_t (&A)[16],
+                                                  uint32_t mA, uint32_t vA) {
+  const int lane = threadIdx.x & 31;
+  const int w = threadIdx.x >> 5;
+  const int nr = (len + kRound - 1) / kRound;
+  uint32_t B[16], mB = 0u, vB = 0u;
+  if (nr > 1) mB = load16_raw<kVec>(vals, mrow, kRound + w * (32 * kLaneTok) + lane * kLaneTok, len, B, vB);
+  int base = 0;
+  uint32_t kmax = 0u;
+  for (int r = 0; r < nr; r += 2) {
+    candidate_round<kVec, kPos>(vals, mrow, src, len, lo, r, nr, sm, A, mA, vA, base, kmax);
+    if (r + 1 < nr) candidate_round<kVec, kPos>(vals, mrow, src, len, lo, r + 1, nr, sm, B, mB, vB, base, kmax);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const uint32_t y = __shfl_xor_sync(0xffffffffu, kmax, o);
+    kmax = y > kmax ? y : kmax;
+  }
+  if (lane == 0) sm.wmax[w] = kmax;
+  __syncthreads();
+  return base;
+}
+
+// Threshold key of rank kTopK among the n candidates (kTopK <= n <= kCandCap,
+// all keys >= lo): a radix select of u = key - lo with 9-bit digits from the
+// top bit of (largest candidate - lo) down.  *above = candidates with a
+// larger key.  sm.hb[0] and sm.hb[1] must be zero on entry.
+__device__ __forceinline__ uint32_t select_candidates(TopkSmem& sm, int n, uint32_t lo, int* above) {
+  constexpr int kDigit = 9;
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int w = tid >> 5;
+  uint32_t kmax = sm.wmax[lane];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const uint32_t y = __shfl_xor_sync(0xffffffffu, kmax, o);
+    kmax = y > kmax ? y : kmax;
+  }
+  const uint32_t span = kmax - lo;
+  const int d = span ? 31 - __clz(span) : 0;  // every u has no bit above d
+  uint32_t pre = 0u;
+  int need = kTopK;
+  int abv = 0;
+  for (int s = d + 1 - kDigit, rnd = 0;; s -= kDigit, ++rnd) {
+    const int sh = s > 0 ? s : 0;
+    const int nb = s + kDigit - sh;  // bits in this digit (the last one may be short)
+    const uint32_t dm = (1u << nb) - 1u;
+    int* h = sm.hb[rnd & 1];
+    for (int i = tid; i < n; i += kTkThreads) {
+      const uint32_t u = sm.cand_key[i] - lo;
+      if ((static_cast<uint64_t>(u) >> (sh + nb)) == pre) atomicAdd(&h[(u >> sh) & dm], 1);
+    }
+    if (tid < 512) sm.hb[(rnd + 1) & 1][tid] = 0;
+    __syncthreads();
+    if (w == 0) warp_find<512>(h, need, sm.res);
+    __syncthreads();
+    abv += sm.res[1];
+    need -= sm.res[1];
+    pre = (pre << nb) | static_cast<uint32_t>(sm.res[0]);
+    if (sh == 0) break;
+  }
+  *above = abv;
+  return lo + pre;
+}
+
+// Output from the candidate list: keys > thr in token order, then the first
+// kTopK - above ties in token order (kSorted: the same set in token order),
+// through the page-table entries copied during the candidate pass.
+// Candidate i goes to thread i / ceil(n / 1024).
+template <bool kSorted>
+__device__ __forceinline__ void write_candidates(TopkSmem& sm, int n, uint32_t thr, int above,
+                                                 int32_t* __restrict__ out, uint32_t* __restrict__ okeys) {
+  const int remaining = kTopK - above;
+  const int per = (n + kTkThreads - 1) / kTkThreads;
+  const int i0 = min(n, static_cast<int>(threadIdx.x) * per);
+  const int i1 = min(n, i0 + per);
+  int na = 0, nt = 0;
+  for (int i = i0; i < i1; ++i) {
+    const uint32_t k = sm.cand_key[i];
+    na += k > thr;
+    nt += k == thr;
+  }
+  cp_async_wait_all();  // the barrier in the scan publishes every thread's page-id copies
+  int total;
+  const int ex = block_excl_scan(na | (nt << 16), sm.wtot, &total);
+  int ea = ex & 0xFFFF;
+  int et = ex >> 16;
+  for (int i = i0; i < i1; ++i) {
+    const uint32_t k = sm.cand_key[i];
+    int p = -1;
+    if (k > thr) {
+      p = kSorted ? ea + min(et, remaining) : ea;
+      ++ea;
+    } else if (k == thr) {
+      if (et < remaining) p = kSorted ? ea + et : above + et;
+      ++et;
+    }
+    if (p >= 0) {
+      out[p] = sm.cand_pid[i];
+      if (okeys) okeys[p] = k;
+    }
+  }
 }
 
 // Visits every token slot of this warp's segment as (valid, key, index i0+j);
@@ -294,118 +529,105 @@ __global__ __launch_bounds__(kTkThreads, 1) void topk_row_kernel(
 
   uint32_t thr = 0;
   int remaining = 0;
-  bool resolved = false;
-  if (pre_ws == nullptr) {
-    // ---- bracket select: sample -> [lo, hi] -> one counting pass -> exact select inside ----
-    const int m = len <= kSmallSample ? len : (len <= (1 << 17) ? kSmallSample : (len <= (1 << 19) ? 4096 : kSample));
-    const float stride_f = static_cast<float>(len) / static_cast<float>(m);
-    for (int k = tid; k < m; k += kTkThreads) {
-      const int i = min(len - 1, static_cast<int>((static_cast<float>(k) + 0.5f) * stride_f));
-      const bool set = (static_cast<uint16_t>(__ldg(mrow + (i >> 4))) >> (i & 15)) & 1u;
-      sm.samp[k] = set ? key_of(__ldg(vals + i)) : kZeroKey;
-    }
-    if (tid == 0) sm.mid_n = 0;
-    __syncthreads();
-    int r_hi = kTopK, r_lo = kTopK;
-    if (m < len) {  // expected sample rank of the threshold +- 4 sigma
-      const float t = static_cast<float>(kTopK) / stride_f;
-      const float d = 4.f * sqrtf(t) + 4.f;
-      r_hi = max(1, static_cast<int>(floorf(t - d)));
-      r_lo = min(m, static_cast<int>(ceilf(t + d)));
-    }
-    int dummy;
-    const uint32_t hi = smem_select_rank(sm.samp, m, r_hi, sm, &dummy);
-    const uint32_t lo = r_lo == r_hi ? hi : smem_select_rank(sm.samp, m, r_lo, sm, &dummy);
-    {
-      int n_gt = 0, n_eh = 0, n_el = 0;
-      for (int c = seg_begin; c < seg_end; c += 32 * 16) {
-        const int i0 = c + 16 * lane;
-        uint32_t k[16];
-        const uint32_t vm = load16<kVec>(vals, mrow, i0, seg_end, k);
-        uint32_t midb = 0;
+  {
+    // ---- candidate path ----
+    // The sample loads go out first (they gate the bound), then round 0's
+    // loads, whose latency overlaps the bound search.
+    const int m = len <= (1 << 17) ? kSmallSample : (len <= (1 << 19) ? 4096 : kSample);
+    const int groups = m / 4;  // m samples in groups of 4 consecutive tokens, one 16-byte load each
+    constexpr int kGpt = kSample / (4 * kTkThreads);  // sample groups per thread (at most)
+    float sv[4 * kGpt];
+    uint32_t smb[kGpt];
+    if (pre_ws == nullptr) {
+      const float stride_g = static_cast<float>(len) / static_cast<float>(groups);
+      const int gmax = (len - 4) & ~3;
 #pragma unroll
-        for (int t = 0; t < 16; ++t) {
-          const uint32_t v = (vm >> t) & 1u;
-          n_gt += v & (k[t] > hi);
-          n_eh += v & (k[t] == hi);
-          n_el += v & (k[t] == lo);
-          midb |= (v & (k[t] > lo) & (k[t] < hi)) << t;
-        }
-        if (__any_sync(0xffffffffu, midb != 0u)) {
-          const int nm = __popc(midb);
-          const int inc = warp_incl_scan(nm);
-          int base = 0;
-          if (lane == 31) base = atomicAdd(&sm.mid_n, inc);
-          base = __shfl_sync(0xffffffffu, base, 31);
-          int pos = base + inc - nm;
-          if (midb) {
+      for (int j = 0; j < kGpt; ++j) {
+        const int g = tid + j * kTkThreads;
+        smb[j] = 0u;
 #pragma unroll
-            for (int t = 0; t < 16; ++t) {
-              if ((midb >> t) & 1u) {
-                if (pos < kMidCap) {
-                  sm.mid_key[pos] = k[t];
-                  sm.mid_warp[pos] = static_cast<uint8_t>(w);
-                }
-                ++pos;
-              }
-            }
+        for (int e = 0; e < 4; ++e) sv[4 * j + e] = 0.f;
+        if (g < groups) {
+          const int i = min(gmax, static_cast<int>((static_cast<float>(g) + 0.5f) * stride_g) & ~3);
+          smb[j] = (static_cast<uint16_t>(__ldg(mrow + (i >> 4))) >> (i & 15)) & 0xFu;
+          if constexpr (kVec) {
+            const float4 f = __ldg(reinterpret_cast<const float4*>(vals + i));
+            sv[4 * j] = f.x;
+            sv[4 * j + 1] = f.y;
+            sv[4 * j + 2] = f.z;
+            sv[4 * j + 3] = f.w;
+          } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) sv[4 * j + e] = __ldg(vals + i + e);
           }
         }
       }
-      n_gt = warp_sum(n_gt);
-      n_eh = warp_sum(n_eh);
-      n_el = warp_sum(n_el);
-      if (lane == 0) {
-        sm.gt_w[w] = n_gt;
-        sm.eh_w[w] = n_eh;
-        sm.el_w[w] = lo != hi ? n_el : 0;
-        sm.mid_above_w[w] = 0;
-        sm.mid_tie_w[w] = 0;
+    }
+    uint32_t b0[16], valid0;
+    const uint32_t mw0 = load16_raw<kVec>(vals, mrow, w * (32 * kLaneTok) + lane * kLaneTok, len, b0, valid0);
+    for (int i = tid; i < 2 * 512; i += kTkThreads) (&sm.hb[0][0])[i] = 0;
+    uint32_t lo = 0u;
+    bool try_cand = false;
+    if (pre_ws == nullptr) {
+      for (int i = tid; i < kBins; i += kTkThreads) sm.hist[i] = 0;
+      __syncthreads();
+      const float stride_f = static_cast<float>(len) / static_cast<float>(m);
+      uint32_t sk[4 * kGpt];
+#pragma unroll
+      for (int j = 0; j < 4 * kGpt; ++j) {
+        sk[j] = ((smb[j / 4] >> (j % 4)) & 1u) ? key_of(sv[j]) : kZeroKey;
+        if (tid + (j / 4) * kTkThreads < groups) atomicAdd(&sm.hist[sk[j] >> 20], 1);
+      }
+      __syncthreads();
+      // sample rank (1 = largest) 4 sigma + 4 below the threshold's expected sample rank
+      const float t = static_cast<float>(kTopK) / stride_f;
+      const int r_lo = min(m, static_cast<int>(ceilf(t + 4.f * sqrtf(t) + 4.f)));
+      find_threshold<kBins>(sm.hist, r_lo, sm.wtot, sm.res);
+      const uint32_t b1 = static_cast<uint32_t>(sm.res[0]);
+      const int need = r_lo - sm.res[1];
+#pragma unroll
+      for (int j = 0; j < 4 * kGpt; ++j)
+        if (tid + (j / 4) * kTkThreads < groups && (sk[j] >> 20) == b1)
+          atomicAdd(&sm.hb[0][(sk[j] >> 12) & 0xFFu], 1);
+      __syncthreads();
+      if (w == 0) warp_find<256>(sm.hb[0], need, sm.res);
+      __syncthreads();
+      lo = (b1 << 20) | (static_cast<uint32_t>(sm.res[0]) << 12);
+      if (tid < 256) sm.hb[0][tid] = 0;  // ordered before the select by the candidate pass's barriers
+      try_cand = true;
+    } else {
+      // the logits kernel's exact pass-1 histogram: lo = the threshold's 12-bit bin
+      const int* h1 = pre_ws + static_cast<int64_t>(row) * kBins;
+      const int* cnt = pre_ws + 2 * static_cast<int64_t>(rows) * kBins + 2 * row;
+      const int positives = cnt[0];
+      const int zeros = cnt[1];
+      if (!(positives <= kTopK && positives + zeros >= kTopK)) {
+        if (tid == 0) {  // a histogram that does not hold kTopK tokens leaves lo = 0 (still exact)
+          sm.res[0] = 0;
+          sm.res[1] = 0;
+        }
+        find_threshold<kBins>(h1, kTopK, sm.wtot, sm.res);
+        const int b1 = sm.res[0];
+        lo = static_cast<uint32_t>(b1) << 20;
+        try_cand = sm.res[1] + h1[b1] <= kCandCap;
+      }
+    }
+    if (try_cand) {
+      const int n = lo > kZeroKey ? collect_candidates<kVec, true>(vals, mrow, src, len, lo, sm, b0, mw0, valid0)
+                                  : collect_candidates<kVec, false>(vals, mrow, src, len, lo, sm, b0, mw0, valid0);
+      if (n < kTopK || n > kCandCap) cp_async_wait_all();  // no copy outlives the candidate path
+      if (n >= kTopK && n <= kCandCap) {
+        int above = 0;
+        thr = select_candidates(sm, n, lo, &above);
+        write_candidates<kSorted>(sm, n, thr, above, out,
+                                  dst_keys ? dst_keys + static_cast<int64_t>(row) * kTopK : nullptr);
+        return;
       }
     }
     __syncthreads();
-    const int G = warp_sum(sm.gt_w[lane]);
-    const int EH = warp_sum(sm.eh_w[lane]);
-    const int EL = warp_sum(sm.el_w[lane]);
-    const int M = sm.mid_n;
-    int mode = 0;  // 0: bracket missed -> full radix below
-    if (G < kTopK) {
-      if (G + EH >= kTopK) {
-        mode = 1;
-        thr = hi;
-        remaining = kTopK - G;
-      } else if (M <= kMidCap && G + EH + M >= kTopK) {
-        mode = 2;
-      } else if (M <= kMidCap && G + EH + M + EL >= kTopK) {
-        mode = 3;
-        thr = lo;
-        remaining = kTopK - (G + EH + M);
-      }
-    }
-    if (mode == 2) {
-      const int need = kTopK - G - EH;
-      int abv = 0;
-      thr = smem_select_rank(sm.mid_key, M, need, sm, &abv);
-      remaining = need - abv;
-    }
-    if (mode != 0) {
-      const int mn = M < kMidCap ? M : kMidCap;
-      for (int i = tid; i < mn; i += kTkThreads) {
-        const uint32_t k = sm.mid_key[i];
-        if (k > thr) atomicAdd(&sm.mid_above_w[sm.mid_warp[i]], 1);
-        else if (k == thr) atomicAdd(&sm.mid_tie_w[sm.mid_warp[i]], 1);
-      }
-      __syncthreads();
-      if (lane == 0) {
-        sm.above[w] = sm.gt_w[w] + (thr < hi ? sm.eh_w[w] : 0) + sm.mid_above_w[w];
-        sm.ties[w] = (thr == hi ? sm.eh_w[w] : 0) + sm.mid_tie_w[w] + (thr == lo ? sm.el_w[w] : 0);
-      }
-      __syncthreads();
-      resolved = true;
-    }
   }
 
-  if (!resolved) {
+  {
     // ---- pass A: key[31:20] histogram, positives and zeros ----
     int positives = 0, zeros = 0;
     const int* hist1 = sm.hist;
