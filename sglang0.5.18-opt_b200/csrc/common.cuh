@@ -156,6 +156,40 @@ __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
   return *reinterpret_cast<float2*>(&d);
 }
 
+// Scale of the saturating ReLU below: 2^25 exceeds |q . k| for any fp8 e4m3
+// q, k of 128 dims (128 * 448 * 448 < 2^25), so sat(x * 2^-25) = relu(x) * 2^-25
+// exactly (power-of-two scaling, clamped to [0, 1], NaN -> 0).
+constexpr float kReluScale = 33554432.f;  // 2^25
+
+// acc += relu(x) * w on a pair of lanes, where w2 = w * 2^25 (the caller
+// pre-scales the weights): the ReLU is one saturating fma.rn.sat.f32 per lane
+// on the FMA pipe and the two products go through one fma.rn.f32x2.  The
+// result equals fma(relu(x), w, acc) bit for bit (both scalings are exact;
+// weights must satisfy |w| < 2^102, where w * relu(x) itself nears overflow).
+__device__ __forceinline__ void relu_fma2(float2& acc, uint32_t x0, uint32_t x1, float w0, float w1) {
+  asm("{\n\t"
+      ".reg .f32 a, b;\n\t"
+      ".reg .b64 p, q, r;\n\t"
+      "fma.rn.sat.f32 a, %2, 0f33000000, 0f00000000;\n\t"
+      "fma.rn.sat.f32 b, %3, 0f33000000, 0f00000000;\n\t"
+      "mov.b64 p, {a, b};\n\t"
+      "mov.b64 q, {%4, %5};\n\t"
+      "mov.b64 r, {%0, %1};\n\t"
+      "fma.rn.f32x2 r, p, q, r;\n\t"
+      "mov.b64 {%0, %1}, r;\n\t"
+      "}"
+      : "+f"(acc.x), "+f"(acc.y)
+      : "f"(__uint_as_float(x0)), "f"(__uint_as_float(x1)), "f"(w0), "f"(w1));
+}
+
+// Shared-memory struct at the first 1024-byte boundary of the dynamic shared
+// buffer, reached by pointer arithmetic on the buffer itself so that the
+// compiler keeps the shared address space (ld.shared, not generic loads).
+template <typename T>
+__device__ __forceinline__ T& smem_aligned_1024(unsigned char* raw) {
+  return *reinterpret_cast<T*>(raw + ((1024u - (smem_u32(raw) & 1023u)) & 1023u));
+}
+
 // Named barrier over `count` threads (a subset of the CTA).
 __device__ __forceinline__ void named_bar(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
@@ -214,6 +248,22 @@ __device__ __forceinline__ void tmem_ld_x32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
         "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
+}
+
+// 32-column TMEM load and its wait in one statement: the registers are
+// defined only after the wait, so no separate register fence is needed.
+__device__ __forceinline__ void tmem_ld_x32_sync(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]),
+        "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
+        "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
 }
 
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }

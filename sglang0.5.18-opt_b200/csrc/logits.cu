@@ -39,10 +39,14 @@ int launch_pass1_hist(const float* logits, int64_t rows, int64_t width, const in
 
 namespace {
 
-constexpr int kLgThreads = 480;  // warps 0 + 14 TMA, warp 1 MMA, warps 2-13 epilogue
 constexpr int kTeams = 3;        // epilogue teams of 4 warps (one per TMEM lane quadrant) on alternate tiles
 constexpr int kEpiWarps = 4 * kTeams;
-constexpr int kProducerB = 2 + kEpiWarps;  // second TMA producer warp
+constexpr int kProducers = 4;  // TMA producer warps; producer k issues every box of the items it % kProducers == k
+constexpr int kProducerB = 2 + kEpiWarps;  // first of the extra TMA producer warps
+constexpr int kLgThreads = (2 + kEpiWarps + kProducers - 1) * 32;  // warp 0 + extra TMA, warp 1 MMA, 2.. epilogue
+// Above 16 warps a thread has at most 96 registers: the epilogue then reads one
+// 32-head TMEM chunk at a time instead of a whole row.
+constexpr bool kPgChunked = kLgThreads > 512;
 constexpr int kMaxAcc = 4;     // TMEM accumulator buffers (4 when N <= 128, else 2)
 constexpr int kStages = 8;
 constexpr int kTileTok = 128;
@@ -57,9 +61,7 @@ struct __align__(1024) LgSmem {
   float sc[kStages][2 * kPage];    // k_scale of the stage's two pages
   float w[kEpiWarps][kMaxN];       // head weights, one copy per epilogue warp
   int lens[kEpiWarps][8];          // row lengths of the current row block, per epilogue warp
-  int bq_ph[2][32];                // producer batch: page id of page `half` of each item (-1: none)
-  int bq_key[2][32];               // producer batch: (group, row block) key of each item
-  int bq_qrow[2][32];              // producer batch: first Q row of each item's row block
+  int bq_ph[kProducers][2][32];    // producer batch (per producer warp): page ids of each item's two pages (-1: none)
   uint64_t full[kStages];
   uint64_t empty[kStages];         // 1 MMA commit + the 4 epilogue warps of the tile's team (they read sc[])
   uint64_t qfull[2];
@@ -151,8 +153,7 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_paged_kernel(const _
                                                                         const __grid_constant__ CUtensorMap tm_q,
                                                                         const PagedArgs p) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  LgSmem& sm = *reinterpret_cast<LgSmem*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  LgSmem& sm = smem_aligned_1024<LgSmem>(smem_raw);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int n_groups = p.batch / p.G;
@@ -211,7 +212,7 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_paged_kernel(const _
   while (ncols < static_cast<uint32_t>(NACC * NC)) ncols <<= 1;
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&sm.full[s], 2);  // one expect_tx arrival per producer warp
+      mbar_init(&sm.full[s], 1);  // the item's producer: one expect_tx arrival
       mbar_init(&sm.empty[s], 1 + 4);  // MMA commit + the 4 warps of the tile's team
     }
     for (int i = 0; i < 2; ++i) {
@@ -239,122 +240,127 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_paged_kernel(const _
   const uint32_t tmem = sm.tmem_base;
   volatile int* abort = &sm.abort;
 
-  if (warp == 0 || warp == kProducerB) {
+  if (warp == 0 || warp >= kProducerB) {
     // ------------------------------------------------ TMA producers
-    // A single issuing thread sustains roughly one TMA op per ~200 cycles and
-    // is slow at dependent scalar code, so (a) the two pages of a tile are
-    // issued by two warps (warp 0: page 0 and the Q rows, warp kProducerB: page 1),
-    // and (b) each warp first resolves the page ids of up to 32 upcoming items
-    // in parallel (one lane per item) into shared memory; lane 0 then only
-    // waits for a free stage and issues the page + scale boxes.
-    const int half = warp == 0 ? 0 : 1;
-    Cursor cur;  // every lane keeps an identical copy, positioned before item `it`
+    // Every mbarrier / TMA instruction of a lone issuing thread costs ~200
+    // cycles (its warp shares a scheduler with epilogue warps), so the items
+    // are dealt round robin to kProducers warps: producer k issues both pages
+    // and both scale boxes of items k, k + kProducers, ...  Each warp first
+    // resolves the page ids of its next 32 items in parallel (one lane per
+    // item) into shared memory; lane 0 then waits for the item's stage and
+    // issues its boxes.  Stage of item i: i % kStages (kStages % kProducers == 0).
+    const int role = warp == 0 ? 0 : warp - kProducerB + 1;
+    Cursor cur;  // every lane keeps an identical copy, positioned before item `it0`
     cur.init(p, sm.start_group, sm.start_local);
-    Ring st;
-    Ring qr;
-    int qkey = -1, issued = 0, qloads = 0, ok = 1;
-    for (int it = 0; it < count && ok; it += 32) {
-      const int nb = min(32, count - it);
+    int issued = 0, last_it = -1, ok = 1;
+    for (int it0 = 0; it0 < count && ok; it0 += 32 * kProducers) {
       {
         Cursor c = cur;
-        int ph = -1, key = 0, qrow = 0;
-        if (lane < nb) {
-          for (int k = 0; k <= lane; ++k) c.next(p);
-          const int pg = 2 * c.tile + half;
+        const int my = it0 + role + lane * kProducers;  // this lane's item
+        int ph0 = -1, ph1 = -1;
+        if (my < count) {
+          for (int k = 0; k <= role + lane * kProducers; ++k) c.next(p);
           const int n_pg = (c.len + kPage - 1) / kPage;
-          if (pg < n_pg) ph = __ldg(p.bt + static_cast<int64_t>(c.g) * p.G * p.bt_stride + pg);
-          key = c.g * n_sub + c.sub;
-          qrow = (c.g * p.G + c.sub * p.R) * H;
+          const int32_t* bt = p.bt + static_cast<int64_t>(c.g) * p.G * p.bt_stride;
+          if (2 * c.tile < n_pg) ph0 = __ldg(bt + 2 * c.tile);
+          if (2 * c.tile + 1 < n_pg) ph1 = __ldg(bt + 2 * c.tile + 1);
         }
         __syncwarp();
-        sm.bq_ph[half][lane] = ph;
-        sm.bq_key[half][lane] = key;
-        sm.bq_qrow[half][lane] = qrow;
-        // every lane advances its copy to the item after this batch
-        const Cursor last = c;
-        cur.g = __shfl_sync(0xffffffffu, last.g, nb - 1);
-        cur.sub = __shfl_sync(0xffffffffu, last.sub, nb - 1);
-        cur.tile = __shfl_sync(0xffffffffu, last.tile, nb - 1);
-        cur.len = __shfl_sync(0xffffffffu, last.len, nb - 1);
-        cur.tiles = __shfl_sync(0xffffffffu, last.tiles, nb - 1);
+        sm.bq_ph[role][0][lane] = ph0;
+        sm.bq_ph[role][1][lane] = ph1;
+        // advance every lane's copy to the end of this window (item it0 + 32 * kProducers - 1);
+        // only needed when the window does not reach past the range
+        if (it0 + 32 * kProducers < count) {
+          for (int k = 0; k < kProducers - 1 - role; ++k) c.next(p);
+          cur.g = __shfl_sync(0xffffffffu, c.g, 31);
+          cur.sub = __shfl_sync(0xffffffffu, c.sub, 31);
+          cur.tile = __shfl_sync(0xffffffffu, c.tile, 31);
+          cur.len = __shfl_sync(0xffffffffu, c.len, 31);
+          cur.tiles = __shfl_sync(0xffffffffu, c.tiles, 31);
+        }
         __syncwarp();
       }
       if (lane == 0) {
-        for (int j = 0; j < nb; ++j) {
-          if (half == 0) {
-            const int key = sm.bq_key[0][j];
-            if (key != qkey) {
-              if (!mbar_wait(&sm.qempty[qr.idx], qr.phase ^ 1, abort, &g_hcu_status)) {
-                ok = 0;
-                break;
-              }
-              mbar_arrive_expect_tx(&sm.qfull[qr.idx], static_cast<uint32_t>(NC * kHeadDim));
-              tma_load_2d(sm.q[qr.idx], &tm_q, &sm.qfull[qr.idx], 0, sm.bq_qrow[0][j]);
-              qr.adv(2);
-              ++qloads;
-              qkey = key;
-            }
-          }
-          if (!mbar_wait(&sm.empty[st.idx], st.phase ^ 1, abort, &g_hcu_status)) {
+        for (int j = 0; j < 32; ++j) {
+          const int it = it0 + role + j * kProducers;
+          if (it >= count) break;
+          const int s = it % kStages;
+          if (!mbar_wait(&sm.empty[s], ((it / kStages) & 1) ^ 1, abort, &g_hcu_status)) {
             ok = 0;
             break;
           }
-          const int ph = sm.bq_ph[half][j];
-          if (ph >= 0) {
-            mbar_arrive_expect_tx(&sm.full[st.idx], kPageFp8Bytes + kPage * 4);
-            tma_load_3d(sm.a[st.idx] + half * kPageFp8Bytes, &tm_kv, &sm.full[st.idx], 0, 0, ph);
-            tma_load_2d(sm.sc[st.idx] + half * kPage, &tm_sc, &sm.full[st.idx], 0, ph);
+          const int ph0 = sm.bq_ph[role][0][j];
+          const int ph1 = sm.bq_ph[role][1][j];
+          const uint32_t bytes = (ph0 >= 0 ? kPageFp8Bytes + kPage * 4 : 0) + (ph1 >= 0 ? kPageFp8Bytes + kPage * 4 : 0);
+          if (bytes) {
+            mbar_arrive_expect_tx(&sm.full[s], bytes);
+            if (ph0 >= 0) {
+              tma_load_3d(sm.a[s], &tm_kv, &sm.full[s], 0, 0, ph0);
+              tma_load_2d(sm.sc[s], &tm_sc, &sm.full[s], 0, ph0);
+            }
+            if (ph1 >= 0) {
+              tma_load_3d(sm.a[s] + kPageFp8Bytes, &tm_kv, &sm.full[s], 0, 0, ph1);
+              tma_load_2d(sm.sc[s] + kPage, &tm_sc, &sm.full[s], 0, ph1);
+            }
           } else {
-            mbar_arrive(&sm.full[st.idx]);  // no such page in this tile
+            mbar_arrive(&sm.full[s]);  // no page in this tile (cannot happen for in-range items)
           }
-          st.adv(kStages);
           ++issued;
+          last_it = it;
         }
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
     }
     if (lane == 0) {
       // Drain: every copy issued must land before the CTA may exit.
-      Ring d;
-      const int first = issued > kStages ? issued - kStages : 0;
-      for (int i2 = 0; i2 < issued; ++i2) {
-        if (i2 >= first) mbar_wait_drain(&sm.full[d.idx], d.phase, &g_hcu_status);
-        d.adv(kStages);
-      }
-      Ring dq;
-      for (int j = 0; j < qloads; ++j) {
-        if (j >= qloads - 2) mbar_wait_drain(&sm.qfull[dq.idx], dq.phase, &g_hcu_status);
-        dq.adv(2);
+      for (int k = 0; k < kStages / kProducers && k < issued; ++k) {
+        const int it = last_it - k * kProducers;
+        mbar_wait_drain(&sm.full[it % kStages], (it / kStages) & 1, &g_hcu_status);
       }
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ------------------------------------------------ MMA issuer
+    // ------------------------------------------------ MMA issuer (also loads Q)
+    // Q of the j-th distinct (group, row block) key goes to slot j & 1; the next
+    // key's Q is prefetched as soon as the current one is in use.
     if (elect_one()) {
       Cursor cur;
       cur.init(p, sm.start_group, sm.start_local);
-      Ring st, acc, qr;
-      int qkey = -1, qn = 0;
+      Ring st, acc;
+      int qkey = -1, kq = -1, nq = 0;
       uint32_t idesc = 0;
-      int q_slot = 0;
-      for (int it = 0; it < count; ++it) {
+      bool ok = true;
+      auto issue_q = [&](int n, int qrow) -> bool {
+        const int slot = n & 1;
+        if (!mbar_wait(&sm.qempty[slot], ((n >> 1) & 1) ^ 1, abort, &g_hcu_status)) return false;
+        mbar_arrive_expect_tx(&sm.qfull[slot], static_cast<uint32_t>(NC * kHeadDim));
+        tma_load_2d(sm.q[slot], &tm_q, &sm.qfull[slot], 0, qrow);
+        nq = n + 1;
+        return true;
+      };
+      for (int it = 0; it < count && ok; ++it) {
         cur.next(p);
         const int key = cur.g * n_sub + cur.sub;
         if (key != qkey) {
-          if (qn > 0) tc_commit(&sm.qempty[q_slot]);
-          if (!mbar_wait(&sm.qfull[qr.idx], qr.phase, abort, &g_hcu_status)) break;
-          q_slot = qr.idx;
-          qr.adv(2);
-          ++qn;
+          if (kq >= 0) tc_commit(&sm.qempty[kq & 1]);  // the slot frees when the old key's MMAs finish
+          ++kq;
+          if (nq <= kq && !issue_q(kq, (cur.g * p.G + cur.sub * p.R) * H)) break;
+          if (!mbar_wait(&sm.qfull[kq & 1], (kq >> 1) & 1, abort, &g_hcu_status)) break;
           qkey = key;
           const int nr = min(p.R, p.G - cur.sub * p.R);
           idesc = idesc_e4m3_f32(128, nr * H);
+          if (count - 1 - it > cur.tiles - 1 - cur.tile) {  // another key follows in this CTA's range
+            Cursor nx = cur;
+            nx.tile = nx.tiles - 1;
+            nx.next(p);
+            if (!issue_q(kq + 1, (nx.g * p.G + nx.sub * p.R) * H)) break;
+          }
         }
         if (!mbar_wait(&sm.full[st.idx], st.phase, abort, &g_hcu_status)) break;
         if (!mbar_wait(&sm.tempty[acc.idx], acc.phase ^ 1, abort, &g_hcu_status)) break;
         tc_fence_after();
         const uint64_t adesc = sw128_kmajor_desc(smem_u32(sm.a[st.idx]));
-        const uint64_t bdesc = sw128_kmajor_desc(smem_u32(sm.q[q_slot]));
+        const uint64_t bdesc = sw128_kmajor_desc(smem_u32(sm.q[kq & 1]));
         const uint32_t d = tmem + static_cast<uint32_t>(acc.idx * NC);
 #pragma unroll
         for (int k = 0; k < kHeadDim / 32; ++k)
@@ -364,6 +370,8 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_paged_kernel(const _
         st.adv(kStages);
         acc.adv(NACC);
       }
+      // every Q copy issued must land before the CTA may exit
+      for (int n = nq > 2 ? nq - 2 : 0; n < nq; ++n) mbar_wait_drain(&sm.qfull[n & 1], (n >> 1) & 1, &g_hcu_status);
       tc_commit(&sm.done);
       mbar_wait_drain(&sm.done, 0, &g_hcu_status);
     }
@@ -399,7 +407,8 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_paged_kernel(const _
       if (key != qkey) {
         nr = min(p.R, p.G - cur.sub * p.R);
         __syncwarp();
-        for (int i = lane; i < nr * H; i += 32) wsm[i] = __ldg(p.weights + static_cast<int64_t>(row0) * H + i);
+        for (int i = lane; i < nr * H; i += 32)
+          wsm[i] = __ldg(p.weights + static_cast<int64_t>(row0) * H + i) * kReluScale;  // pre-scaled for relu_fma2
         if (lane < nr) lsm[lane] = clamp_len(__ldg(p.ctx_lens + row0 + lane), p.width);
         __syncwarp();
         qkey = key;
@@ -414,30 +423,45 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_paged_kernel(const _
       if (lane == 0) mbar_arrive(&sm.empty[s]);  // this warp is done with the stage's scales
       const uint32_t tbase = tmem + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(a * NC);
       for (int r = 0; r < nr; ++r) {
-        uint32_t v[H / 32][32];
-#pragma unroll
-        for (int c = 0; c < H / 32; ++c) tmem_ld_x32(tbase + r * H + c * 32, v[c]);
-        tmem_ld_wait();
-#pragma unroll
-        for (int c = 0; c < H / 32; ++c) tmem_reg_fence(v[c]);
         // 8 independent chains: 4 packed fp32 pairs
         float2 acc0 = make_float2(0.f, 0.f), acc1 = acc0, acc2 = acc0, acc3 = acc0;
+        if constexpr (kPgChunked) {
 #pragma unroll
-        for (int c = 0; c < H / 32; ++c) {
-          const float4* w4 = reinterpret_cast<const float4*>(wsm + r * H + c * 32);
+          for (int c = 0; c < H / 32; ++c) {
+            uint32_t v[32];
+            tmem_ld_x32_sync(tbase + r * H + c * 32, v);
+            const float4* w4 = reinterpret_cast<const float4*>(wsm + r * H + c * 32);
 #pragma unroll
-          for (int j = 0; j < 8; j += 2) {
-            const float4 wa = w4[j];
-            const float4 wb = w4[j + 1];
-            const uint32_t* x = &v[c][4 * j];
-            acc0 = fma2(make_float2(fmaxf(__uint_as_float(x[0]), 0.f), fmaxf(__uint_as_float(x[1]), 0.f)),
-                        make_float2(wa.x, wa.y), acc0);
-            acc1 = fma2(make_float2(fmaxf(__uint_as_float(x[2]), 0.f), fmaxf(__uint_as_float(x[3]), 0.f)),
-                        make_float2(wa.z, wa.w), acc1);
-            acc2 = fma2(make_float2(fmaxf(__uint_as_float(x[4]), 0.f), fmaxf(__uint_as_float(x[5]), 0.f)),
-                        make_float2(wb.x, wb.y), acc2);
-            acc3 = fma2(make_float2(fmaxf(__uint_as_float(x[6]), 0.f), fmaxf(__uint_as_float(x[7]), 0.f)),
-                        make_float2(wb.z, wb.w), acc3);
+            for (int j = 0; j < 8; j += 2) {
+              const float4 wa = w4[j];
+              const float4 wb = w4[j + 1];
+              const uint32_t* x = &v[4 * j];
+              relu_fma2(acc0, x[0], x[1], wa.x, wa.y);
+              relu_fma2(acc1, x[2], x[3], wa.z, wa.w);
+              relu_fma2(acc2, x[4], x[5], wb.x, wb.y);
+              relu_fma2(acc3, x[6], x[7], wb.z, wb.w);
+            }
+          }
+        } else {
+          uint32_t v[H / 32][32];
+#pragma unroll
+          for (int c = 0; c < H / 32; ++c) tmem_ld_x32(tbase + r * H + c * 32, v[c]);
+          tmem_ld_wait();
+#pragma unroll
+          for (int c = 0; c < H / 32; ++c) tmem_reg_fence(v[c]);
+#pragma unroll
+          for (int c = 0; c < H / 32; ++c) {
+            const float4* w4 = reinterpret_cast<const float4*>(wsm + r * H + c * 32);
+#pragma unroll
+            for (int j = 0; j < 8; j += 2) {
+              const float4 wa = w4[j];
+              const float4 wb = w4[j + 1];
+              const uint32_t* x = &v[c][4 * j];
+              relu_fma2(acc0, x[0], x[1], wa.x, wa.y);
+              relu_fma2(acc1, x[2], x[3], wa.z, wa.w);
+              relu_fma2(acc2, x[4], x[5], wb.x, wb.y);
+              relu_fma2(acc3, x[6], x[7], wb.z, wb.w);
+            }
           }
         }
         float s0 = ((acc0.x + acc0.y) + (acc1.x + acc1.y)) + ((acc2.x + acc2.y) + (acc3.x + acc3.y));
@@ -474,12 +498,14 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_paged_kernel(const _
 // per CTA on the device.  Same logits / mask contract as the paged kernel.
 constexpr int kPfStages = 4;
 constexpr int kQB = 4;
-constexpr int kPfEpiWarps = 8;  // warps 2..9; the kernel shares the block size of the paged kernel
+constexpr int kPfEpiWarps = 16;  // warps 2..17: kPfTeams per TMEM lane quadrant
+constexpr int kPfTeams = kPfEpiWarps / 4;  // warp t of a quadrant takes rows r % kPfTeams == t of every row block
+constexpr int kPfThreads = (2 + kPfEpiWarps) * 32;
 
 struct __align__(1024) PfSmem {
   uint8_t q[kQB][kQTile];
   uint8_t a[kPfStages][kATile];
-  float w[kPfEpiWarps][kQB * kMaxN / 2];  // weights of the rows this epilogue warp owns
+  float w[kPfEpiWarps][kQB * kMaxN / kPfTeams];  // weights of the rows this epilogue warp owns
   int rs[kPfEpiWarps][16];
   int re[kPfEpiWarps][16];
   uint64_t full[kPfStages];
@@ -550,14 +576,13 @@ struct RCursor {
 };
 
 template <int H>
-__global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_ragged_kernel(const __grid_constant__ CUtensorMap tm_k,
+__global__ __launch_bounds__(kPfThreads, 1) void mqa_logits_ragged_kernel(const __grid_constant__ CUtensorMap tm_k,
                                                                          const __grid_constant__ CUtensorMap tm_q,
                                                                          const RaggedArgs p) {
   constexpr int RB = kMaxN / H;  // rows per row block (N = 256)
   constexpr int SBR = kQB * RB;  // rows per super-block
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  PfSmem& sm = *reinterpret_cast<PfSmem*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  PfSmem& sm = smem_aligned_1024<PfSmem>(smem_raw);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int n_sb = (p.rows + SBR - 1) / SBR;
@@ -612,7 +637,7 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_ragged_kernel(const 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kPfStages; ++s) {
       mbar_init(&sm.full[s], 1);
-      mbar_init(&sm.empty[s], 1 + kPfEpiWarps);
+      mbar_init(&sm.empty[s], 1);  // the MMAs are the stage's only reader
     }
     mbar_init(&sm.qfull, 1);
     mbar_init(&sm.qempty, 1);
@@ -704,12 +729,12 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_ragged_kernel(const 
       tc_commit(&sm.done);
       mbar_wait_drain(&sm.done, 0, &g_hcu_status);
     }
-  } else if (warp >= 2 && warp < 2 + kPfEpiWarps) {
-    // ------------------------------------------------ epilogue (warps 2..9; warps 10+ idle here)
+  } else {
+    // ------------------------------------------------ epilogue (warps 2..17)
     const int ew = warp - 2;
     const int quad = warp & 3;
-    const int half = ew >> 2;  // rows r % 2 == half of every row block
-    constexpr int RPW = RB / 2;  // rows per row block owned by this warp
+    const int rsel = ew >> 2;  // rows r % kPfTeams == rsel of every row block
+    constexpr int RPW = RB / kPfTeams;  // rows per row block owned by this warp
     float* wsm = sm.w[ew];
     int* rs = sm.rs[ew];
     int* re = sm.re[ew];
@@ -725,10 +750,10 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_ragged_kernel(const 
         nrb = min(kQB, (p.rows - row0 + RB - 1) / RB);
         __syncwarp();
         for (int lr = 0; lr < kQB * RPW; ++lr) {
-          const int row = row0 + (lr / RPW) * RB + (lr % RPW) * 2 + half;
+          const int row = row0 + (lr / RPW) * RB + (lr % RPW) * kPfTeams + rsel;
           const bool in = row < p.rows;
           for (int h = lane; h < H; h += 32)
-            wsm[lr * H + h] = in ? __ldg(p.weights + static_cast<int64_t>(row) * H + h) : 0.f;
+            wsm[lr * H + h] = in ? __ldg(p.weights + static_cast<int64_t>(row) * H + h) * kReluScale : 0.f;
           if (lane == 0) {
             rs[lr] = in ? max(__ldg(p.rs + row), 0) : 0;
             re[lr] = in ? min(__ldg(p.re + row), p.n_tokens) : 0;
@@ -736,7 +761,6 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_ragged_kernel(const 
         }
         __syncwarp();
       }
-      const int s = it % kPfStages;
       const int tok_base = tile * kTileTok + quad * 32;
       const int token = tok_base + lane;
       // k_scale of this thread's token: contiguous K, so a plain load issued before the wait
@@ -748,36 +772,27 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_ragged_kernel(const 
           break;
         }
         tc_fence_after();
-        if (j == 0) {
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&sm.empty[s]);  // the MMAs read the stage; nothing else does
-        }
         const uint32_t tbase = tmem + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(a * kMaxN);
         const int nr = min(RB, p.rows - (row0 + j * RB));
-        for (int r = half, lr = j * RPW; r < nr; r += 2, ++lr) {
-          uint32_t v[H / 32][32];
-#pragma unroll
-          for (int c = 0; c < H / 32; ++c) tmem_ld_x32(tbase + r * H + c * 32, v[c]);
-          tmem_ld_wait();
-#pragma unroll
-          for (int c = 0; c < H / 32; ++c) tmem_reg_fence(v[c]);
+        for (int r = rsel, lr = j * RPW; r < nr; r += kPfTeams, ++lr) {
+          // one 32-head TMEM chunk at a time keeps the epilogue within the 18-warp register budget
           float2 acc0 = make_float2(0.f, 0.f), acc1 = acc0, acc2 = acc0, acc3 = acc0;
 #pragma unroll
           for (int c = 0; c < H / 32; ++c) {
+            uint32_t v[32];
+            tmem_ld_x32(tbase + r * H + c * 32, v);
+            tmem_ld_wait();
+            tmem_reg_fence(v);
             const float4* w4 = reinterpret_cast<const float4*>(wsm + lr * H + c * 32);
 #pragma unroll
             for (int jj = 0; jj < 8; jj += 2) {
               const float4 wa = w4[jj];
               const float4 wb = w4[jj + 1];
-              const uint32_t* x = &v[c][4 * jj];
-              acc0 = fma2(make_float2(fmaxf(__uint_as_float(x[0]), 0.f), fmaxf(__uint_as_float(x[1]), 0.f)),
-                          make_float2(wa.x, wa.y), acc0);
-              acc1 = fma2(make_float2(fmaxf(__uint_as_float(x[2]), 0.f), fmaxf(__uint_as_float(x[3]), 0.f)),
-                          make_float2(wa.z, wa.w), acc1);
-              acc2 = fma2(make_float2(fmaxf(__uint_as_float(x[4]), 0.f), fmaxf(__uint_as_float(x[5]), 0.f)),
-                          make_float2(wb.x, wb.y), acc2);
-              acc3 = fma2(make_float2(fmaxf(__uint_as_float(x[6]), 0.f), fmaxf(__uint_as_float(x[7]), 0.f)),
-                          make_float2(wb.z, wb.w), acc3);
+              const uint32_t* x = &v[4 * jj];
+              relu_fma2(acc0, x[0], x[1], wa.x, wa.y);
+              relu_fma2(acc1, x[2], x[3], wa.z, wa.w);
+              relu_fma2(acc2, x[4], x[5], wb.x, wb.y);
+              relu_fma2(acc3, x[6], x[7], wb.z, wb.w);
             }
           }
           float s0 = ((acc0.x + acc0.y) + (acc1.x + acc1.y)) + ((acc2.x + acc2.y) + (acc3.x + acc3.y));
@@ -965,11 +980,11 @@ extern "C" int hcu_mqa_logits_ragged(const uint8_t* q, int64_t rows, int64_t hea
   if (heads == 64) {
     cudaFuncSetAttribute(mqa_logits_ragged_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          static_cast<int>(smem));
-    mqa_logits_ragged_kernel<64><<<sm_count(), kLgThreads, smem, st>>>(tk, tq, a);
+    mqa_logits_ragged_kernel<64><<<sm_count(), kPfThreads, smem, st>>>(tk, tq, a);
   } else {
     cudaFuncSetAttribute(mqa_logits_ragged_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          static_cast<int>(smem));
-    mqa_logits_ragged_kernel<32><<<sm_count(), kLgThreads, smem, st>>>(tk, tq, a);
+    mqa_logits_ragged_kernel<32><<<sm_count(), kPfThreads, smem, st>>>(tk, tq, a);
   }
   return launch_status();
 }
