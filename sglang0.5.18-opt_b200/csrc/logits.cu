@@ -250,6 +250,7 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_paged_kernel(const _
     // item) into shared memory; lane 0 then waits for the item's stage and
     // issues its boxes.  Stage of item i: i % kStages (kStages % kProducers == 0).
     const int role = warp == 0 ? 0 : warp - kProducerB + 1;
+    const uint64_t pol = l2_evict_first_policy();  // pages are read once; keep L2 for the logits
     Cursor cur;  // every lane keeps an identical copy, positioned before item `it0`
     cur.init(p, sm.start_group, sm.start_local);
     int issued = 0, last_it = -1, ok = 1;
@@ -295,12 +296,12 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_paged_kernel(const _
           if (bytes) {
             mbar_arrive_expect_tx(&sm.full[s], bytes);
             if (ph0 >= 0) {
-              tma_load_3d(sm.a[s], &tm_kv, &sm.full[s], 0, 0, ph0);
-              tma_load_2d(sm.sc[s], &tm_sc, &sm.full[s], 0, ph0);
+              tma_load_3d_hint(sm.a[s], &tm_kv, &sm.full[s], 0, 0, ph0, pol);
+              tma_load_2d_hint(sm.sc[s], &tm_sc, &sm.full[s], 0, ph0, pol);
             }
             if (ph1 >= 0) {
-              tma_load_3d(sm.a[s] + kPageFp8Bytes, &tm_kv, &sm.full[s], 0, 0, ph1);
-              tma_load_2d(sm.sc[s] + kPage, &tm_sc, &sm.full[s], 0, ph1);
+              tma_load_3d_hint(sm.a[s] + kPageFp8Bytes, &tm_kv, &sm.full[s], 0, 0, ph1, pol);
+              tma_load_2d_hint(sm.sc[s] + kPage, &tm_sc, &sm.full[s], 0, ph1, pol);
             }
           } else {
             mbar_arrive(&sm.full[s]);  // no page in this tile (cannot happen for in-range items)
