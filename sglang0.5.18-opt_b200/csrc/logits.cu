@@ -48,7 +48,8 @@ constexpr int kLgThreads = (2 + kEpiWarps + kProducers - 1) * 32;  // warp 0 + e
 // 32-head TMEM chunk at a time instead of a whole row.
 constexpr bool kPgChunked = kLgThreads > 512;
 constexpr int kMaxAcc = 4;     // TMEM accumulator buffers (4 when N <= 128, else 2)
-constexpr int kStages = 8;
+constexpr int kStages = 8;       // K-tile stages when a row block spans more than 128 TMEM columns
+constexpr int kStagesNarrow = 8;   // stages when it spans <= 128 (room for 10 with 16 KB Q slots; 10 measured slower)
 constexpr int kTileTok = 128;
 constexpr int kATile = kTileTok * kHeadDim;  // 16 KB
 constexpr int kMaxN = 256;
@@ -56,14 +57,15 @@ constexpr int kQTile = kMaxN * kHeadDim;  // 32 KB
 
 
 struct __align__(1024) LgSmem {
-  uint8_t a[kStages][kATile];      // K tile: two 64-token pages, 128-byte swizzled rows
-  uint8_t q[2][kQTile];            // Q rows of the current row block (double buffered)
-  float sc[kStages][2 * kPage];    // k_scale of the stage's two pages
+  // n_st K-tile stages (two 64-token pages each, 128-byte swizzled rows) followed by the two
+  // Q slots of NC * 128 bytes (the current and the next row block); see stage_count()
+  uint8_t buf[kStages * kATile + 2 * kQTile];
+  float sc[kStagesNarrow][2 * kPage];  // k_scale of the stage's two pages
   float w[kEpiWarps][kMaxN];       // head weights, one copy per epilogue warp
   int lens[kEpiWarps][8];          // row lengths of the current row block, per epilogue warp
   int bq_ph[kProducers][2][32];    // producer batch (per producer warp): page ids of each item's two pages (-1: none)
-  uint64_t full[kStages];
-  uint64_t empty[kStages];         // 1 MMA commit + the 4 epilogue warps of the tile's team (they read sc[])
+  uint64_t full[kStagesNarrow];
+  uint64_t empty[kStagesNarrow];   // 1 MMA commit + the 4 epilogue warps of the tile's team (they read sc[])
   uint64_t qfull[2];
   uint64_t qempty[2];
   uint64_t tfull[kMaxAcc];
@@ -75,6 +77,10 @@ struct __align__(1024) LgSmem {
   int count;
   int abort;
 };
+
+static_assert(kStagesNarrow * kATile + 2 * (kQTile / 2) <= kStages * kATile + 2 * kQTile, "stage layouts");
+
+__host__ __device__ constexpr int stage_count(int nc) { return nc <= 128 ? kStagesNarrow : kStages; }
 
 struct PagedArgs {
   const uint8_t* kv;
@@ -160,6 +166,9 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_paged_kernel(const _
   const int n_sub = (p.G + p.R - 1) / p.R;
   const int NC = p.R * H;  // TMEM columns per accumulator buffer
   const int NACC = NC <= 128 ? 4 : 2;
+  const int n_st = stage_count(NC);
+  uint8_t* const a_base = sm.buf;
+  uint8_t* const q_base = sm.buf + n_st * kATile;  // slot i at q_base + i * NC * 128 (1024-aligned)
 
   // ---- schedule: this CTA's contiguous item range (warp 0, all lanes) ----
   if (warp == 0) {
@@ -211,7 +220,7 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_paged_kernel(const _
   uint32_t ncols = 32;
   while (ncols < static_cast<uint32_t>(NACC * NC)) ncols <<= 1;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < n_st; ++s) {
       mbar_init(&sm.full[s], 1);  // the item's producer: one expect_tx arrival
       mbar_init(&sm.empty[s], 1 + 4);  // MMA commit + the 4 warps of the tile's team
     }
@@ -248,12 +257,13 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_paged_kernel(const _
     // and both scale boxes of items k, k + kProducers, ...  Each warp first
     // resolves the page ids of its next 32 items in parallel (one lane per
     // item) into shared memory; lane 0 then waits for the item's stage and
-    // issues its boxes.  Stage of item i: i % kStages (kStages % kProducers == 0).
+    // issues its boxes.  Stage of item i: i % n_st, tracked incrementally.
     const int role = warp == 0 ? 0 : warp - kProducerB + 1;
     const uint64_t pol = l2_evict_first_policy();  // pages are read once; keep L2 for the logits
     Cursor cur;  // every lane keeps an identical copy, positioned before item `it0`
     cur.init(p, sm.start_group, sm.start_local);
     int issued = 0, last_it = -1, ok = 1;
+    int st_s = role, st_ph = 0;  // stage and phase of this producer's next item (item i: i % n_st, (i / n_st) & 1)
     for (int it0 = 0; it0 < count && ok; it0 += 32 * kProducers) {
       {
         Cursor c = cur;
@@ -285,8 +295,8 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_paged_kernel(const _
         for (int j = 0; j < 32; ++j) {
           const int it = it0 + role + j * kProducers;
           if (it >= count) break;
-          const int s = it % kStages;
-          if (!mbar_wait(&sm.empty[s], ((it / kStages) & 1) ^ 1, abort, &g_hcu_status)) {
+          const int s = st_s;
+          if (!mbar_wait(&sm.empty[s], st_ph ^ 1, abort, &g_hcu_status)) {
             ok = 0;
             break;
           }
@@ -296,11 +306,11 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_paged_kernel(const _
           if (bytes) {
             mbar_arrive_expect_tx(&sm.full[s], bytes);
             if (ph0 >= 0) {
-              tma_load_3d_hint(sm.a[s], &tm_kv, &sm.full[s], 0, 0, ph0, pol);
+              tma_load_3d_hint(a_base + s * kATile, &tm_kv, &sm.full[s], 0, 0, ph0, pol);
               tma_load_2d_hint(sm.sc[s], &tm_sc, &sm.full[s], 0, ph0, pol);
             }
             if (ph1 >= 0) {
-              tma_load_3d_hint(sm.a[s] + kPageFp8Bytes, &tm_kv, &sm.full[s], 0, 0, ph1, pol);
+              tma_load_3d_hint(a_base + s * kATile + kPageFp8Bytes, &tm_kv, &sm.full[s], 0, 0, ph1, pol);
               tma_load_2d_hint(sm.sc[s] + kPage, &tm_sc, &sm.full[s], 0, ph1, pol);
             }
           } else {
@@ -308,15 +318,23 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_paged_kernel(const _
           }
           ++issued;
           last_it = it;
+          st_s += kProducers;
+          if (st_s >= n_st) {
+            st_s -= n_st;
+            st_ph ^= 1;
+          }
         }
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
     }
     if (lane == 0) {
       // Drain: every copy issued must land before the CTA may exit.
-      for (int k = 0; k < kStages / kProducers && k < issued; ++k) {
+      // Only items no later item shares a stage with: an older phase of a reused stage
+      // has the same parity as the current one and would never read as complete.
+      for (int k = 0; k < issued; ++k) {
         const int it = last_it - k * kProducers;
-        mbar_wait_drain(&sm.full[it % kStages], (it / kStages) & 1, &g_hcu_status);
+        if (it + n_st < count) break;
+        mbar_wait_drain(&sm.full[it % n_st], (it / n_st) & 1, &g_hcu_status);
       }
     }
     __syncwarp();
@@ -335,7 +353,7 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_paged_kernel(const _
         const int slot = n & 1;
         if (!mbar_wait(&sm.qempty[slot], ((n >> 1) & 1) ^ 1, abort, &g_hcu_status)) return false;
         mbar_arrive_expect_tx(&sm.qfull[slot], static_cast<uint32_t>(NC * kHeadDim));
-        tma_load_2d(sm.q[slot], &tm_q, &sm.qfull[slot], 0, qrow);
+        tma_load_2d(q_base + slot * NC * kHeadDim, &tm_q, &sm.qfull[slot], 0, qrow);
         nq = n + 1;
         return true;
       };
@@ -360,15 +378,15 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_paged_kernel(const _
         if (!mbar_wait(&sm.full[st.idx], st.phase, abort, &g_hcu_status)) break;
         if (!mbar_wait(&sm.tempty[acc.idx], acc.phase ^ 1, abort, &g_hcu_status)) break;
         tc_fence_after();
-        const uint64_t adesc = sw128_kmajor_desc(smem_u32(sm.a[st.idx]));
-        const uint64_t bdesc = sw128_kmajor_desc(smem_u32(sm.q[kq & 1]));
+        const uint64_t adesc = sw128_kmajor_desc(smem_u32(a_base + st.idx * kATile));
+        const uint64_t bdesc = sw128_kmajor_desc(smem_u32(q_base + (kq & 1) * NC * kHeadDim));
         const uint32_t d = tmem + static_cast<uint32_t>(acc.idx * NC);
 #pragma unroll
         for (int k = 0; k < kHeadDim / 32; ++k)
           mma_f8f6f4(d, adesc + 2 * k, bdesc + 2 * k, idesc, k > 0 ? 1u : 0u);
         tc_commit(&sm.empty[st.idx]);
         tc_commit(&sm.tfull[acc.idx]);
-        st.adv(kStages);
+        st.adv(n_st);
         acc.adv(NACC);
       }
       // every Q copy issued must land before the CTA may exit
@@ -384,7 +402,10 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_paged_kernel(const _
     const int ew = warp - 2;
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
     const int team = ew >> 2;
-    int turn = 0;  // it % kTeams
+    // A team waits on the TMEM buffer of its item; parity waits stay unambiguous only while a
+    // team cannot run a whole buffer ring ahead of the MMA, i.e. with at most NACC teams.
+    const int n_teams = kTeams < NACC ? kTeams : NACC;
+    int turn = 0;  // it % n_teams
     float* wsm = sm.w[ew];
     int* lsm = sm.lens[ew];
     Cursor cur;
@@ -398,10 +419,10 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_paged_kernel(const _
       const int s = st.idx;
       const int a = acc.idx;
       const int aph = acc.phase;
-      st.adv(kStages);
+      st.adv(n_st);
       acc.adv(NACC);
       const bool mine = turn == team;
-      if (++turn == kTeams) turn = 0;
+      if (++turn == n_teams) turn = 0;
       if (!mine) continue;
       const int key = cur.g * n_sub + cur.sub;
       const int row0 = cur.g * p.G + cur.sub * p.R;

@@ -73,6 +73,19 @@ def test_logits_zero_length_rows_and_padded_table(hcu, dev):
     assert (mk[1] == 0).all()
 
 
+@pytest.mark.parametrize("next_n,heads", [(2, 64), (1, 64), (4, 64), (2, 32)])
+def test_logits_many_items_per_cta(hcu, dev, next_n, heads):
+    """Long contexts: every CTA streams dozens of tiles, so the stage, TMEM-accumulator and
+    Q rings wrap many times (rings of 8 or 10 stages against 4 producers and 3 teams)."""
+    lens = [65536, 60000, 47000, 41000, 33333, 30000, 26000, 20001, 65536, 9000, 4096, 1]
+    w = _decode(len(lens), next_n, lens, heads, seed=31)
+    d = _device(w, dev)
+    lg, mk, _ = _run(hcu, d)
+    rl, rm, fl = _oracle_logits(w)
+    res = compare_logits(lg.cpu().numpy(), mk.cpu().numpy(), rl, rm, fl)
+    assert res["ok"], res
+
+
 def test_hist_workspace_exact_on_device_logits(hcu, dev):
     w = _decode(4, 1, [9000, 2048, 2049, 30000], 64, seed=21)
     d = _device(w, dev)
