@@ -965,6 +965,213 @@ int launch_rows(const float* score, int64_t rows, int64_t width, int64_t score_s
   return launch_status();
 }
 
+
+// ---------------------------------------------------------------------------
+// Context-parallel merge: P per-range top-2048 lists -> the global top-2048.
+//
+// Rank p of a KV-range split owns a contiguous global token range and emits
+// (uint32 key, global index) for its local top-2048 in ascending token order
+// (hcu_topk_keys), so the lists concatenated in rank order list every entry in
+// ascending global index, and the global top-2048 under (key desc, index asc)
+// is a subset of their union.  One 1024-thread CTA per row:
+//   A  2048 strided samples of the concatenated lists give a lower bound lo of
+//      the global threshold (the top-k kernel's sampled bound: a 12-bit and an
+//      8-bit histogram, a sample rank 4 sigma + 4 below the expected one).
+//   B  entries with key >= lo are appended in global index order to the
+//      shared-memory candidate list (one block scan).
+//   C  the top-k kernel's radix select and ordered write over the candidates
+//      write the canonical order of the single-GPU top-k, so the CP result
+//      equals the 1-GPU result exactly.
+// Rows whose total visible length is at most 2048 keep every entry in index
+// order (decided by the length, not the entry count: one range may hold all
+// of a longer row's top-k).  A candidate list past kCandCap, or one shorter
+// than 2048 (the bound missed), falls back to 12/12/8-bit radix passes over all entries.
+// ---------------------------------------------------------------------------
+constexpr int kMaxParts = 16;
+
+__device__ __forceinline__ int64_t merge_off(int c, int rows, int row) {
+  return (static_cast<int64_t>(c >> 11) * rows + row) * kTopK + (c & (kTopK - 1));
+}
+
+// Radix-select fallback over every valid entry (entries [tid*per, (tid+1)*per)).
+__device__ void merge_radix(TopkSmem& sm, const uint32_t* __restrict__ keys, const int32_t* __restrict__ gidx,
+                            int per, int rows, int row, int32_t* __restrict__ out) {
+  const int tid = threadIdx.x;
+  const int c0 = tid * per;
+  uint32_t pre = 0u;
+  int need = kTopK;
+  int above = 0;
+  // three passes: key[31:20], key[19:8] within the 12-bit prefix, key[7:0] within the 24-bit prefix
+  for (int pass = 0; pass < 3; ++pass) {
+    const int nb = pass < 2 ? kBins : 256;
+    const int sh = pass == 0 ? 20 : (pass == 1 ? 8 : 0);
+    for (int i = tid; i < nb; i += kTkThreads) sm.hist[i] = 0;
+    __syncthreads();
+    for (int i = 0; i < per; ++i) {
+      const int64_t o = merge_off(c0 + i, rows, row);
+      const uint32_t k = __ldg(keys + o);
+      const bool ok = __ldg(gidx + o) >= 0 && (pass == 0 || (k >> (sh + (pass == 1 ? 12 : 8))) == pre);
+      if (ok) atomicAdd(&sm.hist[(k >> sh) & (nb - 1)], 1);
+    }
+    __syncthreads();
+    if (pass < 2)
+      find_threshold<kBins>(sm.hist, need, sm.wtot, sm.res);
+    else
+      find_threshold<256>(sm.hist, need, sm.wtot, sm.res);
+    pre = (pre << (pass < 2 ? 12 : 8)) | static_cast<uint32_t>(sm.res[0]);
+    above += sm.res[1];
+    need -= sm.res[1];
+  }
+  const uint32_t thr = pre;
+  const int remaining = need;
+  int na = 0, nt = 0;
+  for (int i = 0; i < per; ++i) {
+    const int64_t o = merge_off(c0 + i, rows, row);
+    const uint32_t k = __ldg(keys + o);
+    const bool v = __ldg(gidx + o) >= 0;
+    na += v & (k > thr);
+    nt += v & (k == thr);
+  }
+  int total;
+  const int ex = block_excl_scan(na | (nt << 16), sm.wtot, &total);
+  int ea = ex & 0xFFFF, et = ex >> 16;
+  for (int i = 0; i < per; ++i) {
+    const int64_t o = merge_off(c0 + i, rows, row);
+    const uint32_t k = __ldg(keys + o);
+    const int g = __ldg(gidx + o);
+    if (g < 0) continue;
+    if (k > thr) {
+      out[ea++] = g;
+    } else if (k == thr) {
+      if (et < remaining) out[above + et] = g;
+      ++et;
+    }
+  }
+}
+
+__global__ __launch_bounds__(kTkThreads, 1) void cp_merge_kernel(const uint32_t* __restrict__ keys,
+                                                                const int32_t* __restrict__ gidx, int parts,
+                                                                int rows, const int32_t* __restrict__ lengths,
+                                                                int32_t* __restrict__ dst) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  TopkSmem& sm = *reinterpret_cast<TopkSmem*>(smem_raw);
+  const int row = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int w = tid >> 5;
+  int32_t* out = dst + static_cast<int64_t>(row) * kTopK;
+  for (int i = tid; i < 2 * 512; i += kTkThreads) (&sm.hb[0][0])[i] = 0;
+
+  // ---- A: lower bound lo from 2048 samples of the concatenated lists (entry j * parts + parts / 2) ----
+  for (int i = tid; i < kBins; i += kTkThreads) sm.hist[i] = 0;
+  __syncthreads();
+  constexpr int kMs = 2048;  // samples
+  uint32_t sk[kMs / kTkThreads];
+#pragma unroll
+  for (int j = 0; j < kMs / kTkThreads; ++j) {
+    const int64_t o = merge_off((tid + j * kTkThreads) * parts + parts / 2, rows, row);
+    sk[j] = __ldg(gidx + o) >= 0 ? __ldg(keys + o) : 0u;  // a missing entry ranks below every key
+    atomicAdd(&sm.hist[sk[j] >> 20], 1);
+  }
+  __syncthreads();
+  // sample rank (1 = largest) 4 sigma + 4 below the threshold's expected sample rank
+  const float t = static_cast<float>(kTopK) / static_cast<float>(parts);
+  const int r_lo = min(kMs, static_cast<int>(ceilf(t + 4.f * sqrtf(t) + 4.f)));
+  find_threshold<kBins>(sm.hist, r_lo, sm.wtot, sm.res);
+  const uint32_t b1 = static_cast<uint32_t>(sm.res[0]);
+  const int need = r_lo - sm.res[1];
+#pragma unroll
+  for (int j = 0; j < kMs / kTkThreads; ++j)
+    if ((sk[j] >> 20) == b1) atomicAdd(&sm.hb[0][(sk[j] >> 12) & 0xFFu], 1);
+  __syncthreads();
+  if (w == 0) warp_find<256>(sm.hb[0], need, sm.res);
+  __syncthreads();
+  uint32_t lo = (b1 << 20) | (static_cast<uint32_t>(sm.res[0]) << 12);
+  if (tid < 256) sm.hb[0][tid] = 0;  // ordered before the select by the barriers below
+  const bool short_row = __ldg(lengths + row) <= kTopK;
+  if (short_row) lo = 0u;  // keep every entry
+
+  // ---- B: entries with key >= lo, appended in global index order ----
+  const int per = parts * 2;
+  const int c0 = tid * per;
+  // thread t: entries [t * per, (t + 1) * per), per <= 32; loads go out 8 at a time
+  int na = 0, nv = 0;
+  uint32_t kmax = 0u, cbits = 0u;
+  for (int i0 = 0; i0 < per; i0 += 8) {
+    uint32_t kk[8];
+    int gg[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      gg[u] = -1;
+      kk[u] = 0u;
+      if (i0 + u < per) {
+        const int64_t o = merge_off(c0 + i0 + u, rows, row);
+        kk[u] = __ldg(keys + o);
+        gg[u] = __ldg(gidx + o);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      if (gg[u] >= 0) {
+        ++nv;
+        if (kk[u] >= lo) {
+          ++na;
+          cbits |= 1u << (i0 + u);
+          kmax = kk[u] > kmax ? kk[u] : kmax;
+        }
+      }
+    }
+  }
+  int packed_total;
+  const int packed = block_excl_scan(na | (nv << 16), sm.wtot, &packed_total);
+  const int n = packed_total & 0xFFFF;
+  const int total = packed_total >> 16;
+  int pos = packed & 0xFFFF;
+  if (n <= kCandCap) {
+    for (int i0 = 0; i0 < per && (cbits >> i0); i0 += 8) {
+      uint32_t kk[8];
+      int gg[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if ((cbits >> (i0 + u)) & 1u) {
+          const int64_t o = merge_off(c0 + i0 + u, rows, row);
+          kk[u] = __ldg(keys + o);
+          gg[u] = __ldg(gidx + o);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if ((cbits >> (i0 + u)) & 1u) {
+          sm.cand_key[pos] = kk[u];
+          sm.cand_pid[pos] = gg[u];
+          ++pos;
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const uint32_t y = __shfl_xor_sync(0xffffffffu, kmax, o);
+    kmax = y > kmax ? y : kmax;
+  }
+  if (lane == 0) sm.wmax[w] = kmax;
+  __syncthreads();
+
+  if (short_row || total < kTopK) {
+    // all entries in index order (fewer than 2048 entries for a longer row is inconsistent input)
+    if (!short_row && tid == 0) atomicOr(&g_hcu_status, HCU_STATUS_BAD_INPUT);
+    for (int i = tid; i < kTopK; i += kTkThreads) out[i] = i < n && i < kCandCap ? sm.cand_pid[i] : -1;
+    return;
+  }
+  if (n > kCandCap || n < kTopK) {  // list overflow, or the sampled bound missed
+    merge_radix(sm, keys, gidx, per, rows, row, out);
+    return;
+  }
+  // ---- C: select and ordered write over the candidates ----
+  int above = 0;
+  const uint32_t thr = select_candidates(sm, n, lo, &above);
+  write_candidates<false>(sm, n, thr, above, out, nullptr);
+}
 }  // namespace
 
 // Used by the logits translation unit for the hist_lens path.
@@ -1048,4 +1255,17 @@ extern "C" int hcu_topk_keys(const float* score, int64_t rows, int64_t width, in
   if (!dst_keys) return HCU_ERR_ARG;
   return launch_rows(score, rows, width, score_stride, mask, mask_stride, lengths, page_table, pt_stride, dst,
                      dst_keys, nullptr, reinterpret_cast<cudaStream_t>(stream), /*sorted=*/true);
+}
+
+extern "C" int hcu_cp_topk_merge(const uint32_t* keys, const int32_t* gidx, int64_t n_parts, int64_t rows,
+                                 const int32_t* lengths, int32_t* dst, hcu_stream_t stream) {
+  using namespace hcu;
+  if (n_parts < 1 || n_parts > kMaxParts || rows < 0 || rows > INT32_MAX) return HCU_ERR_ARG;
+  if (rows == 0) return HCU_OK;
+  if (!keys || !gidx || !lengths || !dst) return HCU_ERR_ARG;
+  const size_t smem = sizeof(TopkSmem);
+  cudaFuncSetAttribute(cp_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  cp_merge_kernel<<<static_cast<unsigned>(rows), kTkThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
+      keys, gidx, static_cast<int>(n_parts), static_cast<int>(rows), lengths, dst);
+  return launch_status();
 }

@@ -40,6 +40,13 @@ class CudaOps:
 
         return topk_keys(score, mask, lengths, page_table)
 
+    def topk(self, score, mask, lengths, page_table):
+        from . import sparse_mask_topk_transform
+
+        rows = score.shape[0]
+        cu = torch.arange(rows + 1, dtype=torch.int32, device=score.device)
+        return sparse_mask_topk_transform(score, mask, lengths, page_table, cu)
+
     def merge(self, keys, gidx, lengths):
         from . import cp_topk_merge
 
@@ -80,10 +87,10 @@ def cp_prefill_topk(q, k_fp8_local, k_scale_local, weights, row_end, n_tokens, g
     lg, mk = ops.logits(q, k_fp8_local, k_scale_local, weights, zeros, lens)
     width = hi - lo
     gtab = (torch.arange(width, dtype=torch.int32, device=dev) + lo).expand(rows, width)
+    if world == 1:  # one range: the canonical top-k is the answer (no exchange, no merge)
+        return ops.topk(lg, mk, lens, gtab)
     idx, keys = ops.local_topk(lg, mk, lens, gtab)
     vis = row_end.clamp(max=n_tokens).to(torch.int32)
-    if world == 1:
-        return ops.merge(keys.unsqueeze(0), idx.unsqueeze(0), vis)
     if mode == "allgather":
         all_k = torch.empty((world * rows, TOPK), dtype=keys.dtype, device=dev)
         all_i = torch.empty((world * rows, TOPK), dtype=idx.dtype, device=dev)

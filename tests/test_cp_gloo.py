@@ -33,6 +33,12 @@ class OracleOps:
             keys[r][v] = keys[r][v][o]
         return torch.from_numpy(idx), torch.from_numpy(keys.view(np.int32))
 
+    def topk(self, score, mask, lengths, pt):
+        from oracle import indexer as O
+
+        return torch.from_numpy(O.topk_transform(score.numpy(), mask.numpy(), lengths.numpy(),
+                                                 np.ascontiguousarray(pt.numpy())))
+
     def merge(self, keys, gidx, lengths):
         from oracle import indexer as O
 
@@ -72,7 +78,7 @@ def _worker(rank, world, port, mode, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,mode", [(2, "rowshard"), (2, "allgather"), (3, "rowshard")])
+@pytest.mark.parametrize("world,mode", [(1, "rowshard"), (2, "rowshard"), (2, "allgather"), (3, "rowshard")])
 def test_cp_driver_equals_single_range(world, mode):
     from hcu_ops.workloads import make_ragged
     from oracle import indexer as O
