@@ -467,7 +467,8 @@ def run_prefill(args, world, rank, local):
     import hcu_ops
 
     dev = torch.device("cuda", local)
-    w = _prefill_inputs(dev, 8192, 65536, seed=rank)
+    p_rows, p_prefix = (8192, 65536) if not args.prefill_shape else args.prefill_shape
+    w = _prefill_inputs(dev, p_rows, p_prefix, seed=rank)
     N = w["k_fp8"].shape[0]
     rows = w["q"].shape[0]
     lens = w["row_end"]
@@ -493,8 +494,9 @@ def run_prefill(args, world, rank, local):
     tflops = flops / (ms_lg * 1e-3) / 1e12
     rec = _base_record(args, world, "prefill indexer G-scores/s (rows x visible KV tokens / s), logits + top-2048",
                        pairs / (ms * 1e-3) / 1e9 * world, "G-scores/s", ms,
-                       "config2: prefill chunk 8192 rows x (65536 + i + 1) tokens, 64 heads; inputs 77 MB, "
-                       "logits 2.4 GB > L2", pairs=pairs)
+                       (f"config2: prefill chunk {rows} rows x ({p_prefix} + i + 1) tokens, 64 heads; "
+                        + ("inputs 77 MB, logits 2.4 GB > L2" if not args.prefill_shape else "reduced shape (profiling)")),
+                       pairs=pairs)
     rec["logits_op_ms"] = ms_lg
     rec["top_k_rows_per_s"] = rows / ((ms - ms_lg) * 1e-3)
     rec["roofline"] = {"bound": "tensor", "achieved": tflops, "peak": fp8_peak, "unit": "TFLOP/s",
@@ -633,6 +635,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="decode")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--prefill-shape", type=int, nargs=2, metavar=("ROWS", "PREFIX"), default=None,
+                    help="prefill workload at a reduced shape (for profiler captures); default config 2")
     args = ap.parse_args()
     world, rank, local = _dist()
     if args.impl == "reference":
