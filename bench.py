@@ -200,8 +200,11 @@ def run_decode(args, world, rank, local):
     l1.record(stream)
     barrier()
     ms_logits = l0.elapsed_time(l1) / args.steps
-    # ---- e2e through the public API with host buffers
-    host = {k: w[k].cpu().pin_memory() for k in ("q", "weights", "context_lens", "block_table", "page_table_size_1")}
+    # ---- e2e through the public API with host buffers: every step copies that step's inputs (query rows,
+    # head weights, context lengths, block table) from pinned host memory and reads the result back.  The KV
+    # cache and the per-token page table (page_table_size_1, built on the device from the request-to-token
+    # pool by the serving engine's metadata step) are device state, like the cache itself.
+    host = {k: w[k].cpu().pin_memory() for k in ("q", "weights", "context_lens", "block_table")}
     dev_in = {k: torch.empty_like(w[k]) for k in host}
     res_host = torch.empty((lens.numel(), 2048), dtype=torch.int32).pin_memory()
     h2d = sum(t.numel() * t.element_size() for t in host.values())
@@ -213,7 +216,7 @@ def run_decode(args, world, rank, local):
         lg, mk = hcu_ops.mqa_logits(dev_in["q"], w["kv_cache"], dev_in["weights"], dev_in["context_lens"],
                                     dev_in["block_table"], w["max_context_len"], w["group_size"],
                                     hist_lens=dev_in["context_lens"])
-        o = hcu_ops.sparse_mask_topk_transform(lg, mk, dev_in["context_lens"], dev_in["page_table_size_1"], cu, 2048)
+        o = hcu_ops.sparse_mask_topk_transform(lg, mk, dev_in["context_lens"], w["page_table_size_1"], cu, 2048)
         res_host.copy_(o, non_blocking=True)
 
     for _ in range(3):
