@@ -458,6 +458,38 @@ def run_dequant(args, world, rank, local, mla=False):
     return rec
 
 
+def run_kstore(args, world, rank, local):
+    """Indexer-K cache writer: 131072 bf16 K rows quantised into permuted slots of a 4096-page pool."""
+    import torch
+
+    import hcu_ops
+
+    dev = torch.device("cuda", local)
+    n, pool_pages = 131072, 4096
+    g = torch.Generator(device=dev)
+    g.manual_seed(rank)
+    k = torch.randn(n, 128, generator=g, device=dev).to(torch.bfloat16)
+    loc = torch.randperm(pool_pages * 64, generator=g, device=dev)[:n].to(torch.int32)
+    pool = torch.zeros(pool_pages, 64, 1, 132, dtype=torch.uint8, device=dev)
+    fn = lambda: hcu_ops.quant_store_index_k(k, loc, pool)  # noqa: E731
+    for _ in range(max(args.warmup, 3)):
+        fn()
+    iters = min(args.steps, 500)
+    ms = _timed_iters(fn, iters, _flusher(dev))
+    per_tok = 256 + 4 + 132
+    alg = per_tok * n
+    gbs = alg / (ms * 1e-3) / 1e9
+    hbm, _, src = _peaks()
+    rec = _base_record(args, world, "indexer-K cache writer throughput (algorithmic bytes / s)", gbs * world, "GB/s",
+                       ms, "indexer-K writer: 131072 bf16 rows -> fp8 + scale into permuted slots of 4096 pages; "
+                       "L2 flushed between launches", tokens=n, bytes_per_token=per_tok)
+    rec["dtype"] = "bf16 -> fp32 -> fp8e4m3"
+    rec["roofline"] = {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                       "traffic": None, "alg_bytes_per_launch": alg, "peak_source": src}
+    rec["gpu_launches"] = iters
+    return rec
+
+
 def _prefill_inputs(dev, rows, prefix, seed):
     from hcu_ops.workloads import make_ragged
 
@@ -564,7 +596,7 @@ def run_cp_prefill(args, world, rank, local):
     return rec
 
 
-WORKLOADS = {"decode0": run_decode0, "dequant": run_dequant,
+WORKLOADS = {"decode0": run_decode0, "dequant": run_dequant, "kstore": run_kstore,
              "mla_dequant": lambda a, w, r, l: run_dequant(a, w, r, l, mla=True),
              "prefill": run_prefill, "cp_prefill": run_cp_prefill}
 
@@ -590,6 +622,16 @@ def run_reference_sample(args):
         O.topk_transform(lg, m, w["context_lens"].numpy(), w["page_table_size_1"].numpy())
         dt = time.perf_counter() - t0
         value, unit, sample = dt * 1e6, "us", "whole config 0"
+    elif wl == "kstore":
+        n, pool_pages = 131072, 4096
+        g = torch.Generator().manual_seed(0)
+        k = torch.randn(n, 128, generator=g).to(torch.bfloat16).float().numpy()
+        loc = torch.randperm(pool_pages * 64, generator=g)[:n].to(torch.int32).numpy()
+        pool = np.zeros((pool_pages, 64 * 132), np.uint8)
+        t0 = time.perf_counter()
+        O.quant_store_index_k(k, loc, pool)
+        dt = time.perf_counter() - t0
+        value, unit, sample = n * (256 + 4 + 132) / dt / 1e9, "GB/s", f"{n} tokens (whole workload)"
     elif wl in ("dequant", "mla_dequant"):
         from hcu_ops.workloads import make_index_k_dequant, make_mla_dequant
 

@@ -39,6 +39,12 @@ enum {
   HCU_ERR_UNSUPPORTED = 4,
 };
 
+/* Element types of typed inputs. */
+enum {
+  HCU_DTYPE_F32 = 0,
+  HCU_DTYPE_BF16 = 1,
+};
+
 /* Device status bits (sticky until cleared). */
 enum {
   HCU_STATUS_WAIT_TIMEOUT = 1u << 0, /* an mbarrier / flag wait hit its bound */
@@ -81,6 +87,22 @@ int hcu_dequant_k_cache_paged(const uint8_t* quant_k_cache, int64_t pool_slots, 
 int hcu_dequant_index_k_paged(const uint8_t* kv_cache, int64_t n_pages, int64_t page_stride,
                               const int32_t* token_loc, int64_t n_tokens, uint16_t* out,
                               hcu_stream_t stream);
+
+/* Indexer-K cache writer (no counterpart among the reference's sources: sglang's
+ * store is not vendored; this produces the page layout the logits op reads,
+ * hcu_ops/csrc/mqa_hist.cu:77-91).  Per token: scale = max(amax, 1e-12) / 448,
+ * fp8 e4m3 of x / scale (IEEE round-to-nearest division, saturating
+ * round-to-nearest-even conversion); the 128 fp8 bytes go to page * page_stride
+ * + offset * 128 and the scale to page * page_stride + 8192 + offset * 4.
+ *   k          fp32 or bf16 (k_dtype) [n_tokens, k_stride >= 128 elements], 16-byte aligned rows;
+ *              bf16 is widened to fp32 exactly before the arithmetic
+ *   token_loc  int32 [n_tokens] = page * 64 + offset; out-of-range slots are
+ *              skipped and flagged HCU_STATUS_BAD_INPUT; two tokens naming one
+ *              slot race (one of them wins)
+ *   kv_cache   uint8 [n_pages, page_stride] (page_stride >= 8448, % 16 == 0), written in place */
+int hcu_quant_store_index_k_paged(const void* k, int32_t k_dtype, int64_t k_stride, const int32_t* token_loc,
+                                  int64_t n_tokens, uint8_t* kv_cache, int64_t n_pages, int64_t page_stride,
+                                  hcu_stream_t stream);
 
 /* ------------------------------------------------------------------------
  * Stage 2: MQA index logits  s = (sum_h w[h] * relu(q_h . k)) * k_scale

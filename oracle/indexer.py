@@ -118,6 +118,31 @@ def dequant_index_k(kv_pages: np.ndarray, token_loc: np.ndarray) -> np.ndarray:
     return f32_to_bf16_bits(prod)
 
 
+def quant_store_index_k(k: np.ndarray, token_loc: np.ndarray, kv_pages: np.ndarray) -> np.ndarray:
+    """Indexer-K cache writer (the producer of the page layout ``mqa_hist.cu:77-91``; sglang's
+    store is not vendored).  Per token, in float32: ``scale = max(amax, 1e-12) / 448``,
+    ``fp8 = e4m3_rne(clamp(x / scale, -448, 448))``; the 128 fp8 bytes go to the slot's row of
+    the page, the scale to byte 8192 + 4 * offset.  Returns a written copy of ``kv_pages``
+    (uint8 ``[n_pages, page_stride]``); out-of-range slots are skipped.  The arithmetic is the
+    per-token amax/448 quantisation BASELINE's configs use for K (``hcu_ops/workloads.py``)."""
+    x = np.asarray(k, dtype=np.float32).reshape(-1, HEAD_DIM)
+    loc = np.asarray(token_loc, dtype=np.int64)
+    out = np.array(kv_pages, dtype=np.uint8, copy=True)
+    n_pages = out.shape[0]
+    amax = np.maximum(np.abs(x).max(axis=1), np.float32(1e-12)).astype(np.float32)
+    scale = (amax / np.float32(448.0)).astype(np.float32)
+    y = np.clip(x / scale[:, None], np.float32(-448.0), np.float32(448.0)).astype(np.float32)
+    q8 = torch.from_numpy(y).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    for t in range(x.shape[0]):
+        l = int(loc[t])
+        if l < 0 or l >= n_pages * PAGE:
+            continue
+        pg, off = divmod(l, PAGE)
+        out[pg, off * HEAD_DIM:(off + 1) * HEAD_DIM] = q8[t]
+        out[pg, PAGE * HEAD_DIM + 4 * off:PAGE * HEAD_DIM + 4 * off + 4] = np.frombuffer(scale[t].tobytes(), np.uint8)
+    return out
+
+
 # ---------------------------------------------------------------------------
 # stage 2: MQA index logits + nonzero mask (+ pass-1 histogram)
 # ---------------------------------------------------------------------------

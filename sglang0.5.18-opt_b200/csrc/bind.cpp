@@ -245,6 +245,26 @@ torch::Tensor dequant_index_k_paged(const torch::Tensor& kv_cache, const torch::
   return out;
 }
 
+torch::Tensor quant_store_index_k(const torch::Tensor& k, const torch::Tensor& token_loc, torch::Tensor kv_cache) {
+  TORCH_CHECK(kv_cache.is_cuda() && kv_cache.scalar_type() == at::kByte && kv_cache.dim() == 4 &&
+                  kv_cache.size(1) == 64 && kv_cache.size(2) == 1 && kv_cache.size(3) == 132 &&
+                  kv_cache.stride(1) == 132 && kv_cache.stride(3) == 1 && kv_cache.stride(0) % 16 == 0,
+              "kv_cache must be packed fp8+scale uint8 [blocks, 64, 1, 132]");
+  TORCH_CHECK(k.device() == kv_cache.device() && (k.scalar_type() == at::kFloat || k.scalar_type() == at::kBFloat16) &&
+                  k.dim() == 2 && k.size(1) == 128 && k.stride(1) == 1,
+              "k must be float32 or bfloat16 [n, 128] with unit last stride");
+  TORCH_CHECK(token_loc.scalar_type() == at::kInt && token_loc.dim() == 1 && token_loc.is_contiguous() &&
+                  token_loc.size(0) == k.size(0),
+              "token_loc must be contiguous int32 [n]");
+  const c10::cuda::CUDAGuard guard(kv_cache.device());
+  const int32_t dt = k.scalar_type() == at::kBFloat16 ? HCU_DTYPE_BF16 : HCU_DTYPE_F32;
+  check_status(hcu_quant_store_index_k_paged(k.data_ptr(), dt, k.stride(0), ptr<const int32_t>(token_loc), k.size(0),
+                                             ptr<uint8_t>(kv_cache), kv_cache.size(0), kv_cache.stride(0),
+                                             cur_stream()),
+               "quant_store_index_k");
+  return kv_cache;
+}
+
 torch::Tensor cp_topk_merge(const torch::Tensor& keys, const torch::Tensor& gidx, const torch::Tensor& lengths) {
   TORCH_CHECK(keys.is_cuda() && keys.scalar_type() == at::kInt && keys.dim() == 3 && keys.size(2) == kTopK &&
                   keys.is_contiguous(),
@@ -287,6 +307,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dequantize_k_cache_paged", &dequantize_k_cache_paged,
         "MLA 656-byte slot paged dequant -> bf16 [n, 1, 576] (sglang dequantize_k_cache_paged drop-in)");
   m.def("dequant_index_k_paged", &dequant_index_k_paged, "indexer-K page dequant -> bf16 [n, 128]");
+  m.def("quant_store_index_k", &quant_store_index_k,
+        "quantise K rows per token to fp8 e4m3 + fp32 scale into indexer-K pages (in place)");
   m.def("cp_topk_merge", &cp_topk_merge, "merge per-range (key, global index) top-2048 lists");
   m.def("read_device_status", &read_device_status, "sticky device status bits of the library (synchronises)");
   m.def("version", []() { return std::string(hcu_version()); });

@@ -9,7 +9,11 @@
 // dequant_index_k_kernel: the indexer-K page (64 x 128 fp8, then 64 fp32
 //   scales) -> bf16 [n, 128]; 8 lanes per token, 4 tokens per warp access.
 //
-// Both issue every load of kUnroll tokens before the first store so that each
+// quant_store_index_k_kernel: the writer of that page layout: per token
+//   scale = max(amax, 1e-12) / 448 and fp8 e4m3 of x / scale (IEEE division,
+//   saturating round-to-nearest-even conversion), 8 lanes per token.
+//
+// All issue every load of kUnroll tokens before the first store so that each
 // warp keeps several KB in flight (HBM latency x bandwidth per SM is ~40 KB).
 #include <cuda_bf16.h>
 #include <cuda_fp8.h>
@@ -137,6 +141,88 @@ __global__ __launch_bounds__(kDqThreads) void dequant_index_k_kernel(const uint8
   }
 }
 
+
+// 16 values of one K row (fp32 or bf16) starting at p (16-byte aligned), as fp32.
+template <bool kBf16>
+__device__ __forceinline__ void load16_k(const void* p, float (&v)[16]) {
+  if constexpr (kBf16) {
+    const uint4 a = ld_stream(p);
+    const uint4 b = ld_stream(static_cast<const uint8_t*>(p) + 16);
+    const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      v[2 * i] = __uint_as_float(w[i] << 16);  // bf16 -> fp32 is exact: the high half of the fp32 word
+      v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint4 a = ld_stream(static_cast<const uint8_t*>(p) + 16 * i);
+      v[4 * i] = __uint_as_float(a.x);
+      v[4 * i + 1] = __uint_as_float(a.y);
+      v[4 * i + 2] = __uint_as_float(a.z);
+      v[4 * i + 3] = __uint_as_float(a.w);
+    }
+  }
+}
+
+template <bool kBf16>
+__global__ __launch_bounds__(kDqThreads) void quant_store_index_k_kernel(const void* __restrict__ k,
+                                                                         int64_t k_stride_bytes,
+                                                                         const int32_t* __restrict__ loc, int64_t n,
+                                                                         uint8_t* __restrict__ kv, int64_t n_pages,
+                                                                         int64_t page_stride) {
+  constexpr int kElem = kBf16 ? 2 : 4;
+  const int lane = threadIdx.x & 31;
+  const int sub = lane >> 3;   // token within the 4-token group
+  const int part = lane & 7;   // 16-value chunk of the token
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * kDqThreads + threadIdx.x) >> 5;
+  const int64_t n_warps = (static_cast<int64_t>(gridDim.x) * kDqThreads) >> 5;
+  const int64_t n_slots = n_pages * kPage;
+  for (int64_t t0 = warp * 4 * kIdxUnroll; t0 < n; t0 += n_warps * 4 * kIdxUnroll) {
+    float v[kIdxUnroll][16];
+    int64_t l[kIdxUnroll];
+#pragma unroll
+    for (int u = 0; u < kIdxUnroll; ++u) {
+      const int64_t t = t0 + 4 * u + sub;
+      const int64_t tt = t < n ? t : n - 1;  // a full 4-token group of loads; the stores check t
+      l[u] = t < n ? static_cast<int64_t>(__ldg(loc + t)) : -1;
+      load16_k<kBf16>(static_cast<const uint8_t*>(k) + tt * k_stride_bytes + 16 * kElem * part, v[u]);
+    }
+#pragma unroll
+    for (int u = 0; u < kIdxUnroll; ++u) {
+      const int64_t t = t0 + 4 * u + sub;
+      float amax = 0.f;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(v[u][j]));
+      // the 8 lanes of this token (xor 1, 2, 4 stays inside the 8-lane group)
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+      const float scale = __fdiv_rn(fmaxf(amax, 1e-12f), 448.f);
+      uint32_t w[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const __nv_fp8x2_storage_t lo2 = __nv_cvt_float2_to_fp8x2(
+            make_float2(__fdiv_rn(v[u][4 * i], scale), __fdiv_rn(v[u][4 * i + 1], scale)), __NV_SATFINITE, __NV_E4M3);
+        const __nv_fp8x2_storage_t hi2 = __nv_cvt_float2_to_fp8x2(
+            make_float2(__fdiv_rn(v[u][4 * i + 2], scale), __fdiv_rn(v[u][4 * i + 3], scale)), __NV_SATFINITE,
+            __NV_E4M3);
+        w[i] = static_cast<uint32_t>(lo2) | (static_cast<uint32_t>(hi2) << 16);
+      }
+      if (t >= n) continue;
+      const bool ok = l[u] >= 0 && l[u] < n_slots;
+      if (!ok) {
+        if (part == 0) atomicOr(&g_hcu_status, HCU_STATUS_BAD_INPUT);
+        continue;
+      }
+      uint8_t* page = kv + (l[u] >> 6) * page_stride;
+      st_v4(page + (l[u] & 63) * kHeadDim + 16 * part, make_uint4(w[0], w[1], w[2], w[3]));
+      if (part == 0) reinterpret_cast<float*>(page + kPageFp8Bytes)[l[u] & 63] = scale;
+    }
+  }
+}
+
 int grid_for(int64_t warps_needed) {
   const int64_t per_block = kDqThreads / 32;
   int64_t blocks = (warps_needed + per_block - 1) / per_block;
@@ -175,5 +261,28 @@ extern "C" int hcu_dequant_index_k_paged(const uint8_t* kv_cache, int64_t n_page
   const int grid = grid_for((n_tokens + 4 * kIdxUnroll - 1) / (4 * kIdxUnroll));
   dequant_index_k_kernel<<<grid, kDqThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       kv_cache, n_pages, page_stride, token_loc, n_tokens, out);
+  return launch_status();
+}
+
+extern "C" int hcu_quant_store_index_k_paged(const void* k, int32_t k_dtype, int64_t k_stride,
+                                             const int32_t* token_loc, int64_t n_tokens, uint8_t* kv_cache,
+                                             int64_t n_pages, int64_t page_stride, hcu_stream_t stream) {
+  using namespace hcu;
+  if (k_dtype != HCU_DTYPE_F32 && k_dtype != HCU_DTYPE_BF16) return HCU_ERR_ARG;
+  const int64_t elem = k_dtype == HCU_DTYPE_BF16 ? 2 : 4;
+  if (n_tokens < 0 || n_pages < 0 || k_stride < kHeadDim || (k_stride * elem) % 16 != 0 ||
+      page_stride < kPage * (kHeadDim + 4) || page_stride % 16 != 0)
+    return HCU_ERR_ARG;
+  if (n_tokens == 0) return HCU_OK;
+  if (!k || !token_loc || !kv_cache) return HCU_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(kv_cache)) % 16 != 0) return HCU_ERR_ARG;
+  const int grid = grid_for((n_tokens + 4 * kIdxUnroll - 1) / (4 * kIdxUnroll));
+  const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (k_dtype == HCU_DTYPE_BF16)
+    quant_store_index_k_kernel<true><<<grid, kDqThreads, 0, st>>>(k, k_stride * elem, token_loc, n_tokens, kv_cache,
+                                                                  n_pages, page_stride);
+  else
+    quant_store_index_k_kernel<false><<<grid, kDqThreads, 0, st>>>(k, k_stride * elem, token_loc, n_tokens, kv_cache,
+                                                                   n_pages, page_stride);
   return launch_status();
 }

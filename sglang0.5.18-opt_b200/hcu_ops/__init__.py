@@ -168,6 +168,16 @@ def mqa_logits_ragged(q, k_fp8, k_scale, weights, row_start, row_end):
     return _C.mqa_logits_ragged(q, k_fp8, k_scale, weights, row_start, row_end)
 
 
+def quant_store_index_k(k, token_loc, kv_cache):
+    """Indexer-K cache writer: quantise each K row (fp32 or bf16 ``[n, 128]``) per token to fp8 e4m3 with an
+    fp32 scale ``max(amax, 1e-12) / 448`` and store it into slot ``token_loc[i] = page * 64 + offset`` of
+    ``kv_cache`` (uint8 ``[blocks, 64, 1, 132]``, the layout ``mqa_logits`` reads), in place.
+
+    sglang's own store for this cache is not part of the reference's sources; this is the producer of the
+    page layout of ``hcu_ops/csrc/mqa_hist.cu:77-91``."""
+    return _C.quant_store_index_k(k, token_loc, kv_cache)
+
+
 def topk_keys(score, nonzero_mask, lengths, page_table):
     """Top-2048 through ``page_table`` plus the selected uint32 keys, in ascending token order."""
     return _C.topk_keys(score, nonzero_mask, lengths, page_table)

@@ -158,3 +158,25 @@ def test_ragged_oracle_equals_paged_oracle():
     assert np.array_equal(mr, mp)
     both = O.mask_bits(mr, N)
     assert np.array_equal(lr[both], lp[both])
+
+
+def test_kstore_oracle_equals_workload_quantisation():
+    """The writer's restatement produces the same pages as the workloads' per-token amax/448
+    quantisation + packing (the K every config's cache is built from), through a scattered slot map."""
+    from hcu_ops.workloads import pack_index_k_pages, quant_rows_fp8
+
+    g = torch.Generator().manual_seed(3)
+    n_pages = 6
+    k = torch.randn(n_pages * 64, 128, generator=g) * 3.0
+    k[5] = 0.0                       # amax 0 -> clamped scale
+    k[6, 17] = 1e30                  # one huge value, the rest flush to 0 in fp8
+    kf, ks = quant_rows_fp8(k)
+    ref = pack_index_k_pages(kf, ks).view(n_pages, -1).numpy()
+    perm = torch.randperm(n_pages * 64, generator=g)
+    loc = perm.to(torch.int32).numpy()
+    # token i of k_perm goes to slot loc[i] = perm[i]; so k_perm[i] = k[perm[i]]
+    got = O.quant_store_index_k(k[perm].numpy(), loc, np.zeros((n_pages, 64 * 132), np.uint8))
+    assert np.array_equal(got, ref)
+    # out-of-range slots are skipped
+    bad = O.quant_store_index_k(k[:2].numpy(), np.array([-1, n_pages * 64], np.int32), np.zeros((n_pages, 64 * 132), np.uint8))
+    assert not bad.any()
