@@ -216,6 +216,18 @@ __device__ __forceinline__ T& smem_aligned_1024(unsigned char* raw) {
   return *reinterpret_cast<T*>(raw + ((1024u - (smem_u32(raw) & 1023u)) & 1023u));
 }
 
+// Predicated global stores (one instruction, no branch around them).
+__device__ __forceinline__ void st_f32_if(float* p, float v, bool pred) {
+  asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %2, 0;\n\t@q st.global.f32 [%0], %1;\n\t}" ::"l"(p), "f"(v),
+               "r"(static_cast<int>(pred))
+               : "memory");
+}
+__device__ __forceinline__ void st_u32_if(uint32_t* p, uint32_t v, bool pred) {
+  asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %2, 0;\n\t@q st.global.u32 [%0], %1;\n\t}" ::"l"(p), "r"(v),
+               "r"(static_cast<int>(pred))
+               : "memory");
+}
+
 // Named barrier over `count` threads (a subset of the CTA).
 __device__ __forceinline__ void named_bar(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");

@@ -63,6 +63,8 @@ struct __align__(1024) LgSmem {
   float sc[kStagesNarrow][2 * kPage];  // k_scale of the stage's two pages
   float w[kEpiWarps][kMaxN];       // head weights, one copy per epilogue warp
   int lens[kEpiWarps][8];          // row lengths of the current row block, per epilogue warp
+  float* lrow[kEpiWarps][8];       // logits rows of the current row block
+  uint32_t* mrow[kEpiWarps][8];    // mask rows (as 32-bit words) of the current row block
   int bq_ph[kProducers][2][32];    // producer batch (per producer warp): page ids of each item's two pages (-1: none)
   uint64_t full[kStagesNarrow];
   uint64_t empty[kStagesNarrow];   // 1 MMA commit + the 4 epilogue warps of the tile's team (they read sc[])
@@ -413,7 +415,6 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_paged_kernel(const _
     Ring st, acc;
     int qkey = -1;
     int nr = 0;
-    const int64_t mstride = p.width / 16;
     for (int it = 0; it < count; ++it) {
       cur.next(p);
       const int s = st.idx;
@@ -431,7 +432,11 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_paged_kernel(const _
         __syncwarp();
         for (int i = lane; i < nr * H; i += 32)
           wsm[i] = __ldg(p.weights + static_cast<int64_t>(row0) * H + i) * kReluScale;  // pre-scaled for relu_fma2
-        if (lane < nr) lsm[lane] = clamp_len(__ldg(p.ctx_lens + row0 + lane), p.width);
+        if (lane < nr) {
+          lsm[lane] = clamp_len(__ldg(p.ctx_lens + row0 + lane), p.width);
+          sm.lrow[ew][lane] = p.logits + static_cast<int64_t>(row0 + lane) * p.width;
+          sm.mrow[ew][lane] = reinterpret_cast<uint32_t*>(p.mask) + static_cast<int64_t>(row0 + lane) * (p.width / 32);
+        }
         __syncwarp();
         qkey = key;
       }
@@ -488,12 +493,10 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_paged_kernel(const _
         }
         float s0 = ((acc0.x + acc0.y) + (acc1.x + acc1.y)) + ((acc2.x + acc2.y) + (acc3.x + acc3.y));
         s0 *= ksc;
-        const int row = row0 + r;
         const bool keep = token < lsm[r] && __float_as_uint(s0) != 0u;
         const uint32_t bits = __ballot_sync(0xffffffffu, keep);
-        if (lane == 0 && tok_base < p.width)
-          reinterpret_cast<uint32_t*>(p.mask)[(static_cast<int64_t>(row) * mstride + tok_base / 16) >> 1] = bits;
-        if (keep) p.logits[static_cast<int64_t>(row) * p.width + token] = s0;
+        st_u32_if(sm.mrow[ew][r] + (tok_base >> 5), bits, lane == 0 && tok_base < p.width);
+        st_f32_if(sm.lrow[ew][r] + token, s0, keep);
       }
       tc_fence_before();
       __syncwarp();
@@ -530,6 +533,8 @@ struct __align__(1024) PfSmem {
   float w[kPfEpiWarps][kQB * kMaxN / kPfTeams];  // weights of the rows this epilogue warp owns
   int rs[kPfEpiWarps][16];
   int re[kPfEpiWarps][16];
+  float* lrow[kPfEpiWarps][16];     // logits row of each owned row (super-block)
+  uint32_t* mrow[kPfEpiWarps][16];  // mask row (as 32-bit words) of each owned row
   uint64_t full[kPfStages];
   uint64_t empty[kPfStages];
   uint64_t qfull;
@@ -779,6 +784,8 @@ __global__ __launch_bounds__(kPfThreads, 1) void mqa_logits_ragged_kernel(const 
           if (lane == 0) {
             rs[lr] = in ? max(__ldg(p.rs + row), 0) : 0;
             re[lr] = in ? min(__ldg(p.re + row), p.n_tokens) : 0;
+            sm.lrow[ew][lr] = p.logits + static_cast<int64_t>(in ? row : 0) * p.stride;
+            sm.mrow[ew][lr] = reinterpret_cast<uint32_t*>(p.mask) + static_cast<int64_t>(in ? row : 0) * (p.stride / 32);
           }
         }
         __syncwarp();
@@ -787,6 +794,8 @@ __global__ __launch_bounds__(kPfThreads, 1) void mqa_logits_ragged_kernel(const 
       const int token = tok_base + lane;
       // k_scale of this thread's token: contiguous K, so a plain load issued before the wait
       const float ksc = token < p.n_tokens ? __ldg(p.k_scale + token) : 0.f;
+      const bool mstore = lane == 0 && tok_base < p.stride;  // this warp's 32-bit mask word exists
+      const int mword = tok_base >> 5;
       for (int j = 0; j < nrb; ++j, ++u) {
         const int a = u & 1;
         if (!mbar_wait(&sm.tfull[a], (u >> 1) & 1, abort, &g_hcu_status)) {
@@ -819,13 +828,10 @@ __global__ __launch_bounds__(kPfThreads, 1) void mqa_logits_ragged_kernel(const 
           }
           float s0 = ((acc0.x + acc0.y) + (acc1.x + acc1.y)) + ((acc2.x + acc2.y) + (acc3.x + acc3.y));
           s0 *= ksc;
-          const int row = row0 + j * RB + r;
           const bool keep = token >= rs[lr] && token < re[lr] && __float_as_uint(s0) != 0u;
           const uint32_t bits = __ballot_sync(0xffffffffu, keep);
-          if (lane == 0 && tok_base < p.stride)
-            reinterpret_cast<uint32_t*>(p.mask)[(static_cast<int64_t>(row) * (p.stride / 16) + tok_base / 16) >> 1] =
-                bits;
-          if (keep) p.logits[static_cast<int64_t>(row) * p.stride + token] = s0;
+          st_u32_if(sm.mrow[ew][lr] + mword, bits, mstore);
+          st_f32_if(sm.lrow[ew][lr] + token, s0, keep);
         }
         tc_fence_before();
         __syncwarp();
