@@ -531,8 +531,8 @@ struct __align__(1024) PfSmem {
   uint8_t q[kQB][kQTile];
   uint8_t a[kPfStages][kATile];
   float w[kPfEpiWarps][kQB * kMaxN / kPfTeams];  // weights of the rows this epilogue warp owns
-  int rs[kPfEpiWarps][16];
-  int re[kPfEpiWarps][16];
+  int rs[kPfEpiWarps][16];          // first visible token of each owned row
+  int re[kPfEpiWarps][16];          // visible length of each owned row
   float* lrow[kPfEpiWarps][16];     // logits row of each owned row (super-block)
   uint32_t* mrow[kPfEpiWarps][16];  // mask row (as 32-bit words) of each owned row
   uint64_t full[kPfStages];
@@ -782,8 +782,10 @@ __global__ __launch_bounds__(kPfThreads, 1) void mqa_logits_ragged_kernel(const 
           for (int h = lane; h < H; h += 32)
             wsm[lr * H + h] = in ? __ldg(p.weights + static_cast<int64_t>(row) * H + h) * kReluScale : 0.f;
           if (lane == 0) {
-            rs[lr] = in ? max(__ldg(p.rs + row), 0) : 0;
-            re[lr] = in ? min(__ldg(p.re + row), p.n_tokens) : 0;
+            const int a0 = in ? max(__ldg(p.rs + row), 0) : 0;
+            const int e0 = in ? min(__ldg(p.re + row), p.n_tokens) : 0;
+            rs[lr] = a0;
+            re[lr] = e0 > a0 ? e0 - a0 : 0;  // visible length: token is visible iff (unsigned)(token - rs) < len
             sm.lrow[ew][lr] = p.logits + static_cast<int64_t>(in ? row : 0) * p.stride;
             sm.mrow[ew][lr] = reinterpret_cast<uint32_t*>(p.mask) + static_cast<int64_t>(in ? row : 0) * (p.stride / 32);
           }
@@ -828,7 +830,8 @@ __global__ __launch_bounds__(kPfThreads, 1) void mqa_logits_ragged_kernel(const 
           }
           float s0 = ((acc0.x + acc0.y) + (acc1.x + acc1.y)) + ((acc2.x + acc2.y) + (acc3.x + acc3.y));
           s0 *= ksc;
-          const bool keep = token >= rs[lr] && token < re[lr] && __float_as_uint(s0) != 0u;
+          const bool keep = static_cast<uint32_t>(token - rs[lr]) < static_cast<uint32_t>(re[lr]) &&
+                            __float_as_uint(s0) != 0u;
           const uint32_t bits = __ballot_sync(0xffffffffu, keep);
           st_u32_if(sm.mrow[ew][lr] + mword, bits, mstore);
           st_f32_if(sm.lrow[ew][lr] + token, s0, keep);
