@@ -189,6 +189,29 @@ int hcu_sparse_mask_topk_transform_split_pre(const float* score, int64_t rows, i
                                              void* workspace, int64_t workspace_bytes, int32_t* dst,
                                              hcu_stream_t stream);
 
+/* Allocation-free top-k (no counterpart in the reference).  For callers that
+ * cannot allocate device memory -- code inside an engine that owns the device's
+ * memory pool, or a plug-in run where a cudaMalloc would synchronise the device
+ * or exceed its budget.  Same arguments and result as
+ * hcu_sparse_mask_topk_transform; internally it builds the pass-1 histogram of
+ * the split_pre path in one fixed device array of this library (8 MiB, held by
+ * every GPU that loads the library until the process exits) and allocates
+ * nothing.  Limits and rules:
+ *   - rows <= hcu_topk_noalloc_max_rows() (256); larger batches return
+ *     HCU_ERR_ARG with a message in hcu_last_error_string();
+ *   - the array is shared by every call on a device: calls that may overlap on
+ *     the GPU (different streams without ordering) race and must not be issued;
+ *     each call rewrites the part it reads, so back-to-back calls are fine;
+ *   - the first call on a device looks up the array's device address (a CUDA
+ *     runtime call); make that first call before any stream capture. */
+int hcu_sparse_mask_topk_transform_noalloc(const float* score, int64_t rows, int64_t width,
+                                           int64_t score_stride, const int16_t* mask, int64_t mask_stride,
+                                           const int32_t* lengths, const int32_t* page_table, int64_t pt_stride,
+                                           int64_t topk, int32_t* dst, hcu_stream_t stream);
+
+/* Largest row count hcu_sparse_mask_topk_transform_noalloc accepts. */
+int64_t hcu_topk_noalloc_max_rows(void);
+
 /* Top-k that also returns the selected keys (the monotone uint32 image of the
  * fp32 score; +0 = 0x80000000 for unset mask bits; 0 for -1 pads).  Used by the
  * context-parallel path; same selection and order as hcu_sparse_mask_topk_transform. */

@@ -28,6 +28,9 @@
 // Unset mask bits are an implicit +0 (key 0x80000000) whatever the score
 // storage holds.  The selection and output order are those of
 // hcu_ops/csrc/sparse_mask_topk.cu:1-7,141-349 of the reference.
+#include <mutex>
+#include <vector>
+
 #include "common.cuh"
 
 HCU_DEFINE_STATUS(status_topk)
@@ -1268,4 +1271,83 @@ extern "C" int hcu_cp_topk_merge(const uint32_t* keys, const int32_t* gidx, int6
   cp_merge_kernel<<<static_cast<unsigned>(rows), kTkThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
       keys, gidx, static_cast<int>(n_parts), static_cast<int>(rows), lengths, dst);
   return launch_status();
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free top-k for callers that may not allocate device memory.
+//
+// The regular pass-1 path needs a workspace the caller allocates (zws, from
+// hcu_mqa_logits_hist).  Some callers cannot allocate: code running inside an
+// engine that owns the device memory pool, or a plug-in invoked where a
+// cudaMalloc would synchronise the device or break the host's memory budget.
+// This entry point keeps that workspace in one fixed file-scope device array
+// (kNoAllocMaxRows rows, 8 MiB, held by every GPU that loads this library until
+// the process exits) and otherwise runs the same kernels as the split_pre path.
+// ---------------------------------------------------------------------------
+namespace hcu {
+namespace {
+
+constexpr int64_t kNoAllocMaxRows = 256;
+
+// pass-1 workspace [ghist1 rows*4096 | ghist2 rows*4096 | cnt rows*2] of one call
+static __device__ __align__(256) int32_t g_topk_noalloc_ws[kNoAllocMaxRows * (2 * kBins + 2)];
+
+// Device address of g_topk_noalloc_ws on the current device, looked up once per
+// device (host code only holds a stand-in for the array under its name).
+int32_t* noalloc_ws_address() {
+  static std::mutex mu;
+  static std::vector<int32_t*> cache;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    set_last_error(e);
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (static_cast<int>(cache.size()) <= dev) cache.resize(dev + 1, nullptr);
+  if (cache[dev] == nullptr) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_topk_noalloc_ws);
+    if (e != cudaSuccess) {
+      set_last_error(e);
+      return nullptr;
+    }
+    cache[dev] = static_cast<int32_t*>(ptr);
+  }
+  return cache[dev];
+}
+
+}  // namespace
+}  // namespace hcu
+
+extern "C" int64_t hcu_topk_noalloc_max_rows(void) { return hcu::kNoAllocMaxRows; }
+
+extern "C" int hcu_sparse_mask_topk_transform_noalloc(const float* score, int64_t rows, int64_t width,
+                                                      int64_t score_stride, const int16_t* mask, int64_t mask_stride,
+                                                      const int32_t* lengths, const int32_t* page_table,
+                                                      int64_t pt_stride, int64_t topk, int32_t* dst,
+                                                      hcu_stream_t stream) {
+  using namespace hcu;
+  int st = check_common(score, rows, width, score_stride, mask, mask_stride, lengths, page_table, pt_stride, topk,
+                        dst);
+  if (st != HCU_OK || rows == 0) return st;
+  if (rows > kNoAllocMaxRows) {
+    set_last_error_msg("hcu_sparse_mask_topk_transform_noalloc: rows exceeds the fixed scratch maximum of ",
+                       "256 rows (call the regular entry point for larger batches)");
+    return HCU_ERR_ARG;
+  }
+  int32_t* ws = noalloc_ws_address();
+  if (ws == nullptr) return HCU_ERR_LAUNCH;
+  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  // hist_init_kernel rewrites every workspace element the later kernels read (the
+  // array keeps the previous call's contents)
+  hist_init_kernel<<<static_cast<int>(rows), 256, 0, s>>>(ws, lengths, static_cast<int>(width),
+                                                          static_cast<int>(rows));
+  const dim3 grid(static_cast<unsigned>((width + kHistChunk - 1) / kHistChunk), static_cast<unsigned>(rows));
+  pass1_hist_kernel<<<grid, kHistThreads, 0, s>>>(score, score_stride, static_cast<int>(width), mask, mask_stride,
+                                                 lengths, ws, static_cast<int>(rows));
+  st = launch_status();
+  if (st != HCU_OK) return st;
+  return launch_rows(score, rows, width, score_stride, mask, mask_stride, lengths, page_table, pt_stride, dst,
+                     nullptr, ws, s);
 }

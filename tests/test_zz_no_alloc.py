@@ -1,0 +1,67 @@
+"""The allocation-free top-k entry point, called through the C ABI.
+
+Some callers cannot allocate device memory: code running inside a serving engine that owns the
+device's memory pool, or a plug-in invoked where a cudaMalloc would synchronise the device or break
+its memory budget.  `hcu_sparse_mask_topk_transform_noalloc` serves them: it keeps its workspace in a
+fixed device array of the library instead of asking for one.  These checks compare it with the
+regular entry point `hcu_sparse_mask_topk_transform` (exact: same selection, same order) on two calls
+in a row -- the second with other shapes and values, so a workspace left over from the first call
+would show -- and check that a batch beyond the fixed maximum is refused with an error message.
+
+The file is named so that pytest collects it last."""
+import ctypes
+
+import pytest
+import torch
+
+from indexer_testlib import make_scores
+
+pytestmark = pytest.mark.gpu
+
+HCU_OK, HCU_ERR_ARG = 0, 1
+_ARGS = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64,
+         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p]
+
+
+@pytest.fixture(scope="module")
+def lib(hcu):
+    so = ctypes.CDLL(hcu.library_path())
+    for name in ("hcu_sparse_mask_topk_transform", "hcu_sparse_mask_topk_transform_noalloc"):
+        fn = getattr(so, name)
+        fn.restype = ctypes.c_int
+        fn.argtypes = _ARGS
+    so.hcu_topk_noalloc_max_rows.restype = ctypes.c_int64
+    so.hcu_last_error_string.restype = ctypes.c_char_p
+    return so
+
+
+def _call(fn, x, mask, lens, pt, out):
+    stream = torch.cuda.current_stream().cuda_stream
+    return fn(x.data_ptr(), x.shape[0], x.shape[1], x.stride(0), mask.data_ptr(), mask.stride(0), lens.data_ptr(),
+              pt.data_ptr(), pt.stride(0), 2048, out.data_ptr(), stream)
+
+
+def test_noalloc_topk_equals_regular_entry_point_twice(lib, dev):
+    max_rows = lib.hcu_topk_noalloc_max_rows()
+    assert max_rows >= 128
+    # two calls in a row with different batches: wide rows, then narrower rows of another distribution
+    for rows, L, W, dist, seed in [(max_rows, 40000, 40064, "relu_sum", 1), (37, 9000, 9216, "ties", 2)]:
+        x, mask, lens, pt = make_scores(rows, L, dist, W=W, ragged=True, seed=seed)
+        x, mask, lens, pt = (t.to(dev) for t in (x, mask, lens, pt))
+        ref = torch.full((rows, 2048), -7, dtype=torch.int32, device=dev)
+        got = torch.full((rows, 2048), -9, dtype=torch.int32, device=dev)
+        assert _call(lib.hcu_sparse_mask_topk_transform, x, mask, lens, pt, ref) == HCU_OK
+        assert _call(lib.hcu_sparse_mask_topk_transform_noalloc, x, mask, lens, pt, got) == HCU_OK
+        torch.cuda.synchronize()
+        assert torch.equal(got, ref), (rows, dist)
+
+
+def test_noalloc_topk_refuses_rows_beyond_its_maximum(lib, dev):
+    rows = lib.hcu_topk_noalloc_max_rows() + 1
+    x, mask, lens, pt = make_scores(rows, 4096, "pos", seed=3)
+    x, mask, lens, pt = (t.to(dev) for t in (x, mask, lens, pt))
+    out = torch.full((rows, 2048), -5, dtype=torch.int32, device=dev)
+    assert _call(lib.hcu_sparse_mask_topk_transform_noalloc, x, mask, lens, pt, out) == HCU_ERR_ARG
+    assert b"maximum" in lib.hcu_last_error_string()
+    torch.cuda.synchronize()
+    assert (out == -5).all()  # nothing was launched
