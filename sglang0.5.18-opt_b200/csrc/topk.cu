@@ -38,36 +38,52 @@ HCU_DEFINE_STATUS(status_topk)
 namespace hcu {
 namespace {
 
-constexpr int kTkThreads = 1024;
-constexpr int kTkWarps = kTkThreads / 32;
 constexpr int kStep = 128;  // tokens per warp step (32 lanes x 4)
 constexpr int kTkUnroll = 4;
-constexpr int kHistTrash = kTkWarps * 256;  // trash slots follow the per-warp histograms
-
 constexpr int kSmallSample = 2048;  // row samples used to bound the threshold (rows <= 128K)
 constexpr int kSample = 8192;       // sample count for rows > 512K
-constexpr int kCandCap = 8192;      // candidate list capacity (tokens with key >= lo)
 constexpr int kLaneTok = 16;        // consecutive tokens per lane in a streaming round
-constexpr int kRound = kTkThreads * kLaneTok;  // tokens per streaming round
+constexpr int kNarrowWidth = 32768; // rows up to this width run the 512-thread kernel (two CTAs per SM)
 
-struct __align__(16) TopkSmem {
-  int hist[kTkWarps * 256 + 32 + 256];  // A/B: [0,4096) + trash; C: 32 x 256 + trash + merged[256]
+// Per-CTA-size constants: 1024 threads (one CTA per SM) for wide rows, 512 threads for
+// narrow ones, so that two CTAs per SM overlap their rows' latency-bound phases.
+template <int kT>
+struct Tk {
+  static constexpr int kThreads = kT;
+  static constexpr int kWarps = kT / 32;
+  static constexpr int kRound = kT * kLaneTok;               // tokens per streaming round
+  static constexpr int kCandCap = kT >= 1024 ? 8192 : 4096;  // candidate list capacity
+  static constexpr int kHistTrash = kWarps * 256;            // trash slots follow the per-warp histograms
+  static constexpr int kMaxSample = kT >= 1024 ? kSample : kSmallSample;
+  static constexpr int kHist = kWarps * 256 + 32 + 256 > kBins + 32 ? kWarps * 256 + 32 + 256 : kBins + 32;
+};
+
+struct TopkOutStage {  // pass D staging of the radix fallback
   int out_idx[kTopK + 32];
   uint32_t out_key[kTopK + 32];
-  uint32_t cand_key[kCandCap];
-  int32_t cand_idx[kCandCap];
-  int32_t cand_pid[kCandCap];  // page-table entry of each candidate (async copies)
-  uint4 scr[kLaneTok / 4][kTkThreads];  // this thread's current 16 score words (candidate pass)
+};
+
+template <int kT>
+struct __align__(16) TopkSmem {
+  int hist[Tk<kT>::kHist];  // A/B: [0,4096) + trash; C: warps x 256 + trash + merged[256]
+  union {
+    uint4 scr[kLaneTok / 4][kT];  // candidate pass: this thread's current 16 score words
+    TopkOutStage d;               // radix fallback: ordered output staging
+  };
+  uint32_t cand_key[Tk<kT>::kCandCap];
+  int32_t cand_idx[Tk<kT>::kCandCap];
+  int32_t cand_pid[Tk<kT>::kCandCap];  // page-table entry of each candidate (async copies)
   int hb[2][512];  // digit histograms (sample refinement: 256 bins, candidate select: 512)
-  int wcnt[2][kTkWarps];
-  uint32_t wmax[kTkWarps];
-  int above[kTkWarps];
-  int ties[kTkWarps];
-  int zeros[kTkWarps];
-  int pos[kTkWarps];
-  int wtot[kTkWarps];
+  int wcnt[2][Tk<kT>::kWarps];
+  uint32_t wmax[Tk<kT>::kWarps];
+  int above[Tk<kT>::kWarps];
+  int ties[Tk<kT>::kWarps];
+  int zeros[Tk<kT>::kWarps];
+  int pos[Tk<kT>::kWarps];
+  int wtot[32];
   int res[4];
 };
+static_assert(sizeof(TopkOutStage) <= sizeof(uint4) * 4 * 512, "fallback staging fits the scratch area");
 
 // 4-byte global -> shared copy that does not hold a register (LDGSTS).
 __device__ __forceinline__ void cp_async4(void* smem_dst, const void* gsrc) {
@@ -110,9 +126,9 @@ __device__ __forceinline__ uint32_t keys4(int i0, int lim, const float (&v)[4], 
 
 // Bin b of an NB-bin histogram with suffix(b) >= need > suffix(b+1):
 // res[0] = b, res[1] = suffix(b+1).  Requires sum(hist) >= need >= 1.
-template <int NB>
+template <int kT, int NB>
 __device__ __forceinline__ void find_threshold(const int* hist, int need, int* wtot, int* res) {
-  constexpr int BPT = NB >= kTkThreads ? NB / kTkThreads : 1;
+  constexpr int BPT = NB >= kT ? NB / kT : 1;
   constexpr int ACTIVE = NB / BPT;
   const int tid = threadIdx.x;
   const int lane = tid & 31;
@@ -133,7 +149,7 @@ __device__ __forceinline__ void find_threshold(const int* hist, int need, int* w
   if (lane == 0) wtot[w] = x;
   __syncthreads();
   // suffix of the warp totals after warp w, by a shuffle scan (no serial loop)
-  int t = wtot[lane];
+  int t = lane < kT / 32 ? wtot[lane] : 0;
   int sx = t;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -248,13 +264,14 @@ __device__ __forceinline__ void warp_find(const int* h, int need, int* res) {
 
 // Exclusive block-wide prefix sum of x; *total = the block sum.  One barrier;
 // consecutive calls must be separated by a barrier (wtot is reused).
+template <int kT>
 __device__ __forceinline__ int block_excl_scan(int x, int* wtot, int* total) {
   const int lane = threadIdx.x & 31;
   const int w = threadIdx.x >> 5;
   const int inc = warp_incl_scan(x);
   if (lane == 31) wtot[w] = inc;
   __syncthreads();
-  const int t = wtot[lane];
+  const int t = lane < kT / 32 ? wtot[lane] : 0;
   const int ti = warp_incl_scan(t);
   *total = __shfl_sync(0xffffffffu, ti, 31);
   return __shfl_sync(0xffffffffu, ti - t, w) + inc - x;
@@ -295,15 +312,15 @@ __device__ __forceinline__ uint32_t load16_raw(const float* __restrict__ vals, c
 // bits are in X (round r).  The words go to this thread's scratch slot, X is
 // refilled with round r + 2, and after the round's barrier the candidates are
 // appended at their block-wide prefix position, visiting set bits only.
-template <bool kVec, bool kPos>
+template <int kT, bool kVec, bool kPos>
 __device__ __forceinline__ void candidate_round(const float* __restrict__ vals, const int16_t* __restrict__ mrow,
                                                 const int32_t* __restrict__ src, int len, uint32_t lo, int r, int nr,
-                                                TopkSmem& sm,
+                                                TopkSmem<kT>& sm,
                                                 uint32_t (&X)[16], uint32_t& mX, uint32_t& vX, int& base,
                                                 uint32_t& kmax) {
   const int lane = threadIdx.x & 31;
   const int w = threadIdx.x >> 5;
-  const int i0 = r * kRound + w * (32 * kLaneTok) + lane * kLaneTok;
+  const int i0 = r * Tk<kT>::kRound + w * (32 * kLaneTok) + lane * kLaneTok;
   const int lim_pos = static_cast<int>(lo ^ kZeroKey);
   uint32_t cb = 0u;
 #pragma unroll
@@ -325,9 +342,9 @@ __device__ __forceinline__ void candidate_round(const float* __restrict__ vals, 
   const int nc = __popc(cb);
   const int inc = warp_incl_scan(nc);
   if (lane == 31) sm.wcnt[r & 1][w] = inc;
-  if (r + 2 < nr) mX = load16_raw<kVec>(vals, mrow, i0 + 2 * kRound, len, X, vX);
+  if (r + 2 < nr) mX = load16_raw<kVec>(vals, mrow, i0 + 2 * Tk<kT>::kRound, len, X, vX);
   __syncthreads();
-  const int wc = sm.wcnt[r & 1][lane];
+  const int wc = lane < kT / 32 ? sm.wcnt[r & 1][lane] : 0;  // one entry per warp
   const int wi = warp_incl_scan(wc);
   const int wbase = __shfl_sync(0xffffffffu, wi - wc, w);
   const int rtot = __shfl_sync(0xffffffffu, wi, 31);
@@ -336,7 +353,7 @@ __device__ __forceinline__ void candidate_round(const float* __restrict__ vals, 
   while (cb) {
     const int t = __ffs(cb) - 1;
     cb &= cb - 1u;
-    const uint32_t raw = mine[(t >> 2) * (4 * kTkThreads) + (t & 3)];
+    const uint32_t raw = mine[(t >> 2) * (4 * kT) + (t & 3)];
     uint32_t key;
     if constexpr (kPos) {
       key = raw | kZeroKey;
@@ -344,7 +361,7 @@ __device__ __forceinline__ void candidate_round(const float* __restrict__ vals, 
       key = ((mcur >> t) & 1u) ? key_of(__uint_as_float(raw)) : kZeroKey;
     }
     kmax = key > kmax ? key : kmax;
-    if (pos < kCandCap) {
+    if (pos < Tk<kT>::kCandCap) {
       sm.cand_key[pos] = key;
       sm.cand_idx[pos] = i0 + t;
       cp_async4(&sm.cand_pid[pos], src + i0 + t);
@@ -364,21 +381,21 @@ __device__ __forceinline__ void candidate_round(const float* __restrict__ vals, 
 // stored); sm.wmax receives each warp's largest candidate key.  Each stored
 // candidate's page-table entry src[idx] is copied to sm.cand_pid
 // asynchronously (waited for in write_candidates).
-template <bool kVec, bool kPos>
+template <int kT, bool kVec, bool kPos>
 __device__ __forceinline__ int collect_candidates(const float* __restrict__ vals, const int16_t* __restrict__ mrow,
-                                                  const int32_t* __restrict__ src, int len, uint32_t lo, TopkSmem& sm,
+                                                  const int32_t* __restrict__ src, int len, uint32_t lo, TopkSmem<kT>& sm,
                                                   uint32_t (&A)[16],
                                                   uint32_t mA, uint32_t vA) {
   const int lane = threadIdx.x & 31;
   const int w = threadIdx.x >> 5;
-  const int nr = (len + kRound - 1) / kRound;
+  const int nr = (len + Tk<kT>::kRound - 1) / Tk<kT>::kRound;
   uint32_t B[16], mB = 0u, vB = 0u;
-  if (nr > 1) mB = load16_raw<kVec>(vals, mrow, kRound + w * (32 * kLaneTok) + lane * kLaneTok, len, B, vB);
+  if (nr > 1) mB = load16_raw<kVec>(vals, mrow, Tk<kT>::kRound + w * (32 * kLaneTok) + lane * kLaneTok, len, B, vB);
   int base = 0;
   uint32_t kmax = 0u;
   for (int r = 0; r < nr; r += 2) {
-    candidate_round<kVec, kPos>(vals, mrow, src, len, lo, r, nr, sm, A, mA, vA, base, kmax);
-    if (r + 1 < nr) candidate_round<kVec, kPos>(vals, mrow, src, len, lo, r + 1, nr, sm, B, mB, vB, base, kmax);
+    candidate_round<kT, kVec, kPos>(vals, mrow, src, len, lo, r, nr, sm, A, mA, vA, base, kmax);
+    if (r + 1 < nr) candidate_round<kT, kVec, kPos>(vals, mrow, src, len, lo, r + 1, nr, sm, B, mB, vB, base, kmax);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
@@ -394,12 +411,13 @@ __device__ __forceinline__ int collect_candidates(const float* __restrict__ vals
 // all keys >= lo): a radix select of u = key - lo with 9-bit digits from the
 // top bit of (largest candidate - lo) down.  *above = candidates with a
 // larger key.  sm.hb[0] and sm.hb[1] must be zero on entry.
-__device__ __forceinline__ uint32_t select_candidates(TopkSmem& sm, int n, uint32_t lo, int* above) {
+template <int kT>
+__device__ __forceinline__ uint32_t select_candidates(TopkSmem<kT>& sm, int n, uint32_t lo, int* above) {
   constexpr int kDigit = 9;
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int w = tid >> 5;
-  uint32_t kmax = sm.wmax[lane];
+  uint32_t kmax = lane < kT / 32 ? sm.wmax[lane] : 0u;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const uint32_t y = __shfl_xor_sync(0xffffffffu, kmax, o);
@@ -415,11 +433,11 @@ __device__ __forceinline__ uint32_t select_candidates(TopkSmem& sm, int n, uint3
     const int nb = s + kDigit - sh;  // bits in this digit (the last one may be short)
     const uint32_t dm = (1u << nb) - 1u;
     int* h = sm.hb[rnd & 1];
-    for (int i = tid; i < n; i += kTkThreads) {
+    for (int i = tid; i < n; i += kT) {
       const uint32_t u = sm.cand_key[i] - lo;
       if ((static_cast<uint64_t>(u) >> (sh + nb)) == pre) atomicAdd(&h[(u >> sh) & dm], 1);
     }
-    if (tid < 512) sm.hb[(rnd + 1) & 1][tid] = 0;
+    for (int i = tid; i < 512; i += kT) sm.hb[(rnd + 1) & 1][i] = 0;
     __syncthreads();
     if (w == 0) warp_find<512>(h, need, sm.res);
     __syncthreads();
@@ -436,11 +454,11 @@ __device__ __forceinline__ uint32_t select_candidates(TopkSmem& sm, int n, uint3
 // kTopK - above ties in token order (kSorted: the same set in token order),
 // through the page-table entries copied during the candidate pass.
 // Candidate i goes to thread i / ceil(n / 1024).
-template <bool kSorted>
-__device__ __forceinline__ void write_candidates(TopkSmem& sm, int n, uint32_t thr, int above,
+template <int kT, bool kSorted>
+__device__ __forceinline__ void write_candidates(TopkSmem<kT>& sm, int n, uint32_t thr, int above,
                                                  int32_t* __restrict__ out, uint32_t* __restrict__ okeys) {
   const int remaining = kTopK - above;
-  const int per = (n + kTkThreads - 1) / kTkThreads;
+  const int per = (n + kT - 1) / kT;
   const int i0 = min(n, static_cast<int>(threadIdx.x) * per);
   const int i1 = min(n, i0 + per);
   int na = 0, nt = 0;
@@ -451,7 +469,7 @@ __device__ __forceinline__ void write_candidates(TopkSmem& sm, int n, uint32_t t
   }
   cp_async_wait_all();  // the barrier in the scan publishes every thread's page-id copies
   int total;
-  const int ex = block_excl_scan(na | (nt << 16), sm.wtot, &total);
+  const int ex = block_excl_scan<kT>(na | (nt << 16), sm.wtot, &total);
   int ea = ex & 0xFFFF;
   int et = ex >> 16;
   for (int i = i0; i < i1; ++i) {
@@ -491,13 +509,17 @@ __device__ __forceinline__ void write_candidates(TopkSmem& sm, int n, uint32_t t
     }                                                                                 \
   }
 
-template <bool kVec, bool kSorted>
-__global__ __launch_bounds__(kTkThreads, 1) void topk_row_kernel(
+template <int kT, bool kVec, bool kSorted>
+__global__ __launch_bounds__(kT, 1024 / kT) void topk_row_kernel(
     const float* __restrict__ score, int64_t score_stride, int width, const int16_t* __restrict__ mask,
     int64_t mask_stride, const int32_t* __restrict__ lengths, const int32_t* __restrict__ pt, int64_t pt_stride,
     int32_t* __restrict__ dst, uint32_t* __restrict__ dst_keys, const int32_t* __restrict__ pre_ws, int rows) {
+  constexpr int kTkThreads = kT;
+  constexpr int kTkWarps = kT / 32;
+  constexpr int kCandCap = Tk<kT>::kCandCap;
+  constexpr int kHistTrash = Tk<kT>::kHistTrash;
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  TopkSmem& sm = *reinterpret_cast<TopkSmem*>(smem_raw);
+  TopkSmem<kT>& sm = *reinterpret_cast<TopkSmem<kT>*>(smem_raw);
   const int row = blockIdx.x;
   const int tid = threadIdx.x;
   const int lane = tid & 31;
@@ -536,9 +558,9 @@ __global__ __launch_bounds__(kTkThreads, 1) void topk_row_kernel(
     // ---- candidate path ----
     // The sample loads go out first (they gate the bound), then round 0's
     // loads, whose latency overlaps the bound search.
-    const int m = len <= (1 << 17) ? kSmallSample : (len <= (1 << 19) ? 4096 : kSample);
+    const int m = min(Tk<kT>::kMaxSample, len <= (1 << 17) ? kSmallSample : (len <= (1 << 19) ? 4096 : kSample));
     const int groups = m / 4;  // m samples in groups of 4 consecutive tokens, one 16-byte load each
-    constexpr int kGpt = kSample / (4 * kTkThreads);  // sample groups per thread (at most)
+    constexpr int kGpt = Tk<kT>::kMaxSample / (4 * kTkThreads);  // sample groups per thread (at most)
     float sv[4 * kGpt];
     uint32_t smb[kGpt];
     if (pre_ws == nullptr) {
@@ -585,7 +607,7 @@ __global__ __launch_bounds__(kTkThreads, 1) void topk_row_kernel(
       // sample rank (1 = largest) 4 sigma + 4 below the threshold's expected sample rank
       const float t = static_cast<float>(kTopK) / stride_f;
       const int r_lo = min(m, static_cast<int>(ceilf(t + 4.f * sqrtf(t) + 4.f)));
-      find_threshold<kBins>(sm.hist, r_lo, sm.wtot, sm.res);
+      find_threshold<kT, kBins>(sm.hist, r_lo, sm.wtot, sm.res);
       const uint32_t b1 = static_cast<uint32_t>(sm.res[0]);
       const int need = r_lo - sm.res[1];
 #pragma unroll
@@ -609,20 +631,20 @@ __global__ __launch_bounds__(kTkThreads, 1) void topk_row_kernel(
           sm.res[0] = 0;
           sm.res[1] = 0;
         }
-        find_threshold<kBins>(h1, kTopK, sm.wtot, sm.res);
+        find_threshold<kT, kBins>(h1, kTopK, sm.wtot, sm.res);
         const int b1 = sm.res[0];
         lo = static_cast<uint32_t>(b1) << 20;
         try_cand = sm.res[1] + h1[b1] <= kCandCap;
       }
     }
     if (try_cand) {
-      const int n = lo > kZeroKey ? collect_candidates<kVec, true>(vals, mrow, src, len, lo, sm, b0, mw0, valid0)
-                                  : collect_candidates<kVec, false>(vals, mrow, src, len, lo, sm, b0, mw0, valid0);
+      const int n = lo > kZeroKey ? collect_candidates<kT, kVec, true>(vals, mrow, src, len, lo, sm, b0, mw0, valid0)
+                                  : collect_candidates<kT, kVec, false>(vals, mrow, src, len, lo, sm, b0, mw0, valid0);
       if (n < kTopK || n > kCandCap) cp_async_wait_all();  // no copy outlives the candidate path
       if (n >= kTopK && n <= kCandCap) {
         int above = 0;
         thr = select_candidates(sm, n, lo, &above);
-        write_candidates<kSorted>(sm, n, thr, above, out,
+        write_candidates<kT, kSorted>(sm, n, thr, above, out,
                                   dst_keys ? dst_keys + static_cast<int64_t>(row) * kTopK : nullptr);
         return;
       }
@@ -658,8 +680,8 @@ __global__ __launch_bounds__(kTkThreads, 1) void topk_row_kernel(
         sm.zeros[w] = zc;
       }
       __syncthreads();
-      positives = warp_sum(sm.pos[lane]);
-      zeros = warp_sum(sm.zeros[lane]);
+      positives = warp_sum(lane < kTkWarps ? sm.pos[lane] : 0);
+      zeros = warp_sum(lane < kTkWarps ? sm.zeros[lane] : 0);
       have_warp_counts = true;
     }
 
@@ -686,7 +708,7 @@ __global__ __launch_bounds__(kTkThreads, 1) void topk_row_kernel(
       }
       __syncthreads();
     } else {
-      find_threshold<kBins>(hist1, kTopK, sm.wtot, sm.res);
+      find_threshold<kT, kBins>(hist1, kTopK, sm.wtot, sm.res);
       const uint32_t t1 = static_cast<uint32_t>(sm.res[0]);
       const int need1 = kTopK - sm.res[1];
 
@@ -699,7 +721,7 @@ __global__ __launch_bounds__(kTkThreads, 1) void topk_row_kernel(
         atomicAdd(&sm.hist[cand ? static_cast<int>((key >> 8) & 0xFFFu) : trash], 1);
       })
       __syncthreads();
-      find_threshold<kBins>(sm.hist, need1, sm.wtot, sm.res);
+      find_threshold<kT, kBins>(sm.hist, need1, sm.wtot, sm.res);
       const uint32_t prefix24 = (t1 << 12) | static_cast<uint32_t>(sm.res[0]);
       const int need2 = need1 - sm.res[1];
 
@@ -731,7 +753,7 @@ __global__ __launch_bounds__(kTkThreads, 1) void topk_row_kernel(
         merged[tid] = s;
       }
       __syncthreads();
-      find_threshold<256>(merged, need2, sm.wtot, sm.res);
+      find_threshold<kT, 256>(merged, need2, sm.wtot, sm.res);
       const uint32_t t3 = static_cast<uint32_t>(sm.res[0]);
       thr = (prefix24 << 8) | t3;
       remaining = need2 - sm.res[1];
@@ -759,8 +781,8 @@ __global__ __launch_bounds__(kTkThreads, 1) void topk_row_kernel(
   // threshold ties in token order.  kSorted: the same set in token order.
   int above_pos, tie_pos, sel_pos;
   {
-    const int av = sm.above[lane];
-    const int tv = sm.ties[lane];
+    const int av = lane < kTkWarps ? sm.above[lane] : 0;  // one entry per warp
+    const int tv = lane < kTkWarps ? sm.ties[lane] : 0;
     const int a_inc = warp_incl_scan(av);
     const int t_inc = warp_incl_scan(tv);
     const int t_exc = t_inc - tv;
@@ -794,13 +816,13 @@ __global__ __launch_bounds__(kTkThreads, 1) void topk_row_kernel(
 #pragma unroll
         for (int t = 0; t < 16; ++t) {
           if ((ab >> t) & 1u) {
-            sm.out_idx[pa] = i0 + t;
-            sm.out_key[pa] = k[t];
+            sm.d.out_idx[pa] = i0 + t;
+            sm.d.out_key[pa] = k[t];
             ++pa;
           } else if ((tb >> t) & 1u) {
             if (pq < remaining) {
-              sm.out_idx[tie_base + pq] = i0 + t;
-              sm.out_key[tie_base + pq] = k[t];
+              sm.d.out_idx[tie_base + pq] = i0 + t;
+              sm.d.out_key[tie_base + pq] = k[t];
             }
             ++pq;
           }
@@ -824,8 +846,8 @@ __global__ __launch_bounds__(kTkThreads, 1) void topk_row_kernel(
 #pragma unroll
         for (int t = 0; t < 16; ++t) {
           if ((sel >> t) & 1u) {
-            sm.out_idx[ps] = i0 + t;
-            sm.out_key[ps] = k[t];
+            sm.d.out_idx[ps] = i0 + t;
+            sm.d.out_key[ps] = k[t];
             ++ps;
           }
         }
@@ -837,8 +859,8 @@ __global__ __launch_bounds__(kTkThreads, 1) void topk_row_kernel(
   }
   __syncthreads();
   for (int i = tid; i < kTopK; i += kTkThreads) {
-    out[i] = src[sm.out_idx[i]];
-    if (dst_keys) dst_keys[static_cast<int64_t>(row) * kTopK + i] = sm.out_key[i];
+    out[i] = src[sm.d.out_idx[i]];
+    if (dst_keys) dst_keys[static_cast<int64_t>(row) * kTopK + i] = sm.d.out_key[i];
   }
 }
 #undef TK_FOR_EACH
@@ -935,16 +957,33 @@ int check_common(const float* score, int64_t rows, int64_t width, int64_t score_
   return HCU_OK;
 }
 
-template <bool kVec, bool kSorted>
+template <int kT, bool kVec, bool kSorted>
 void launch_rows_t(const float* score, int rows, int width, int64_t score_stride, const int16_t* mask,
                    int64_t mask_stride, const int32_t* lengths, const int32_t* pt, int64_t pt_stride, int32_t* dst,
                    uint32_t* dst_keys, const int32_t* pre_ws, cudaStream_t stream) {
-  const size_t smem = sizeof(TopkSmem);
-  cudaFuncSetAttribute(topk_row_kernel<kVec, kSorted>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  const size_t smem = sizeof(TopkSmem<kT>);
+  cudaFuncSetAttribute(topk_row_kernel<kT, kVec, kSorted>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        static_cast<int>(smem));
-  topk_row_kernel<kVec, kSorted><<<rows, kTkThreads, smem, stream>>>(score, score_stride, width, mask, mask_stride,
-                                                                    lengths, pt, pt_stride, dst, dst_keys, pre_ws,
-                                                                    rows);
+  topk_row_kernel<kT, kVec, kSorted><<<rows, kT, smem, stream>>>(score, score_stride, width, mask, mask_stride,
+                                                                lengths, pt, pt_stride, dst, dst_keys, pre_ws, rows);
+}
+
+template <int kT>
+void launch_rows_sized(const float* score, int r, int w, int64_t score_stride, const int16_t* mask,
+                       int64_t mask_stride, const int32_t* lengths, const int32_t* pt, int64_t pt_stride, int32_t* dst,
+                       uint32_t* dst_keys, const int32_t* pre_ws, cudaStream_t stream, bool vec, bool sorted) {
+  if (vec && !sorted)
+    launch_rows_t<kT, true, false>(score, r, w, score_stride, mask, mask_stride, lengths, pt, pt_stride, dst, dst_keys,
+                                   pre_ws, stream);
+  else if (vec)
+    launch_rows_t<kT, true, true>(score, r, w, score_stride, mask, mask_stride, lengths, pt, pt_stride, dst, dst_keys,
+                                  pre_ws, stream);
+  else if (!sorted)
+    launch_rows_t<kT, false, false>(score, r, w, score_stride, mask, mask_stride, lengths, pt, pt_stride, dst,
+                                    dst_keys, pre_ws, stream);
+  else
+    launch_rows_t<kT, false, true>(score, r, w, score_stride, mask, mask_stride, lengths, pt, pt_stride, dst, dst_keys,
+                                   pre_ws, stream);
 }
 
 int launch_rows(const float* score, int64_t rows, int64_t width, int64_t score_stride, const int16_t* mask,
@@ -953,21 +992,14 @@ int launch_rows(const float* score, int64_t rows, int64_t width, int64_t score_s
   const int w = static_cast<int>(width);
   const int r = static_cast<int>(rows);
   const bool vec = use_vec(score, width, score_stride);
-  if (vec && !sorted)
-    launch_rows_t<true, false>(score, r, w, score_stride, mask, mask_stride, lengths, pt, pt_stride, dst, dst_keys,
-                               pre_ws, stream);
-  else if (vec)
-    launch_rows_t<true, true>(score, r, w, score_stride, mask, mask_stride, lengths, pt, pt_stride, dst, dst_keys,
-                              pre_ws, stream);
-  else if (!sorted)
-    launch_rows_t<false, false>(score, r, w, score_stride, mask, mask_stride, lengths, pt, pt_stride, dst, dst_keys,
-                                pre_ws, stream);
+  if (width <= kNarrowWidth)  // narrow rows: 512 threads, two CTAs per SM
+    launch_rows_sized<512>(score, r, w, score_stride, mask, mask_stride, lengths, pt, pt_stride, dst, dst_keys, pre_ws,
+                           stream, vec, sorted);
   else
-    launch_rows_t<false, true>(score, r, w, score_stride, mask, mask_stride, lengths, pt, pt_stride, dst, dst_keys,
-                               pre_ws, stream);
+    launch_rows_sized<1024>(score, r, w, score_stride, mask, mask_stride, lengths, pt, pt_stride, dst, dst_keys,
+                            pre_ws, stream, vec, sorted);
   return launch_status();
 }
-
 
 // ---------------------------------------------------------------------------
 // Context-parallel merge: P per-range top-2048 lists -> the global top-2048.
@@ -991,13 +1023,16 @@ int launch_rows(const float* score, int64_t rows, int64_t width, int64_t score_s
 // than 2048 (the bound missed), falls back to 12/12/8-bit radix passes over all entries.
 // ---------------------------------------------------------------------------
 constexpr int kMaxParts = 16;
+constexpr int kTkThreads = 1024;  // one CTA per row
+constexpr int kTkWarps = kTkThreads / 32;
+constexpr int kCandCap = Tk<kTkThreads>::kCandCap;
 
 __device__ __forceinline__ int64_t merge_off(int c, int rows, int row) {
   return (static_cast<int64_t>(c >> 11) * rows + row) * kTopK + (c & (kTopK - 1));
 }
 
 // Radix-select fallback over every valid entry (entries [tid*per, (tid+1)*per)).
-__device__ void merge_radix(TopkSmem& sm, const uint32_t* __restrict__ keys, const int32_t* __restrict__ gidx,
+__device__ void merge_radix(TopkSmem<kTkThreads>& sm, const uint32_t* __restrict__ keys, const int32_t* __restrict__ gidx,
                             int per, int rows, int row, int32_t* __restrict__ out) {
   const int tid = threadIdx.x;
   const int c0 = tid * per;
@@ -1018,9 +1053,9 @@ __device__ void merge_radix(TopkSmem& sm, const uint32_t* __restrict__ keys, con
     }
     __syncthreads();
     if (pass < 2)
-      find_threshold<kBins>(sm.hist, need, sm.wtot, sm.res);
+      find_threshold<kTkThreads, kBins>(sm.hist, need, sm.wtot, sm.res);
     else
-      find_threshold<256>(sm.hist, need, sm.wtot, sm.res);
+      find_threshold<kTkThreads, 256>(sm.hist, need, sm.wtot, sm.res);
     pre = (pre << (pass < 2 ? 12 : 8)) | static_cast<uint32_t>(sm.res[0]);
     above += sm.res[1];
     need -= sm.res[1];
@@ -1036,7 +1071,7 @@ __device__ void merge_radix(TopkSmem& sm, const uint32_t* __restrict__ keys, con
     nt += v & (k == thr);
   }
   int total;
-  const int ex = block_excl_scan(na | (nt << 16), sm.wtot, &total);
+  const int ex = block_excl_scan<kTkThreads>(na | (nt << 16), sm.wtot, &total);
   int ea = ex & 0xFFFF, et = ex >> 16;
   for (int i = 0; i < per; ++i) {
     const int64_t o = merge_off(c0 + i, rows, row);
@@ -1057,7 +1092,7 @@ __global__ __launch_bounds__(kTkThreads, 1) void cp_merge_kernel(const uint32_t*
                                                                 int rows, const int32_t* __restrict__ lengths,
                                                                 int32_t* __restrict__ dst) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  TopkSmem& sm = *reinterpret_cast<TopkSmem*>(smem_raw);
+  TopkSmem<kTkThreads>& sm = *reinterpret_cast<TopkSmem<kTkThreads>*>(smem_raw);
   const int row = blockIdx.x;
   const int tid = threadIdx.x;
   const int lane = tid & 31;
@@ -1080,7 +1115,7 @@ __global__ __launch_bounds__(kTkThreads, 1) void cp_merge_kernel(const uint32_t*
   // sample rank (1 = largest) 4 sigma + 4 below the threshold's expected sample rank
   const float t = static_cast<float>(kTopK) / static_cast<float>(parts);
   const int r_lo = min(kMs, static_cast<int>(ceilf(t + 4.f * sqrtf(t) + 4.f)));
-  find_threshold<kBins>(sm.hist, r_lo, sm.wtot, sm.res);
+  find_threshold<kTkThreads, kBins>(sm.hist, r_lo, sm.wtot, sm.res);
   const uint32_t b1 = static_cast<uint32_t>(sm.res[0]);
   const int need = r_lo - sm.res[1];
 #pragma unroll
@@ -1126,7 +1161,7 @@ __global__ __launch_bounds__(kTkThreads, 1) void cp_merge_kernel(const uint32_t*
     }
   }
   int packed_total;
-  const int packed = block_excl_scan(na | (nv << 16), sm.wtot, &packed_total);
+  const int packed = block_excl_scan<kTkThreads>(na | (nv << 16), sm.wtot, &packed_total);
   const int n = packed_total & 0xFFFF;
   const int total = packed_total >> 16;
   int pos = packed & 0xFFFF;
@@ -1173,7 +1208,7 @@ __global__ __launch_bounds__(kTkThreads, 1) void cp_merge_kernel(const uint32_t*
   // ---- C: select and ordered write over the candidates ----
   int above = 0;
   const uint32_t thr = select_candidates(sm, n, lo, &above);
-  write_candidates<false>(sm, n, thr, above, out, nullptr);
+  write_candidates<kTkThreads, false>(sm, n, thr, above, out, nullptr);
 }
 }  // namespace
 
@@ -1266,7 +1301,7 @@ extern "C" int hcu_cp_topk_merge(const uint32_t* keys, const int32_t* gidx, int6
   if (n_parts < 1 || n_parts > kMaxParts || rows < 0 || rows > INT32_MAX) return HCU_ERR_ARG;
   if (rows == 0) return HCU_OK;
   if (!keys || !gidx || !lengths || !dst) return HCU_ERR_ARG;
-  const size_t smem = sizeof(TopkSmem);
+  const size_t smem = sizeof(TopkSmem<kTkThreads>);
   cudaFuncSetAttribute(cp_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   cp_merge_kernel<<<static_cast<unsigned>(rows), kTkThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
       keys, gidx, static_cast<int>(n_parts), static_cast<int>(rows), lengths, dst);

@@ -97,27 +97,31 @@ def test_topk_rows_and_empty_batch(hcu, dev):
     assert tuple(out.shape) == (0, 2048)
 
 
-def _adversarial_rows():
+def _adversarial_rows(W):
     """Rows aimed at the candidate path's limits: a sample-derived bound that misses (large
-    values exactly at the sampled positions), candidates clustered at the row end, more than
-    8192 tokens tied at the bound, an all-negative row, a sparse row (threshold +0) and a
-    short mixed-sign row.  Each must still equal the oracle exactly."""
+    values exactly at the sampled 4-token groups), candidates clustered at the row end, more
+    tokens tied at the bound than the candidate list holds (8192 on the 1024-thread kernel,
+    4096 on the 512-thread one used for rows up to 32K tokens), an all-negative row, a sparse
+    row (threshold +0) and a short mixed-sign row.  Each must still equal the oracle exactly."""
     rng = np.random.default_rng(23)
-    W = 65536
     x = rng.random((6, W), dtype=np.float32)
     mask_bits = np.ones((6, W), dtype=bool)
-    lens = np.array([65536, 65536, 40000, 30000, 30000, 5000], dtype=np.int32)
-    stride = np.float32(65536) / np.float32(2048)
-    pos = ((np.arange(2048, dtype=np.float32) + np.float32(0.5)) * stride).astype(np.int64)
-    x[0, pos] = 1000.0 + rng.random(2048, dtype=np.float32)
+    l2 = W * 5 // 8
+    lens = np.array([W, W, l2, W // 2, W // 2, 5000], dtype=np.int32)
+    groups = 512  # 2048 samples in groups of 4 consecutive tokens
+    stride_g = np.float32(W) / np.float32(groups)
+    start = ((np.arange(groups, dtype=np.float32) + np.float32(0.5)) * stride_g).astype(np.int64) & ~3
+    start = np.minimum(start, (W - 4) & ~3)
+    pos = (start[:, None] + np.arange(4)).reshape(-1)
+    x[0, pos] = 1000.0 + rng.random(pos.size, dtype=np.float32)
     x[1] = np.arange(W, dtype=np.float32) + rng.random(W, dtype=np.float32)
-    x[2, :40000] = rng.random(40000, dtype=np.float32) * 0.25
-    x[2, rng.permutation(40000)[:1000]] = 2.0 + rng.random(1000, dtype=np.float32)
-    tied = rng.permutation(40000)
-    tied = tied[~np.isin(tied, np.flatnonzero(x[2] >= 2.0))][:9000]
+    x[2, :l2] = rng.random(l2, dtype=np.float32) * 0.25
+    x[2, rng.permutation(l2)[:1000]] = 2.0 + rng.random(1000, dtype=np.float32)
+    tied = rng.permutation(l2)
+    tied = tied[~np.isin(tied, np.flatnonzero(x[2] >= 2.0))][:9000 if W > 32768 else 5000]
     x[2, tied] = 0.5
     x[3] = -1.0 - rng.random(W, dtype=np.float32)
-    mask_bits[4] = rng.random(W) < 0.05  # ~1500 positives over 30000 tokens
+    mask_bits[4] = rng.random(W) < 0.05  # ~5 % positives: threshold +0 for the shorter rows
     x[5] = rng.standard_normal(W).astype(np.float32)
     x[~mask_bits] = np.nan
     mask = O.pack_mask(mask_bits)
@@ -125,13 +129,14 @@ def _adversarial_rows():
     return torch.from_numpy(x), torch.from_numpy(mask), torch.from_numpy(lens), torch.from_numpy(pt)
 
 
-def test_topk_candidate_bound_edge_cases(hcu, dev):
-    x, mask, lens, pt = _adversarial_rows()
-    assert np.array_equal(O.mask_bits(mask.numpy(), 65536), ~np.isnan(x.numpy()))
+@pytest.mark.parametrize("W", [65536, 32768])
+def test_topk_candidate_bound_edge_cases(hcu, dev, W):
+    x, mask, lens, pt = _adversarial_rows(W)
+    assert np.array_equal(O.mask_bits(mask.numpy(), W), ~np.isnan(x.numpy()))
     ref, rkeys = O.topk_transform(x.numpy(), mask.numpy(), lens.numpy(), pt.numpy(), return_keys=True)
     for name, out in _run_all(hcu, x, mask, lens, pt, dev).items():
         assert np.array_equal(out.cpu().numpy(), ref), name
-    ident = torch.arange(65536, dtype=torch.int32).repeat(6, 1)
+    ident = torch.arange(W, dtype=torch.int32).repeat(6, 1)
     refi = O.topk_transform(x.numpy(), mask.numpy(), lens.numpy(), ident.numpy())
     idx, keys = hcu.topk_keys(x.to(dev), mask.to(dev), lens.to(dev), ident.to(dev))
     idx = idx.cpu().numpy()
