@@ -73,7 +73,7 @@ struct __align__(16) TopkSmem {
   uint32_t cand_key[Tk<kT>::kCandCap];
   int32_t cand_idx[Tk<kT>::kCandCap];
   int32_t cand_pid[Tk<kT>::kCandCap];  // page-table entry of each candidate (async copies)
-  int hb[2][512];  // digit histograms (sample refinement: 256 bins, candidate select: 512)
+  alignas(16) int hb[2][512];  // digit histograms (sample refinement: 256 bins, candidate select: 512); read as int4
   int wcnt[2][Tk<kT>::kWarps];
   uint32_t wmax[Tk<kT>::kWarps];
   int above[Tk<kT>::kWarps];
