@@ -147,9 +147,17 @@ def quant_store_index_k(k: np.ndarray, token_loc: np.ndarray, kv_pages: np.ndarr
 # stage 2: MQA index logits + nonzero mask (+ pass-1 histogram)
 # ---------------------------------------------------------------------------
 
+def _relu(acc: torch.Tensor) -> torch.Tensor:
+    """``fmaxf(acc, 0.0f)`` (``mqa_hist.cu:203``): NaN -> 0."""
+    return torch.where(acc > 0, acc, torch.zeros_like(acc))
+
+
 def _head_sum(acc: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
-    """sum_h relu(acc[h, t]) * w[h] in float32 (``mqa_hist.cu:195-203``)."""
-    return (torch.clamp_min(acc, 0.0) * w[:, None]).sum(0)
+    """sum_h relu(acc[h, t]) * w[h] in float32 (``mqa_hist.cu:195-203``).
+
+    The ReLU is ``fmaxf(acc, 0.0f)`` (``:203``): a NaN dot product (from a NaN
+    fp8 byte in q or k) contributes 0, like any non-positive one."""
+    return (_relu(acc) * w[:, None]).sum(0)
 
 
 def mqa_logits_paged(q: np.ndarray, kv_pages: np.ndarray, weights: np.ndarray,
@@ -201,7 +209,7 @@ def mqa_logits_paged(q: np.ndarray, kv_pages: np.ndarray, weights: np.ndarray,
             logits[b, :L][nz] = sn[nz]
             keep[b, :L] = nz
             if want_floor:
-                fl = (torch.clamp_min(acc, 0.0) * wf[b].abs()[:, None]).sum(0) * ks[:L].abs()
+                fl = (_relu(acc) * wf[b].abs()[:, None]).sum(0) * ks[:L].abs()
                 floor[b, :L] = 1e-2 * fl.numpy()
     return logits, pack_mask(keep), floor
 
@@ -239,7 +247,7 @@ def mqa_logits_ragged(q: np.ndarray, k_fp8: np.ndarray, k_scale: np.ndarray, wei
         seg[nz] = s[nz]
         keep[i, a:e] = nz
         if want_floor:
-            fl = (torch.clamp_min(acc, 0.0) * wf[r].abs()[:, None]).sum(0) * ks[a:e].abs()
+            fl = (_relu(acc) * wf[r].abs()[:, None]).sum(0) * ks[a:e].abs()
             floor[i, a:e] = 1e-2 * fl.numpy()
     return logits, pack_mask(keep), floor
 

@@ -62,6 +62,24 @@ def test_logits_vs_oracle(hcu, dev, case):
     assert res["n_set"] > 0
 
 
+def test_logits_nan_inputs_follow_fmaxf(hcu, dev):
+    """NaN fp8 bytes (e4m3fn 0x7F / 0xFF) in the K pages and in q: the reference's ReLU is fmaxf,
+    so a NaN dot product contributes 0 and every stored logit is finite."""
+    w = _decode(2, 2, [3000, 1500], 64, seed=21)
+    kv = w["kv_cache"].view(w["kv_cache"].shape[0], -1)
+    page = int(w["block_table"][0, 0])
+    kv[page, 5 * 128:6 * 128] = 0x7F       # token 5 of request 0: every byte NaN
+    kv[page, 20 * 128 + 3] = 0xFF          # token 20: one negative-NaN byte
+    qb = w["q"].view(torch.uint8).view(w["q"].shape[0], w["heads"], 128)
+    qb[1, 9, 0] = 0x7F                     # one head of row 1
+    lg, mk, _ = _run(hcu, _device(w, dev))
+    rl, rm, fl = _oracle_logits(w)
+    res = compare_logits(lg.cpu().numpy(), mk.cpu().numpy(), rl, rm, fl)
+    assert res["ok"], res
+    got = lg.cpu().numpy()
+    assert np.isfinite(got[O.mask_bits(mk.cpu().numpy(), got.shape[1])]).all()
+
+
 def test_logits_zero_length_rows_and_padded_table(hcu, dev):
     w = _decode(3, 1, [200, 300, 100], 64, seed=3, width_pages=64)
     w["context_lens"][1] = 0

@@ -54,6 +54,26 @@ def test_ragged_logits_vs_oracle(hcu, dev, case):
     assert res["ok"], res
 
 
+def test_ragged_nan_inputs_follow_fmaxf(hcu, dev):
+    """NaN fp8 bytes (e4m3fn 0x7F / 0xFF) in K and q: the reference's ReLU is fmaxf, so a NaN dot
+    product contributes 0 and every stored logit is finite (the saturating-FMA ReLU flushes NaN
+    to +0)."""
+    w = _ragged(16, 1000, 64, seed=9)
+    kb = w["k_fp8"].view(torch.uint8)
+    kb[5, :] = 0x7F          # a whole NaN token (positive NaN dot products)
+    kb[700, 3] = 0xFF        # one negative-NaN byte
+    kb[1010, 127] = 0x7F
+    qb = w["q"].view(torch.uint8).view(w["q"].shape[0], w["heads"], 128)
+    qb[2, 7, 0] = 0x7F       # one head of one row
+    lg, mk, _ = _run(hcu, w, dev)
+    rl, rm, fl = _oracle(w)
+    assert np.isfinite(np.where(O.mask_bits(rm, rl.shape[1]), rl, 0.0)).all()
+    res = compare_logits(lg.cpu().numpy(), mk.cpu().numpy(), rl, rm, fl)
+    assert res["ok"], res
+    got = lg.cpu().numpy()
+    assert np.isfinite(got[O.mask_bits(mk.cpu().numpy(), got.shape[1])]).all()
+
+
 def test_ragged_arbitrary_ranges(hcu, dev):
     """Non-causal windows: empty ranges, ranges starting mid-tile, ranges past the end."""
     w = _ragged(24, 1500, 64, seed=4)
