@@ -7,17 +7,21 @@
 //     that order and cut into one contiguous range per CTA (balanced to one
 //     tile; Q changes only at group boundaries).  It is derived on the device
 //     from the context lengths, so the launch is CUDA-graph capturable;
-//   * warp 0 (TMA producer): per tile two 3-D TMA box loads {128 B, 64 tok, 1}
-//     of the two 64-token K pages named by the block table (128-byte swizzle,
-//     a K-major UMMA operand), into an 8-stage ring; per group the R*H Q rows
-//     (2-D TMA) into a double buffer;
-//   * warp 1 (MMA issuer): tcgen05.mma.cta_group::1.kind::f8f6f4, M = 128
-//     tokens, N = R*H query heads, K = 128 as 4 x 32, accumulating fp32 in a
-//     double-buffered TMEM accumulator; tcgen05.commit frees the stage and
-//     publishes the accumulator;
-//   * warps 2-5 (epilogue): thread = token = TMEM lane; tcgen05.ld of the row's
+//   * TMA producers (warp 0 and kProducers - 1 more warps, items dealt round
+//     robin): per tile two 3-D TMA box loads {128 B, 64 tok, 1} of the two
+//     64-token K pages named by the block table (128-byte swizzle, a K-major
+//     UMMA operand) and their scale boxes, into an 8-stage ring;
+//   * warp 1 (MMA issuer): loads each row block's R*H Q rows (2-D TMA, two
+//     slots), then tcgen05.mma.cta_group::1.kind::f8f6f4, M = 128 tokens,
+//     N = R*H query heads, K = 128 as 4 x 32, accumulating fp32 in 4 TMEM
+//     buffers (2 when N > 128); tcgen05.commit frees the stage and publishes
+//     the accumulator;
+//   * epilogue (kTeams teams of 4 warps, one per TMEM lane quadrant, taking
+//     tiles round robin): thread = token = TMEM lane; tcgen05.ld of the row's
 //     H columns, ReLU * w head sum in registers, * k_scale, mask bit via warp
-//     ballot, logits stored only where the bit is set.
+//     ballot, logits stored only where the bit is set; with hist_lens the
+//     same epilogue does pass 1 of the top-k (key[31:20] bins, +0 and
+//     positive counts) with global atomics into the workspace (kHist).
 // Semantics follow hcu_ops/csrc/mqa_hist.cu:97-273 of the reference: lengths
 // clamped to [0, width], every row of a group reads the group's first block
 // table row, mask bit = token < len && bits(s) != 0.
@@ -34,8 +38,7 @@
 HCU_DEFINE_STATUS(status_logits)
 
 namespace hcu {
-int launch_pass1_hist(const float* logits, int64_t rows, int64_t width, const int16_t* mask, int64_t mask_stride,
-                      const int32_t* hist_lens, int32_t* zws, cudaStream_t stream);
+int launch_hist_init(int32_t* zws, const int32_t* hist_lens, int64_t rows, int64_t width, cudaStream_t stream);
 
 namespace {
 
@@ -63,6 +66,7 @@ struct __align__(1024) LgSmem {
   float sc[kStagesNarrow][2 * kPage];  // k_scale of the stage's two pages
   float w[kEpiWarps][kMaxN];       // head weights, one copy per epilogue warp
   int lens[kEpiWarps][8];          // row lengths of the current row block, per epilogue warp
+  int hlen[kEpiWarps][8];          // histogram lengths of the current row block (0: no histogram)
   float* lrow[kEpiWarps][8];       // logits rows of the current row block
   uint32_t* mrow[kEpiWarps][8];    // mask rows (as 32-bit words) of the current row block
   int bq_ph[kProducers][2][32];    // producer batch (per producer warp): page ids of each item's two pages (-1: none)
@@ -94,6 +98,8 @@ struct PagedArgs {
   int64_t bt_stride;
   float* logits;
   int16_t* mask;
+  const int32_t* hist_lens;  // fused pass-1 histogram: rows' histogram lengths, or null
+  int32_t* zws;              // its workspace [ghist1 batch*4096 | ghist2 batch*4096 | cnt batch*2]
   int batch;
   int G;       // rows per request group (share the first row's block table)
   int R;       // rows per CTA row block (R * H <= 256)
@@ -155,7 +161,28 @@ struct Ring {
   }
 };
 
-template <int H>
+// Fused pass 1 (mqa_hist.cu:219-226,239-272 of the reference): a token whose
+// mask bit is set and that lies below the row's histogram length adds 1 to its
+// key[31:20] bin and moves one count out of the +0 bin, where the init kernel
+// put the whole length; positives are counted too.  One warp-row per call
+// (every lane calls it).
+__device__ __forceinline__ void pass1_count(const PagedArgs& p, int row, float s0, bool cnt) {
+  int32_t* g1 = p.zws + static_cast<int64_t>(row) * kBins;
+  const uint32_t key = to_key(s0);
+  if (cnt) atomicAdd(g1 + (key >> 20), 1);
+  const int nz = __popc(__ballot_sync(0xffffffffu, cnt));
+  const int pos = __popc(__ballot_sync(0xffffffffu, cnt && key > kZeroKey));
+  if ((threadIdx.x & 31) == 0 && nz) {
+    int32_t* c = p.zws + 2 * static_cast<int64_t>(p.batch) * kBins + 2 * static_cast<int64_t>(row);
+    atomicSub(g1 + kZeroBin, nz);
+    atomicSub(c + 1, nz);
+    if (pos) atomicAdd(c, pos);
+  }
+}
+
+// kHist: the fused pass-1 histogram (p.zws set); a separate instance so the
+// common path's epilogue is compiled without it.
+template <int H, bool kHist>
 __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_paged_kernel(const __grid_constant__ CUtensorMap tm_kv,
                                                                         const __grid_constant__ CUtensorMap tm_sc,
                                                                         const __grid_constant__ CUtensorMap tm_q,
@@ -434,6 +461,10 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_paged_kernel(const _
           wsm[i] = __ldg(p.weights + static_cast<int64_t>(row0) * H + i) * kReluScale;  // pre-scaled for relu_fma2
         if (lane < nr) {
           lsm[lane] = clamp_len(__ldg(p.ctx_lens + row0 + lane), p.width);
+          if constexpr (kHist) {
+            const int hl = clamp_len(__ldg(p.hist_lens + row0 + lane), p.width);
+            sm.hlen[ew][lane] = hl > kTopK ? hl : 0;  // rows of at most kTopK tokens need no histogram
+          }
           sm.lrow[ew][lane] = p.logits + static_cast<int64_t>(row0 + lane) * p.width;
           sm.mrow[ew][lane] = reinterpret_cast<uint32_t*>(p.mask) + static_cast<int64_t>(row0 + lane) * (p.width / 32);
         }
@@ -497,6 +528,10 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_paged_kernel(const _
         const uint32_t bits = __ballot_sync(0xffffffffu, keep);
         st_u32_if(sm.mrow[ew][r] + (tok_base >> 5), bits, lane == 0 && tok_base < p.width);
         st_f32_if(sm.lrow[ew][r] + token, s0, keep);
+        if constexpr (kHist) {
+          const int hl = sm.hlen[ew][r];
+          if (hl) pass1_count(p, row0 + r, s0, keep && token < hl);
+        }
       }
       tc_fence_before();
       __syncwarp();
@@ -907,14 +942,20 @@ int map_error(const char* what) {
   return HCU_ERR_LAUNCH;
 }
 
+template <int H, bool kHist>
+int launch_paged_t(const CUtensorMap& tkv, const CUtensorMap& tsc, const CUtensorMap& tq, const PagedArgs& a,
+                   cudaStream_t stream) {
+  const size_t smem = sizeof(LgSmem) + 1024;
+  cudaFuncSetAttribute(mqa_logits_paged_kernel<H, kHist>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       static_cast<int>(smem));
+  mqa_logits_paged_kernel<H, kHist><<<sm_count(), kLgThreads, smem, stream>>>(tkv, tsc, tq, a);
+  return launch_status();
+}
+
 template <int H>
 int launch_paged(const CUtensorMap& tkv, const CUtensorMap& tsc, const CUtensorMap& tq, const PagedArgs& a,
                  cudaStream_t stream) {
-  const size_t smem = sizeof(LgSmem) + 1024;
-  cudaFuncSetAttribute(mqa_logits_paged_kernel<H>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       static_cast<int>(smem));
-  mqa_logits_paged_kernel<H><<<sm_count(), kLgThreads, smem, stream>>>(tkv, tsc, tq, a);
-  return launch_status();
+  return a.zws ? launch_paged_t<H, true>(tkv, tsc, tq, a, stream) : launch_paged_t<H, false>(tkv, tsc, tq, a, stream);
 }
 
 }  // namespace
@@ -962,14 +1003,17 @@ extern "C" int hcu_mqa_logits_hist(const uint8_t* q, int64_t batch, int64_t head
   a.bt_stride = bt_stride;
   a.logits = logits;
   a.mask = mask;
+  a.hist_lens = hist_lens;
+  a.zws = hist_lens ? zws : nullptr;
   a.batch = static_cast<int>(batch);
   a.G = static_cast<int>(group_size);
   a.R = static_cast<int>(R);
   a.width = static_cast<int>(max_context_len);
-  int stt = heads == 64 ? launch_paged<64>(tkv, tsc, tq, a, st) : launch_paged<32>(tkv, tsc, tq, a, st);
-  if (stt != HCU_OK) return stt;
-  if (hist_lens) return launch_pass1_hist(logits, batch, max_context_len, mask, mask_words, hist_lens, zws, st);
-  return HCU_OK;
+  if (hist_lens) {  // the workspace's bins and counts, filled by the kernel's epilogue
+    const int hs = launch_hist_init(zws, hist_lens, batch, max_context_len, st);
+    if (hs != HCU_OK) return hs;
+  }
+  return heads == 64 ? launch_paged<64>(tkv, tsc, tq, a, st) : launch_paged<32>(tkv, tsc, tq, a, st);
 }
 
 extern "C" int hcu_mqa_logits_ragged(const uint8_t* q, int64_t rows, int64_t heads, const uint8_t* k_fp8,

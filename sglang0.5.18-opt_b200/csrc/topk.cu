@@ -49,7 +49,6 @@ constexpr int kNarrowWidth = 32768; // rows up to this width run the 512-thread 
 // narrow ones, so that two CTAs per SM overlap their rows' latency-bound phases.
 template <int kT>
 struct Tk {
-  static constexpr int kThreads = kT;
   static constexpr int kWarps = kT / 32;
   static constexpr int kRound = kT * kLaneTok;               // tokens per streaming round
   static constexpr int kCandCap = kT >= 1024 ? 8192 : 4096;  // candidate list capacity
@@ -1024,7 +1023,6 @@ int launch_rows(const float* score, int64_t rows, int64_t width, int64_t score_s
 // ---------------------------------------------------------------------------
 constexpr int kMaxParts = 16;
 constexpr int kTkThreads = 1024;  // one CTA per row
-constexpr int kTkWarps = kTkThreads / 32;
 constexpr int kCandCap = Tk<kTkThreads>::kCandCap;
 
 __device__ __forceinline__ int64_t merge_off(int c, int rows, int row) {
@@ -1212,15 +1210,13 @@ __global__ __launch_bounds__(kTkThreads, 1) void cp_merge_kernel(const uint32_t*
 }
 }  // namespace
 
-// Used by the logits translation unit for the hist_lens path.
-int launch_pass1_hist(const float* logits, int64_t rows, int64_t width, const int16_t* mask, int64_t mask_stride,
-                      const int32_t* hist_lens, int32_t* zws, cudaStream_t stream) {
+// Used by the logits translation unit for the hist_lens path: zeroes the
+// pass-1 workspace and preloads each row's +0 bin and zero count with its
+// histogram length; the logits kernel's epilogue then does pass 1.
+int launch_hist_init(int32_t* zws, const int32_t* hist_lens, int64_t rows, int64_t width, cudaStream_t stream) {
   if (rows == 0) return HCU_OK;
   hist_init_kernel<<<static_cast<int>(rows), 256, 0, stream>>>(zws, hist_lens, static_cast<int>(width),
                                                               static_cast<int>(rows));
-  const dim3 grid(static_cast<unsigned>((width + kHistChunk - 1) / kHistChunk), static_cast<unsigned>(rows));
-  pass1_hist_kernel<<<grid, kHistThreads, 0, stream>>>(logits, width, static_cast<int>(width), mask, mask_stride,
-                                                      hist_lens, zws, static_cast<int>(rows));
   return launch_status();
 }
 
