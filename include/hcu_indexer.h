@@ -171,7 +171,10 @@ int hcu_sparse_mask_topk_transform(const float* score, int64_t rows, int64_t wid
                                    int32_t* dst, hcu_stream_t stream);
 
 /* Same result; a row is spread over up to max_splits CTAs when rows are few
- * (replaces _C.sparse_mask_topk_transform_split, sparse_mask_topk.cu:910-981). */
+ * (replaces _C.sparse_mask_topk_transform_split, sparse_mask_topk.cu:910-981):
+ * min(ceil(width / 8192), SMs / rows, max_splits, 8) CTAs per row, launched as
+ * one thread-block cluster per row, each taking at least 8192 of the row's
+ * visible tokens.  The workspace is not used (hcu_topk_workspace_bytes = 0). */
 int hcu_sparse_mask_topk_transform_split(const float* score, int64_t rows, int64_t width,
                                          int64_t score_stride, const int16_t* mask, int64_t mask_stride,
                                          const int32_t* lengths, const int32_t* page_table,

@@ -28,6 +28,8 @@
 // Unset mask bits are an implicit +0 (key 0x80000000) whatever the score
 // storage holds.  The selection and output order are those of
 // hcu_ops/csrc/sparse_mask_topk.cu:1-7,141-349 of the reference.
+#include <cooperative_groups.h>
+
 #include <mutex>
 #include <vector>
 
@@ -44,6 +46,8 @@ constexpr int kSmallSample = 2048;  // row samples used to bound the threshold (
 constexpr int kSample = 8192;       // sample count for rows > 512K
 constexpr int kLaneTok = 16;        // consecutive tokens per lane in a streaming round
 constexpr int kNarrowWidth = 32768; // rows up to this width run the 512-thread kernel (two CTAs per SM)
+constexpr int kMaxClusterSplits = 8;  // CTAs per row of a split row (portable cluster size)
+constexpr int kSplitMinTok = 8192;    // a split row gives each CTA at least this many visible tokens
 
 // Per-CTA-size constants: 1024 threads (one CTA per SM) for wide rows, 512 threads for
 // narrow ones, so that two CTAs per SM overlap their rows' latency-bound phases.
@@ -81,6 +85,7 @@ struct __align__(16) TopkSmem {
   int pos[Tk<kT>::kWarps];
   int wtot[32];
   int res[4];
+  int ncand;  // split rows: this CTA's candidate count (read by the cluster's rank 0)
 };
 static_assert(sizeof(TopkOutStage) <= sizeof(uint4) * 4 * 512, "fallback staging fits the scratch area");
 
@@ -313,13 +318,14 @@ __device__ __forceinline__ uint32_t load16_raw(const float* __restrict__ vals, c
 // appended at their block-wide prefix position, visiting set bits only.
 template <int kT, bool kVec, bool kPos>
 __device__ __forceinline__ void candidate_round(const float* __restrict__ vals, const int16_t* __restrict__ mrow,
-                                                const int32_t* __restrict__ src, int len, uint32_t lo, int r, int nr,
+                                                const int32_t* __restrict__ src, int seg0, int len, uint32_t lo, int r,
+                                                int nr,
                                                 TopkSmem<kT>& sm,
                                                 uint32_t (&X)[16], uint32_t& mX, uint32_t& vX, int& base,
                                                 uint32_t& kmax) {
   const int lane = threadIdx.x & 31;
   const int w = threadIdx.x >> 5;
-  const int i0 = r * Tk<kT>::kRound + w * (32 * kLaneTok) + lane * kLaneTok;
+  const int i0 = seg0 + r * Tk<kT>::kRound + w * (32 * kLaneTok) + lane * kLaneTok;
   const int lim_pos = static_cast<int>(lo ^ kZeroKey);
   uint32_t cb = 0u;
 #pragma unroll
@@ -370,10 +376,11 @@ __device__ __forceinline__ void candidate_round(const float* __restrict__ vals, 
   base += rtot;
 }
 
-// Candidate pass: appends every token of [0, len) whose key is >= lo to
+// Candidate pass: appends every token of [seg0, len) whose key is >= lo to
 // sm.cand_key / sm.cand_idx in token order, in block-wide rounds of kRound
 // tokens (warp w takes tokens [w*512, w*512+512) of a round, lane l 16 of
-// them).  A / mA / vA hold round 0's loads on entry; two rounds of loads are
+// them; rounds start at seg0, a multiple of 16).  A / mA / vA hold round 0's
+// loads on entry; two rounds of loads are
 // in flight at every barrier.  kPos (lo > +0): a token is a candidate iff its
 // mask bit is set and its float bits, as a signed integer, are >=
 // lo ^ 0x80000000.  Returns the candidate count (nothing past kCandCap is
@@ -382,19 +389,20 @@ __device__ __forceinline__ void candidate_round(const float* __restrict__ vals, 
 // asynchronously (waited for in write_candidates).
 template <int kT, bool kVec, bool kPos>
 __device__ __forceinline__ int collect_candidates(const float* __restrict__ vals, const int16_t* __restrict__ mrow,
-                                                  const int32_t* __restrict__ src, int len, uint32_t lo, TopkSmem<kT>& sm,
-                                                  uint32_t (&A)[16],
-                                                  uint32_t mA, uint32_t vA) {
+                                                  const int32_t* __restrict__ src, int seg0, int len, uint32_t lo,
+                                                  TopkSmem<kT>& sm, uint32_t (&A)[16], uint32_t mA, uint32_t vA) {
   const int lane = threadIdx.x & 31;
   const int w = threadIdx.x >> 5;
-  const int nr = (len + Tk<kT>::kRound - 1) / Tk<kT>::kRound;
+  const int nr = (len - seg0 + Tk<kT>::kRound - 1) / Tk<kT>::kRound;
   uint32_t B[16], mB = 0u, vB = 0u;
-  if (nr > 1) mB = load16_raw<kVec>(vals, mrow, Tk<kT>::kRound + w * (32 * kLaneTok) + lane * kLaneTok, len, B, vB);
+  if (nr > 1)
+    mB = load16_raw<kVec>(vals, mrow, seg0 + Tk<kT>::kRound + w * (32 * kLaneTok) + lane * kLaneTok, len, B, vB);
   int base = 0;
   uint32_t kmax = 0u;
   for (int r = 0; r < nr; r += 2) {
-    candidate_round<kT, kVec, kPos>(vals, mrow, src, len, lo, r, nr, sm, A, mA, vA, base, kmax);
-    if (r + 1 < nr) candidate_round<kT, kVec, kPos>(vals, mrow, src, len, lo, r + 1, nr, sm, B, mB, vB, base, kmax);
+    candidate_round<kT, kVec, kPos>(vals, mrow, src, seg0, len, lo, r, nr, sm, A, mA, vA, base, kmax);
+    if (r + 1 < nr)
+      candidate_round<kT, kVec, kPos>(vals, mrow, src, seg0, len, lo, r + 1, nr, sm, B, mB, vB, base, kmax);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
@@ -488,6 +496,44 @@ __device__ __forceinline__ void write_candidates(TopkSmem<kT>& sm, int n, uint32
   }
 }
 
+// Cluster gather of a split row, called by every CTA of the cluster after its
+// candidate pass (sm.ncand = its count, sm.wmax its warps' maxima).  Rank 0
+// appends the lists of ranks 1.. after its own (rank order = token order) by
+// distributed shared-memory loads and folds their warp maxima into sm.wmax;
+// the second cluster barrier keeps every CTA resident until rank 0 has read
+// its list.  Returns the total candidate count on rank 0 (past kCandCap when
+// any list or the union overflows), 0 elsewhere.
+template <int kT>
+__device__ __noinline__ int split_gather(TopkSmem<kT>& sm, int splits, int rank) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  cluster.sync();
+  int n = 0;
+  if (rank == 0) {
+    n = sm.ncand;
+    bool over = n > Tk<kT>::kCandCap;
+    for (int r = 1; r < splits; ++r) {
+      TopkSmem<kT>* rs = cluster.map_shared_rank(&sm, r);
+      const int nr = rs->ncand;
+      if (nr > Tk<kT>::kCandCap || n + nr > Tk<kT>::kCandCap) over = true;
+      if (!over)
+        for (int i = threadIdx.x; i < nr; i += kT) {
+          sm.cand_key[n + i] = rs->cand_key[i];
+          sm.cand_idx[n + i] = rs->cand_idx[i];
+          sm.cand_pid[n + i] = rs->cand_pid[i];
+        }
+      if (threadIdx.x < kT / 32) {
+        const uint32_t m = rs->wmax[threadIdx.x];
+        if (m > sm.wmax[threadIdx.x]) sm.wmax[threadIdx.x] = m;
+      }
+      n += nr;
+    }
+    if (over) n = Tk<kT>::kCandCap + 1;
+  }
+  cluster.sync();
+  return n;
+}
+
 // Visits every token slot of this warp's segment as (valid, key, index i0+j);
 // lane l takes tokens c + 4l .. c + 4l + 3 of each 128-token step (fallback passes).
 #define TK_FOR_EACH(BODY)                                                             \
@@ -508,18 +554,24 @@ __device__ __forceinline__ void write_candidates(TopkSmem<kT>& sm, int n, uint32
     }                                                                                 \
   }
 
-template <int kT, bool kVec, bool kSorted>
+// kSplit: the row is split over a cluster of `splits` CTAs (blockIdx.x = row *
+// splits + rank): each derives the same bound lo over the whole row and
+// collects the candidates of its own token range; rank 0 gathers the lists
+// from the other CTAs' shared memory (rank order = token order) and selects.
+template <int kT, bool kVec, bool kSorted, bool kSplit>
 __global__ __launch_bounds__(kT, 1024 / kT) void topk_row_kernel(
     const float* __restrict__ score, int64_t score_stride, int width, const int16_t* __restrict__ mask,
     int64_t mask_stride, const int32_t* __restrict__ lengths, const int32_t* __restrict__ pt, int64_t pt_stride,
-    int32_t* __restrict__ dst, uint32_t* __restrict__ dst_keys, const int32_t* __restrict__ pre_ws, int rows) {
+    int32_t* __restrict__ dst, uint32_t* __restrict__ dst_keys, const int32_t* __restrict__ pre_ws, int rows,
+    int splits) {
   constexpr int kTkThreads = kT;
   constexpr int kTkWarps = kT / 32;
   constexpr int kCandCap = Tk<kT>::kCandCap;
   constexpr int kHistTrash = Tk<kT>::kHistTrash;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   TopkSmem<kT>& sm = *reinterpret_cast<TopkSmem<kT>*>(smem_raw);
-  const int row = blockIdx.x;
+  const int row = kSplit ? static_cast<int>(blockIdx.x) / splits : static_cast<int>(blockIdx.x);
+  const int rank = kSplit ? static_cast<int>(blockIdx.x) % splits : 0;
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int w = tid >> 5;
@@ -531,7 +583,16 @@ __global__ __launch_bounds__(kT, 1024 / kT) void topk_row_kernel(
   const float* vals = score + static_cast<int64_t>(row) * score_stride;
   const int16_t* mrow = mask + static_cast<int64_t>(row) * mask_stride;
 
+  // split rows: CTAs that share the row (at most one per kSplitMinTok visible tokens); with one,
+  // rank 0 runs the plain single-CTA path and the others leave at once
+  int s_eff = 1;
+  if constexpr (kSplit) {
+    s_eff = min(splits, max(1, len / kSplitMinTok));
+    if (s_eff == 1 && rank != 0) return;
+  }
+
   if (len <= kTopK) {
+    if (rank != 0) return;
     for (int i = tid; i < kTopK; i += kTkThreads) {
       out[i] = i < len ? src[i] : -1;
       if (dst_keys) {
@@ -550,6 +611,10 @@ __global__ __launch_bounds__(kT, 1024 / kT) void topk_row_kernel(
   const int seg_begin = min(w * seg, len);
   const int seg_end = min(seg_begin + seg, len);
   const int trash = kBins + lane;
+  // this CTA's token range of the candidate pass (the whole row unless split)
+  const int cseg = s_eff > 1 ? (len + s_eff * 512 - 1) / (s_eff * 512) * 512 : len;
+  const int cs0 = min(rank * cseg, len);
+  const int cs1 = min(cs0 + cseg, len);
 
   uint32_t thr = 0;
   int remaining = 0;
@@ -588,7 +653,7 @@ __global__ __launch_bounds__(kT, 1024 / kT) void topk_row_kernel(
       }
     }
     uint32_t b0[16], valid0;
-    const uint32_t mw0 = load16_raw<kVec>(vals, mrow, w * (32 * kLaneTok) + lane * kLaneTok, len, b0, valid0);
+    const uint32_t mw0 = load16_raw<kVec>(vals, mrow, cs0 + w * (32 * kLaneTok) + lane * kLaneTok, cs1, b0, valid0);
     for (int i = tid; i < 2 * 512; i += kTkThreads) (&sm.hb[0][0])[i] = 0;
     uint32_t lo = 0u;
     bool try_cand = false;
@@ -636,9 +701,29 @@ __global__ __launch_bounds__(kT, 1024 / kT) void topk_row_kernel(
         try_cand = sm.res[1] + h1[b1] <= kCandCap;
       }
     }
+    if (kSplit && s_eff > 1) {
+      // every CTA of the cluster reaches both cluster barriers (s_eff and try_cand are the same for all of them)
+      int n = 0;
+      if (try_cand) {
+        const int nl = lo > kZeroKey ? collect_candidates<kT, kVec, true>(vals, mrow, src, cs0, cs1, lo, sm, b0, mw0, valid0)
+                                     : collect_candidates<kT, kVec, false>(vals, mrow, src, cs0, cs1, lo, sm, b0, mw0, valid0);
+        cp_async_wait_all();  // this CTA's page ids are in its shared memory before the gather
+        if (tid == 0) sm.ncand = nl;
+        n = split_gather(sm, splits, rank);
+      }
+      if (rank != 0) return;
+      if (try_cand && n >= kTopK && n <= kCandCap) {
+        int above = 0;
+        thr = select_candidates(sm, n, lo, &above);
+        write_candidates<kT, kSorted>(sm, n, thr, above, out,
+                                      dst_keys ? dst_keys + static_cast<int64_t>(row) * kTopK : nullptr);
+        return;
+      }
+      try_cand = false;  // rank 0 alone runs the radix passes over the whole row
+    }
     if (try_cand) {
-      const int n = lo > kZeroKey ? collect_candidates<kT, kVec, true>(vals, mrow, src, len, lo, sm, b0, mw0, valid0)
-                                  : collect_candidates<kT, kVec, false>(vals, mrow, src, len, lo, sm, b0, mw0, valid0);
+      const int n = lo > kZeroKey ? collect_candidates<kT, kVec, true>(vals, mrow, src, 0, len, lo, sm, b0, mw0, valid0)
+                                  : collect_candidates<kT, kVec, false>(vals, mrow, src, 0, len, lo, sm, b0, mw0, valid0);
       if (n < kTopK || n > kCandCap) cp_async_wait_all();  // no copy outlives the candidate path
       if (n >= kTopK && n <= kCandCap) {
         int above = 0;
@@ -956,48 +1041,129 @@ int check_common(const float* score, int64_t rows, int64_t width, int64_t score_
   return HCU_OK;
 }
 
+template <int kT, bool kVec>
+void launch_split(const float* score, int rows, int width, int64_t score_stride, const int16_t* mask,
+                  int64_t mask_stride, const int32_t* lengths, const int32_t* pt, int64_t pt_stride, int32_t* dst,
+                  const int32_t* pre_ws, cudaStream_t stream, int splits);
+
 template <int kT, bool kVec, bool kSorted>
 void launch_rows_t(const float* score, int rows, int width, int64_t score_stride, const int16_t* mask,
                    int64_t mask_stride, const int32_t* lengths, const int32_t* pt, int64_t pt_stride, int32_t* dst,
-                   uint32_t* dst_keys, const int32_t* pre_ws, cudaStream_t stream) {
+                   uint32_t* dst_keys, const int32_t* pre_ws, cudaStream_t stream, int splits) {
   const size_t smem = sizeof(TopkSmem<kT>);
-  cudaFuncSetAttribute(topk_row_kernel<kT, kVec, kSorted>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       static_cast<int>(smem));
-  topk_row_kernel<kT, kVec, kSorted><<<rows, kT, smem, stream>>>(score, score_stride, width, mask, mask_stride,
-                                                                lengths, pt, pt_stride, dst, dst_keys, pre_ws, rows);
+  if (kSorted || splits <= 1) {
+    cudaFuncSetAttribute(topk_row_kernel<kT, kVec, kSorted, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(smem));
+    topk_row_kernel<kT, kVec, kSorted, false><<<rows, kT, smem, stream>>>(
+        score, score_stride, width, mask, mask_stride, lengths, pt, pt_stride, dst, dst_keys, pre_ws, rows, 1);
+    return;
+  }
+  if constexpr (!kSorted) launch_split<kT, kVec>(score, rows, width, score_stride, mask, mask_stride, lengths, pt,
+                                                 pt_stride, dst, pre_ws, stream, splits);
+}
+
+// One cluster of `splits` CTAs per row (splits <= kMaxClusterSplits).
+template <int kT, bool kVec>
+void launch_split(const float* score, int rows, int width, int64_t score_stride, const int16_t* mask,
+                  int64_t mask_stride, const int32_t* lengths, const int32_t* pt, int64_t pt_stride, int32_t* dst,
+                  const int32_t* pre_ws, cudaStream_t stream, int splits) {
+  const size_t smem = sizeof(TopkSmem<kT>);
+  uint32_t* dst_keys = nullptr;
+  auto kern = topk_row_kernel<kT, kVec, false, true>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  // clusters of this size must fit the device (one query per size and device), else fewer CTAs per row
+  static std::mutex mu;
+  static std::vector<int> fits;  // [device * (kMaxClusterSplits + 1) + splits]: -1 unknown, 0 no, 1 yes
+  int dev = 0;
+  cudaGetDevice(&dev);
+  for (; splits > 1; splits /= 2) {
+    std::lock_guard<std::mutex> lk(mu);
+    const size_t k = static_cast<size_t>(dev) * (kMaxClusterSplits + 1) + splits;
+    if (fits.size() <= k) fits.resize(k + 1, -1);
+    if (fits[k] < 0) {
+      cudaLaunchConfig_t q = {};
+      q.gridDim = dim3(static_cast<unsigned>(splits));
+      q.blockDim = dim3(kT);
+      q.dynamicSmemBytes = smem;
+      cudaLaunchAttribute qa[1];
+      qa[0].id = cudaLaunchAttributeClusterDimension;
+      qa[0].val.clusterDim.x = static_cast<unsigned>(splits);
+      qa[0].val.clusterDim.y = 1;
+      qa[0].val.clusterDim.z = 1;
+      q.attrs = qa;
+      q.numAttrs = 1;
+      int n = 0;
+      fits[k] = cudaOccupancyMaxActiveClusters(&n, kern, &q) == cudaSuccess && n > 0 ? 1 : 0;
+      cudaGetLastError();  // a refused query is not a launch error
+    }
+    if (fits[k]) break;
+  }
+  if (splits <= 1) {
+    launch_rows_t<kT, kVec, false>(score, rows, width, score_stride, mask, mask_stride, lengths, pt, pt_stride, dst,
+                                   nullptr, pre_ws, stream, 1);
+    return;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(rows * splits));
+  cfg.blockDim = dim3(kT);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(splits);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kern, score, score_stride, width, mask, mask_stride, lengths, pt, pt_stride, dst, dst_keys,
+                     pre_ws, rows, splits);
 }
 
 template <int kT>
 void launch_rows_sized(const float* score, int r, int w, int64_t score_stride, const int16_t* mask,
                        int64_t mask_stride, const int32_t* lengths, const int32_t* pt, int64_t pt_stride, int32_t* dst,
-                       uint32_t* dst_keys, const int32_t* pre_ws, cudaStream_t stream, bool vec, bool sorted) {
+                       uint32_t* dst_keys, const int32_t* pre_ws, cudaStream_t stream, bool vec, bool sorted,
+                       int splits) {
   if (vec && !sorted)
     launch_rows_t<kT, true, false>(score, r, w, score_stride, mask, mask_stride, lengths, pt, pt_stride, dst, dst_keys,
-                                   pre_ws, stream);
+                                   pre_ws, stream, splits);
   else if (vec)
     launch_rows_t<kT, true, true>(score, r, w, score_stride, mask, mask_stride, lengths, pt, pt_stride, dst, dst_keys,
-                                  pre_ws, stream);
+                                  pre_ws, stream, splits);
   else if (!sorted)
     launch_rows_t<kT, false, false>(score, r, w, score_stride, mask, mask_stride, lengths, pt, pt_stride, dst,
-                                    dst_keys, pre_ws, stream);
+                                    dst_keys, pre_ws, stream, splits);
   else
     launch_rows_t<kT, false, true>(score, r, w, score_stride, mask, mask_stride, lengths, pt, pt_stride, dst, dst_keys,
-                                   pre_ws, stream);
+                                   pre_ws, stream, splits);
 }
 
 int launch_rows(const float* score, int64_t rows, int64_t width, int64_t score_stride, const int16_t* mask,
                 int64_t mask_stride, const int32_t* lengths, const int32_t* pt, int64_t pt_stride, int32_t* dst,
-                uint32_t* dst_keys, const int32_t* pre_ws, cudaStream_t stream, bool sorted = false) {
+                uint32_t* dst_keys, const int32_t* pre_ws, cudaStream_t stream, bool sorted = false, int splits = 1) {
   const int w = static_cast<int>(width);
   const int r = static_cast<int>(rows);
   const bool vec = use_vec(score, width, score_stride);
-  if (width <= kNarrowWidth)  // narrow rows: 512 threads, two CTAs per SM
+  // narrow rows (or row parts): 512 threads, two CTAs per SM
+  if ((width + splits - 1) / splits <= kNarrowWidth)
     launch_rows_sized<512>(score, r, w, score_stride, mask, mask_stride, lengths, pt, pt_stride, dst, dst_keys, pre_ws,
-                           stream, vec, sorted);
+                           stream, vec, sorted, splits);
   else
     launch_rows_sized<1024>(score, r, w, score_stride, mask, mask_stride, lengths, pt, pt_stride, dst, dst_keys,
-                            pre_ws, stream, vec, sorted);
+                            pre_ws, stream, vec, sorted, splits);
   return launch_status();
+}
+
+// CTAs per row of the split entry points: the reference's heuristic
+// (hcu_ops/__init__.py:52-57, sparse_mask_topk.cu:925-933) -- one per 8192 of
+// width, no more than the SMs per row, at most max_splits -- capped at the
+// portable cluster size.
+int split_count(int64_t rows, int64_t width, int64_t max_splits) {
+  int64_t s = std::max<int64_t>((width + 8191) / 8192, 1);
+  s = std::min<int64_t>(s, sm_count() / std::max<int64_t>(rows, 1));
+  s = std::min<int64_t>(s, std::min<int64_t>(max_splits, 64));
+  s = std::min<int64_t>(s, kMaxClusterSplits);
+  return static_cast<int>(std::max<int64_t>(s, 1));
 }
 
 // ---------------------------------------------------------------------------
@@ -1257,7 +1423,8 @@ extern "C" int hcu_sparse_mask_topk_transform_split(const float* score, int64_t 
                         dst);
   if (st != HCU_OK || rows == 0) return st;
   return launch_rows(score, rows, width, score_stride, mask, mask_stride, lengths, page_table, pt_stride, dst,
-                     nullptr, nullptr, reinterpret_cast<cudaStream_t>(stream));
+                     nullptr, nullptr, reinterpret_cast<cudaStream_t>(stream), false,
+                     split_count(rows, width, max_splits));
 }
 
 extern "C" int hcu_sparse_mask_topk_transform_split_pre(const float* score, int64_t rows, int64_t width,
@@ -1275,7 +1442,7 @@ extern "C" int hcu_sparse_mask_topk_transform_split_pre(const float* score, int6
                         dst);
   if (st != HCU_OK || rows == 0) return st;
   return launch_rows(score, rows, width, score_stride, mask, mask_stride, lengths, page_table, pt_stride, dst,
-                     nullptr, zws, reinterpret_cast<cudaStream_t>(stream));
+                     nullptr, zws, reinterpret_cast<cudaStream_t>(stream), false, split_count(rows, width, max_splits));
 }
 
 extern "C" int hcu_topk_keys(const float* score, int64_t rows, int64_t width, int64_t score_stride,

@@ -57,6 +57,19 @@ def test_topk_production_width(hcu, dev, L, dist):
         assert np.array_equal(out.cpu().numpy(), ref), name
 
 
+@pytest.mark.parametrize("dist", ["relu_sum", "ties", "sparse2"])
+def test_topk_split_rows_mixed_lengths(hcu, dev, dist):
+    """One cluster launch (6 rows of width 131136: 8 CTAs per row) whose rows take every path:
+    at most 2048 tokens, one CTA's worth (< 2 x 8192 visible tokens: rank 0 alone), and 4, 6
+    and 8 CTAs gathering their candidate lists through distributed shared memory."""
+    W = 131072 + 64
+    x, mask, lens, pt = make_scores(6, 131072, dist, W=W, ragged=False, seed=23)
+    lens = torch.tensor([100, 2048, 12000, 32768, 50000, 131072], dtype=torch.int32)
+    ref = O.topk_transform(x.numpy(), mask.numpy(), lens.numpy(), pt.numpy())
+    for name, out in _run_all(hcu, x, mask, lens, pt, dev).items():
+        assert np.array_equal(out.cpu().numpy(), ref), (name, dist)
+
+
 def test_topk_split_pre_uses_pass1_workspace(hcu, dev):
     x, mask, lens, pt = make_scores(6, 20000, "relu_sum", W=20480, ragged=True, seed=9)
     lens[2] = 1500
