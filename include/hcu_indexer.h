@@ -236,6 +236,39 @@ int hcu_topk_keys(const float* score, int64_t rows, int64_t width, int64_t score
 int hcu_cp_topk_merge(const uint32_t* keys, const int32_t* gidx, int64_t n_parts, int64_t rows,
                       const int32_t* lengths, int32_t* dst, hcu_stream_t stream);
 
+/* Context-parallel bounded exchange (no counterpart in the reference, whose CP8
+ * splits the queries instead; see hcu_ops/cp.py).  Three steps per rank:
+ *
+ * hcu_cp_local_bound: per row an order-preserving int32 (key ^ 0x80000000) of a
+ * sampled estimate of the row's global top-2048 threshold on this rank's range
+ * (lengths = visible tokens in the range, totals = visible tokens of the whole
+ * row); rows with totals <= 2048 and empty ranges give INT32_MAX.  The caller
+ * takes the minimum over ranks (an all-reduce MIN) as the row's bound. */
+int hcu_cp_local_bound(const float* score, int64_t rows, int64_t width, int64_t score_stride,
+                       const int16_t* mask, int64_t mask_stride, const int32_t* lengths, const int32_t* totals,
+                       int32_t* bounds, hcu_stream_t stream);
+
+/* hcu_cp_filter: every token of the row's range with key >= bound, in token
+ * order, as (key, page_table entry) into cap (<= 2048) slots; key 0 / entry -1
+ * pads.  Row r's list starts at (r / rows_per_block) * block_stride +
+ * (r % rows_per_block) * cap of keys and of gidx, so the lists land directly in
+ * a row-sharded exchange buffer.  counts (optional) = tokens at or above the
+ * bound; *flag |= 1 when a row has more than cap of them. */
+int hcu_cp_filter(const float* score, int64_t rows, int64_t width, int64_t score_stride, const int16_t* mask,
+                  int64_t mask_stride, const int32_t* lengths, const int32_t* page_table, int64_t pt_stride,
+                  const int32_t* bounds, int64_t cap, uint32_t* keys, int32_t* gidx, int64_t rows_per_block,
+                  int64_t block_stride, int32_t* counts, int32_t* flag, hcu_stream_t stream);
+
+/* hcu_cp_topk_merge with lists of list_len (a power of two in [256, 2048],
+ * n_parts * list_len >= 2048) entries, part p's lists at p * part_stride.
+ * flag (optional): *flag |= 1 for a row longer than 2048 tokens whose lists hold
+ * fewer than 2048 entries (a bound that missed; without flag such input sets
+ * HCU_STATUS_BAD_INPUT).  short_identity: rows of at most 2048 visible tokens
+ * are written as 0, 1, .., len - 1 (identity page table) without reading lists. */
+int hcu_cp_topk_merge_lists(const uint32_t* keys, const int32_t* gidx, int64_t n_parts, int64_t list_len,
+                            int64_t part_stride, int64_t rows, const int32_t* lengths, int32_t* flag,
+                            int32_t short_identity, int32_t* dst, hcu_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

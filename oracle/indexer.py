@@ -368,3 +368,101 @@ def cp_merge(keys: np.ndarray, gidx: np.ndarray, lengths: np.ndarray, topk: int 
             sel = np.concatenate([above, np.nonzero(k == thr)[0][: topk - above.shape[0]]])
         out[r, : sel.shape[0]] = g[sel]
     return out
+
+
+# ---------------------------------------------------------------------------
+# context-parallel bounded exchange (this build's CP protocol; the reference's
+# CP splits queries instead, so these pin the device ops, not reference code)
+# ---------------------------------------------------------------------------
+
+BOUND_SAMPLES = 1024
+
+
+def _transport(key: np.ndarray) -> np.ndarray:
+    """uint32 key -> order-preserving int32 (key ^ 0x80000000)."""
+    return (np.asarray(key, dtype=np.uint32) ^ np.uint32(0x80000000)).view(np.int32)
+
+
+def cp_local_bound(score: np.ndarray, nonzero_mask: np.ndarray, lengths: np.ndarray,
+                   totals: np.ndarray) -> np.ndarray:
+    """Per-row sampled bound of the row's global top-2048 threshold on one range (device:
+    ``cp_bound_kernel``): with n = visible tokens in the range and N = visible tokens of the
+    row, m = min(n, 1024) samples (every token when n <= 1024, else 256 groups of 4 consecutive
+    tokens starting at min((2g+1) n // 512, n - 4) rounded down to a multiple of 4), t = 2048 m / N,
+    r_lo = ceil(t + 3 sqrt(t) + 2); the bound is the r_lo-th largest sample key (1 = largest),
+    key 0 when r_lo >= m, the largest key when N <= 2048 or 2048 n < N (n = 0 included).
+    Returns int32 [rows] (key ^ 0x80000000)."""
+    score = np.asarray(score, dtype=np.float32)
+    rows, W = score.shape
+    bits = mask_bits(nonzero_mask, W)
+    out = np.empty(rows, np.uint32)
+    for r in range(rows):
+        n = int(np.clip(lengths[r], 0, W))
+        N = int(totals[r])
+        if N <= TOPK or TOPK * n < N:
+            out[r] = 0xFFFFFFFF
+            continue
+        m = min(n, BOUND_SAMPLES)
+        t = np.float32(TOPK) * np.float32(m) / np.float32(N)
+        r_lo = int(np.ceil(np.float32(t + np.float32(3.0) * np.sqrt(t) + np.float32(2.0))))
+        if r_lo >= m:
+            out[r] = 0
+            continue
+        if n <= BOUND_SAMPLES:
+            i = np.arange(n, dtype=np.int64)
+        else:
+            g = np.arange(BOUND_SAMPLES // 4, dtype=np.int64)
+            i0 = np.minimum((2 * g + 1) * n // (2 * (BOUND_SAMPLES // 4)), n - 4) & ~3
+            i = (i0[:, None] + np.arange(4)).reshape(-1)
+        k = np.where(bits[r, i], to_key(score[r, i]), ZERO_KEY).astype(np.uint32)
+        out[r] = np.sort(k)[::-1][r_lo - 1]
+    return _transport(out)
+
+
+def cp_filter(score: np.ndarray, nonzero_mask: np.ndarray, lengths: np.ndarray, page_table: np.ndarray,
+              bounds: np.ndarray, cap: int):
+    """Tokens of [0, len) with key >= the row's bound, in token order, as (key, page-table entry)
+    lists of cap slots (key 0 / entry -1 pads).  A row with more than cap such tokens: with
+    cap = 2048, the range's top-2048 among them (canonical selection) in token order; otherwise,
+    or past the device's candidate capacity (4096 for widths up to 32768, else 8192), the flag.
+    Returns (keys uint32 [rows, cap], gidx int32 [rows, cap], counts int32 [rows], flag)."""
+    score = np.asarray(score, dtype=np.float32)
+    rows, W = score.shape
+    bits = mask_bits(nonzero_mask, W)
+    lo = (np.asarray(bounds, dtype=np.int32).view(np.uint32) ^ np.uint32(0x80000000)).astype(np.uint32)
+    keys = np.zeros((rows, cap), np.uint32)
+    gidx = np.full((rows, cap), -1, np.int32)
+    counts = np.zeros(rows, np.int32)
+    flag = 0
+    for r in range(rows):
+        n = int(np.clip(lengths[r], 0, W))
+        k = np.where(bits[r, :n], to_key(score[r, :n]), ZERO_KEY).astype(np.uint32)
+        sel = np.nonzero(k >= lo[r])[0]
+        counts[r] = sel.shape[0]
+        cand_cap = 4096 if W <= 32768 else 8192
+        if sel.shape[0] > cap and cap == TOPK and sel.shape[0] <= cand_cap:
+            sel = sel[np.sort(select_topk(k[sel]))]
+        else:
+            flag |= int(sel.shape[0] > cap)
+        kept = sel[:cap]
+        keys[r, :kept.shape[0]] = k[kept]
+        gidx[r, :kept.shape[0]] = np.asarray(page_table)[r, kept]
+    return keys, gidx, counts, flag
+
+
+def cp_merge_lists(keys: np.ndarray, gidx: np.ndarray, lengths: np.ndarray):
+    """Merge of bounded lists ``[P, rows, C]``: rows of at most 2048 visible tokens are the
+    identity 0..len-1 (device: short_identity); the others are ``cp_merge`` of their lists, and
+    a row whose lists hold fewer than 2048 entries raises the flag.  Returns (out, flag)."""
+    rows = keys.shape[1]
+    out = np.full((rows, TOPK), -1, np.int32)
+    flag = 0
+    for r in range(rows):
+        L = int(lengths[r])
+        if L <= TOPK:
+            out[r] = np.where(np.arange(TOPK) < L, np.arange(TOPK), -1)
+        elif int((gidx[:, r, :] >= 0).sum()) < TOPK:
+            flag = 1  # the row's result is not defined; the caller reruns exactly
+        else:
+            out[r] = cp_merge(keys[:, r:r + 1], gidx[:, r:r + 1], lengths[r:r + 1])[0]
+    return out, flag

@@ -284,6 +284,69 @@ torch::Tensor cp_topk_merge(const torch::Tensor& keys, const torch::Tensor& gidx
   return dst;
 }
 
+torch::Tensor cp_local_bound(const torch::Tensor& score, const torch::Tensor& nonzero_mask, const torch::Tensor& lengths,
+                             const torch::Tensor& totals) {
+  check_topk_inputs(score, nonzero_mask, lengths, torch::empty({score.size(0), 1}, lengths.options()),
+                    torch::empty({score.size(0) + 1}, lengths.options()), kTopK);
+  TORCH_CHECK(totals.scalar_type() == at::kInt && totals.dim() == 1 && totals.size(0) == score.size(0) &&
+                  totals.is_contiguous() && totals.device() == score.device(),
+              "totals must be contiguous int32 [rows]");
+  const c10::cuda::CUDAGuard guard(score.device());
+  auto bounds = torch::empty({score.size(0)}, lengths.options());
+  if (score.size(0) == 0) return bounds;
+  check_status(hcu_cp_local_bound(ptr<const float>(score), score.size(0), score.size(1), score.stride(0),
+                                  ptr<const int16_t>(nonzero_mask), nonzero_mask.stride(0), ptr<const int32_t>(lengths),
+                                  ptr<const int32_t>(totals), ptr<int32_t>(bounds), cur_stream()),
+               "cp_local_bound");
+  return bounds;
+}
+
+// Writes the filtered lists into send [P, 2, rps, C] (keys then global indices per destination).
+void cp_filter(const torch::Tensor& score, const torch::Tensor& nonzero_mask, const torch::Tensor& lengths,
+               const torch::Tensor& page_table, const torch::Tensor& bounds, torch::Tensor& send, torch::Tensor& flag) {
+  check_topk_inputs(score, nonzero_mask, lengths, page_table, torch::empty({score.size(0) + 1}, lengths.options()),
+                    kTopK);
+  TORCH_CHECK(bounds.scalar_type() == at::kInt && bounds.dim() == 1 && bounds.size(0) == score.size(0) &&
+                  bounds.is_contiguous(),
+              "bounds must be contiguous int32 [rows]");
+  TORCH_CHECK(send.scalar_type() == at::kInt && send.dim() == 4 && send.size(1) == 2 && send.is_contiguous() &&
+                  send.size(0) * send.size(2) >= score.size(0),
+              "send must be contiguous int32 [P, 2, rows per rank, C] covering the rows");
+  TORCH_CHECK(flag.scalar_type() == at::kInt && flag.numel() >= 1 && flag.is_contiguous(), "flag must be int32 [1]");
+  const c10::cuda::CUDAGuard guard(score.device());
+  if (score.size(0) == 0) return;
+  const int64_t rps = send.size(2), cap = send.size(3);
+  int32_t* base = ptr<int32_t>(send);
+  check_status(hcu_cp_filter(ptr<const float>(score), score.size(0), score.size(1), score.stride(0),
+                             ptr<const int16_t>(nonzero_mask), nonzero_mask.stride(0), ptr<const int32_t>(lengths),
+                             ptr<const int32_t>(page_table), page_table.stride(0), ptr<const int32_t>(bounds), cap,
+                             reinterpret_cast<uint32_t*>(base), base + rps * cap, rps, 2 * rps * cap, nullptr,
+                             ptr<int32_t>(flag), cur_stream()),
+               "cp_filter");
+}
+
+// Merges recv [P, 2, rows, C] (the exchanged lists of this rank's rows).
+torch::Tensor cp_topk_merge_lists(const torch::Tensor& recv, const torch::Tensor& lengths,
+                                  const c10::optional<torch::Tensor>& flag, bool short_identity) {
+  TORCH_CHECK(recv.is_cuda() && recv.scalar_type() == at::kInt && recv.dim() == 4 && recv.size(1) == 2 &&
+                  recv.is_contiguous(),
+              "recv must be contiguous int32 [P, 2, rows, C]");
+  const int64_t rows = recv.size(2), cap = recv.size(3);
+  TORCH_CHECK(lengths.scalar_type() == at::kInt && lengths.dim() == 1 && lengths.size(0) == rows &&
+                  lengths.is_contiguous(),
+              "lengths must be contiguous int32 [rows]");
+  const c10::cuda::CUDAGuard guard(recv.device());
+  auto dst = torch::empty({rows, kTopK}, recv.options());
+  if (rows == 0) return dst;
+  const int32_t* base = ptr<const int32_t>(recv);
+  check_status(hcu_cp_topk_merge_lists(reinterpret_cast<const uint32_t*>(base), base + rows * cap, recv.size(0), cap,
+                                       2 * rows * cap, rows, ptr<const int32_t>(lengths),
+                                       flag ? ptr<int32_t>(*flag) : nullptr, short_identity ? 1 : 0,
+                                       ptr<int32_t>(dst), cur_stream()),
+               "cp_topk_merge_lists");
+  return dst;
+}
+
 int64_t read_device_status(bool clear) {
   uint32_t s = 0;
   check_status(hcu_read_device_status(&s, clear ? 1 : 0), "read_device_status");
@@ -301,6 +364,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "sparse_mask_topk_transform_split with pass 1 (histogram) taken from mqa_logits_hist's workspace");
   m.def("mqa_logits_hist", &mqa_logits_hist,
         "paged fp8 indexer logits -> {logits, mask, zws}; with hist_lens also top-k pass 1 into zws");
+  m.def("cp_local_bound", &cp_local_bound, "context-parallel: per-row sampled bound of the global top-2048 threshold");
+  m.def("cp_filter", &cp_filter, "context-parallel: tokens at or above the bound into the exchange buffer");
+  m.def("cp_topk_merge_lists", &cp_topk_merge_lists, "context-parallel: merge of the exchanged bounded lists");
   m.def("mqa_logits_ragged", &mqa_logits_ragged,
         "prefill fp8 indexer logits over a contiguous K with per-row [start, end) -> {logits, mask}");
   m.def("topk_keys", &topk_keys, "top-2048 indices through a page table plus the selected uint32 keys");

@@ -1191,15 +1191,19 @@ constexpr int kMaxParts = 16;
 constexpr int kTkThreads = 1024;  // one CTA per row
 constexpr int kCandCap = Tk<kTkThreads>::kCandCap;
 
-__device__ __forceinline__ int64_t merge_off(int c, int rows, int row) {
-  return (static_cast<int64_t>(c >> 11) * rows + row) * kTopK + (c & (kTopK - 1));
+// Entry c of a row's concatenated lists: part c >> lshift, position c & (2^lshift - 1);
+// part p's list of row r starts at p * pstride + r * 2^lshift.
+__device__ __forceinline__ int64_t merge_off(int c, int lshift, int64_t pstride, int row) {
+  return static_cast<int64_t>(c >> lshift) * pstride + (static_cast<int64_t>(row) << lshift) +
+         (c & ((1 << lshift) - 1));
 }
 
-// Radix-select fallback over every valid entry (entries [tid*per, (tid+1)*per)).
+// Radix-select fallback over every valid entry (entries [tid*per, (tid+1)*per) below n_ent).
 __device__ void merge_radix(TopkSmem<kTkThreads>& sm, const uint32_t* __restrict__ keys, const int32_t* __restrict__ gidx,
-                            int per, int rows, int row, int32_t* __restrict__ out) {
+                            int per, int n_ent, int lshift, int64_t pstride, int row, int32_t* __restrict__ out) {
   const int tid = threadIdx.x;
   const int c0 = tid * per;
+  per = max(0, min(per, n_ent - c0));
   uint32_t pre = 0u;
   int need = kTopK;
   int above = 0;
@@ -1210,7 +1214,7 @@ __device__ void merge_radix(TopkSmem<kTkThreads>& sm, const uint32_t* __restrict
     for (int i = tid; i < nb; i += kTkThreads) sm.hist[i] = 0;
     __syncthreads();
     for (int i = 0; i < per; ++i) {
-      const int64_t o = merge_off(c0 + i, rows, row);
+      const int64_t o = merge_off(c0 + i, lshift, pstride, row);
       const uint32_t k = __ldg(keys + o);
       const bool ok = __ldg(gidx + o) >= 0 && (pass == 0 || (k >> (sh + (pass == 1 ? 12 : 8))) == pre);
       if (ok) atomicAdd(&sm.hist[(k >> sh) & (nb - 1)], 1);
@@ -1228,7 +1232,7 @@ __device__ void merge_radix(TopkSmem<kTkThreads>& sm, const uint32_t* __restrict
   const int remaining = need;
   int na = 0, nt = 0;
   for (int i = 0; i < per; ++i) {
-    const int64_t o = merge_off(c0 + i, rows, row);
+    const int64_t o = merge_off(c0 + i, lshift, pstride, row);
     const uint32_t k = __ldg(keys + o);
     const bool v = __ldg(gidx + o) >= 0;
     na += v & (k > thr);
@@ -1238,7 +1242,7 @@ __device__ void merge_radix(TopkSmem<kTkThreads>& sm, const uint32_t* __restrict
   const int ex = block_excl_scan<kTkThreads>(na | (nt << 16), sm.wtot, &total);
   int ea = ex & 0xFFFF, et = ex >> 16;
   for (int i = 0; i < per; ++i) {
-    const int64_t o = merge_off(c0 + i, rows, row);
+    const int64_t o = merge_off(c0 + i, lshift, pstride, row);
     const uint32_t k = __ldg(keys + o);
     const int g = __ldg(gidx + o);
     if (g < 0) continue;
@@ -1251,10 +1255,17 @@ __device__ void merge_radix(TopkSmem<kTkThreads>& sm, const uint32_t* __restrict
   }
 }
 
+// Lists of 2^lshift entries per (part, row), part p at p * pstride; flag
+// (optional): set when a row longer than kTopK holds fewer than kTopK entries
+// (a caller-side bound missed), instead of the sticky bad-input status;
+// short_identity: rows of at most kTopK visible tokens [0, len) output
+// 0, 1, .., len - 1 without reading the lists (identity page table).
 __global__ __launch_bounds__(kTkThreads, 1) void cp_merge_kernel(const uint32_t* __restrict__ keys,
                                                                 const int32_t* __restrict__ gidx, int parts,
-                                                                int rows, const int32_t* __restrict__ lengths,
-                                                                int32_t* __restrict__ dst) {
+                                                                int lshift, int64_t pstride,
+                                                                const int32_t* __restrict__ lengths,
+                                                                int32_t* __restrict__ dst, int32_t* __restrict__ flag,
+                                                                int short_identity) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   TopkSmem<kTkThreads>& sm = *reinterpret_cast<TopkSmem<kTkThreads>*>(smem_raw);
   const int row = blockIdx.x;
@@ -1262,22 +1273,31 @@ __global__ __launch_bounds__(kTkThreads, 1) void cp_merge_kernel(const uint32_t*
   const int lane = tid & 31;
   const int w = tid >> 5;
   int32_t* out = dst + static_cast<int64_t>(row) * kTopK;
+  if (short_identity) {
+    const int vl = __ldg(lengths + row);
+    if (vl <= kTopK) {
+      for (int i = tid; i < kTopK; i += kTkThreads) out[i] = i < vl ? i : -1;
+      return;
+    }
+  }
   for (int i = tid; i < 2 * 512; i += kTkThreads) (&sm.hb[0][0])[i] = 0;
 
-  // ---- A: lower bound lo from 2048 samples of the concatenated lists (entry j * parts + parts / 2) ----
+  const int n_ent = parts << lshift;  // entries of the row's concatenated lists
+  // ---- A: lower bound lo from 2048 evenly spaced samples of the concatenated lists ----
   for (int i = tid; i < kBins; i += kTkThreads) sm.hist[i] = 0;
   __syncthreads();
   constexpr int kMs = 2048;  // samples
   uint32_t sk[kMs / kTkThreads];
 #pragma unroll
   for (int j = 0; j < kMs / kTkThreads; ++j) {
-    const int64_t o = merge_off((tid + j * kTkThreads) * parts + parts / 2, rows, row);
+    const int c = static_cast<int>(static_cast<int64_t>(tid + j * kTkThreads) * n_ent / kMs) + n_ent / (2 * kMs);
+    const int64_t o = merge_off(min(c, n_ent - 1), lshift, pstride, row);
     sk[j] = __ldg(gidx + o) >= 0 ? __ldg(keys + o) : 0u;  // a missing entry ranks below every key
     atomicAdd(&sm.hist[sk[j] >> 20], 1);
   }
   __syncthreads();
   // sample rank (1 = largest) 4 sigma + 4 below the threshold's expected sample rank
-  const float t = static_cast<float>(kTopK) / static_cast<float>(parts);
+  const float t = static_cast<float>(kMs) * static_cast<float>(kTopK) / static_cast<float>(n_ent);
   const int r_lo = min(kMs, static_cast<int>(ceilf(t + 4.f * sqrtf(t) + 4.f)));
   find_threshold<kTkThreads, kBins>(sm.hist, r_lo, sm.wtot, sm.res);
   const uint32_t b1 = static_cast<uint32_t>(sm.res[0]);
@@ -1294,7 +1314,7 @@ __global__ __launch_bounds__(kTkThreads, 1) void cp_merge_kernel(const uint32_t*
   if (short_row) lo = 0u;  // keep every entry
 
   // ---- B: entries with key >= lo, appended in global index order ----
-  const int per = parts * 2;
+  const int per = (n_ent + kTkThreads - 1) / kTkThreads;  // <= 32
   const int c0 = tid * per;
   // thread t: entries [t * per, (t + 1) * per), per <= 32; loads go out 8 at a time
   int na = 0, nv = 0;
@@ -1306,8 +1326,8 @@ __global__ __launch_bounds__(kTkThreads, 1) void cp_merge_kernel(const uint32_t*
     for (int u = 0; u < 8; ++u) {
       gg[u] = -1;
       kk[u] = 0u;
-      if (i0 + u < per) {
-        const int64_t o = merge_off(c0 + i0 + u, rows, row);
+      if (i0 + u < per && c0 + i0 + u < n_ent) {
+        const int64_t o = merge_off(c0 + i0 + u, lshift, pstride, row);
         kk[u] = __ldg(keys + o);
         gg[u] = __ldg(gidx + o);
       }
@@ -1327,7 +1347,7 @@ __global__ __launch_bounds__(kTkThreads, 1) void cp_merge_kernel(const uint32_t*
   int packed_total;
   const int packed = block_excl_scan<kTkThreads>(na | (nv << 16), sm.wtot, &packed_total);
   const int n = packed_total & 0xFFFF;
-  const int total = packed_total >> 16;
+  const int total = static_cast<int>(static_cast<uint32_t>(packed_total) >> 16);
   int pos = packed & 0xFFFF;
   if (n <= kCandCap) {
     for (int i0 = 0; i0 < per && (cbits >> i0); i0 += 8) {
@@ -1336,7 +1356,7 @@ __global__ __launch_bounds__(kTkThreads, 1) void cp_merge_kernel(const uint32_t*
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
         if ((cbits >> (i0 + u)) & 1u) {
-          const int64_t o = merge_off(c0 + i0 + u, rows, row);
+          const int64_t o = merge_off(c0 + i0 + u, lshift, pstride, row);
           kk[u] = __ldg(keys + o);
           gg[u] = __ldg(gidx + o);
         }
@@ -1360,19 +1380,182 @@ __global__ __launch_bounds__(kTkThreads, 1) void cp_merge_kernel(const uint32_t*
   __syncthreads();
 
   if (short_row || total < kTopK) {
-    // all entries in index order (fewer than 2048 entries for a longer row is inconsistent input)
-    if (!short_row && tid == 0) atomicOr(&g_hcu_status, HCU_STATUS_BAD_INPUT);
+    // all entries in index order; fewer than 2048 entries for a longer row is inconsistent input,
+    // or (with flag) a caller's bound that missed
+    if (!short_row && tid == 0) {
+      if (flag)
+        atomicOr(flag, 1);
+      else
+        atomicOr(&g_hcu_status, HCU_STATUS_BAD_INPUT);
+    }
     for (int i = tid; i < kTopK; i += kTkThreads) out[i] = i < n && i < kCandCap ? sm.cand_pid[i] : -1;
     return;
   }
   if (n > kCandCap || n < kTopK) {  // list overflow, or the sampled bound missed
-    merge_radix(sm, keys, gidx, per, rows, row, out);
+    merge_radix(sm, keys, gidx, per, n_ent, lshift, pstride, row, out);
     return;
   }
   // ---- C: select and ordered write over the candidates ----
   int above = 0;
   const uint32_t thr = select_candidates(sm, n, lo, &above);
   write_candidates<kTkThreads, false>(sm, n, thr, above, out, nullptr);
+}
+// ---------------------------------------------------------------------------
+// Context-parallel candidate filter (the bounded exchange of hcu_ops/cp.py).
+//
+// Instead of a local top-2048 per range, each rank keeps only the tokens that
+// can still be in the row's global top-2048: those with key >= b, where b is
+// the minimum over ranks of a sampled estimate of the row's global threshold
+// on each rank's own range (cp_bound_kernel, then an all-reduce MIN).  The
+// filter (cp_filter_kernel) emits every such token in token order into a short
+// fixed-capacity list.  The union is exact iff it holds at least kTopK entries
+// per row (then the global threshold is >= b, so every token of the global
+// top-k passed the filter) and no list overflowed; the merge and the filter
+// flag the rows where either fails, and the caller then runs the exact path.
+// ---------------------------------------------------------------------------
+constexpr int kBoundWarps = 8;        // rows per CTA of the bound kernel (one warp each)
+constexpr int kBoundSamples = 1024;   // samples of a row's local range
+
+struct __align__(16) BoundSmem {
+  uint32_t k[kBoundWarps][kBoundSamples];
+  alignas(16) int h[kBoundWarps][256];
+  int res[kBoundWarps][4];
+};
+
+// Bound of row `row` on this range, as an order-preserving int32 (key ^ 0x80000000):
+// the sample key of rank r_lo = t + 3 sqrt(t) + 2 (1 = largest) among m
+// samples of the local range (m / 4 evenly spaced groups of 4 consecutive
+// tokens, one 16-byte load and one mask word each; every token when n <= m),
+// t = kTopK * m / total the expected sample rank of the global threshold.  The largest key (no constraint on the minimum)
+// for rows of at most kTopK visible tokens (the merge writes them as the
+// identity), for empty ranges, and for ranges expected to hold less than one
+// token of the row's top-kTopK (kTopK * n < total): their few tokens are
+// covered by the other ranges' margins, and their noisy estimate would pull
+// every range's bound down.  Exactness never rests on the estimate: the merge
+// checks that the union holds kTopK entries.
+template <bool kVec>
+__global__ __launch_bounds__(kBoundWarps * 32) void cp_bound_kernel(
+    const float* __restrict__ score, int64_t score_stride, int width, const int16_t* __restrict__ mask,
+    int64_t mask_stride, const int32_t* __restrict__ lengths, const int32_t* __restrict__ totals, int rows,
+    int32_t* __restrict__ bounds) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  BoundSmem& sm = *reinterpret_cast<BoundSmem*>(smem_raw);
+  const int lane = threadIdx.x & 31;
+  const int w = threadIdx.x >> 5;
+  const int row = blockIdx.x * kBoundWarps + w;
+  if (row >= rows) return;  // whole warps; the kernel has no block barrier
+  int n = __ldg(lengths + row);
+  n = n < 0 ? 0 : (n > width ? width : n);
+  const int total = __ldg(totals + row);
+  uint32_t v = 0xFFFFFFFFu;
+  if (total > kTopK && static_cast<int64_t>(kTopK) * n >= total) {
+    v = 0u;
+    {
+      const int m = n <= kBoundSamples ? n : kBoundSamples;
+      const float t = static_cast<float>(kTopK) * static_cast<float>(m) / static_cast<float>(total);
+      const int r_lo = static_cast<int>(ceilf(t + 3.f * sqrtf(t) + 2.f));
+      if (r_lo < m) {
+        const float* vals = score + static_cast<int64_t>(row) * score_stride;
+        const int16_t* mrow = mask + static_cast<int64_t>(row) * mask_stride;
+        uint32_t* ks = sm.k[w];
+        if (n <= kBoundSamples) {  // every token
+          for (int i = lane; i < n; i += 32) {
+            const bool set = (static_cast<uint16_t>(__ldg(mrow + (i >> 4))) >> (i & 15)) & 1u;
+            ks[i] = set ? to_key(__ldg(vals + i)) : kZeroKey;
+          }
+        } else {  // group g: tokens i .. i + 3 < n, i = ((2g + 1) n / (2 m / 4)) rounded down to a multiple of 4
+          constexpr int kGroups = kBoundSamples / 4;
+          for (int g = lane; g < kGroups; g += 32) {
+            const int i = min(static_cast<int>((2 * static_cast<int64_t>(g) + 1) * n / (2 * kGroups)), n - 4) & ~3;
+            const uint32_t mb = static_cast<uint16_t>(__ldg(mrow + (i >> 4))) >> (i & 15);
+            float f[4];
+            if constexpr (kVec) {
+              const float4 q = __ldg(reinterpret_cast<const float4*>(vals + i));
+              f[0] = q.x; f[1] = q.y; f[2] = q.z; f[3] = q.w;
+            } else {
+#pragma unroll
+              for (int e = 0; e < 4; ++e) f[e] = __ldg(vals + i + e);
+            }
+#pragma unroll
+            for (int e = 0; e < 4; ++e) ks[4 * g + e] = ((mb >> e) & 1u) ? to_key(f[e]) : kZeroKey;
+          }
+        }
+        // r_lo-th largest sample key: four 8-bit radix passes over the warp's samples
+        uint32_t pre = 0u;
+        int need = r_lo;
+        int* h = sm.h[w];
+        for (int pass = 0; pass < 4; ++pass) {
+          const int sh = 24 - 8 * pass;
+          for (int i = lane; i < 256; i += 32) h[i] = 0;
+          __syncwarp();
+          for (int j = lane; j < m; j += 32) {
+            const uint32_t k = ks[j];
+            if (pass == 0 || (k >> (sh + 8)) == pre) atomicAdd(&h[(k >> sh) & 0xFFu], 1);
+          }
+          __syncwarp();
+          warp_find<256>(h, need, sm.res[w]);
+          __syncwarp();
+          pre = (pre << 8) | static_cast<uint32_t>(sm.res[w][0]);
+          need -= sm.res[w][1];
+          __syncwarp();
+        }
+        v = pre;
+      }
+    }
+  }
+  if (lane == 0) bounds[row] = static_cast<int32_t>(v ^ kZeroKey);
+}
+
+// One CTA per row: every token of [0, len) with key >= the row's bound, in
+// token order, as (key, page-table entry) into list slots [0, cap) of the row
+// (key 0 / entry -1 pads); row r's list starts at (r / rows_per_block) *
+// block_stride + (r % rows_per_block) * cap (so a row-sharded exchange buffer
+// is written in place); counts[row] (optional) = all such tokens.  More than
+// cap of them: with cap = kTopK the list holds the range's top-kTopK among them
+// (exact for the merge), else (or past the candidate capacity) *flag |= 1.
+template <int kT, bool kVec>
+__global__ __launch_bounds__(kT, 1024 / kT) void cp_filter_kernel(
+    const float* __restrict__ score, int64_t score_stride, int width, const int16_t* __restrict__ mask,
+    int64_t mask_stride, const int32_t* __restrict__ lengths, const int32_t* __restrict__ pt, int64_t pt_stride,
+    const int32_t* __restrict__ bounds, int cap, uint32_t* __restrict__ out_keys, int32_t* __restrict__ out_gidx,
+    int rows_per_block, int64_t block_stride, int32_t* __restrict__ counts, int32_t* __restrict__ flag) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  TopkSmem<kT>& sm = *reinterpret_cast<TopkSmem<kT>*>(smem_raw);
+  const int row = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int w = tid >> 5;
+  int len = __ldg(lengths + row);
+  len = len < 0 ? 0 : (len > width ? width : len);
+  const uint32_t lo = static_cast<uint32_t>(__ldg(bounds + row)) ^ kZeroKey;
+  const float* vals = score + static_cast<int64_t>(row) * score_stride;
+  const int16_t* mrow = mask + static_cast<int64_t>(row) * mask_stride;
+  const int32_t* src = pt + static_cast<int64_t>(row) * pt_stride;
+  uint32_t b0[16], valid0 = 0u;
+  const uint32_t mw0 = load16_raw<kVec>(vals, mrow, w * (32 * kLaneTok) + lane * kLaneTok, len, b0, valid0);
+  for (int i = tid; i < 2 * 512; i += kT) (&sm.hb[0][0])[i] = 0;  // the select's digit histograms
+  const int n = lo > kZeroKey ? collect_candidates<kT, kVec, true>(vals, mrow, src, 0, len, lo, sm, b0, mw0, valid0)
+                              : collect_candidates<kT, kVec, false>(vals, mrow, src, 0, len, lo, sm, b0, mw0, valid0);
+  cp_async_wait_all();
+  __syncthreads();
+  const int64_t lo_off = (row / rows_per_block) * block_stride + static_cast<int64_t>(row % rows_per_block) * cap;
+  uint32_t* ok = out_keys + lo_off;
+  int32_t* og = out_gidx + lo_off;
+  if (n > cap && cap == kTopK && n <= Tk<kT>::kCandCap) {
+    // more candidates than slots: the range's exact top-kTopK among them, in token order, holds
+    // every token of the row's global top-kTopK that lies in this range
+    int above = 0;
+    const uint32_t thr = select_candidates(sm, n, lo, &above);
+    write_candidates<kT, true>(sm, n, thr, above, og, ok);
+  } else {
+    const int kept = min(n, cap);  // cap <= kTopK <= kCandCap: every kept entry is in the list
+    for (int i = tid; i < cap; i += kT) {
+      ok[i] = i < kept ? sm.cand_key[i] : 0u;
+      og[i] = i < kept ? sm.cand_pid[i] : -1;
+    }
+    if (tid == 0 && n > cap) atomicOr(flag, 1);
+  }
+  if (tid == 0 && counts) counts[row] = n;
 }
 }  // namespace
 
@@ -1458,16 +1641,104 @@ extern "C" int hcu_topk_keys(const float* score, int64_t rows, int64_t width, in
                      dst_keys, nullptr, reinterpret_cast<cudaStream_t>(stream), /*sorted=*/true);
 }
 
-extern "C" int hcu_cp_topk_merge(const uint32_t* keys, const int32_t* gidx, int64_t n_parts, int64_t rows,
-                                 const int32_t* lengths, int32_t* dst, hcu_stream_t stream) {
+extern "C" int hcu_cp_topk_merge_lists(const uint32_t* keys, const int32_t* gidx, int64_t n_parts,
+                                       int64_t list_len, int64_t part_stride, int64_t rows, const int32_t* lengths,
+                                       int32_t* flag, int32_t short_identity, int32_t* dst, hcu_stream_t stream) {
   using namespace hcu;
   if (n_parts < 1 || n_parts > kMaxParts || rows < 0 || rows > INT32_MAX) return HCU_ERR_ARG;
+  if (part_stride < rows * list_len) return HCU_ERR_ARG;
+  int lshift = 0;
+  while ((int64_t{1} << lshift) < list_len) ++lshift;
+  if ((int64_t{1} << lshift) != list_len || list_len < 256 || list_len > kTopK || n_parts * list_len < kTopK)
+    return HCU_ERR_ARG;
   if (rows == 0) return HCU_OK;
   if (!keys || !gidx || !lengths || !dst) return HCU_ERR_ARG;
   const size_t smem = sizeof(TopkSmem<kTkThreads>);
   cudaFuncSetAttribute(cp_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   cp_merge_kernel<<<static_cast<unsigned>(rows), kTkThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
-      keys, gidx, static_cast<int>(n_parts), static_cast<int>(rows), lengths, dst);
+      keys, gidx, static_cast<int>(n_parts), lshift, part_stride, lengths, dst, flag, short_identity);
+  return launch_status();
+}
+
+extern "C" int hcu_cp_topk_merge(const uint32_t* keys, const int32_t* gidx, int64_t n_parts, int64_t rows,
+                                 const int32_t* lengths, int32_t* dst, hcu_stream_t stream) {
+  return hcu_cp_topk_merge_lists(keys, gidx, n_parts, hcu::kTopK, rows * hcu::kTopK, rows, lengths, nullptr, 0, dst,
+                                 stream);
+}
+
+extern "C" int hcu_cp_local_bound(const float* score, int64_t rows, int64_t width, int64_t score_stride,
+                                  const int16_t* mask, int64_t mask_stride, const int32_t* lengths,
+                                  const int32_t* totals, int32_t* bounds, hcu_stream_t stream) {
+  using namespace hcu;
+  if (rows < 0 || rows > INT32_MAX || width < 0 || width > INT32_MAX / 2) return HCU_ERR_ARG;
+  if (rows == 0) return HCU_OK;
+  if (!score || !mask || !lengths || !totals || !bounds) return HCU_ERR_ARG;
+  if (score_stride < width || mask_stride < (width + 15) / 16) return HCU_ERR_ARG;
+  const size_t smem = sizeof(BoundSmem);
+  const unsigned grid = static_cast<unsigned>((rows + kBoundWarps - 1) / kBoundWarps);
+  const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (use_vec(score, width, score_stride)) {
+    cudaFuncSetAttribute(cp_bound_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    cp_bound_kernel<true><<<grid, kBoundWarps * 32, smem, st>>>(score, score_stride, static_cast<int>(width), mask,
+                                                                mask_stride, lengths, totals, static_cast<int>(rows),
+                                                                bounds);
+  } else {
+    cudaFuncSetAttribute(cp_bound_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    cp_bound_kernel<false><<<grid, kBoundWarps * 32, smem, st>>>(score, score_stride, static_cast<int>(width), mask,
+                                                                 mask_stride, lengths, totals, static_cast<int>(rows),
+                                                                 bounds);
+  }
+  return launch_status();
+}
+
+namespace hcu {
+namespace {
+template <int kT, bool kVec>
+void launch_filter(const float* score, int rows, int width, int64_t score_stride, const int16_t* mask,
+                   int64_t mask_stride, const int32_t* lengths, const int32_t* pt, int64_t pt_stride,
+                   const int32_t* bounds, int cap, uint32_t* keys, int32_t* gidx, int rpb, int64_t bstride,
+                   int32_t* counts, int32_t* flag, cudaStream_t st) {
+  const size_t smem = sizeof(TopkSmem<kT>);
+  cudaFuncSetAttribute(cp_filter_kernel<kT, kVec>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  cp_filter_kernel<kT, kVec><<<static_cast<unsigned>(rows), kT, smem, st>>>(
+      score, score_stride, width, mask, mask_stride, lengths, pt, pt_stride, bounds, cap, keys, gidx, rpb, bstride,
+      counts, flag);
+}
+}  // namespace
+}  // namespace hcu
+
+extern "C" int hcu_cp_filter(const float* score, int64_t rows, int64_t width, int64_t score_stride,
+                             const int16_t* mask, int64_t mask_stride, const int32_t* lengths,
+                             const int32_t* page_table, int64_t pt_stride, const int32_t* bounds, int64_t cap,
+                             uint32_t* keys, int32_t* gidx, int64_t rows_per_block, int64_t block_stride,
+                             int32_t* counts, int32_t* flag, hcu_stream_t stream) {
+  using namespace hcu;
+  int st = check_common(score, rows, width, score_stride, mask, mask_stride, lengths, page_table, pt_stride, kTopK,
+                        gidx);
+  if (st != HCU_OK || rows == 0) return st;
+  if (!bounds || !keys || !flag || cap < 1 || cap > kTopK) return HCU_ERR_ARG;
+  if (rows_per_block < 1 || rows_per_block > INT32_MAX ||
+      (rows > rows_per_block && block_stride < rows_per_block * cap))
+    return HCU_ERR_ARG;
+  const int r = static_cast<int>(rows), w = static_cast<int>(width), c = static_cast<int>(cap);
+  const int rpb = static_cast<int>(rows_per_block);
+  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const bool vec = use_vec(score, width, score_stride);
+  if (width <= kNarrowWidth) {
+    if (vec)
+      launch_filter<512, true>(score, r, w, score_stride, mask, mask_stride, lengths, page_table, pt_stride, bounds, c,
+                               keys, gidx, rpb, block_stride, counts, flag, s);
+    else
+      launch_filter<512, false>(score, r, w, score_stride, mask, mask_stride, lengths, page_table, pt_stride, bounds,
+                                c, keys, gidx, rpb, block_stride, counts, flag, s);
+  } else {
+    if (vec)
+      launch_filter<1024, true>(score, r, w, score_stride, mask, mask_stride, lengths, page_table, pt_stride, bounds,
+                                c, keys, gidx, rpb, block_stride, counts, flag, s);
+    else
+      launch_filter<1024, false>(score, r, w, score_stride, mask, mask_stride, lengths, page_table, pt_stride, bounds,
+                                 c, keys, gidx, rpb, block_stride, counts, flag, s);
+  }
   return launch_status();
 }
 

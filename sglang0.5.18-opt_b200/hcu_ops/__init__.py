@@ -190,6 +190,25 @@ def cp_topk_merge(keys, gidx, lengths):
     return _C.cp_topk_merge(keys, gidx, lengths)
 
 
+def cp_local_bound(score, nonzero_mask, lengths, totals):
+    """Per-row sampled estimate of the row's global top-2048 threshold on this KV range, as an
+    order-preserving int32 (key ^ 0x80000000); the context-parallel bound is its minimum over ranks."""
+    return _C.cp_local_bound(score, nonzero_mask, lengths, totals)
+
+
+def cp_filter(score, nonzero_mask, lengths, page_table, bounds, send, flag):
+    """Tokens with key >= bound, in token order, into the exchange buffer ``send`` int32
+    ``[P, 2, rows per rank, C]`` (keys, then global indices; -1 pads); ``flag[0] |= 1`` when a row
+    has more than C of them."""
+    _C.cp_filter(score, nonzero_mask, lengths, page_table, bounds, send, flag)
+
+
+def cp_topk_merge_lists(recv, lengths, flag=None, short_identity=True):
+    """Merge the exchanged bounded lists ``recv`` int32 ``[P, 2, rows, C]`` into the global top-2048
+    of those rows; ``flag[0] |= 1`` for a row whose lists hold fewer than 2048 entries."""
+    return _C.cp_topk_merge_lists(recv, lengths, flag, short_identity)
+
+
 def read_device_status(clear=True):
     """Sticky device status bits (1: a bounded wait expired, 2: an out-of-range index was skipped)."""
     return _C.read_device_status(clear)

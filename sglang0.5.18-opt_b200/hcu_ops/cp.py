@@ -9,6 +9,17 @@ ranks exchange and merge those lists:
   1/P share of the rows, rank r merges them, and an all-gather of the final
   int32 indices gives every rank the whole ``[rows, 2048]`` result.  Each rank
   receives ``(P-1)/P`` of one rank's lists instead of ``P-1`` whole lists.
+  The lists are bounded (``bounded=True``, default): instead of a local
+  top-2048, each rank keeps the tokens at or above the row's bound b, the
+  minimum over ranks of a sampled estimate of the row's global threshold on
+  each range (one all-reduce MIN of an int32 per row), in lists of 2048 entries
+  (a range with more tokens at or above b sends its top-2048 among them: every
+  token of the row's global top-2048 in that range is one of them).  The union
+  is exact when every row holds at least 2048 entries (then the global
+  threshold is >= b); the merge flags the rows where that fails (and the filter
+  a range past its candidate capacity), one all-reduce MAX of the flag tells
+  every rank, and the step then reruns with local top-2048 lists (the exact
+  path).
 * ``mode="allgather"``: every rank all-gathers all lists and merges all rows.
 
 The global top-2048 under (key desc, global index asc) is a subset of the union
@@ -29,6 +40,21 @@ TOPK = 2048
 
 class CudaOps:
     """The device ops the CP driver needs (the product path)."""
+
+    def bound(self, score, mask, lengths, totals):
+        from . import cp_local_bound
+
+        return cp_local_bound(score, mask, lengths, totals)
+
+    def filter(self, score, mask, lengths, page_table, bounds, send, flag):
+        from . import cp_filter
+
+        cp_filter(score, mask, lengths, page_table, bounds, send, flag)
+
+    def merge_lists(self, recv, lengths, flag):
+        from . import cp_topk_merge_lists
+
+        return cp_topk_merge_lists(recv, lengths, flag, True)
 
     def logits(self, q, k_fp8, k_scale, weights, row_start, row_end):
         from . import mqa_logits_ragged
@@ -66,8 +92,18 @@ def local_rows(row_end: torch.Tensor, lo: int, hi: int) -> torch.Tensor:
     return (row_end.clamp(max=hi) - lo).clamp(min=0).to(torch.int32)
 
 
+def list_len(world: int) -> int:
+    """Slots per (rank, row) list of the bounded exchange: 2048 (a range may hold a whole row's
+    top-2048).  HCU_CP_LIST_LEN (a power of two in [256, 2048], times world >= 2048) trades
+    exchange bytes for the exact rerun whenever a range has more candidates than that."""
+    import os
+
+    env = os.environ.get("HCU_CP_LIST_LEN")
+    return int(env) if env else 2048
+
+
 def cp_prefill_topk(q, k_fp8_local, k_scale_local, weights, row_end, n_tokens, group=None, mode="rowshard",
-                    ops=None):
+                    ops=None, bounded=True):
     """Global top-2048 token indices of every query row, computed over P KV ranges.
 
     q: fp8 ``[rows, H, 128]`` (replicated); ``k_fp8_local``/``k_scale_local``: this rank's
@@ -89,16 +125,19 @@ def cp_prefill_topk(q, k_fp8_local, k_scale_local, weights, row_end, n_tokens, g
     gtab = (torch.arange(width, dtype=torch.int32, device=dev) + lo).expand(rows, width)
     if world == 1:  # one range: the canonical top-k is the answer (no exchange, no merge)
         return ops.topk(lg, mk, lens, gtab)
-    idx, keys = ops.local_topk(lg, mk, lens, gtab)
     vis = row_end.clamp(max=n_tokens).to(torch.int32)
+    rps = (rows + world - 1) // world  # row-sharded exchange: rank d merges rows [d*rps, (d+1)*rps)
+    if mode == "rowshard" and bounded:
+        out = _bounded_rowshard(ops, lg, mk, lens, gtab, vis, rows, rps, world, rank, group)
+        if out is not None:
+            return out[:rows]
+    idx, keys = ops.local_topk(lg, mk, lens, gtab)
     if mode == "allgather":
         all_k = torch.empty((world * rows, TOPK), dtype=keys.dtype, device=dev)
         all_i = torch.empty((world * rows, TOPK), dtype=idx.dtype, device=dev)
         dist.all_gather_into_tensor(all_k, keys.contiguous(), group=group)
         dist.all_gather_into_tensor(all_i, idx.contiguous(), group=group)
         return ops.merge(all_k.view(world, rows, TOPK), all_i.view(world, rows, TOPK), vis)
-    # row-sharded exchange: rank d merges rows [d*rps, (d+1)*rps)
-    rps = (rows + world - 1) // world
     pad = rps * world - rows
     if pad:
         keys = torch.cat([keys, torch.zeros((pad, TOPK), dtype=keys.dtype, device=dev)])
@@ -111,3 +150,27 @@ def cp_prefill_topk(q, k_fp8_local, k_scale_local, weights, row_end, n_tokens, g
     out = torch.empty((world * rps, TOPK), dtype=mine.dtype, device=dev)
     dist.all_gather_into_tensor(out, mine.contiguous(), group=group)
     return out[:rows]
+
+
+def _bounded_rowshard(ops, lg, mk, lens, gtab, vis, rows, rps, world, rank, group):
+    """The bounded exchange; None when some row's union was not exact (every rank sees the same flag)."""
+    dev = lg.device
+    cap = list_len(world)
+    bounds = ops.bound(lg, mk, lens, vis)
+    dist.all_reduce(bounds, op=dist.ReduceOp.MIN, group=group)
+    send = torch.empty((world, 2, rps, cap), dtype=torch.int32, device=dev)
+    pad = rps * world - rows
+    if pad:
+        send[world - 1, 1, rps - pad:] = -1  # rows past the batch: empty lists
+    flag = torch.zeros(1, dtype=torch.int32, device=dev)
+    ops.filter(lg, mk, lens, gtab, bounds, send, flag)
+    recv = torch.empty_like(send)
+    dist.all_to_all_single(recv, send, group=group)
+    vis_p = torch.cat([vis, torch.zeros(pad, dtype=vis.dtype, device=dev)]) if pad else vis
+    mine = ops.merge_lists(recv, vis_p[rank * rps:(rank + 1) * rps].contiguous(), flag)
+    dist.all_reduce(flag, op=dist.ReduceOp.MAX, group=group)
+    if int(flag.item()):
+        return None
+    out = torch.empty((world * rps, TOPK), dtype=mine.dtype, device=dev)
+    dist.all_gather_into_tensor(out, mine.contiguous(), group=group)
+    return out

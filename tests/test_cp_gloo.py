@@ -44,6 +44,43 @@ class OracleOps:
 
         return torch.from_numpy(O.cp_merge(keys.numpy().view(np.uint32), gidx.numpy(), lengths.numpy()))
 
+    def bound(self, score, mask, lengths, totals):
+        from oracle import indexer as O
+
+        return torch.from_numpy(O.cp_local_bound(score.numpy(), mask.numpy(), lengths.numpy(), totals.numpy()))
+
+    def filter(self, score, mask, lengths, pt, bounds, send, flag):
+        from oracle import indexer as O
+
+        P, _, rps, cap = send.shape
+        k, g, _, f = O.cp_filter(score.numpy(), mask.numpy(), lengths.numpy(), np.ascontiguousarray(pt.numpy()),
+                                 bounds.numpy(), cap)
+        for r in range(score.shape[0]):
+            send[r // rps, 0, r % rps] = torch.from_numpy(k[r].view(np.int32))
+            send[r // rps, 1, r % rps] = torch.from_numpy(g[r])
+        flag |= f
+
+    def merge_lists(self, recv, lengths, flag):
+        from oracle import indexer as O
+
+        out, f = O.cp_merge_lists(recv[:, 0].numpy().view(np.uint32), recv[:, 1].numpy(), lengths.numpy())
+        flag |= f
+        return torch.from_numpy(out)
+
+
+class MissOps(OracleOps):
+    """A bound above every key: the lists hold fewer than 2048 entries, the merge flags it."""
+
+    def bound(self, score, mask, lengths, totals):
+        return torch.full((score.shape[0],), 2**31 - 1, dtype=torch.int32)
+
+
+class OverflowOps(OracleOps):
+    """A bound of 0: every token passes, the lists overflow, the filter flags it."""
+
+    def bound(self, score, mask, lengths, totals):
+        return torch.full((score.shape[0],), -2**31, dtype=torch.int32)
+
 
 def _free_port():
     s = socket.socket()
@@ -53,7 +90,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, mode, q):
+def _worker(rank, world, port, mode, variant, q):
     import sys
 
     here = os.path.dirname(os.path.abspath(__file__))
@@ -68,22 +105,29 @@ def _worker(rank, world, port, mode, q):
         from hcu_ops.cp import cp_prefill_topk, kv_range
         from hcu_ops.workloads import make_ragged
 
-        w = make_ragged(23, 5000, heads=32, seed=11)  # same seed on every rank: replicated q
+        w = make_ragged(23, 2600, heads=32, seed=11)  # same seed on every rank: replicated q
         N = w["k_fp8"].shape[0]
         lo, hi = kv_range(rank, world, N)
+        ops = {"miss": MissOps, "overflow": OverflowOps}.get(variant, OracleOps)()
         out = cp_prefill_topk(w["q"], w["k_fp8"][lo:hi].contiguous(), w["k_scale"][lo:hi].contiguous(),
-                              w["weights"], w["row_end"], N, mode=mode, ops=OracleOps())
+                              w["weights"], w["row_end"], N, mode=mode, ops=ops, bounded=variant != "exact")
         q.put((rank, out.numpy()))
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,mode", [(1, "rowshard"), (2, "rowshard"), (2, "allgather"), (3, "rowshard")])
-def test_cp_driver_equals_single_range(world, mode):
+@pytest.mark.parametrize("world,mode,variant", [(1, "rowshard", "bounded"), (2, "rowshard", "bounded"),
+                                                (2, "rowshard", "exact"), (2, "allgather", "exact"),
+                                                (3, "rowshard", "bounded"), (2, "rowshard", "miss"),
+                                                (3, "rowshard", "overflow")])
+def test_cp_driver_equals_single_range(world, mode, variant):
+    """Every rank's result equals the single-range top-k: the bounded exchange, the exact one,
+    and the bounded exchange whose bound misses (too high) or overflows the lists (too low),
+    which every rank detects and reruns exactly."""
     from hcu_ops.workloads import make_ragged
     from oracle import indexer as O
 
-    w = make_ragged(23, 5000, heads=32, seed=11)
+    w = make_ragged(23, 2600, heads=32, seed=11)
     lg, m, _ = O.mqa_logits_ragged(w["q"].view(torch.uint8).numpy(), w["k_fp8"].view(torch.uint8).numpy(),
                                    w["k_scale"].numpy(), w["weights"].numpy(), w["row_start"].numpy(),
                                    w["row_end"].numpy())
@@ -94,7 +138,7 @@ def test_cp_driver_equals_single_range(world, mode):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, mode, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, mode, variant, q)) for r in range(world)]
     for p in procs:
         p.start()
     got = {}

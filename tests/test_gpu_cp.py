@@ -35,3 +35,102 @@ def test_cp_merge_equals_single_range(hcu, dev, parts, dist):
         keys[p], gidx[p] = k, idx
     merged = hcu.cp_topk_merge(keys, gidx, vis.to(dev))
     assert np.array_equal(merged.cpu().numpy(), full)
+
+
+def _ranges(N, parts):
+    b = [(N * p // parts) // 16 * 16 for p in range(parts)] + [N]
+    return [(b[p], b[p + 1]) for p in range(parts)]
+
+
+def _local(xd, md, vis, a, b, dev):
+    rows = xd.shape[0]
+    lens = (torch.clamp(vis, max=b) - a).clamp(min=0).to(torch.int32).to(dev)
+    sx = xd[:, a:b].contiguous()
+    sm = md[:, a // 16: (b + 15) // 16].contiguous()
+    pt = (torch.arange(b - a, dtype=torch.int32, device=dev) + a).expand(rows, b - a)
+    return sx, sm, lens, pt
+
+
+def test_cp_bound_matches_oracle(hcu, dev):
+    """The sampled bound is bit-exact against its restatement: long and short rows, an empty
+    local range, a range smaller than the sample count, one where every token passes, and a range
+    too small to constrain the bound."""
+    rows, W = 10, 20000
+    x, mask, _, _ = make_scores(rows, W, "relu_sum", W=W, seed=31)
+    lens = torch.tensor([20000, 20000, 0, 1500, 300, 20000, 5000, 2049, 20000, 40], dtype=torch.int32)
+    totals = torch.tensor([160000, 20000, 50000, 1500, 2100, 2048, 9000, 100000, 40000, 100000], dtype=torch.int32)
+    ref = O.cp_local_bound(x.numpy(), mask.numpy(), lens.numpy(), totals.numpy())
+    got = hcu.cp_local_bound(x.to(dev), mask.to(dev), lens.to(dev), totals.to(dev)).cpu().numpy()
+    assert np.array_equal(got, ref)
+
+
+@pytest.mark.parametrize("cap", [1024, 2048])
+def test_cp_filter_matches_oracle(hcu, dev, cap):
+    rows, W = 10, 16384
+    x, mask, lens, _ = make_scores(rows, W, "ties", W=W, ragged=True, seed=cap)
+    pt = (torch.arange(W, dtype=torch.int32) + 5000).expand(rows, W)
+    totals = torch.full((rows,), 130000, dtype=torch.int32)
+    bounds = torch.from_numpy(O.cp_local_bound(x.numpy(), mask.numpy(), lens.numpy(), totals.numpy()))
+    bounds[3] = -2**31  # key 0: every token passes (overflows the list)
+    k, g, cnt, f = O.cp_filter(x.numpy(), mask.numpy(), lens.numpy(), pt.numpy(), bounds.numpy(), cap)
+    rps, P = 4, 3  # the rows land row-sharded in a [P, 2, rps, cap] exchange buffer
+    send = torch.full((P, 2, rps, cap), 7, dtype=torch.int32, device=dev)
+    flag = torch.zeros(1, dtype=torch.int32, device=dev)
+    hcu.cp_filter(x.to(dev), mask.to(dev), lens.to(dev), pt.to(dev), bounds.to(dev), send, flag)
+    s = send.cpu().numpy()
+    for r in range(rows):
+        assert np.array_equal(s[r // rps, 0, r % rps].view(np.uint32), k[r]), r
+        assert np.array_equal(s[r // rps, 1, r % rps], g[r]), r
+    assert int(flag.item()) == f == 1
+
+
+@pytest.mark.parametrize("parts", [2, 4, 8])
+@pytest.mark.parametrize("dist", ["relu_sum", "ties", "narrow"])
+def test_cp_bounded_exchange_on_one_gpu(hcu, dev, parts, dist):
+    """P ranges on one device through the bounded protocol (bounds -> MIN -> filter into row-sharded
+    buffers -> exchange by indexing -> merge) equal the single-range top-k exactly."""
+    from hcu_ops.cp import list_len
+
+    rows, N = 13, 32768
+    x, mask, _, _ = make_scores(rows, N, dist, W=N, seed=parts + 100)
+    vis = torch.tensor([N, 30000, 2048, 100, 6001, 2049, 1, 12000, 20000, 4097, 8191, 0, 25000], dtype=torch.int32)
+    ident = torch.arange(N, dtype=torch.int32).repeat(rows, 1)
+    full = O.topk_transform(x.numpy(), mask.numpy(), vis.numpy(), ident.numpy())
+    xd, md, visd = x.to(dev), mask.to(dev), vis.to(dev)
+    cap = list_len(parts)
+    rps = (rows + parts - 1) // parts
+    pad = rps * parts - rows
+    rng = _ranges(N, parts)
+    locs = [_local(xd, md, vis, a, b, dev) for a, b in rng]
+    bounds = torch.stack([hcu.cp_local_bound(sx, sm, lens, visd) for sx, sm, lens, _ in locs]).min(0).values
+    flag = torch.zeros(1, dtype=torch.int32, device=dev)
+    sends = []
+    for sx, sm, lens, pt in locs:
+        send = torch.empty((parts, 2, rps, cap), dtype=torch.int32, device=dev)
+        if pad:
+            send[parts - 1, 1, rps - pad:] = -1
+        hcu.cp_filter(sx, sm, lens, pt, bounds, send, flag)
+        sends.append(send)
+    vis_p = torch.cat([visd, torch.zeros(pad, dtype=torch.int32, device=dev)])
+    outs = []
+    for d in range(parts):
+        recv = torch.stack([sends[src][d] for src in range(parts)]).contiguous()
+        outs.append(hcu.cp_topk_merge_lists(recv, vis_p[d * rps:(d + 1) * rps].contiguous(), flag))
+    assert int(flag.item()) == 0
+    got = torch.cat(outs)[:rows].cpu().numpy()
+    assert np.array_equal(got, full)
+
+
+def test_cp_merge_lists_flags_a_missed_bound(hcu, dev):
+    """Lists holding fewer than 2048 entries for a long row raise the flag (not the device status)."""
+    rows, cap, P = 3, 1024, 2
+    recv = torch.full((P, 2, rows, cap), -1, dtype=torch.int32, device=dev)
+    recv[:, 0] = 5
+    recv[0, 1, :, :100] = torch.arange(100, dtype=torch.int32, device=dev)
+    lengths = torch.tensor([5000, 100, 2048], dtype=torch.int32, device=dev)
+    flag = torch.zeros(1, dtype=torch.int32, device=dev)
+    out = hcu.cp_topk_merge_lists(recv, lengths, flag).cpu().numpy()
+    assert int(flag.item()) == 1
+    assert hcu.read_device_status(clear=False) == 0
+    assert np.array_equal(out[1], np.where(np.arange(2048) < 100, np.arange(2048), -1))
+    assert np.array_equal(out[2], np.arange(2048))

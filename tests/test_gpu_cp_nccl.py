@@ -1,8 +1,9 @@
 """Context-parallel prefill over NCCL on 2 GPUs: every rank's result equals the 1-GPU result.
 
-Each rank scores its own KV range with the ragged logits kernel, selects a local top-2048 in
-token order, and the ranks exchange and merge the lists (row-sharded all-to-all, then an
-all-gather of the final indices; the all-gather mode is checked too).  Skipped with fewer
+Each rank scores its own KV range with the ragged logits kernel and the ranks exchange and merge
+per-range lists: the bounded lists (an all-reduce MIN of sampled bounds, then every token at or
+above the bound) or local top-2048 lists (the exact path), row-sharded all-to-all then an
+all-gather of the final indices; the all-gather mode is checked too.  Skipped with fewer
 than two visible GPUs.  Ranks are spawned processes with NVLS off and a short process-group
 timeout, so a rank that fails ends the others' collectives with an error instead of a wait."""
 import os
@@ -27,6 +28,7 @@ def _free_port():
 
 
 def _rank(rank, world, port, mode, q):
+    mode, _, variant = mode.partition(":")
     import datetime
     import sys
 
@@ -49,7 +51,7 @@ def _rank(rank, world, port, mode, q):
         lo, hi = kv_range(rank, world, N)
         out = cp_prefill_topk(w["q"].to(dev), w["k_fp8"][lo:hi].contiguous().to(dev),
                               w["k_scale"][lo:hi].contiguous().to(dev), w["weights"].to(dev),
-                              w["row_end"].to(dev), N, mode=mode)
+                              w["row_end"].to(dev), N, mode=mode, bounded=variant != "exact")
         torch.cuda.synchronize()
         q.put((rank, out.cpu().numpy()))
     except Exception as e:  # reported to the parent; the process group timeout ends the peer
@@ -60,7 +62,7 @@ def _rank(rank, world, port, mode, q):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("mode", ["rowshard", "allgather"])
+@pytest.mark.parametrize("mode", ["rowshard", "rowshard:exact", "allgather"])
 def test_cp_nccl_two_gpus_equals_one_gpu(hcu, dev, mode):
     from hcu_ops.cp import cp_prefill_topk
     from hcu_ops.workloads import make_ragged
