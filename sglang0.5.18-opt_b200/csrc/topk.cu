@@ -1188,8 +1188,6 @@ int split_count(int64_t rows, int64_t width, int64_t max_splits) {
 // than 2048 (the bound missed), falls back to 12/12/8-bit radix passes over all entries.
 // ---------------------------------------------------------------------------
 constexpr int kMaxParts = 16;
-constexpr int kTkThreads = 1024;  // one CTA per row
-constexpr int kCandCap = Tk<kTkThreads>::kCandCap;
 
 // Entry c of a row's concatenated lists: part c >> lshift, position c & (2^lshift - 1);
 // part p's list of row r starts at p * pstride + r * 2^lshift.
@@ -1199,7 +1197,8 @@ __device__ __forceinline__ int64_t merge_off(int c, int lshift, int64_t pstride,
 }
 
 // Radix-select fallback over every valid entry (entries [tid*per, (tid+1)*per) below n_ent).
-__device__ void merge_radix(TopkSmem<kTkThreads>& sm, const uint32_t* __restrict__ keys, const int32_t* __restrict__ gidx,
+template <int kT>
+__device__ void merge_radix(TopkSmem<kT>& sm, const uint32_t* __restrict__ keys, const int32_t* __restrict__ gidx,
                             int per, int n_ent, int lshift, int64_t pstride, int row, int32_t* __restrict__ out) {
   const int tid = threadIdx.x;
   const int c0 = tid * per;
@@ -1211,7 +1210,7 @@ __device__ void merge_radix(TopkSmem<kTkThreads>& sm, const uint32_t* __restrict
   for (int pass = 0; pass < 3; ++pass) {
     const int nb = pass < 2 ? kBins : 256;
     const int sh = pass == 0 ? 20 : (pass == 1 ? 8 : 0);
-    for (int i = tid; i < nb; i += kTkThreads) sm.hist[i] = 0;
+    for (int i = tid; i < nb; i += kT) sm.hist[i] = 0;
     __syncthreads();
     for (int i = 0; i < per; ++i) {
       const int64_t o = merge_off(c0 + i, lshift, pstride, row);
@@ -1221,9 +1220,9 @@ __device__ void merge_radix(TopkSmem<kTkThreads>& sm, const uint32_t* __restrict
     }
     __syncthreads();
     if (pass < 2)
-      find_threshold<kTkThreads, kBins>(sm.hist, need, sm.wtot, sm.res);
+      find_threshold<kT, kBins>(sm.hist, need, sm.wtot, sm.res);
     else
-      find_threshold<kTkThreads, 256>(sm.hist, need, sm.wtot, sm.res);
+      find_threshold<kT, 256>(sm.hist, need, sm.wtot, sm.res);
     pre = (pre << (pass < 2 ? 12 : 8)) | static_cast<uint32_t>(sm.res[0]);
     above += sm.res[1];
     need -= sm.res[1];
@@ -1239,7 +1238,7 @@ __device__ void merge_radix(TopkSmem<kTkThreads>& sm, const uint32_t* __restrict
     nt += v & (k == thr);
   }
   int total;
-  const int ex = block_excl_scan<kTkThreads>(na | (nt << 16), sm.wtot, &total);
+  const int ex = block_excl_scan<kT>(na | (nt << 16), sm.wtot, &total);
   int ea = ex & 0xFFFF, et = ex >> 16;
   for (int i = 0; i < per; ++i) {
     const int64_t o = merge_off(c0 + i, lshift, pstride, row);
@@ -1260,14 +1259,15 @@ __device__ void merge_radix(TopkSmem<kTkThreads>& sm, const uint32_t* __restrict
 // (a caller-side bound missed), instead of the sticky bad-input status;
 // short_identity: rows of at most kTopK visible tokens [0, len) output
 // 0, 1, .., len - 1 without reading the lists (identity page table).
-__global__ __launch_bounds__(kTkThreads, 1) void cp_merge_kernel(const uint32_t* __restrict__ keys,
+template <int kT>
+__global__ __launch_bounds__(kT, 1024 / kT) void cp_merge_kernel(const uint32_t* __restrict__ keys,
                                                                 const int32_t* __restrict__ gidx, int parts,
                                                                 int lshift, int64_t pstride,
                                                                 const int32_t* __restrict__ lengths,
                                                                 int32_t* __restrict__ dst, int32_t* __restrict__ flag,
                                                                 int short_identity) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  TopkSmem<kTkThreads>& sm = *reinterpret_cast<TopkSmem<kTkThreads>*>(smem_raw);
+  TopkSmem<kT>& sm = *reinterpret_cast<TopkSmem<kT>*>(smem_raw);
   const int row = blockIdx.x;
   const int tid = threadIdx.x;
   const int lane = tid & 31;
@@ -1276,21 +1276,21 @@ __global__ __launch_bounds__(kTkThreads, 1) void cp_merge_kernel(const uint32_t*
   if (short_identity) {
     const int vl = __ldg(lengths + row);
     if (vl <= kTopK) {
-      for (int i = tid; i < kTopK; i += kTkThreads) out[i] = i < vl ? i : -1;
+      for (int i = tid; i < kTopK; i += kT) out[i] = i < vl ? i : -1;
       return;
     }
   }
-  for (int i = tid; i < 2 * 512; i += kTkThreads) (&sm.hb[0][0])[i] = 0;
+  for (int i = tid; i < 2 * 512; i += kT) (&sm.hb[0][0])[i] = 0;
 
   const int n_ent = parts << lshift;  // entries of the row's concatenated lists
   // ---- A: lower bound lo from 2048 evenly spaced samples of the concatenated lists ----
-  for (int i = tid; i < kBins; i += kTkThreads) sm.hist[i] = 0;
+  for (int i = tid; i < kBins; i += kT) sm.hist[i] = 0;
   __syncthreads();
   constexpr int kMs = 2048;  // samples
-  uint32_t sk[kMs / kTkThreads];
+  uint32_t sk[kMs / kT];
 #pragma unroll
-  for (int j = 0; j < kMs / kTkThreads; ++j) {
-    const int c = static_cast<int>(static_cast<int64_t>(tid + j * kTkThreads) * n_ent / kMs) + n_ent / (2 * kMs);
+  for (int j = 0; j < kMs / kT; ++j) {
+    const int c = static_cast<int>(static_cast<int64_t>(tid + j * kT) * n_ent / kMs) + n_ent / (2 * kMs);
     const int64_t o = merge_off(min(c, n_ent - 1), lshift, pstride, row);
     sk[j] = __ldg(gidx + o) >= 0 ? __ldg(keys + o) : 0u;  // a missing entry ranks below every key
     atomicAdd(&sm.hist[sk[j] >> 20], 1);
@@ -1299,11 +1299,11 @@ __global__ __launch_bounds__(kTkThreads, 1) void cp_merge_kernel(const uint32_t*
   // sample rank (1 = largest) 4 sigma + 4 below the threshold's expected sample rank
   const float t = static_cast<float>(kMs) * static_cast<float>(kTopK) / static_cast<float>(n_ent);
   const int r_lo = min(kMs, static_cast<int>(ceilf(t + 4.f * sqrtf(t) + 4.f)));
-  find_threshold<kTkThreads, kBins>(sm.hist, r_lo, sm.wtot, sm.res);
+  find_threshold<kT, kBins>(sm.hist, r_lo, sm.wtot, sm.res);
   const uint32_t b1 = static_cast<uint32_t>(sm.res[0]);
   const int need = r_lo - sm.res[1];
 #pragma unroll
-  for (int j = 0; j < kMs / kTkThreads; ++j)
+  for (int j = 0; j < kMs / kT; ++j)
     if ((sk[j] >> 20) == b1) atomicAdd(&sm.hb[0][(sk[j] >> 12) & 0xFFu], 1);
   __syncthreads();
   if (w == 0) warp_find<256>(sm.hb[0], need, sm.res);
@@ -1314,7 +1314,7 @@ __global__ __launch_bounds__(kTkThreads, 1) void cp_merge_kernel(const uint32_t*
   if (short_row) lo = 0u;  // keep every entry
 
   // ---- B: entries with key >= lo, appended in global index order ----
-  const int per = (n_ent + kTkThreads - 1) / kTkThreads;  // <= 32
+  const int per = (n_ent + kT - 1) / kT;  // <= 32
   const int c0 = tid * per;
   // thread t: entries [t * per, (t + 1) * per), per <= 32; loads go out 8 at a time
   int na = 0, nv = 0;
@@ -1345,11 +1345,11 @@ __global__ __launch_bounds__(kTkThreads, 1) void cp_merge_kernel(const uint32_t*
     }
   }
   int packed_total;
-  const int packed = block_excl_scan<kTkThreads>(na | (nv << 16), sm.wtot, &packed_total);
+  const int packed = block_excl_scan<kT>(na | (nv << 16), sm.wtot, &packed_total);
   const int n = packed_total & 0xFFFF;
   const int total = static_cast<int>(static_cast<uint32_t>(packed_total) >> 16);
   int pos = packed & 0xFFFF;
-  if (n <= kCandCap) {
+  if (n <= Tk<kT>::kCandCap) {
     for (int i0 = 0; i0 < per && (cbits >> i0); i0 += 8) {
       uint32_t kk[8];
       int gg[8];
@@ -1388,17 +1388,17 @@ __global__ __launch_bounds__(kTkThreads, 1) void cp_merge_kernel(const uint32_t*
       else
         atomicOr(&g_hcu_status, HCU_STATUS_BAD_INPUT);
     }
-    for (int i = tid; i < kTopK; i += kTkThreads) out[i] = i < n && i < kCandCap ? sm.cand_pid[i] : -1;
+    for (int i = tid; i < kTopK; i += kT) out[i] = i < n && i < Tk<kT>::kCandCap ? sm.cand_pid[i] : -1;
     return;
   }
-  if (n > kCandCap || n < kTopK) {  // list overflow, or the sampled bound missed
+  if (n > Tk<kT>::kCandCap || n < kTopK) {  // list overflow, or the sampled bound missed
     merge_radix(sm, keys, gidx, per, n_ent, lshift, pstride, row, out);
     return;
   }
   // ---- C: select and ordered write over the candidates ----
   int above = 0;
   const uint32_t thr = select_candidates(sm, n, lo, &above);
-  write_candidates<kTkThreads, false>(sm, n, thr, above, out, nullptr);
+  write_candidates<kT, false>(sm, n, thr, above, out, nullptr);
 }
 // ---------------------------------------------------------------------------
 // Context-parallel candidate filter (the bounded exchange of hcu_ops/cp.py).
@@ -1653,9 +1653,12 @@ extern "C" int hcu_cp_topk_merge_lists(const uint32_t* keys, const int32_t* gidx
     return HCU_ERR_ARG;
   if (rows == 0) return HCU_OK;
   if (!keys || !gidx || !lengths || !dst) return HCU_ERR_ARG;
-  const size_t smem = sizeof(TopkSmem<kTkThreads>);
-  cudaFuncSetAttribute(cp_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-  cp_merge_kernel<<<static_cast<unsigned>(rows), kTkThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
+  // one 1024-thread CTA per row (a 512-thread instance, two CTAs per SM, measured slower: its
+  // 4096-entry candidate list overflows into the radix passes on the bounded exchange's lists)
+  const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const size_t smem = sizeof(TopkSmem<1024>);
+  cudaFuncSetAttribute(cp_merge_kernel<1024>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  cp_merge_kernel<1024><<<static_cast<unsigned>(rows), 1024, smem, st>>>(
       keys, gidx, static_cast<int>(n_parts), lshift, part_stride, lengths, dst, flag, short_identity);
   return launch_status();
 }
