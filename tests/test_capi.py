@@ -90,3 +90,28 @@ def test_merge_rejects_too_many_parts(lib):
     p = ctypes.c_void_p(16)
     assert f(p, p, ctypes.c_int64(17), ctypes.c_int64(4), p, p, None) == HCU_ERR_ARG
     assert f(p, p, ctypes.c_int64(2), ctypes.c_int64(0), p, p, None) == HCU_OK
+
+
+def test_cp_bounded_exchange_argument_checks(lib):
+    """The bounded-exchange entry points refuse bad shapes before launching anything."""
+    p = ctypes.c_void_p(16)
+    i64 = ctypes.c_int64
+    m = lib.hcu_cp_topk_merge_lists
+    m.restype = ctypes.c_int
+    # list length not a power of two / too short for 2048 entries / past 2048
+    assert m(p, p, i64(2), i64(1000), i64(4000), i64(2), p, None, ctypes.c_int32(1), p, None) == HCU_ERR_ARG
+    assert m(p, p, i64(2), i64(512), i64(1024), i64(2), p, None, ctypes.c_int32(1), p, None) == HCU_ERR_ARG
+    assert m(p, p, i64(2), i64(4096), i64(8192), i64(2), p, None, ctypes.c_int32(1), p, None) == HCU_ERR_ARG
+    assert m(p, p, i64(2), i64(2048), i64(100), i64(2), p, None, ctypes.c_int32(1), p, None) == HCU_ERR_ARG  # part stride
+    assert m(p, p, i64(2), i64(2048), i64(4096), i64(0), p, None, ctypes.c_int32(1), p, None) == HCU_OK  # no rows
+    f = lib.hcu_cp_filter
+    f.restype = ctypes.c_int
+    # cap past 2048, and a row block smaller than its lists
+    assert f(p, i64(4), i64(64), i64(64), p, i64(4), p, p, i64(0), p, i64(4096), p, p, i64(4), i64(0), None, p,
+             None) == HCU_ERR_ARG
+    assert f(p, i64(4), i64(64), i64(64), p, i64(4), p, p, i64(0), p, i64(2048), p, p, i64(2), i64(100), None, p,
+             None) == HCU_ERR_ARG
+    b = lib.hcu_cp_local_bound
+    b.restype = ctypes.c_int
+    assert b(p, i64(4), i64(64), i64(32), p, i64(4), p, p, p, None) == HCU_ERR_ARG  # stride below width
+    assert b(p, i64(0), i64(64), i64(64), p, i64(4), p, p, p, None) == HCU_OK
