@@ -550,14 +550,14 @@ def run_cp_prefill(args, world, rank, local):
     rows, prefix = 16384, 131072 - 16384
     w = _prefill_inputs(dev, rows, prefix, seed=0)  # identical on every rank (replicated q, full K generated)
     N = w["k_fp8"].shape[0]
-    lo, hi = kv_range(rank, world, N)
+    lo, hi = kv_range(rank, world, N, causal_rows=rows)  # ranges balanced by visible pairs
     kf = w["k_fp8"][lo:hi].contiguous()
     ks = w["k_scale"][lo:hi].contiguous()
     del w["k_fp8"], w["k_scale"]
     torch.cuda.empty_cache()
 
     def step():
-        return cp_prefill_topk(w["q"], kf, ks, w["weights"], w["row_end"], N)
+        return cp_prefill_topk(w["q"], kf, ks, w["weights"], w["row_end"], N, causal_rows=rows)
 
     for _ in range(max(min(args.warmup, 2), 1)):
         out = step()

@@ -423,9 +423,11 @@ def cp_filter(score: np.ndarray, nonzero_mask: np.ndarray, lengths: np.ndarray, 
               bounds: np.ndarray, cap: int):
     """Tokens of [0, len) with key >= the row's bound, in token order, as (key, page-table entry)
     lists of cap slots (key 0 / entry -1 pads).  A row with more than cap such tokens: with
-    cap = 2048, the range's top-2048 among them (canonical selection) in token order; otherwise,
-    or past the device's candidate capacity (4096 for widths up to 32768, else 8192), the flag.
-    Returns (keys uint32 [rows, cap], gidx int32 [rows, cap], counts int32 [rows], flag)."""
+    cap = 2048, the range's top-2048 among them (canonical selection) in token order; with
+    cap < 2048, its top-(cap - 1) in token order and a marker in the last slot (entry -2, key =
+    the (cap - 1)-th largest key); past the device's candidate capacity (4096 for widths up to
+    32768, else 8192) the flag.  Returns (keys uint32 [rows, cap], gidx int32 [rows, cap],
+    counts int32 [rows], flag)."""
     score = np.asarray(score, dtype=np.float32)
     rows, W = score.shape
     bits = mask_bits(nonzero_mask, W)
@@ -440,20 +442,29 @@ def cp_filter(score: np.ndarray, nonzero_mask: np.ndarray, lengths: np.ndarray, 
         sel = np.nonzero(k >= lo[r])[0]
         counts[r] = sel.shape[0]
         cand_cap = 4096 if W <= 32768 else 8192
-        if sel.shape[0] > cap and cap == TOPK and sel.shape[0] <= cand_cap:
-            sel = sel[np.sort(select_topk(k[sel]))]
+        marker = None
+        if cap < sel.shape[0] <= cand_cap:
+            kk = cap if cap == TOPK else cap - 1
+            order = np.argsort(~k[sel], kind="stable")
+            if kk < cap:
+                marker = k[sel][order[kk - 1]]
+            sel = sel[np.sort(select_topk(k[sel], kk))]
         else:
             flag |= int(sel.shape[0] > cap)
         kept = sel[:cap]
         keys[r, :kept.shape[0]] = k[kept]
         gidx[r, :kept.shape[0]] = np.asarray(page_table)[r, kept]
+        if marker is not None:
+            keys[r, cap - 1] = marker
+            gidx[r, cap - 1] = -2
     return keys, gidx, counts, flag
 
 
 def cp_merge_lists(keys: np.ndarray, gidx: np.ndarray, lengths: np.ndarray):
     """Merge of bounded lists ``[P, rows, C]``: rows of at most 2048 visible tokens are the
     identity 0..len-1 (device: short_identity); the others are ``cp_merge`` of their lists, and
-    a row whose lists hold fewer than 2048 entries raises the flag.  Returns (out, flag)."""
+    a row whose lists hold fewer than 2048 entries, or whose threshold (the 2048th largest key)
+    is not above a truncation marker's key (entry -2), raises the flag.  Returns (out, flag)."""
     rows = keys.shape[1]
     out = np.full((rows, TOPK), -1, np.int32)
     flag = 0
@@ -465,4 +476,9 @@ def cp_merge_lists(keys: np.ndarray, gidx: np.ndarray, lengths: np.ndarray):
             flag = 1  # the row's result is not defined; the caller reruns exactly
         else:
             out[r] = cp_merge(keys[:, r:r + 1], gidx[:, r:r + 1], lengths[r:r + 1])[0]
+            marks = keys[:, r, :][gidx[:, r, :] == -2]
+            if marks.size:
+                v = keys[:, r, :][gidx[:, r, :] >= 0]
+                thr = np.sort(v)[::-1][TOPK - 1]
+                flag |= int(marks.max() >= thr)
     return out, flag

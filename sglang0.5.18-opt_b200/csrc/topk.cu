@@ -86,6 +86,8 @@ struct __align__(16) TopkSmem {
   int wtot[32];
   int res[4];
   int ncand;  // split rows: this CTA's candidate count (read by the cluster's rank 0)
+  int mark_any;        // CP merge: some list of the row was truncated (marker entry -2)
+  uint32_t mark_max;   // CP merge: the largest marker key
 };
 static_assert(sizeof(TopkOutStage) <= sizeof(uint4) * 4 * 512, "fallback staging fits the scratch area");
 
@@ -414,12 +416,13 @@ __device__ __forceinline__ int collect_candidates(const float* __restrict__ vals
   return base;
 }
 
-// Threshold key of rank kTopK among the n candidates (kTopK <= n <= kCandCap,
+// Threshold key of rank k (kTopK by default) among the n candidates (k <= n <= kCandCap,
 // all keys >= lo): a radix select of u = key - lo with 9-bit digits from the
 // top bit of (largest candidate - lo) down.  *above = candidates with a
 // larger key.  sm.hb[0] and sm.hb[1] must be zero on entry.
 template <int kT>
-__device__ __forceinline__ uint32_t select_candidates(TopkSmem<kT>& sm, int n, uint32_t lo, int* above) {
+__device__ __forceinline__ uint32_t select_candidates(TopkSmem<kT>& sm, int n, uint32_t lo, int* above,
+                                                     int k = kTopK) {
   constexpr int kDigit = 9;
   const int tid = threadIdx.x;
   const int lane = tid & 31;
@@ -433,7 +436,7 @@ __device__ __forceinline__ uint32_t select_candidates(TopkSmem<kT>& sm, int n, u
   const uint32_t span = kmax - lo;
   const int d = span ? 31 - __clz(span) : 0;  // every u has no bit above d
   uint32_t pre = 0u;
-  int need = kTopK;
+  int need = k;
   int abv = 0;
   for (int s = d + 1 - kDigit, rnd = 0;; s -= kDigit, ++rnd) {
     const int sh = s > 0 ? s : 0;
@@ -458,13 +461,14 @@ __device__ __forceinline__ uint32_t select_candidates(TopkSmem<kT>& sm, int n, u
 }
 
 // Output from the candidate list: keys > thr in token order, then the first
-// kTopK - above ties in token order (kSorted: the same set in token order),
+// k - above ties in token order (kSorted: the same set in token order),
 // through the page-table entries copied during the candidate pass.
 // Candidate i goes to thread i / ceil(n / 1024).
 template <int kT, bool kSorted>
 __device__ __forceinline__ void write_candidates(TopkSmem<kT>& sm, int n, uint32_t thr, int above,
-                                                 int32_t* __restrict__ out, uint32_t* __restrict__ okeys) {
-  const int remaining = kTopK - above;
+                                                 int32_t* __restrict__ out, uint32_t* __restrict__ okeys,
+                                                 int k = kTopK) {
+  const int remaining = k - above;
   const int per = (n + kT - 1) / kT;
   const int i0 = min(n, static_cast<int>(threadIdx.x) * per);
   const int i1 = min(n, i0 + per);
@@ -1199,7 +1203,8 @@ __device__ __forceinline__ int64_t merge_off(int c, int lshift, int64_t pstride,
 // Radix-select fallback over every valid entry (entries [tid*per, (tid+1)*per) below n_ent).
 template <int kT>
 __device__ void merge_radix(TopkSmem<kT>& sm, const uint32_t* __restrict__ keys, const int32_t* __restrict__ gidx,
-                            int per, int n_ent, int lshift, int64_t pstride, int row, int32_t* __restrict__ out) {
+                            int per, int n_ent, int lshift, int64_t pstride, int row, int32_t* __restrict__ out,
+                            int32_t* __restrict__ flag) {
   const int tid = threadIdx.x;
   const int c0 = tid * per;
   per = max(0, min(per, n_ent - c0));
@@ -1229,6 +1234,7 @@ __device__ void merge_radix(TopkSmem<kT>& sm, const uint32_t* __restrict__ keys,
   }
   const uint32_t thr = pre;
   const int remaining = need;
+  if (threadIdx.x == 0 && flag && sm.mark_any && sm.mark_max >= thr) atomicOr(flag, 1);  // a truncated list
   int na = 0, nt = 0;
   for (int i = 0; i < per; ++i) {
     const int64_t o = merge_off(c0 + i, lshift, pstride, row);
@@ -1256,7 +1262,9 @@ __device__ void merge_radix(TopkSmem<kT>& sm, const uint32_t* __restrict__ keys,
 
 // Lists of 2^lshift entries per (part, row), part p at p * pstride; flag
 // (optional): set when a row longer than kTopK holds fewer than kTopK entries
-// (a caller-side bound missed), instead of the sticky bad-input status;
+// (a caller-side bound missed), instead of the sticky bad-input status, or
+// when the row's threshold is not above the key of a truncation marker (entry
+// -2: the largest key its list may have dropped);
 // short_identity: rows of at most kTopK visible tokens [0, len) output
 // 0, 1, .., len - 1 without reading the lists (identity page table).
 template <int kT>
@@ -1281,6 +1289,10 @@ __global__ __launch_bounds__(kT, 1024 / kT) void cp_merge_kernel(const uint32_t*
     }
   }
   for (int i = tid; i < 2 * 512; i += kT) (&sm.hb[0][0])[i] = 0;
+  if (tid == 0) {
+    sm.mark_any = 0;
+    sm.mark_max = 0u;
+  }
 
   const int n_ent = parts << lshift;  // entries of the row's concatenated lists
   // ---- A: lower bound lo from 2048 evenly spaced samples of the concatenated lists ----
@@ -1317,8 +1329,8 @@ __global__ __launch_bounds__(kT, 1024 / kT) void cp_merge_kernel(const uint32_t*
   const int per = (n_ent + kT - 1) / kT;  // <= 32
   const int c0 = tid * per;
   // thread t: entries [t * per, (t + 1) * per), per <= 32; loads go out 8 at a time
-  int na = 0, nv = 0;
-  uint32_t kmax = 0u, cbits = 0u;
+  int na = 0, nv = 0, mk = 0;
+  uint32_t kmax = 0u, cbits = 0u, mmax = 0u;
   for (int i0 = 0; i0 < per; i0 += 8) {
     uint32_t kk[8];
     int gg[8];
@@ -1341,6 +1353,9 @@ __global__ __launch_bounds__(kT, 1024 / kT) void cp_merge_kernel(const uint32_t*
           cbits |= 1u << (i0 + u);
           kmax = kk[u] > kmax ? kk[u] : kmax;
         }
+      } else if (gg[u] == -2) {  // marker of a truncated list: the largest key it may have dropped
+        mk = 1;
+        mmax = kk[u] > mmax ? kk[u] : mmax;
       }
     }
   }
@@ -1375,8 +1390,14 @@ __global__ __launch_bounds__(kT, 1024 / kT) void cp_merge_kernel(const uint32_t*
   for (int o = 16; o > 0; o >>= 1) {
     const uint32_t y = __shfl_xor_sync(0xffffffffu, kmax, o);
     kmax = y > kmax ? y : kmax;
+    const uint32_t z = __shfl_xor_sync(0xffffffffu, mmax, o);
+    mmax = z > mmax ? z : mmax;
   }
   if (lane == 0) sm.wmax[w] = kmax;
+  if (__any_sync(0xffffffffu, mk) && lane == 0) {
+    atomicOr(&sm.mark_any, 1);
+    atomicMax(&sm.mark_max, mmax);
+  }
   __syncthreads();
 
   if (short_row || total < kTopK) {
@@ -1392,12 +1413,13 @@ __global__ __launch_bounds__(kT, 1024 / kT) void cp_merge_kernel(const uint32_t*
     return;
   }
   if (n > Tk<kT>::kCandCap || n < kTopK) {  // list overflow, or the sampled bound missed
-    merge_radix(sm, keys, gidx, per, n_ent, lshift, pstride, row, out);
+    merge_radix(sm, keys, gidx, per, n_ent, lshift, pstride, row, out, flag);
     return;
   }
   // ---- C: select and ordered write over the candidates ----
   int above = 0;
   const uint32_t thr = select_candidates(sm, n, lo, &above);
+  if (tid == 0 && flag && sm.mark_any && sm.mark_max >= thr) atomicOr(flag, 1);  // a truncated list
   write_candidates<kT, false>(sm, n, thr, above, out, nullptr);
 }
 // ---------------------------------------------------------------------------
@@ -1512,7 +1534,9 @@ __global__ __launch_bounds__(kBoundWarps * 32) void cp_bound_kernel(
 // block_stride + (r % rows_per_block) * cap (so a row-sharded exchange buffer
 // is written in place); counts[row] (optional) = all such tokens.  More than
 // cap of them: with cap = kTopK the list holds the range's top-kTopK among them
-// (exact for the merge), else (or past the candidate capacity) *flag |= 1.
+// (exact for the merge); with cap < kTopK its top-(cap - 1) and a marker slot
+// (entry -2, key = the largest key it may have dropped) that the merge checks;
+// past the candidate capacity *flag |= 1.
 template <int kT, bool kVec>
 __global__ __launch_bounds__(kT, 1024 / kT) void cp_filter_kernel(
     const float* __restrict__ score, int64_t score_stride, int width, const int16_t* __restrict__ mask,
@@ -1541,19 +1565,27 @@ __global__ __launch_bounds__(kT, 1024 / kT) void cp_filter_kernel(
   const int64_t lo_off = (row / rows_per_block) * block_stride + static_cast<int64_t>(row % rows_per_block) * cap;
   uint32_t* ok = out_keys + lo_off;
   int32_t* og = out_gidx + lo_off;
-  if (n > cap && cap == kTopK && n <= Tk<kT>::kCandCap) {
-    // more candidates than slots: the range's exact top-kTopK among them, in token order, holds
-    // every token of the row's global top-kTopK that lies in this range
+  if (n > cap && n <= Tk<kT>::kCandCap) {
+    // More candidates than slots.  cap = kTopK: the range's exact top-kTopK among them, in token
+    // order, holds every token of the row's global top-kTopK that lies in this range.  cap < kTopK:
+    // its top-(cap - 1) in token order and, in the last slot, a marker (entry -2) whose key is the
+    // (cap - 1)-th largest key: every dropped token has a key <= it, and the merge accepts the
+    // row only when the global threshold is above every marker.
+    const int k = cap == kTopK ? kTopK : cap - 1;
     int above = 0;
-    const uint32_t thr = select_candidates(sm, n, lo, &above);
-    write_candidates<kT, true>(sm, n, thr, above, og, ok);
+    const uint32_t thr = select_candidates(sm, n, lo, &above, k);
+    write_candidates<kT, true>(sm, n, thr, above, og, ok, k);
+    if (k < cap && tid == 0) {
+      ok[cap - 1] = thr;
+      og[cap - 1] = -2;
+    }
   } else {
     const int kept = min(n, cap);  // cap <= kTopK <= kCandCap: every kept entry is in the list
     for (int i = tid; i < cap; i += kT) {
       ok[i] = i < kept ? sm.cand_key[i] : 0u;
       og[i] = i < kept ? sm.cand_pid[i] : -1;
     }
-    if (tid == 0 && n > cap) atomicOr(flag, 1);
+    if (tid == 0 && n > cap) atomicOr(flag, 1);  // past the candidate capacity
   }
   if (tid == 0 && counts) counts[row] = n;
 }

@@ -12,14 +12,16 @@ ranks exchange and merge those lists:
   The lists are bounded (``bounded=True``, default): instead of a local
   top-2048, each rank keeps the tokens at or above the row's bound b, the
   minimum over ranks of a sampled estimate of the row's global threshold on
-  each range (one all-reduce MIN of an int32 per row), in lists of 2048 entries
-  (a range with more tokens at or above b sends its top-2048 among them: every
-  token of the row's global top-2048 in that range is one of them).  The union
-  is exact when every row holds at least 2048 entries (then the global
-  threshold is >= b); the merge flags the rows where that fails (and the filter
-  a range past its candidate capacity), one all-reduce MAX of the flag tells
-  every rank, and the step then reruns with local top-2048 lists (the exact
-  path).
+  each range (one all-reduce MIN of an int32 per row), in lists of C entries
+  (``list_len``: 2048, or 1024 from 8 ranks on).  A range with more tokens at or
+  above b sends its top-2048 among them when C = 2048 (every token of the row's
+  global top-2048 in that range is one of them), else its top-(C - 1) and a
+  marker carrying the largest key it may have dropped.  The union is exact when
+  every row holds at least 2048 entries (then the global threshold is >= b) and
+  the row's threshold is above every marker; the merge flags the rows where that
+  fails (and the filter a range past its candidate capacity), one all-reduce MAX
+  of the flag tells every rank, and the step then reruns with local top-2048
+  lists (the exact path).
 * ``mode="allgather"``: every rank all-gathers all lists and merges all rows.
 
 The global top-2048 under (key desc, global index asc) is a subset of the union
@@ -79,10 +81,44 @@ class CudaOps:
         return cp_topk_merge(keys, gidx, lengths)
 
 
-def kv_range(rank: int, world: int, n_tokens: int):
-    """Contiguous KV range of a rank; boundaries are multiples of 16 (mask words stay aligned)."""
+def kv_range(rank: int, world: int, n_tokens: int, causal_rows: int = 0):
+    """Contiguous KV range of a rank; boundaries are multiples of 16 (mask words stay aligned).
+
+    ``causal_rows = 0``: equal token counts.  ``causal_rows = R``: the query rows are the last R
+    positions of the context (row i sees tokens [0, n_tokens - R + i + 1)), and the boundaries
+    give every rank about the same number of visible (row, token) pairs, so the rank that holds
+    the causal triangle takes a longer range instead of idling."""
+    if rank >= world:
+        return n_tokens, n_tokens
+    if causal_rows <= 0:
+        def b(r):
+            return (n_tokens * r // world) // 16 * 16 if r < world else n_tokens
+        return b(rank), b(rank + 1)
+    R = min(int(causal_rows), n_tokens)
+    p = n_tokens - R
+
+    def pairs(x):  # visible pairs in [0, x)
+        if x <= p:
+            return R * x
+        d = x - p
+        return R * p + d * (d + 1) // 2 + (R - d) * d
+
+    total = pairs(n_tokens)
+
     def b(r):
-        return (n_tokens * r // world) // 16 * 16 if r < world else n_tokens
+        if r <= 0:
+            return 0
+        if r >= world:
+            return n_tokens
+        target = total * r // world
+        lo, hi = 0, n_tokens  # smallest x with pairs(x) >= target, then down to a multiple of 16
+        while lo < hi:
+            mid = (lo + hi) // 2
+            if pairs(mid) >= target:
+                hi = mid
+            else:
+                lo = mid + 1
+        return lo // 16 * 16
 
     return b(rank), b(rank + 1)
 
@@ -93,21 +129,22 @@ def local_rows(row_end: torch.Tensor, lo: int, hi: int) -> torch.Tensor:
 
 
 def list_len(world: int) -> int:
-    """Slots per (rank, row) list of the bounded exchange: 2048 (a range may hold a whole row's
-    top-2048).  HCU_CP_LIST_LEN (a power of two in [256, 2048], times world >= 2048) trades
-    exchange bytes for the exact rerun whenever a range has more candidates than that."""
+    """Slots per (rank, row) list of the bounded exchange: 2048 below 8 ranks, 1024 from 8 on
+    (HCU_CP_LIST_LEN overrides: a power of two in [256, 2048], times world >= 2048).  A shorter
+    list that overflows is truncated to its top entries plus a marker holding the largest key it
+    may have dropped; the merge checks the row's threshold against it (a rerun when not above)."""
     import os
 
     env = os.environ.get("HCU_CP_LIST_LEN")
-    return int(env) if env else 2048
+    return int(env) if env else (1024 if world >= 8 else 2048)
 
 
 def cp_prefill_topk(q, k_fp8_local, k_scale_local, weights, row_end, n_tokens, group=None, mode="rowshard",
-                    ops=None, bounded=True):
+                    ops=None, bounded=True, causal_rows=0):
     """Global top-2048 token indices of every query row, computed over P KV ranges.
 
     q: fp8 ``[rows, H, 128]`` (replicated); ``k_fp8_local``/``k_scale_local``: this rank's
-    KV range ``kv_range(rank, P, n_tokens)``; ``row_end``: int32 ``[rows]`` global visible end
+    KV range ``kv_range(rank, P, n_tokens, causal_rows)``; ``row_end``: int32 ``[rows]`` global visible end
     (row r sees tokens ``[0, row_end[r])``).  Returns int32 ``[rows, 2048]`` (-1 pads) on
     every rank.  Every rank takes the same collective steps in the same order.
     """
@@ -116,7 +153,7 @@ def cp_prefill_topk(q, k_fp8_local, k_scale_local, weights, row_end, n_tokens, g
     rank = dist.get_rank(group) if dist.is_initialized() else 0
     rows = q.shape[0]
     dev = q.device
-    lo, hi = kv_range(rank, world, n_tokens)
+    lo, hi = kv_range(rank, world, n_tokens, causal_rows)
     assert k_fp8_local.shape[0] == hi - lo, "local K does not match this rank's range"
     lens = local_rows(row_end, lo, hi)
     zeros = torch.zeros_like(lens)

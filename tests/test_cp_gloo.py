@@ -98,6 +98,8 @@ def _worker(rank, world, port, mode, variant, q):
         sys.path.insert(0, p)
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
+    if variant == "short_lists":  # 1024-slot lists: truncated lists and their markers
+        os.environ["HCU_CP_LIST_LEN"] = "1024"
     import datetime
 
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
@@ -107,10 +109,12 @@ def _worker(rank, world, port, mode, variant, q):
 
         w = make_ragged(23, 2600, heads=32, seed=11)  # same seed on every rank: replicated q
         N = w["k_fp8"].shape[0]
-        lo, hi = kv_range(rank, world, N)
+        cr = 23 if variant == "balanced" else 0
+        lo, hi = kv_range(rank, world, N, causal_rows=cr)
         ops = {"miss": MissOps, "overflow": OverflowOps}.get(variant, OracleOps)()
         out = cp_prefill_topk(w["q"], w["k_fp8"][lo:hi].contiguous(), w["k_scale"][lo:hi].contiguous(),
-                              w["weights"], w["row_end"], N, mode=mode, ops=ops, bounded=variant != "exact")
+                              w["weights"], w["row_end"], N, mode=mode, ops=ops, bounded=variant != "exact",
+                              causal_rows=cr)
         q.put((rank, out.numpy()))
     finally:
         dist.destroy_process_group()
@@ -119,11 +123,12 @@ def _worker(rank, world, port, mode, variant, q):
 @pytest.mark.parametrize("world,mode,variant", [(1, "rowshard", "bounded"), (2, "rowshard", "bounded"),
                                                 (2, "rowshard", "exact"), (2, "allgather", "exact"),
                                                 (3, "rowshard", "bounded"), (2, "rowshard", "miss"),
-                                                (3, "rowshard", "overflow")])
+                                                (3, "rowshard", "overflow"), (3, "rowshard", "balanced"),
+                                                (2, "rowshard", "short_lists")])
 def test_cp_driver_equals_single_range(world, mode, variant):
     """Every rank's result equals the single-range top-k: the bounded exchange, the exact one,
     and the bounded exchange whose bound misses (too high) or overflows the lists (too low),
-    which every rank detects and reruns exactly."""
+    which every rank detects and reruns exactly; and ranges balanced by visible pairs."""
     from hcu_ops.workloads import make_ragged
     from oracle import indexer as O
 

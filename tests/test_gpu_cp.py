@@ -71,7 +71,10 @@ def test_cp_filter_matches_oracle(hcu, dev, cap):
     pt = (torch.arange(W, dtype=torch.int32) + 5000).expand(rows, W)
     totals = torch.full((rows,), 130000, dtype=torch.int32)
     bounds = torch.from_numpy(O.cp_local_bound(x.numpy(), mask.numpy(), lens.numpy(), totals.numpy()))
-    bounds[3] = -2**31  # key 0: every token passes (overflows the list)
+    bounds[3] = -2**31  # key 0: every token passes (past the candidate capacity: the flag)
+    kr = np.sort(np.where(O.mask_bits(mask.numpy(), W)[5, :int(lens[5])], O.to_key(x.numpy()[5, :int(lens[5])]),
+                          O.ZERO_KEY).astype(np.uint32))[::-1]
+    bounds[5] = int(np.int64(kr[3000]) - 2**31)  # ~3000 candidates: more than the slots, within capacity
     k, g, cnt, f = O.cp_filter(x.numpy(), mask.numpy(), lens.numpy(), pt.numpy(), bounds.numpy(), cap)
     rps, P = 4, 3  # the rows land row-sharded in a [P, 2, rps, cap] exchange buffer
     send = torch.full((P, 2, rps, cap), 7, dtype=torch.int32, device=dev)
@@ -84,20 +87,11 @@ def test_cp_filter_matches_oracle(hcu, dev, cap):
     assert int(flag.item()) == f == 1
 
 
-@pytest.mark.parametrize("parts", [2, 4, 8])
-@pytest.mark.parametrize("dist", ["relu_sum", "ties", "narrow"])
-def test_cp_bounded_exchange_on_one_gpu(hcu, dev, parts, dist):
+def _bounded_on_one_gpu(hcu, dev, x, mask, vis, parts, cap):
     """P ranges on one device through the bounded protocol (bounds -> MIN -> filter into row-sharded
-    buffers -> exchange by indexing -> merge) equal the single-range top-k exactly."""
-    from hcu_ops.cp import list_len
-
-    rows, N = 13, 32768
-    x, mask, _, _ = make_scores(rows, N, dist, W=N, seed=parts + 100)
-    vis = torch.tensor([N, 30000, 2048, 100, 6001, 2049, 1, 12000, 20000, 4097, 8191, 0, 25000], dtype=torch.int32)
-    ident = torch.arange(N, dtype=torch.int32).repeat(rows, 1)
-    full = O.topk_transform(x.numpy(), mask.numpy(), vis.numpy(), ident.numpy())
+    buffers -> exchange by indexing -> merge); returns (result rows, flag)."""
+    rows, N = x.shape
     xd, md, visd = x.to(dev), mask.to(dev), vis.to(dev)
-    cap = list_len(parts)
     rps = (rows + parts - 1) // parts
     pad = rps * parts - rows
     rng = _ranges(N, parts)
@@ -116,9 +110,41 @@ def test_cp_bounded_exchange_on_one_gpu(hcu, dev, parts, dist):
     for d in range(parts):
         recv = torch.stack([sends[src][d] for src in range(parts)]).contiguous()
         outs.append(hcu.cp_topk_merge_lists(recv, vis_p[d * rps:(d + 1) * rps].contiguous(), flag))
-    assert int(flag.item()) == 0
-    got = torch.cat(outs)[:rows].cpu().numpy()
+    return torch.cat(outs)[:rows].cpu().numpy(), int(flag.item())
+
+
+@pytest.mark.parametrize("parts", [2, 4, 8])
+@pytest.mark.parametrize("dist", ["relu_sum", "ties", "narrow"])
+def test_cp_bounded_exchange_on_one_gpu(hcu, dev, parts, dist):
+    """The bounded exchange with 2048-slot lists equals the single-range top-k exactly, also for rows
+    that one range holds almost entirely."""
+    rows, N = 13, 32768
+    x, mask, _, _ = make_scores(rows, N, dist, W=N, seed=parts + 100)
+    vis = torch.tensor([N, 30000, 2048, 100, 6001, 2049, 1, 12000, 20000, 4097, 8191, 0, 25000], dtype=torch.int32)
+    ident = torch.arange(N, dtype=torch.int32).repeat(rows, 1)
+    full = O.topk_transform(x.numpy(), mask.numpy(), vis.numpy(), ident.numpy())
+    got, flag = _bounded_on_one_gpu(hcu, dev, x, mask, vis, parts, 2048)
+    assert flag == 0
     assert np.array_equal(got, full)
+
+
+@pytest.mark.parametrize("dist", ["relu_sum", "ties"])
+def test_cp_truncated_lists(hcu, dev, dist):
+    """1024-slot lists at P = 8 (the default there): long rows spread over the ranges merge exactly
+    with no flag; a row that one range holds almost entirely overflows its list, whose marker is not
+    below the row's threshold, and the merge raises the flag (the caller's rerun)."""
+    rows, N, parts = 12, 65536, 8
+    x, mask, _, _ = make_scores(rows, N, dist, W=N, seed=7)
+    ident = torch.arange(N, dtype=torch.int32).repeat(rows, 1)
+    vis = torch.tensor([N, 60000, 50000, 40000, 65000, 33000, 64000, 58000, 45000, 38000, 62000, 36000],
+                       dtype=torch.int32)
+    full = O.topk_transform(x.numpy(), mask.numpy(), vis.numpy(), ident.numpy())
+    got, flag = _bounded_on_one_gpu(hcu, dev, x, mask, vis, parts, 1024)
+    assert flag == 0
+    assert np.array_equal(got, full)
+    vis[3] = 7000  # range 0 (8192 tokens) holds the whole row: its 1023rd largest key is above the threshold
+    _, flag = _bounded_on_one_gpu(hcu, dev, x, mask, vis, parts, 1024)
+    assert flag == 1
 
 
 def test_cp_merge_lists_flags_a_missed_bound(hcu, dev):

@@ -48,10 +48,11 @@ def _rank(rank, world, port, mode, q):
 
         w = make_ragged(ROWS, PREFIX, heads=64, seed=5)
         N = w["k_fp8"].shape[0]
-        lo, hi = kv_range(rank, world, N)
+        cr = ROWS if variant == "balanced" else 0
+        lo, hi = kv_range(rank, world, N, causal_rows=cr)
         out = cp_prefill_topk(w["q"].to(dev), w["k_fp8"][lo:hi].contiguous().to(dev),
                               w["k_scale"][lo:hi].contiguous().to(dev), w["weights"].to(dev),
-                              w["row_end"].to(dev), N, mode=mode, bounded=variant != "exact")
+                              w["row_end"].to(dev), N, mode=mode, bounded=variant != "exact", causal_rows=cr)
         torch.cuda.synchronize()
         q.put((rank, out.cpu().numpy()))
     except Exception as e:  # reported to the parent; the process group timeout ends the peer
@@ -62,7 +63,7 @@ def _rank(rank, world, port, mode, q):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("mode", ["rowshard", "rowshard:exact", "allgather"])
+@pytest.mark.parametrize("mode", ["rowshard", "rowshard:exact", "rowshard:balanced", "allgather"])
 def test_cp_nccl_two_gpus_equals_one_gpu(hcu, dev, mode):
     from hcu_ops.cp import cp_prefill_topk
     from hcu_ops.workloads import make_ragged
