@@ -242,6 +242,14 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_paged_kernel(const _
       sm.count = static_cast<int>(end - begin);
     }
   }
+  // Mask words past each row's processed tiles (the tiles write their own words): zeroed here,
+  // rows strided over the grid, by every CTA (also those without tiles), instead of a memset.
+  for (int row = blockIdx.x; row < p.batch; row += gridDim.x) {
+    const int tiles = (group_len(p, row / p.G) + kTileTok - 1) / kTileTok;
+    uint32_t* mw = reinterpret_cast<uint32_t*>(p.mask) + static_cast<int64_t>(row) * (p.width / 32);
+    for (int wd = tiles * (kTileTok / 32) + static_cast<int>(threadIdx.x); wd < p.width / 32; wd += blockDim.x)
+      mw[wd] = 0u;
+  }
   __syncthreads();
   const int count = sm.count;
   if (count <= 0) return;  // uniform: before any barrier init or TMEM allocation
@@ -539,6 +547,9 @@ __global__ __launch_bounds__(kLgThreads, 1) void mqa_logits_paged_kernel(const _
     }
   }
 
+  // Programmatic dependent launch: the next kernel of the stream (the top-k) may be scheduled once
+  // every CTA got here; it still waits (griddepcontrol.wait) for this grid's completion and writes.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
@@ -982,9 +993,6 @@ extern "C" int hcu_mqa_logits_hist(const uint8_t* q, int64_t batch, int64_t head
   int64_t R = std::min<int64_t>(group_size, kMaxN / heads);
   if (rows_per_cta > 0 && rows_per_cta < R) R = rows_per_cta;
   const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const int64_t mask_words = max_context_len / 16;
-  if (cudaMemsetAsync(mask, 0, static_cast<size_t>(batch * mask_words) * sizeof(int16_t), st) != cudaSuccess)
-    return launch_status();
   CUtensorMap tkv, tsc, tq;
   if (!make_map_pages(&tkv, kv_cache, static_cast<uint64_t>(n_pages), static_cast<uint64_t>(page_stride)))
     return map_error("kv_cache pages");

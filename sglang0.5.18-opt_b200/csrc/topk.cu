@@ -574,6 +574,9 @@ __global__ __launch_bounds__(kT, 1024 / kT) void topk_row_kernel(
   constexpr int kHistTrash = Tk<kT>::kHistTrash;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   TopkSmem<kT>& sm = *reinterpret_cast<TopkSmem<kT>*>(smem_raw);
+  // launched with programmatic stream serialization: wait for the previous kernel (the logits that
+  // this reads) to complete before the first global read; a no-op after an ordinary dependency
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int row = kSplit ? static_cast<int>(blockIdx.x) / splits : static_cast<int>(blockIdx.x);
   const int rank = kSplit ? static_cast<int>(blockIdx.x) % splits : 0;
   const int tid = threadIdx.x;
@@ -1056,10 +1059,21 @@ void launch_rows_t(const float* score, int rows, int width, int64_t score_stride
                    uint32_t* dst_keys, const int32_t* pre_ws, cudaStream_t stream, int splits) {
   const size_t smem = sizeof(TopkSmem<kT>);
   if (kSorted || splits <= 1) {
-    cudaFuncSetAttribute(topk_row_kernel<kT, kVec, kSorted, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         static_cast<int>(smem));
-    topk_row_kernel<kT, kVec, kSorted, false><<<rows, kT, smem, stream>>>(
-        score, score_stride, width, mask, mask_stride, lengths, pt, pt_stride, dst, dst_keys, pre_ws, rows, 1);
+    // programmatic stream serialization: the grid may be scheduled while the previous kernel drains
+    auto kern = topk_row_kernel<kT, kVec, kSorted, false>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(rows));
+    cfg.blockDim = dim3(kT);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kern, score, score_stride, width, mask, mask_stride, lengths, pt, pt_stride, dst,
+                       dst_keys, pre_ws, rows, 1);
     return;
   }
   if constexpr (!kSorted) launch_split<kT, kVec>(score, rows, width, score_stride, mask, mask_stride, lengths, pt,
