@@ -46,11 +46,13 @@ constexpr int kSmallSample = 2048;  // row samples used to bound the threshold (
 constexpr int kSample = 8192;       // sample count for rows > 512K
 constexpr int kLaneTok = 16;        // consecutive tokens per lane in a streaming round
 constexpr int kNarrowWidth = 32768; // rows up to this width run the 512-thread kernel (two CTAs per SM)
+constexpr int kManyRowsWidth = 98304;  // ... and up to this width when the rows fill the SMs twice over
 constexpr int kMaxClusterSplits = 8;  // CTAs per row of a split row (portable cluster size)
 constexpr int kSplitMinTok = 8192;    // a split row gives each CTA at least this many visible tokens
 
 // Per-CTA-size constants: 1024 threads (one CTA per SM) for wide rows, 512 threads for
-// narrow ones, so that two CTAs per SM overlap their rows' latency-bound phases.
+// narrow ones (and for rows up to 96K tokens when there are at least two rows per SM), so
+// that two CTAs per SM overlap their rows' latency-bound phases.
 template <int kT>
 struct Tk {
   static constexpr int kWarps = kT / 32;
@@ -1162,8 +1164,11 @@ int launch_rows(const float* score, int64_t rows, int64_t width, int64_t score_s
   const int w = static_cast<int>(width);
   const int r = static_cast<int>(rows);
   const bool vec = use_vec(score, width, score_stride);
-  // narrow rows (or row parts): 512 threads, two CTAs per SM
-  if ((width + splits - 1) / splits <= kNarrowWidth)
+  // narrow rows (or row parts), or rows up to 96K tokens when there are at least two per SM: 512
+  // threads, two CTAs per SM (their latency-bound phases overlap; past 96K tokens the 4096-entry
+  // candidate list of the 512-thread instance overflows too often)
+  const int64_t part = (width + splits - 1) / splits;
+  if (part <= kNarrowWidth || (rows >= 2 * static_cast<int64_t>(sm_count()) && part <= kManyRowsWidth))
     launch_rows_sized<512>(score, r, w, score_stride, mask, mask_stride, lengths, pt, pt_stride, dst, dst_keys, pre_ws,
                            stream, vec, sorted, splits);
   else
@@ -1773,7 +1778,7 @@ extern "C" int hcu_cp_filter(const float* score, int64_t rows, int64_t width, in
   const int rpb = static_cast<int>(rows_per_block);
   const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const bool vec = use_vec(score, width, score_stride);
-  if (width <= kNarrowWidth) {
+  if (width <= kNarrowWidth || (rows >= 2 * static_cast<int64_t>(sm_count()) && width <= kManyRowsWidth)) {
     if (vec)
       launch_filter<512, true>(score, r, w, score_stride, mask, mask_stride, lengths, page_table, pt_stride, bounds, c,
                                keys, gidx, rpb, block_stride, counts, flag, s);

@@ -70,6 +70,16 @@ def test_topk_split_rows_mixed_lengths(hcu, dev, dist):
         assert np.array_equal(out.cpu().numpy(), ref), (name, dist)
 
 
+@pytest.mark.parametrize("dist", ["relu_sum", "ties", "sparse2"])
+def test_topk_many_rows_up_to_96k(hcu, dev, dist):
+    """Rows of 60K tokens, more than two per SM: the 512-thread instance (two CTAs per SM)."""
+    rows = 2 * torch.cuda.get_device_properties(dev).multi_processor_count + 7
+    x, mask, lens, pt = make_scores(rows, 60000, dist, W=60032, ragged=True, seed=41)
+    ref = O.topk_transform(x.numpy(), mask.numpy(), lens.numpy(), pt.numpy())
+    for name, out in _run_all(hcu, x, mask, lens, pt, dev).items():
+        assert np.array_equal(out.cpu().numpy(), ref), (name, dist)
+
+
 def test_topk_split_pre_uses_pass1_workspace(hcu, dev):
     x, mask, lens, pt = make_scores(6, 20000, "relu_sum", W=20480, ragged=True, seed=9)
     lens[2] = 1500
