@@ -88,6 +88,30 @@ int hcu_dequant_index_k_paged(const uint8_t* kv_cache, int64_t n_pages, int64_t 
                               const int32_t* token_loc, int64_t n_tokens, uint16_t* out,
                               hcu_stream_t stream);
 
+/* MLA decode front end in one launch (replaces _C.rope_qout_kv_store,
+ * hcu_ops/csrc/mla_kv.cu:183-240 / bind.cpp:32): for each of n_tokens tokens,
+ *   q_out[t, h] = rope(q_pe[t, h]) for the nq heads (q_out may be q_pe itself);
+ *   kv_c[t] = bf16((x * rstd) * w), rstd = rsqrt(sum(x^2) / 512 + norm_eps), in place
+ *     (rsqrt_mode 2: 1 / sqrtf, IEEE; modes 0 and 1: rsqrtf);
+ *   k_pe[t] = rope(k_pe[t]) in place;
+ *   for t < n_loc, the 656-byte slot kv_buffer[loc[t]]: the fp8 e4m3 bytes of kv_c[t] in four
+ *     128-element groups (scale = max(amax, store_eps) / 448, bytes of y * (1 / scale), round to
+ *     nearest even, saturated), the four fp32 scales at +512, the rotated k_pe as bf16 at +528.
+ * rope: bf16 [*, 64] with cos_sin_cache[pos] = 32 cos then 32 sin (bf16); pairs (2r, 2r+1), or
+ * (r, 32 + r) with is_neox; every product and the difference / sum rounded to bf16.
+ * All tensors bf16 except positions (int32, or int64 with positions_int64), loc (int64) and
+ * kv_buffer (uint8); strides in elements.  kv_c rows and kv_weight 16-byte aligned
+ * (kv_tok % 8 == 0); kv_buffer 16-byte aligned with slot_stride % 16 == 0, >= 656.  A position
+ * outside [0, n_pos) skips its token, a slot outside [0, n_slots) is not written; both set
+ * HCU_STATUS_BAD_INPUT. */
+int hcu_rope_qout_kv_store(const void* positions, int32_t positions_int64, int64_t n_tokens, const uint16_t* q_pe,
+                           int64_t nq, int64_t q_tok, int64_t q_head, uint16_t* q_out, int64_t qo_tok,
+                           int64_t qo_head, uint16_t* kv_c, int64_t kv_tok, const uint16_t* kv_weight,
+                           float norm_eps, uint16_t* k_pe, int64_t k_tok, const uint16_t* cos_sin_cache,
+                           int64_t n_pos, int32_t is_neox, uint8_t* kv_buffer, int64_t n_slots,
+                           int64_t slot_stride, const int64_t* loc, int64_t n_loc, float store_eps,
+                           int32_t rsqrt_mode, hcu_stream_t stream);
+
 /* Indexer-K cache writer (no counterpart among the reference's sources: sglang's
  * store is not vendored; this produces the page layout the logits op reads,
  * hcu_ops/csrc/mqa_hist.cu:77-91).  Per token: scale = max(amax, 1e-12) / 448,

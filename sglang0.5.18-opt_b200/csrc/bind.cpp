@@ -265,6 +265,50 @@ torch::Tensor quant_store_index_k(const torch::Tensor& k, const torch::Tensor& t
   return kv_cache;
 }
 
+// kv_c [T, 512] / [T, 1, 512] and k_pe [T, 64] / [T, 1, 64]: the row stride of dim 0.
+int64_t row_stride(const torch::Tensor& x, int64_t width) {
+  TORCH_CHECK(x.size(-1) == width && x.stride(-1) == 1 && (x.dim() == 2 || (x.dim() == 3 && x.size(1) == 1)),
+              "expected [T, ", width, "] or [T, 1, ", width, "] with a unit last stride");
+  return x.stride(0);
+}
+
+void rope_qout_kv_store(const torch::Tensor& positions, const torch::Tensor& q_pe, torch::Tensor& q_out,
+                        torch::Tensor& kv_c, const torch::Tensor& kv_weight, double norm_eps, torch::Tensor& k_pe,
+                        const torch::Tensor& cos_sin_cache, bool is_neox, torch::Tensor& kv_buffer,
+                        const torch::Tensor& loc, double store_eps, int64_t rsqrt_mode) {
+  const int64_t T = positions.numel();
+  TORCH_CHECK(positions.is_cuda() && positions.is_contiguous() &&
+                  (positions.scalar_type() == at::kLong || positions.scalar_type() == at::kInt),
+              "rope_qout_kv_store: positions must be contiguous int32/int64");
+  const auto bf = at::kBFloat16;
+  TORCH_CHECK(q_pe.scalar_type() == bf && q_out.scalar_type() == bf && kv_c.scalar_type() == bf &&
+                  kv_weight.scalar_type() == bf && k_pe.scalar_type() == bf && cos_sin_cache.scalar_type() == bf,
+              "rope_qout_kv_store: bf16 only");
+  TORCH_CHECK(q_pe.dim() == 3 && q_pe.size(0) == T && q_pe.size(2) == 64 && q_pe.stride(2) == 1 &&
+                  q_out.sizes() == q_pe.sizes() && q_out.stride(2) == 1,
+              "rope_qout_kv_store: q_pe / q_out must be [T, nq, 64] with a unit last stride");
+  TORCH_CHECK(cos_sin_cache.is_contiguous() && cos_sin_cache.dim() == 2 && cos_sin_cache.size(1) == 64,
+              "rope_qout_kv_store: cos_sin_cache must be a contiguous [max_pos, 64]");
+  TORCH_CHECK(kv_c.size(0) == T && k_pe.size(0) == T, "rope_qout_kv_store: kv_c / k_pe must have T rows");
+  const int64_t kv_tok = row_stride(kv_c, 512), k_tok = row_stride(k_pe, 64);
+  TORCH_CHECK(kv_weight.is_contiguous() && kv_weight.numel() == 512, "rope_qout_kv_store: weight must be [512]");
+  TORCH_CHECK(kv_buffer.scalar_type() == at::kByte && kv_buffer.dim() >= 2 &&
+                  kv_buffer.numel() / std::max<int64_t>(kv_buffer.size(0), 1) >= 656,
+              "rope_qout_kv_store: kv_buffer must be uint8 with >= 656 bytes a slot");
+  TORCH_CHECK(loc.scalar_type() == at::kLong && loc.is_contiguous() && loc.numel() <= T,
+              "rope_qout_kv_store: loc must be a contiguous int64 of at most T slots");
+  const c10::cuda::CUDAGuard guard(q_pe.device());
+  check_status(hcu_rope_qout_kv_store(positions.data_ptr(), positions.scalar_type() == at::kLong ? 1 : 0, T,
+                                      ptr<const uint16_t>(q_pe), q_pe.size(1), q_pe.stride(0), q_pe.stride(1),
+                                      ptr<uint16_t>(q_out), q_out.stride(0), q_out.stride(1), ptr<uint16_t>(kv_c),
+                                      kv_tok, ptr<const uint16_t>(kv_weight), static_cast<float>(norm_eps),
+                                      ptr<uint16_t>(k_pe), k_tok, ptr<const uint16_t>(cos_sin_cache),
+                                      cos_sin_cache.size(0), is_neox ? 1 : 0, ptr<uint8_t>(kv_buffer),
+                                      kv_buffer.size(0), kv_buffer.stride(0), ptr<const int64_t>(loc), loc.numel(),
+                                      static_cast<float>(store_eps), static_cast<int32_t>(rsqrt_mode), cur_stream()),
+               "rope_qout_kv_store");
+}
+
 torch::Tensor cp_topk_merge(const torch::Tensor& keys, const torch::Tensor& gidx, const torch::Tensor& lengths) {
   TORCH_CHECK(keys.is_cuda() && keys.scalar_type() == at::kInt && keys.dim() == 3 && keys.size(2) == kTopK &&
                   keys.is_contiguous(),
@@ -364,6 +408,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "sparse_mask_topk_transform_split with pass 1 (histogram) taken from mqa_logits_hist's workspace");
   m.def("mqa_logits_hist", &mqa_logits_hist,
         "paged fp8 indexer logits -> {logits, mask, zws}; with hist_lens also top-k pass 1 into zws");
+  m.def("rope_qout_kv_store", &rope_qout_kv_store,
+        "MLA decode front end: q rope, kv_a RMS norm in place, k rope, fp8 656-byte KV slot store");
   m.def("cp_local_bound", &cp_local_bound, "context-parallel: per-row sampled bound of the global top-2048 threshold");
   m.def("cp_filter", &cp_filter, "context-parallel: tokens at or above the bound into the exchange buffer");
   m.def("cp_topk_merge_lists", &cp_topk_merge_lists, "context-parallel: merge of the exchanged bounded lists");

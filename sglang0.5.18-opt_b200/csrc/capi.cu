@@ -56,6 +56,7 @@ extern "C" int hcu_read_device_status(uint32_t* status, int clear) {
   if (e == cudaSuccess) e = hcu::status_dequant(status, clear);
   if (e == cudaSuccess) e = hcu::status_topk(status, clear);
   if (e == cudaSuccess) e = hcu::status_logits(status, clear);
+  if (e == cudaSuccess) e = hcu::status_mla(status, clear);
   if (e != cudaSuccess) {
     hcu::set_last_error(e);
     return HCU_ERR_LAUNCH;

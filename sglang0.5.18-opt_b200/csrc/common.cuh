@@ -365,4 +365,5 @@ int sm_count();       // SM count of the current device (cached per device)
 cudaError_t status_dequant(uint32_t* out, int clear);
 cudaError_t status_topk(uint32_t* out, int clear);
 cudaError_t status_logits(uint32_t* out, int clear);
+cudaError_t status_mla(uint32_t* out, int clear);
 }  // namespace hcu

@@ -209,6 +209,51 @@ def cp_topk_merge_lists(recv, lengths, flag=None, short_identity=True):
     return _C.cp_topk_merge_lists(recv, lengths, flag, short_identity)
 
 
+# --- MLA decode front end (SGLANG_HCU_MLA_KV_FUSED in the reference's sglang patches) --------------
+# HCU_NORM_RSQRT_MODE: the rsqrt of the RMS norm (0 and 1: rsqrtf; 2: 1 / sqrtf, IEEE).
+_RSQRT_MODE = int(os.environ.get("HCU_NORM_RSQRT_MODE", "0"))
+
+
+def _rows(x, width):
+    """x is [T, width] / [T, 1, width] with a unit last stride."""
+    return (x.shape[-1] == width and x.stride(-1) == 1
+            and (x.dim() == 2 or (x.dim() == 3 and x.shape[1] == 1)))
+
+
+def kv_fused_supported(positions, q_pe, q_out, kv_c, kv_weight, k_pe, cos_sin_cache, kv_buffer, loc):
+    """Whether rope_qout_kv_store takes these operands (MLA: kv_lora_rank 512, rope 64, bf16,
+    656-byte fp8 slots; ``hcu_ops/__init__.py:427-444`` of the reference)."""
+    t = positions.numel()
+    bf = torch.bfloat16
+
+    def al(x):
+        return x.data_ptr() % 16 == 0
+
+    return (q_pe.dtype == bf and q_out.dtype == bf and kv_c.dtype == bf and kv_weight.dtype == bf
+            and k_pe.dtype == bf and cos_sin_cache.dtype == bf
+            and positions.dtype in (torch.int32, torch.int64) and positions.is_contiguous()
+            and q_pe.dim() == 3 and q_pe.shape[0] == t and q_pe.shape[2] == 64 and q_pe.stride(2) == 1
+            and q_out.shape == q_pe.shape and q_out.stride(2) == 1
+            and cos_sin_cache.dim() == 2 and cos_sin_cache.shape[1] == 64 and cos_sin_cache.is_contiguous()
+            and _rows(kv_c, 512) and kv_c.shape[0] == t and kv_c.stride(0) % 8 == 0
+            and _rows(k_pe, 64) and k_pe.shape[0] == t
+            and kv_weight.is_contiguous() and kv_weight.numel() == 512
+            and kv_buffer.dtype == torch.uint8 and kv_buffer.dim() >= 2
+            and kv_buffer.numel() // max(kv_buffer.shape[0], 1) >= 656 and kv_buffer.stride(0) % 16 == 0
+            and loc.dtype == torch.int64 and loc.is_contiguous() and loc.numel() <= t
+            and al(kv_c) and al(kv_weight) and al(kv_buffer))
+
+
+def rope_qout_kv_store(positions, q_pe, q_out, kv_c, kv_weight, norm_eps, k_pe, cos_sin_cache, is_neox,
+                       kv_buffer, loc, store_eps=1e-6):
+    """One launch for sglang's DSA decode front end (``hcu_ops/__init__.py:447-455`` of the reference):
+    kv_c = rms_norm(kv_c, kv_weight, norm_eps) in place, q_out = rope(q_pe) (q_out may be q_pe),
+    k_pe = rope(k_pe) in place, and the fp8 656-byte slots kv_buffer[loc] (512 fp8 in four
+    128-element groups, 4 fp32 scales, the rotated k_pe as bf16)."""
+    _C.rope_qout_kv_store(positions.reshape(-1), q_pe, q_out, kv_c, kv_weight, float(norm_eps), k_pe,
+                          cos_sin_cache, bool(is_neox), kv_buffer, loc, float(store_eps), _RSQRT_MODE)
+
+
 def read_device_status(clear=True):
     """Sticky device status bits (1: a bounded wait expired, 2: an out-of-range index was skipped)."""
     return _C.read_device_status(clear)

@@ -115,3 +115,22 @@ def test_cp_bounded_exchange_argument_checks(lib):
     b.restype = ctypes.c_int
     assert b(p, i64(4), i64(64), i64(32), p, i64(4), p, p, p, None) == HCU_ERR_ARG  # stride below width
     assert b(p, i64(0), i64(64), i64(64), p, i64(4), p, p, p, None) == HCU_OK
+
+
+def test_rope_qout_kv_store_argument_checks(lib):
+    """The MLA front end refuses bad arguments before launching anything."""
+    f = lib.hcu_rope_qout_kv_store
+    f.restype = ctypes.c_int
+    p, i64, i32 = ctypes.c_void_p(16), ctypes.c_int64, ctypes.c_int32
+    flt = ctypes.c_float
+
+    def call(T=4, kv_tok=512, mode=2, n_loc=4, slot_stride=656):
+        return f(p, i32(1), i64(T), p, i64(64), i64(64 * 64), i64(64), p, i64(64 * 64), i64(64), p, i64(kv_tok), p,
+                 flt(1e-6), p, i64(64), p, i64(100), i32(0), p, i64(8), i64(slot_stride), p, i64(n_loc), flt(1e-6),
+                 i32(mode), None)
+
+    assert call(mode=3) == HCU_ERR_ARG           # no such rsqrt form
+    assert call(kv_tok=500) == HCU_ERR_ARG       # latent rows shorter than 512 / not 16-byte multiples
+    assert call(n_loc=5) == HCU_ERR_ARG          # more slots than tokens
+    assert call(slot_stride=648) == HCU_ERR_ARG  # slots shorter than 656 bytes
+    assert call(T=0, n_loc=0) == HCU_OK          # nothing to do

@@ -180,3 +180,36 @@ def test_kstore_oracle_equals_workload_quantisation():
     # out-of-range slots are skipped
     bad = O.quant_store_index_k(k[:2].numpy(), np.array([-1, n_pages * 64], np.int32), np.zeros((n_pages, 64 * 132), np.uint8))
     assert not bad.any()
+
+
+def test_mla_writer_restatement_round_trips_through_the_dequant():
+    """The MLA writer's restatement (oracle/mla.py) and the 656-byte dequant's restatement agree on
+    the slot layout: fp8 bytes times group scales give back the normed latent within fp8 precision,
+    and the rope part is the rotated k_pe bit for bit; a rotation keeps the pairs' norms."""
+    from oracle import mla as M
+
+    g = torch.Generator().manual_seed(3)
+    T, slots = 6, 16
+    kv_c = M.to_bf(torch.randn(T, 512, generator=g).numpy() * 3)
+    w = M.to_bf((torch.rand(512, generator=g) * 2).numpy())
+    k_pe = M.to_bf(torch.randn(T, 64, generator=g).numpy())
+    q_pe = M.to_bf(torch.randn(T, 4, 64, generator=g).numpy())
+    ang = torch.arange(100)[:, None] * (10000.0 ** (-torch.arange(32) / 32))
+    cache = M.to_bf(torch.cat([ang.cos(), ang.sin()], dim=-1).numpy())
+    pos = np.array([0, 5, 99, 17, 42, 3])
+    loc = np.array([15, 0, 7, 3, 9, 11])
+    for neox in (False, True):
+        q_out, y, kp, buf = M.rope_qout_kv_store(pos, q_pe, kv_c, w, 1e-6, k_pe, cache, neox,
+                                                 np.zeros((slots, 656), np.uint8), loc)
+        deq = O.dequant_mla_656(buf.reshape(slots, 1, 656), loc.astype(np.int32))  # bf16 bits [T, 1, 576]
+        yf = M.bf(y)
+        dv = M.bf(deq.reshape(T, 576)[:, :512])
+        scale = np.abs(yf).reshape(T, 4, 128).max(axis=2) / 448
+        assert (np.abs(dv - yf) <= 2.0 ** -4 * np.abs(yf) + np.repeat(scale, 128, axis=1) * 2.0 ** -9).all()
+        assert np.array_equal(deq.reshape(T, 576)[:, 512:], kp)
+        assert np.array_equal(q_out[0], q_pe[0])  # position 0: cos 1, sin 0
+        r = np.arange(32)
+        xi, yi = (r, 32 + r) if neox else (2 * r, 2 * r + 1)
+        n0 = M.bf(k_pe[:, xi]) ** 2 + M.bf(k_pe[:, yi]) ** 2
+        n1 = M.bf(kp[:, xi]) ** 2 + M.bf(kp[:, yi]) ** 2
+        assert np.allclose(n0, n1, rtol=2 ** -5, atol=1e-3)
