@@ -354,7 +354,7 @@ def run_reference(args):
 
 
 # ------------------------------------------------------------------------------------------------
-# secondary workloads: bench.py --workload decode0 | prefill | dequant | mla_dequant | cp_prefill
+# secondary workloads: bench.py --workload decode0 | prefill | dequant | mla_dequant | kstore | mla_kv | cp_prefill
 # (2, 3, the 656-byte MLA dequant, and 4).  Inputs that fit in L2 are timed one
 # launch at a time with a 256 MB L2 flush between launches (events around the launch only).
 # ------------------------------------------------------------------------------------------------
@@ -490,6 +490,57 @@ def run_kstore(args, world, rank, local):
     return rec
 
 
+MLA_T, MLA_H = 128, 64  # decode tokens of one MLA front-end call, q heads
+MLA_BYTES_PER_TOKEN = 2 * MLA_H * 64 * 2 + 2 * 512 * 2 + 2 * 64 * 2 + 128 + 656 + 16  # q, latent, k_pe rw; cos/sin; slot
+
+
+def _mla_inputs(dev, T, seed):
+    """The reference test's layout (hcu_ops/tests/test_kv_fused.py:18-46): a packed [T, 2048 + 576]
+    latent, q [T, 64, 256] with the rope tail at 192, a 70000-position cos/sin cache, 4096 slots."""
+    import torch
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    packed = torch.randn(T, 2048 + 576, generator=g, device=dev).bfloat16()
+    q = torch.randn(T, MLA_H, 256, generator=g, device=dev).bfloat16()
+    pos = torch.randint(0, 70000, (T,), generator=g, device=dev)
+    ang = torch.arange(70000, device=dev)[:, None] * (10000.0 ** (-torch.arange(32, device=dev) / 32))
+    cache = torch.cat([ang.cos(), ang.sin()], dim=-1).bfloat16().contiguous()
+    w = (torch.rand(512, generator=g, device=dev) * 2).bfloat16()
+    loc = torch.randperm(4096, generator=g, device=dev)[:T].contiguous()
+    buf = torch.zeros(4096, 1, 656, dtype=torch.uint8, device=dev)
+    return packed, q, pos, cache, w, loc, buf
+
+
+def run_mla_kv(args, world, rank, local):
+    """MLA decode front end (rope_qout_kv_store): 128 tokens x 64 q heads per call, q rotated in place."""
+    import torch
+
+    import hcu_ops
+
+    dev = torch.device("cuda", local)
+    packed, q, pos, cache, w, loc, buf = _mla_inputs(dev, MLA_T, rank)
+    kv_c, k_pe, q_pe = packed[:, 2048:2560], packed[:, 2560:].unsqueeze(1), q[..., 192:]
+    fn = lambda: hcu_ops.rope_qout_kv_store(pos, q_pe, q_pe, kv_c, w, 1e-6, k_pe, cache, False, buf, loc)  # noqa
+    for _ in range(max(args.warmup, 3)):
+        fn()
+    iters = min(args.steps, 500)
+    ms = _timed_iters(fn, iters, _flusher(dev))
+    alg = MLA_BYTES_PER_TOKEN * MLA_T + 1024
+    gbs = alg / (ms * 1e-3) / 1e9
+    hbm, _, src = _peaks()
+    rec = _base_record(args, world, "MLA decode front end latency (us per call, 128 tokens x 64 q heads)",
+                       ms * 1e3, "us", ms, "MLA front end: q rope (64 heads), latent RMS norm in place, k rope, fp8 "
+                       "656-byte slot store, 128 decode tokens; L2 flushed between launches", tokens=MLA_T,
+                       bytes_per_token=MLA_BYTES_PER_TOKEN)
+    rec["higher_is_better"] = False
+    rec["dtype"] = "bf16 -> fp32 -> bf16 / fp8e4m3"
+    rec["roofline"] = {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                       "traffic": None, "alg_bytes_per_launch": alg, "peak_source": src}
+    rec["gpu_launches"] = iters
+    return rec
+
+
 def _prefill_inputs(dev, rows, prefix, seed):
     from hcu_ops.workloads import make_ragged
 
@@ -596,7 +647,7 @@ def run_cp_prefill(args, world, rank, local):
     return rec
 
 
-WORKLOADS = {"decode0": run_decode0, "dequant": run_dequant, "kstore": run_kstore,
+WORKLOADS = {"decode0": run_decode0, "dequant": run_dequant, "kstore": run_kstore, "mla_kv": run_mla_kv,
              "mla_dequant": lambda a, w, r, l: run_dequant(a, w, r, l, mla=True),
              "prefill": run_prefill, "cp_prefill": run_cp_prefill}
 
@@ -632,6 +683,16 @@ def run_reference_sample(args):
         O.quant_store_index_k(k, loc, pool)
         dt = time.perf_counter() - t0
         value, unit, sample = n * (256 + 4 + 132) / dt / 1e9, "GB/s", f"{n} tokens (whole workload)"
+    elif wl == "mla_kv":
+        from oracle import mla as M
+
+        packed, q, pos, cache, w, loc, buf = _mla_inputs(torch.device("cpu"), MLA_T, 0)
+        u = lambda x: x.contiguous().view(torch.int16).numpy().view(np.uint16)  # noqa: E731
+        t0 = time.perf_counter()
+        M.rope_qout_kv_store(pos.numpy(), u(q[..., 192:]), u(packed[:, 2048:2560]), u(w), 1e-6, u(packed[:, 2560:]),
+                             u(cache), False, buf.numpy(), loc.numpy())
+        dt = time.perf_counter() - t0
+        value, unit, sample = dt * 1e6, "us", f"one call, {MLA_T} tokens x {MLA_H} q heads (whole workload)"
     elif wl in ("dequant", "mla_dequant"):
         from hcu_ops.workloads import make_index_k_dequant, make_mla_dequant
 
