@@ -206,8 +206,10 @@ def _bounded_rowshard(ops, lg, mk, lens, gtab, vis, rows, rps, world, rank, grou
     vis_p = torch.cat([vis, torch.zeros(pad, dtype=vis.dtype, device=dev)]) if pad else vis
     mine = ops.merge_lists(recv, vis_p[rank * rps:(rank + 1) * rps].contiguous(), flag)
     dist.all_reduce(flag, op=dist.ReduceOp.MAX, group=group)
-    if int(flag.item()):
-        return None
+    # the gather goes out before the flag is read (one host wait per step, after the last
+    # collective); every rank reads the same flag, so all discard it and rerun together
     out = torch.empty((world * rps, TOPK), dtype=mine.dtype, device=dev)
     dist.all_gather_into_tensor(out, mine.contiguous(), group=group)
+    if int(flag.item()):
+        return None
     return out
