@@ -1,6 +1,6 @@
 // Stage 3: exact top-2048 over masked scores + page-table transform.
 //
-// topk_row_kernel: one 1024-thread CTA (32 warps) per row.
+// topk_row_kernel: one CTA (1024 or 512 threads) per row.
 // Candidate path (the normal case, one streaming pass over the row):
 //   S  m strided samples (2048 for rows <= 128K tokens) go into a 12-bit and
 //      then an 8-bit histogram; the sample order statistic a few sigma below
@@ -11,23 +11,26 @@
 //      token with key >= lo is appended to a shared-memory candidate list at
 //      its block-wide prefix position, so the list is in token order.  For a
 //      positive lo the test is one signed compare of the raw float bits.
-//   Q  an 8-bit-digit radix select over the candidates (digits below the
+//   Q  a 9-bit-digit radix select over the candidates (digits below the
 //      common prefix of lo and the largest candidate) gives the threshold key,
 //      the count above it and the number of ties to take.
 //   R  one block scan of (above, tie) flags over the list writes the output.
-// If the list holds fewer than 2048 tokens (the bound missed) or overflows,
-// the full radix passes run instead (the row stays L2-resident):
-//   A  12-bit histogram of key[31:20] + per-warp positive / zero counts
-//      (skipped on the "pre" path); positives <= 2048 <= positives + zeros ->
-//      the threshold is +0 (sparse fast path)
-//   B  12-bit histogram of key[19:8] inside the threshold bin
-//   C  per-warp 8-bit histograms of key[7:0] inside the 24-bit prefix, per-warp
-//      count of keys above the prefix and of exact zeros
-//   D  compaction: keys > thr in token order, then the first `remaining`
-//      threshold ties in token order, then one coalesced page-table gather.
+// Exact fallback, when the list holds fewer than 2048 tokens (the bound
+// missed) or more than its capacity (heavy ties, a sparse row whose threshold
+// is +0); the row stays L2-resident:
+//   X  the threshold key by a descent over four 8-bit key digits, most
+//      significant first: per level one streaming pass builds per-warp digit
+//      histograms of the keys that share the digits found so far (the +0 key
+//      of unset mask bits counted in registers), and a rank search over their
+//      sum picks the next digit;
+//   Y  one streaming pass in block-wide rounds writes the selection in order:
+//      a block scan of each thread's (above, tie) counts gives every selected
+//      token its output position directly.
 // Unset mask bits are an implicit +0 (key 0x80000000) whatever the score
 // storage holds.  The selection and output order are those of
-// hcu_ops/csrc/sparse_mask_topk.cu:1-7,141-349 of the reference.
+// hcu_ops/csrc/sparse_mask_topk.cu:1-7,141-349 of the reference: keys larger
+// than the threshold in token order, then the first threshold ties in token
+// order (ties broken toward the lower index).
 #include <cooperative_groups.h>
 
 #include <mutex>
@@ -40,8 +43,6 @@ HCU_DEFINE_STATUS(status_topk)
 namespace hcu {
 namespace {
 
-constexpr int kStep = 128;  // tokens per warp step (32 lanes x 4)
-constexpr int kTkUnroll = 4;
 constexpr int kSmallSample = 2048;  // row samples used to bound the threshold (rows <= 128K)
 constexpr int kSample = 8192;       // sample count for rows > 512K
 constexpr int kLaneTok = 16;        // consecutive tokens per lane in a streaming round
@@ -58,23 +59,15 @@ struct Tk {
   static constexpr int kWarps = kT / 32;
   static constexpr int kRound = kT * kLaneTok;               // tokens per streaming round
   static constexpr int kCandCap = kT >= 1024 ? 8192 : 4096;  // candidate list capacity
-  static constexpr int kHistTrash = kWarps * 256;            // trash slots follow the per-warp histograms
   static constexpr int kMaxSample = kT >= 1024 ? kSample : kSmallSample;
-  static constexpr int kHist = kWarps * 256 + 32 + 256 > kBins + 32 ? kWarps * 256 + 32 + 256 : kBins + 32;
-};
-
-struct TopkOutStage {  // pass D staging of the radix fallback
-  int out_idx[kTopK + 32];
-  uint32_t out_key[kTopK + 32];
+  // sampled bound: one kBins histogram; exact fallback: per-warp 256-bin digit histograms + their sum
+  static constexpr int kHist = kWarps * 256 + 256 > kBins ? kWarps * 256 + 256 : kBins;
 };
 
 template <int kT>
 struct __align__(16) TopkSmem {
-  int hist[Tk<kT>::kHist];  // A/B: [0,4096) + trash; C: warps x 256 + trash + merged[256]
-  union {
-    uint4 scr[kLaneTok / 4][kT];  // candidate pass: this thread's current 16 score words
-    TopkOutStage d;               // radix fallback: ordered output staging
-  };
+  int hist[Tk<kT>::kHist];  // sampled bound: [0, 4096); fallback: warps x 256 digit counts, then their sum
+  uint4 scr[kLaneTok / 4][kT];  // candidate pass: this thread's current 16 score words
   uint32_t cand_key[Tk<kT>::kCandCap];
   int32_t cand_idx[Tk<kT>::kCandCap];
   int32_t cand_pid[Tk<kT>::kCandCap];  // page-table entry of each candidate (async copies)
@@ -91,7 +84,6 @@ struct __align__(16) TopkSmem {
   int mark_any;        // CP merge: some list of the row was truncated (marker entry -2)
   uint32_t mark_max;   // CP merge: the largest marker key
 };
-static_assert(sizeof(TopkOutStage) <= sizeof(uint4) * 4 * 512, "fallback staging fits the scratch area");
 
 // 4-byte global -> shared copy that does not hold a register (LDGSTS).
 __device__ __forceinline__ void cp_async4(void* smem_dst, const void* gsrc) {
@@ -103,83 +95,6 @@ __device__ __forceinline__ int warp_sum(int x) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
   return x;
-}
-
-// Loads tokens [i0, i0+4) (i0 a multiple of 4) and their 16-bit mask word.
-// Positions at or past `lim` read token 0 (always valid here) so the loads of
-// an unrolled group are branch-free.
-template <bool kVec>
-__device__ __forceinline__ void load4(const float* __restrict__ vals, const int16_t* __restrict__ mask, int i0,
-                                      int lim, float (&v)[4], uint32_t& mw) {
-  const int safe = i0 < lim ? i0 : 0;
-  mw = static_cast<uint16_t>(__ldg(mask + (safe >> 4)));
-  if constexpr (kVec) {
-    const float4 f = __ldg(reinterpret_cast<const float4*>(vals + safe));
-    v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
-  } else {
-#pragma unroll
-    for (int j = 0; j < 4; ++j) v[j] = __ldg(vals + (safe + j < lim ? safe + j : lim - 1));
-  }
-}
-
-// Keys of tokens [i0, i0+4); returns the bitmask of tokens below `lim`.
-__device__ __forceinline__ uint32_t keys4(int i0, int lim, const float (&v)[4], uint32_t mw, uint32_t (&k)[4]) {
-  const uint32_t m = (mw >> (i0 & 15)) & 0xFu;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) k[j] = ((m >> j) & 1u) ? to_key(v[j]) : kZeroKey;
-  const int rem = lim - i0;
-  const int nv = rem <= 0 ? 0 : (rem < 4 ? rem : 4);
-  return (1u << nv) - 1u;
-}
-
-// Bin b of an NB-bin histogram with suffix(b) >= need > suffix(b+1):
-// res[0] = b, res[1] = suffix(b+1).  Requires sum(hist) >= need >= 1.
-template <int kT, int NB>
-__device__ __forceinline__ void find_threshold(const int* hist, int need, int* wtot, int* res) {
-  constexpr int BPT = NB >= kT ? NB / kT : 1;
-  constexpr int ACTIVE = NB / BPT;
-  const int tid = threadIdx.x;
-  const int lane = tid & 31;
-  const int w = tid >> 5;
-  int h[BPT];
-  int s = 0;
-#pragma unroll
-  for (int j = 0; j < BPT; ++j) {
-    h[j] = tid < ACTIVE ? hist[tid * BPT + j] : 0;
-    s += h[j];
-  }
-  int x = s;  // inclusive suffix over lanes >= lane
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int y = __shfl_down_sync(0xffffffffu, x, o);
-    if (lane + o < 32) x += y;
-  }
-  if (lane == 0) wtot[w] = x;
-  __syncthreads();
-  // suffix of the warp totals after warp w, by a shuffle scan (no serial loop)
-  int t = lane < kT / 32 ? wtot[lane] : 0;
-  int sx = t;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int y = __shfl_down_sync(0xffffffffu, sx, o);
-    if (lane + o < 32) sx += y;
-  }
-  const int after = __shfl_sync(0xffffffffu, sx - t, w);
-  const int suf = x + after;
-  const int suf_next = suf - s;
-  if (tid < ACTIVE && suf >= need && suf_next < need) {
-    int acc = suf_next;
-#pragma unroll
-    for (int j = BPT - 1; j >= 0; --j) {
-      if (acc + h[j] >= need) {
-        res[0] = tid * BPT + j;
-        res[1] = acc;
-        break;
-      }
-      acc += h[j];
-    }
-  }
-  __syncthreads();
 }
 
 // Branch-free monotone key.
@@ -283,6 +198,42 @@ __device__ __forceinline__ int block_excl_scan(int x, int* wtot, int* total) {
   const int ti = warp_incl_scan(t);
   *total = __shfl_sync(0xffffffffu, ti, 31);
   return __shfl_sync(0xffffffffu, ti - t, w) + inc - x;
+}
+
+// Rank search over an NB-bin histogram h (shared or global memory): the bin b
+// holding the need-th largest key, i.e. S(b) >= need > S(b + 1) with S(b) the
+// count in bins >= b; res[0] = b, res[1] = S(b + 1).  Requires sum(h) >= need
+// >= 1.  Thread t takes the t-th run of NB / kT bins counted down from the top
+// bin, so an exclusive block scan of the run totals in thread order is the
+// count above each run.  Called by every thread after a barrier that published
+// h; ends with a barrier (res is then visible to all).
+template <int kT, int NB>
+__device__ __forceinline__ void block_rank_bin(const int* h, int need, int* wtot, int* res) {
+  constexpr int kRun = NB >= kT ? NB / kT : 1;
+  constexpr int kRuns = NB / kRun;
+  const int t = threadIdx.x;
+  const int top = NB - 1 - t * kRun;  // highest bin of this thread's run
+  int c[kRun];
+  int s = 0;
+#pragma unroll
+  for (int j = 0; j < kRun; ++j) {
+    c[j] = t < kRuns ? h[top - j] : 0;
+    s += c[j];
+  }
+  int total;
+  int acc = block_excl_scan<kT>(s, wtot, &total);  // keys in the runs above this one
+  if (t < kRuns && acc < need && acc + s >= need) {
+#pragma unroll
+    for (int j = 0; j < kRun; ++j) {
+      if (acc + c[j] >= need) {
+        res[0] = top - j;
+        res[1] = acc;
+        break;
+      }
+      acc += c[j];
+    }
+  }
+  __syncthreads();
 }
 
 // Raw float bits of this lane's 16 consecutive tokens [i0, i0 + 16) (0 at and
@@ -540,25 +491,134 @@ __device__ __noinline__ int split_gather(TopkSmem<kT>& sm, int splits, int rank)
   return n;
 }
 
-// Visits every token slot of this warp's segment as (valid, key, index i0+j);
-// lane l takes tokens c + 4l .. c + 4l + 3 of each 128-token step (fallback passes).
-#define TK_FOR_EACH(BODY)                                                             \
-  for (int c = seg_begin; c < seg_end; c += kStep * kTkUnroll) {                      \
-    float rv[kTkUnroll][4];                                                           \
-    uint32_t rm[kTkUnroll];                                                           \
-    _Pragma("unroll") for (int u = 0; u < kTkUnroll; ++u)                             \
-        load4<kVec>(vals, mrow, c + u * kStep + lane * 4, seg_end, rv[u], rm[u]);     \
-    _Pragma("unroll") for (int u = 0; u < kTkUnroll; ++u) {                           \
-      const int i0 = c + u * kStep + lane * 4;                                        \
-      uint32_t kk[4];                                                                 \
-      const uint32_t vv = keys4(i0, seg_end, rv[u], rm[u], kk);                       \
-      _Pragma("unroll") for (int j = 0; j < 4; ++j) {                                 \
-        const bool valid = (vv >> j) & 1u;                                            \
-        const uint32_t key = kk[j];                                                   \
-        BODY                                                                          \
-      }                                                                               \
-    }                                                                                 \
+// ---------------------------------------------------------------------------
+// Exact fallback (X, Y of the header).  A "key source" visits, for the calling
+// thread, every valid key it owns: f(key) per key.  The digit descent works
+// on any source (row tokens here, exchanged list entries in the CP merge).
+// ---------------------------------------------------------------------------
+
+// Row tokens [0, len): thread t owns the 16-token chunks starting at
+// 16 (t + k kT) (one 64-byte run per lane, 2 KB per warp and round).
+template <int kT, bool kVec>
+struct RowKeys {
+  const float* vals;
+  const int16_t* mrow;
+  int len;
+  template <class F>
+  __device__ __forceinline__ void operator()(F&& f) const {
+    for (int i0 = static_cast<int>(threadIdx.x) * kLaneTok; i0 < len; i0 += kT * kLaneTok) {
+      uint32_t k[16];
+      const uint32_t vm = load16<kVec>(vals, mrow, i0, len, k);
+#pragma unroll
+      for (int t = 0; t < 16; ++t)
+        if ((vm >> t) & 1u) f(k[t]);
+    }
   }
+};
+
+// The key of rank k (1 = largest) among the source's keys and *above = the
+// number of keys strictly larger (the k - *above first ties complete the
+// selection).  Requires k <= number of keys.  Four levels of 8-bit digits:
+// level L histograms digit L of the keys whose higher digits equal the prefix
+// found so far, into one 256-bin histogram per warp (no inter-warp atomics);
+// the +0 key, which dominates sparse rows, is counted in registers and added
+// once per warp.  Every thread of the CTA calls it.
+template <int kT, class Src>
+__device__ __noinline__ uint32_t digit_descent(TopkSmem<kT>& sm, const Src& src, int k, int* above) {
+  constexpr int kW = kT / 32;
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  int* wh = sm.hist + (tid >> 5) * 256;
+  int* sum = sm.hist + kW * 256;  // 16-byte aligned (warp_find reads it as int4)
+  uint32_t prefix = 0u;
+  int need = k;
+  int abv = 0;
+#pragma unroll 1
+  for (int level = 0; level < 4; ++level) {
+    const int sh = 24 - 8 * level;
+    for (int i = tid; i < kW * 256; i += kT) sm.hist[i] = 0;
+    __syncthreads();
+    int zc = 0;
+    src([&](uint32_t key) {
+      if (key == kZeroKey) {
+        ++zc;
+      } else if (level == 0 || (key >> (sh + 8)) == prefix) {
+        atomicAdd(&wh[(key >> sh) & 0xFFu], 1);
+      }
+    });
+    zc = warp_sum(zc);
+    if (lane == 0 && zc && (level == 0 || (kZeroKey >> (sh + 8)) == prefix))
+      atomicAdd(&wh[(kZeroKey >> sh) & 0xFFu], zc);
+    __syncthreads();
+    if (tid < 256) {
+      int c = 0;
+#pragma unroll 4
+      for (int v = 0; v < kW; ++v) c += sm.hist[v * 256 + tid];
+      sum[tid] = c;
+    }
+    __syncthreads();
+    if ((tid >> 5) == 0) warp_find<256>(sum, need, sm.res);
+    __syncthreads();
+    prefix = (prefix << 8) | static_cast<uint32_t>(sm.res[0]);
+    abv += sm.res[1];
+    need -= sm.res[1];
+  }
+  *above = abv;
+  return prefix;
+}
+
+// Writes the selection of a row given its threshold: keys > thr, then the
+// first `remaining` ties, both in token order (kSorted: the same set in token
+// order), through the page table.  Block-wide rounds of kT x 16 tokens; one
+// block scan per round of each thread's packed (above, tie) counts (a round
+// holds at most 16384 tokens, so 16 bits each suffice) gives each selected
+// token its position.  Stops once every output slot is written.
+template <int kT, bool kVec, bool kSorted>
+__device__ __noinline__ void ordered_write_row(TopkSmem<kT>& sm, const float* __restrict__ vals,
+                                               const int16_t* __restrict__ mrow, const int32_t* __restrict__ src,
+                                               int len, uint32_t thr, int above, int32_t* __restrict__ out,
+                                               uint32_t* __restrict__ okeys) {
+  const int remaining = kTopK - above;
+  int base_a = 0, base_t = 0;  // above / tie tokens in earlier rounds
+  for (int r0 = 0; r0 < len; r0 += kT * kLaneTok) {
+    const int i0 = r0 + static_cast<int>(threadIdx.x) * kLaneTok;
+    uint32_t k[16];
+    const uint32_t vm = load16<kVec>(vals, mrow, i0, len, k);
+    uint32_t ab = 0u, tb = 0u;
+#pragma unroll
+    for (int t = 0; t < 16; ++t) {
+      ab |= static_cast<uint32_t>(k[t] > thr) << t;
+      tb |= static_cast<uint32_t>(k[t] == thr) << t;
+    }
+    ab &= vm;
+    tb &= vm;
+    int total;
+    const int ex = block_excl_scan<kT>(__popc(ab) | (__popc(tb) << 16), sm.wtot, &total);
+    int pa = base_a + (ex & 0xFFFF);
+    int pq = base_t + (ex >> 16);
+    if (ab | tb) {
+#pragma unroll
+      for (int t = 0; t < 16; ++t) {  // static indices: k[] stays in registers
+        int p = -1;
+        if ((ab >> t) & 1u) {
+          p = kSorted ? pa + min(pq, remaining) : pa;
+          ++pa;
+        } else if ((tb >> t) & 1u) {
+          if (pq < remaining) p = kSorted ? pa + pq : above + pq;
+          ++pq;
+        }
+        if (p >= 0) {
+          out[p] = __ldg(src + i0 + t);
+          if (okeys) okeys[p] = k[t];
+        }
+      }
+    }
+    base_a += total & 0xFFFF;
+    base_t += total >> 16;
+    __syncthreads();  // wtot is reused by the next round's scan
+    if (base_a >= above && base_t >= remaining) break;  // block-uniform
+  }
+}
 
 // kSplit: the row is split over a cluster of `splits` CTAs (blockIdx.x = row *
 // splits + rank): each derives the same bound lo over the whole row and
@@ -571,9 +631,7 @@ __global__ __launch_bounds__(kT, 1024 / kT) void topk_row_kernel(
     int32_t* __restrict__ dst, uint32_t* __restrict__ dst_keys, const int32_t* __restrict__ pre_ws, int rows,
     int splits) {
   constexpr int kTkThreads = kT;
-  constexpr int kTkWarps = kT / 32;
   constexpr int kCandCap = Tk<kT>::kCandCap;
-  constexpr int kHistTrash = Tk<kT>::kHistTrash;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   TopkSmem<kT>& sm = *reinterpret_cast<TopkSmem<kT>*>(smem_raw);
   // launched with programmatic stream serialization: wait for the previous kernel (the logits that
@@ -616,17 +674,12 @@ __global__ __launch_bounds__(kT, 1024 / kT) void topk_row_kernel(
     return;
   }
 
-  const int seg = (len + kTkWarps * kStep - 1) / (kTkWarps * kStep) * kStep;
-  const int seg_begin = min(w * seg, len);
-  const int seg_end = min(seg_begin + seg, len);
-  const int trash = kBins + lane;
   // this CTA's token range of the candidate pass (the whole row unless split)
   const int cseg = s_eff > 1 ? (len + s_eff * 512 - 1) / (s_eff * 512) * 512 : len;
   const int cs0 = min(rank * cseg, len);
   const int cs1 = min(cs0 + cseg, len);
 
-  uint32_t thr = 0;
-  int remaining = 0;
+  uint32_t* const okeys = dst_keys ? dst_keys + static_cast<int64_t>(row) * kTopK : nullptr;
   {
     // ---- candidate path ----
     // The sample loads go out first (they gate the bound), then round 0's
@@ -680,7 +733,7 @@ __global__ __launch_bounds__(kT, 1024 / kT) void topk_row_kernel(
       // sample rank (1 = largest) 4 sigma + 4 below the threshold's expected sample rank
       const float t = static_cast<float>(kTopK) / stride_f;
       const int r_lo = min(m, static_cast<int>(ceilf(t + 4.f * sqrtf(t) + 4.f)));
-      find_threshold<kT, kBins>(sm.hist, r_lo, sm.wtot, sm.res);
+      block_rank_bin<kT, kBins>(sm.hist, r_lo, sm.wtot, sm.res);
       const uint32_t b1 = static_cast<uint32_t>(sm.res[0]);
       const int need = r_lo - sm.res[1];
 #pragma unroll
@@ -704,7 +757,8 @@ __global__ __launch_bounds__(kT, 1024 / kT) void topk_row_kernel(
           sm.res[0] = 0;
           sm.res[1] = 0;
         }
-        find_threshold<kT, kBins>(h1, kTopK, sm.wtot, sm.res);
+        __syncthreads();  // res written above before the search (and wtot free)
+        block_rank_bin<kT, kBins>(h1, kTopK, sm.wtot, sm.res);
         const int b1 = sm.res[0];
         lo = static_cast<uint32_t>(b1) << 20;
         try_cand = sm.res[1] + h1[b1] <= kCandCap;
@@ -723,12 +777,11 @@ __global__ __launch_bounds__(kT, 1024 / kT) void topk_row_kernel(
       if (rank != 0) return;
       if (try_cand && n >= kTopK && n <= kCandCap) {
         int above = 0;
-        thr = select_candidates(sm, n, lo, &above);
-        write_candidates<kT, kSorted>(sm, n, thr, above, out,
-                                      dst_keys ? dst_keys + static_cast<int64_t>(row) * kTopK : nullptr);
+        const uint32_t thr = select_candidates(sm, n, lo, &above);
+        write_candidates<kT, kSorted>(sm, n, thr, above, out, okeys);
         return;
       }
-      try_cand = false;  // rank 0 alone runs the radix passes over the whole row
+      try_cand = false;  // rank 0 alone runs the exact fallback over the whole row
     }
     if (try_cand) {
       const int n = lo > kZeroKey ? collect_candidates<kT, kVec, true>(vals, mrow, src, 0, len, lo, sm, b0, mw0, valid0)
@@ -736,227 +789,19 @@ __global__ __launch_bounds__(kT, 1024 / kT) void topk_row_kernel(
       if (n < kTopK || n > kCandCap) cp_async_wait_all();  // no copy outlives the candidate path
       if (n >= kTopK && n <= kCandCap) {
         int above = 0;
-        thr = select_candidates(sm, n, lo, &above);
-        write_candidates<kT, kSorted>(sm, n, thr, above, out,
-                                  dst_keys ? dst_keys + static_cast<int64_t>(row) * kTopK : nullptr);
+        const uint32_t thr = select_candidates(sm, n, lo, &above);
+        write_candidates<kT, kSorted>(sm, n, thr, above, out, okeys);
         return;
       }
     }
     __syncthreads();
   }
 
-  {
-    // ---- pass A: key[31:20] histogram, positives and zeros ----
-    int positives = 0, zeros = 0;
-    const int* hist1 = sm.hist;
-    bool have_warp_counts = false;
-    if (pre_ws != nullptr) {
-      hist1 = pre_ws + static_cast<int64_t>(row) * kBins;
-      const int* cnt = pre_ws + 2 * static_cast<int64_t>(rows) * kBins + 2 * row;
-      positives = cnt[0];
-      zeros = cnt[1];
-    } else {
-      for (int i = tid; i < kBins + 32; i += kTkThreads) sm.hist[i] = 0;
-      __syncthreads();
-      int zc = 0, pc = 0;
-      TK_FOR_EACH({
-        const bool nz = key != kZeroKey;
-        zc += valid & !nz;
-        pc += valid & (key > kZeroKey);
-        atomicAdd(&sm.hist[(valid & nz) ? static_cast<int>(key >> 20) : trash], 1);
-      })
-      zc = warp_sum(zc);
-      pc = warp_sum(pc);
-      if (lane == 0) {
-        if (zc) atomicAdd(&sm.hist[kZeroBin], zc);
-        sm.pos[w] = pc;
-        sm.zeros[w] = zc;
-      }
-      __syncthreads();
-      positives = warp_sum(lane < kTkWarps ? sm.pos[lane] : 0);
-      zeros = warp_sum(lane < kTkWarps ? sm.zeros[lane] : 0);
-      have_warp_counts = true;
-    }
-
-    if (positives <= kTopK && positives + zeros >= kTopK) {
-      // Sparse fast path: every positive plus the lowest-index zeros.
-      thr = kZeroKey;
-      remaining = kTopK - positives;
-      if (!have_warp_counts) {
-        int zc = 0, pc = 0;
-        TK_FOR_EACH({
-          zc += valid & (key == kZeroKey);
-          pc += valid & (key > kZeroKey);
-        })
-        zc = warp_sum(zc);
-        pc = warp_sum(pc);
-        if (lane == 0) {
-          sm.pos[w] = pc;
-          sm.zeros[w] = zc;
-        }
-      }
-      if (lane == 0) {
-        sm.above[w] = sm.pos[w];
-        sm.ties[w] = sm.zeros[w];
-      }
-      __syncthreads();
-    } else {
-      find_threshold<kT, kBins>(hist1, kTopK, sm.wtot, sm.res);
-      const uint32_t t1 = static_cast<uint32_t>(sm.res[0]);
-      const int need1 = kTopK - sm.res[1];
-
-      // ---- pass B: key[19:8] inside bin t1 ----
-      for (int i = tid; i < kBins + 32; i += kTkThreads) sm.hist[i] = 0;
-      __syncthreads();
-      if (tid == 0 && t1 == (kZeroKey >> 20) && zeros) atomicAdd(&sm.hist[(kZeroKey >> 8) & 0xFFFu], zeros);
-      TK_FOR_EACH({
-        const bool cand = valid & ((key >> 20) == t1) & (key != kZeroKey);
-        atomicAdd(&sm.hist[cand ? static_cast<int>((key >> 8) & 0xFFFu) : trash], 1);
-      })
-      __syncthreads();
-      find_threshold<kT, kBins>(sm.hist, need1, sm.wtot, sm.res);
-      const uint32_t prefix24 = (t1 << 12) | static_cast<uint32_t>(sm.res[0]);
-      const int need2 = need1 - sm.res[1];
-
-      // ---- pass C: per-warp key[7:0] inside prefix24 + per-warp above / zeros ----
-      for (int i = tid; i < kTkWarps * 256 + 32; i += kTkThreads) sm.hist[i] = 0;
-      __syncthreads();
-      {
-        int above = 0, zc = 0;
-        int* wh = sm.hist + w * 256;
-        TK_FOR_EACH({
-          const uint32_t hk = key >> 8;
-          above += valid & (hk > prefix24);
-          zc += valid & (key == kZeroKey);
-          const bool cand = valid & (hk == prefix24) & (key != kZeroKey);
-          atomicAdd(cand ? &wh[key & 0xFFu] : &sm.hist[kHistTrash + lane], 1);
-        })
-        above = warp_sum(above);
-        zc = warp_sum(zc);
-        if (lane == 0) {
-          if (zc && prefix24 == (kZeroKey >> 8)) atomicAdd(&wh[kZeroKey & 0xFFu], zc);
-          sm.above[w] = above;
-        }
-      }
-      __syncthreads();
-      int* merged = sm.hist + kTkWarps * 256 + 32;
-      if (tid < 256) {
-        int s = 0;
-        for (int v = 0; v < kTkWarps; ++v) s += sm.hist[v * 256 + tid];
-        merged[tid] = s;
-      }
-      __syncthreads();
-      find_threshold<kT, 256>(merged, need2, sm.wtot, sm.res);
-      const uint32_t t3 = static_cast<uint32_t>(sm.res[0]);
-      thr = (prefix24 << 8) | t3;
-      remaining = need2 - sm.res[1];
-      {
-        const int* wh = sm.hist + w * 256;
-        int a = 0;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const uint32_t d = lane * 8 + j;
-          if (d > t3) a += wh[d];
-        }
-        a = warp_sum(a);
-        if (lane == 0) {
-          sm.above[w] += a;
-          sm.ties[w] = wh[t3];
-        }
-      }
-      __syncthreads();
-    }
-  }
-  const int tie_base = kTopK - remaining;
-
-  // ---- pass D: ordered compaction into shared memory ----
-  // Canonical order: keys > thr in token order, then the first `remaining`
-  // threshold ties in token order.  kSorted: the same set in token order.
-  int above_pos, tie_pos, sel_pos;
-  {
-    const int av = lane < kTkWarps ? sm.above[lane] : 0;  // one entry per warp
-    const int tv = lane < kTkWarps ? sm.ties[lane] : 0;
-    const int a_inc = warp_incl_scan(av);
-    const int t_inc = warp_incl_scan(tv);
-    const int t_exc = t_inc - tv;
-    const int take = min(max(remaining - t_exc, 0), tv);
-    const int s_inc = warp_incl_scan(av + take);
-    above_pos = __shfl_sync(0xffffffffu, a_inc - av, w);
-    tie_pos = __shfl_sync(0xffffffffu, t_exc, w);
-    sel_pos = __shfl_sync(0xffffffffu, s_inc - (av + take), w);
-  }
-  for (int c = seg_begin; c < seg_end; c += 32 * 16) {
-    const int i0 = c + 16 * lane;
-    uint32_t k[16];
-    const uint32_t vm = load16<kVec>(vals, mrow, i0, seg_end, k);
-    uint32_t ab = 0, tb = 0;
-#pragma unroll
-    for (int t = 0; t < 16; ++t) {
-      const uint32_t v = (vm >> t) & 1u;
-      ab |= (v & (k[t] > thr)) << t;
-      tb |= (v & (k[t] == thr)) << t;
-    }
-    const int na = __popc(ab);
-    const int nt = __popc(tb);
-    const int packed = na | (nt << 16);
-    const int inc = warp_incl_scan(packed);
-    const int total = __shfl_sync(0xffffffffu, inc, 31);
-    const int ex = inc - packed;
-    if constexpr (!kSorted) {
-      if (ab | tb) {
-        int pa = above_pos + (ex & 0xFFFF);
-        int pq = tie_pos + (ex >> 16);
-#pragma unroll
-        for (int t = 0; t < 16; ++t) {
-          if ((ab >> t) & 1u) {
-            sm.d.out_idx[pa] = i0 + t;
-            sm.d.out_key[pa] = k[t];
-            ++pa;
-          } else if ((tb >> t) & 1u) {
-            if (pq < remaining) {
-              sm.d.out_idx[tie_base + pq] = i0 + t;
-              sm.d.out_key[tie_base + pq] = k[t];
-            }
-            ++pq;
-          }
-        }
-      }
-    } else {
-      int pq = tie_pos + (ex >> 16);
-      uint32_t sel = ab;
-#pragma unroll
-      for (int t = 0; t < 16; ++t) {
-        if ((tb >> t) & 1u) {
-          if (pq < remaining) sel |= 1u << t;
-          ++pq;
-        }
-      }
-      const int ns = __popc(sel);
-      const int sinc = warp_incl_scan(ns);
-      const int stot = __shfl_sync(0xffffffffu, sinc, 31);
-      int ps = sel_pos + sinc - ns;
-      if (sel) {
-#pragma unroll
-        for (int t = 0; t < 16; ++t) {
-          if ((sel >> t) & 1u) {
-            sm.d.out_idx[ps] = i0 + t;
-            sm.d.out_key[ps] = k[t];
-            ++ps;
-          }
-        }
-      }
-      sel_pos += stot;
-    }
-    above_pos += total & 0xFFFF;
-    tie_pos += total >> 16;
-  }
-  __syncthreads();
-  for (int i = tid; i < kTopK; i += kTkThreads) {
-    out[i] = src[sm.d.out_idx[i]];
-    if (dst_keys) dst_keys[static_cast<int64_t>(row) * kTopK + i] = sm.d.out_key[i];
-  }
+  // ---- exact fallback: threshold by digit descent, then the ordered write ----
+  int above = 0;
+  const uint32_t thr = digit_descent(sm, RowKeys<kT, kVec>{vals, mrow, len}, kTopK, &above);
+  ordered_write_row<kT, kVec, kSorted>(sm, vals, mrow, src, len, thr, above, out, okeys);
 }
-#undef TK_FOR_EACH
 
 // ---------------------------------------------------------------------------
 // Pass 1 as its own kernels (used by hcu_mqa_logits_hist when hist_lens is
@@ -1208,7 +1053,7 @@ int split_count(int64_t rows, int64_t width, int64_t max_splits) {
 // Rows whose total visible length is at most 2048 keep every entry in index
 // order (decided by the length, not the entry count: one range may hold all
 // of a longer row's top-k).  A candidate list past kCandCap, or one shorter
-// than 2048 (the bound missed), falls back to 12/12/8-bit radix passes over all entries.
+// than 2048 (the bound missed), falls back to the digit descent over all entries.
 // ---------------------------------------------------------------------------
 constexpr int kMaxParts = 16;
 
@@ -1219,62 +1064,55 @@ __device__ __forceinline__ int64_t merge_off(int c, int lshift, int64_t pstride,
          (c & ((1 << lshift) - 1));
 }
 
-// Radix-select fallback over every valid entry (entries [tid*per, (tid+1)*per) below n_ent).
-template <int kT>
-__device__ void merge_radix(TopkSmem<kT>& sm, const uint32_t* __restrict__ keys, const int32_t* __restrict__ gidx,
-                            int per, int n_ent, int lshift, int64_t pstride, int row, int32_t* __restrict__ out,
-                            int32_t* __restrict__ flag) {
-  const int tid = threadIdx.x;
-  const int c0 = tid * per;
-  per = max(0, min(per, n_ent - c0));
-  uint32_t pre = 0u;
-  int need = kTopK;
-  int above = 0;
-  // three passes: key[31:20], key[19:8] within the 12-bit prefix, key[7:0] within the 24-bit prefix
-  for (int pass = 0; pass < 3; ++pass) {
-    const int nb = pass < 2 ? kBins : 256;
-    const int sh = pass == 0 ? 20 : (pass == 1 ? 8 : 0);
-    for (int i = tid; i < nb; i += kT) sm.hist[i] = 0;
-    __syncthreads();
+// Valid entries (global index >= 0) of a row's concatenated lists: thread t
+// owns entries [c0, c0 + per), in global index order across threads.
+struct ListKeys {
+  const uint32_t* keys;
+  const int32_t* gidx;
+  int c0, per, lshift, row;
+  int64_t pstride;
+  template <class F>
+  __device__ __forceinline__ void operator()(F&& f) const {
     for (int i = 0; i < per; ++i) {
       const int64_t o = merge_off(c0 + i, lshift, pstride, row);
-      const uint32_t k = __ldg(keys + o);
-      const bool ok = __ldg(gidx + o) >= 0 && (pass == 0 || (k >> (sh + (pass == 1 ? 12 : 8))) == pre);
-      if (ok) atomicAdd(&sm.hist[(k >> sh) & (nb - 1)], 1);
+      if (__ldg(gidx + o) >= 0) f(__ldg(keys + o));
     }
-    __syncthreads();
-    if (pass < 2)
-      find_threshold<kT, kBins>(sm.hist, need, sm.wtot, sm.res);
-    else
-      find_threshold<kT, 256>(sm.hist, need, sm.wtot, sm.res);
-    pre = (pre << (pass < 2 ? 12 : 8)) | static_cast<uint32_t>(sm.res[0]);
-    above += sm.res[1];
-    need -= sm.res[1];
   }
-  const uint32_t thr = pre;
-  const int remaining = need;
+};
+
+// Exact fallback of the merge (its candidate list overflowed or the sampled
+// bound missed): the threshold by the digit descent over every valid entry,
+// then, since each thread's entries are contiguous in index order, one block
+// scan of (above, tie) counts places every selected entry.
+template <int kT>
+__device__ void merge_exact(TopkSmem<kT>& sm, const uint32_t* __restrict__ keys, const int32_t* __restrict__ gidx,
+                            int per, int n_ent, int lshift, int64_t pstride, int row, int32_t* __restrict__ out,
+                            int32_t* __restrict__ flag) {
+  const int c0 = static_cast<int>(threadIdx.x) * per;
+  per = max(0, min(per, n_ent - c0));
+  const ListKeys src{keys, gidx, c0, per, lshift, row, pstride};
+  int above = 0;
+  const uint32_t thr = digit_descent(sm, src, kTopK, &above);
+  const int remaining = kTopK - above;
   if (threadIdx.x == 0 && flag && sm.mark_any && sm.mark_max >= thr) atomicOr(flag, 1);  // a truncated list
   int na = 0, nt = 0;
-  for (int i = 0; i < per; ++i) {
-    const int64_t o = merge_off(c0 + i, lshift, pstride, row);
-    const uint32_t k = __ldg(keys + o);
-    const bool v = __ldg(gidx + o) >= 0;
-    na += v & (k > thr);
-    nt += v & (k == thr);
-  }
+  src([&](uint32_t k) {
+    na += k > thr;
+    nt += k == thr;
+  });
   int total;
   const int ex = block_excl_scan<kT>(na | (nt << 16), sm.wtot, &total);
-  int ea = ex & 0xFFFF, et = ex >> 16;
+  int pa = ex & 0xFFFF, pq = ex >> 16;
   for (int i = 0; i < per; ++i) {
     const int64_t o = merge_off(c0 + i, lshift, pstride, row);
-    const uint32_t k = __ldg(keys + o);
     const int g = __ldg(gidx + o);
     if (g < 0) continue;
+    const uint32_t k = __ldg(keys + o);
     if (k > thr) {
-      out[ea++] = g;
+      out[pa++] = g;
     } else if (k == thr) {
-      if (et < remaining) out[above + et] = g;
-      ++et;
+      if (pq < remaining) out[above + pq] = g;
+      ++pq;
     }
   }
 }
@@ -1330,7 +1168,7 @@ __global__ __launch_bounds__(kT, 1024 / kT) void cp_merge_kernel(const uint32_t*
   // sample rank (1 = largest) 4 sigma + 4 below the threshold's expected sample rank
   const float t = static_cast<float>(kMs) * static_cast<float>(kTopK) / static_cast<float>(n_ent);
   const int r_lo = min(kMs, static_cast<int>(ceilf(t + 4.f * sqrtf(t) + 4.f)));
-  find_threshold<kT, kBins>(sm.hist, r_lo, sm.wtot, sm.res);
+  block_rank_bin<kT, kBins>(sm.hist, r_lo, sm.wtot, sm.res);
   const uint32_t b1 = static_cast<uint32_t>(sm.res[0]);
   const int need = r_lo - sm.res[1];
 #pragma unroll
@@ -1432,7 +1270,7 @@ __global__ __launch_bounds__(kT, 1024 / kT) void cp_merge_kernel(const uint32_t*
     return;
   }
   if (n > Tk<kT>::kCandCap || n < kTopK) {  // list overflow, or the sampled bound missed
-    merge_radix(sm, keys, gidx, per, n_ent, lshift, pstride, row, out, flag);
+    merge_exact(sm, keys, gidx, per, n_ent, lshift, pstride, row, out, flag);
     return;
   }
   // ---- C: select and ordered write over the candidates ----
@@ -1705,7 +1543,7 @@ extern "C" int hcu_cp_topk_merge_lists(const uint32_t* keys, const int32_t* gidx
   if (rows == 0) return HCU_OK;
   if (!keys || !gidx || !lengths || !dst) return HCU_ERR_ARG;
   // one 1024-thread CTA per row (a 512-thread instance, two CTAs per SM, measured slower: its
-  // 4096-entry candidate list overflows into the radix passes on the bounded exchange's lists)
+  // 4096-entry candidate list overflows into the exact fallback on the bounded exchange's lists)
   const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const size_t smem = sizeof(TopkSmem<1024>);
   cudaFuncSetAttribute(cp_merge_kernel<1024>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
@@ -1859,9 +1697,12 @@ extern "C" int hcu_sparse_mask_topk_transform_noalloc(const float* score, int64_
                        "256 rows (call the regular entry point for larger batches)");
     return HCU_ERR_ARG;
   }
+  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (width <= kTopK)  // every row is short (its first `len` page-table entries, -1 pads): no histogram needed
+    return launch_rows(score, rows, width, score_stride, mask, mask_stride, lengths, page_table, pt_stride, dst,
+                       nullptr, nullptr, s);
   int32_t* ws = noalloc_ws_address();
   if (ws == nullptr) return HCU_ERR_LAUNCH;
-  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   // hist_init_kernel rewrites every workspace element the later kernels read (the
   // array keeps the previous call's contents)
   hist_init_kernel<<<static_cast<int>(rows), 256, 0, s>>>(ws, lengths, static_cast<int>(width),

@@ -136,7 +136,17 @@ def list_len(world: int) -> int:
     import os
 
     env = os.environ.get("HCU_CP_LIST_LEN")
-    return int(env) if env else (1024 if world >= 8 else 2048)
+    if not env:
+        return 1024 if world >= 8 else 2048
+    try:
+        n = int(env)
+    except ValueError:
+        n = -1
+    # checked here, before the step's first collective, so every rank fails at the same point
+    if n < 256 or n > TOPK or n & (n - 1) or n * world < TOPK:
+        raise ValueError(f"HCU_CP_LIST_LEN={env!r}: need a power of two in [256, {TOPK}] "
+                         f"with value x world ({world}) >= {TOPK}")
+    return n
 
 
 def cp_prefill_topk(q, k_fp8_local, k_scale_local, weights, row_end, n_tokens, group=None, mode="rowshard",

@@ -137,3 +137,47 @@ def overlap(a, b):
         sy = set(y[y >= 0].tolist())
         fr.append(len(sx & sy) / max(len(sx), 1))
     return float(np.mean(fr)) if fr else 1.0
+
+
+def e2e_vs_oracle(got, ref_logits, ref_mask, floor, lengths, pt, rows=None, rtol=LOGITS_RTOL):
+    """End-to-end selection check against the oracle's own logits.
+
+    ``got``: device top-k page-table entries ``[n, 2048]`` for oracle rows ``rows`` (default all);
+    ``ref_logits``/``ref_mask``/``floor``: the oracle's logits of those rows.  Returns (overlap,
+    n_bad): the mean per-row fraction of the oracle's selection the device also selected, and the
+    number of disagreeing tokens that are NOT near-ties -- a token may fall on either side only
+    when its oracle value is within the two values' combined tolerance of the oracle's threshold
+    (the 2048th largest value of the row)."""
+    from oracle.indexer import TOPK, mask_bits, row_keys, select_topk
+
+    got = np.asarray(got)
+    rl = np.asarray(ref_logits)
+    W = rl.shape[1]
+    mb = mask_bits(np.asarray(ref_mask), W)
+    fl = np.asarray(floor)
+    lens = np.minimum(np.asarray(lengths, dtype=np.int64), W)
+    fr, bad = [], 0
+    for i in range(got.shape[0]):
+        L = int(max(lens[i], 0))
+        keys = row_keys(rl[i], mb[i], L)
+        sel = select_topk(keys)
+        ptr = np.asarray(pt[i][:L]).astype(np.int64)
+        ref_set = set(ptr[sel].tolist())
+        g = got[i][got[i] >= 0]
+        dev_set = set(g.tolist())
+        fr.append(len(ref_set & dev_set) / max(len(ref_set), 1))
+        if L <= TOPK or ref_set == dev_set:
+            continue
+        inv = {int(e): t for t, e in enumerate(ptr.tolist())}
+        val = np.where(mb[i, :L], np.nan_to_num(rl[i, :L]), 0.0)
+        t_thr = int(sel[-1]) if sel.shape[0] == TOPK else int(sel[np.argmin(keys[sel])])
+        thr = val[t_thr]
+        tol_thr = rtol * max(abs(thr), fl[i, t_thr])
+        for e in ref_set ^ dev_set:
+            t = inv.get(int(e))
+            if t is None:
+                bad += 1
+                continue
+            if abs(val[t] - thr) > rtol * max(abs(val[t]), fl[i, t]) + tol_thr:
+                bad += 1
+    return float(np.mean(fr)) if fr else 1.0, bad

@@ -155,3 +155,19 @@ def test_cp_driver_equals_single_range(world, mode, variant):
         assert p.exitcode == 0
     for r in range(world):
         assert np.array_equal(got[r], ref), f"rank {r}"
+
+
+@pytest.mark.parametrize("value, world, ok", [("1024", 8, True), ("2048", 2, True), ("256", 8, True),
+                                              ("512", 2, False), ("1000", 8, False), ("4096", 2, False),
+                                              ("128", 16, False), ("x", 8, False)])
+def test_cp_list_len_override_is_checked(monkeypatch, value, world, ok):
+    """HCU_CP_LIST_LEN is validated on the host before any collective: a power of two in
+    [256, 2048] whose product with the world size covers 2048 entries per row."""
+    from hcu_ops.cp import list_len
+
+    monkeypatch.setenv("HCU_CP_LIST_LEN", value)
+    if ok:
+        assert list_len(world) == int(value)
+    else:
+        with pytest.raises(ValueError):
+            list_len(world)

@@ -56,6 +56,49 @@ def test_noalloc_topk_equals_regular_entry_point_twice(lib, dev):
         assert torch.equal(got, ref), (rows, dist)
 
 
+def _edge_case(kind, dev):
+    """Scores whose rows take the entry point's edge paths: an empty width (nothing to select, every
+    output -1), widths of at most 2048 (every row short: its page-table entries in order), and a score
+    row stride that is not a multiple of 4 floats (the scalar-load kernel instance)."""
+    g = torch.Generator().manual_seed(5)
+    if kind == "width0":
+        rows, W = 7, 0
+        x = torch.rand(rows, 16, generator=g)
+        mask = torch.zeros(rows, 1, dtype=torch.int16)
+        lens = torch.tensor([0, 5, 100, 0, 3000, 1, 2], dtype=torch.int32)
+    elif kind == "short":
+        rows, W = 19, 2048
+        x = torch.rand(rows, W, generator=g)
+        mask = torch.full((rows, W // 16), -1, dtype=torch.int16)
+        lens = torch.randint(0, 2100, (rows,), generator=g, dtype=torch.int32)
+    else:  # "odd_stride"
+        rows, W = 23, 12000
+        x = torch.rand(rows, W + 3, generator=g)[:, :W]
+        mask = torch.full((rows, (W + 15) // 16), -1, dtype=torch.int16)
+        lens = torch.randint(1000, W + 1, (rows,), generator=g, dtype=torch.int32)
+    pt = torch.randint(0, 1 << 30, (rows, max(W, 16)), generator=g, dtype=torch.int32)
+    x, mask, lens, pt = (t.to(dev) for t in (x, mask, lens, pt))
+    if kind == "width0":
+        x = x[:, :0]  # a zero-width view of a real device allocation (non-null pointer, row stride 16)
+    return x, mask, lens, pt
+
+
+@pytest.mark.parametrize("kind", ["width0", "short", "odd_stride"])
+def test_noalloc_topk_edge_shapes_twice(lib, dev, kind):
+    x, mask, lens, pt = _edge_case(kind, dev)
+    assert x.data_ptr() != 0
+    rows = x.shape[0]
+    for _ in range(2):  # the second call sees whatever the first left in the fixed array
+        ref = torch.full((rows, 2048), -7, dtype=torch.int32, device=dev)
+        got = torch.full((rows, 2048), -9, dtype=torch.int32, device=dev)
+        assert _call(lib.hcu_sparse_mask_topk_transform, x, mask, lens, pt, ref) == HCU_OK
+        assert _call(lib.hcu_sparse_mask_topk_transform_noalloc, x, mask, lens, pt, got) == HCU_OK
+        torch.cuda.synchronize()
+        assert torch.equal(got, ref), kind
+    if kind == "width0":
+        assert (got == -1).all()
+
+
 def test_noalloc_topk_refuses_rows_beyond_its_maximum(lib, dev):
     rows = lib.hcu_topk_noalloc_max_rows() + 1
     x, mask, lens, pt = make_scores(rows, 4096, "pos", seed=3)
