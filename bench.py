@@ -1,23 +1,32 @@
 #!/usr/bin/env python
 """Benchmark of the DSA lightning-indexer path on B200.
 
-Default workload (the decode indexer the metric is quoted on):
-64 requests x next_n=2 rows, contexts U[4096, 65536], 64 index heads x 128 dim fp8,
-shared shuffled pool of 64-token pages.  One step = one CUDA-graph replay of the
-sglang decode call pair: hcu_ops.mqa_logits (tcgen05 fp8 paged logits + mask) ->
-hcu_ops.sparse_mask_topk_transform (exact top-2048 + page-table transform).
+Headline (the decode indexer the metric is quoted on): 64 requests x next_n=2
+rows, contexts U[4096, 65536], 64 index heads x 128 dim fp8, shared shuffled pool of 64-token pages.
+One step = one CUDA-graph replay of the sglang decode call pair: hcu_ops.mqa_logits (tcgen05 fp8
+paged logits + mask) -> hcu_ops.sparse_mask_topk_transform (exact top-2048 + page-table transform).
+metric: G-scores/s = (sum over rows of visible KV tokens) / step time.  The decode indexer does not
+shard: under torchrun every rank runs its own replica ("scaling": "weak"); value = all ranks' scores /
+the slowest rank's time.  A stratified row sample of the headline step is checked against the CPU
+oracle in the same run ("oracle_check").
 
-metric: G-scores/s = (sum over rows of visible KV tokens) / step time.
-Multi-GPU (torchrun): the decode indexer does not shard, so every rank runs its
-own replica of the workload ("scaling": "weak"); value = all ranks' scores / the
-slowest rank's time.  --impl reference times the CPU restatement of the same
-pipeline (the reference's kernels are HIP-only) on the host cores, rank 0 only.
+Sub-records of the same JSON line:
+  cp_prefill  BASELINE config 4 at this N (every N, 1 included): 16384 rows over a 131072-token
+              context split into N KV ranges (hcu_ops.cp); per-rank time spread, clocks, list length,
+              reruns, and equality with the one-range result computed on rank 0.
+  secondary   (N = 1) configs 0, 2, 3, the 656-byte MLA dequant, the indexer-K writer and the MLA
+              front end, each with its roofline, clocks and CPU baseline.
 
-Other workloads (--workload): prefill (config 2), dequant (config 3), mla_dequant.
+--impl reference: the CPU restatement of the reference's algorithm (the reference's kernels are HIP
+for gfx938 and its oracle library is closed) on the host cores, rank 0 only, same metric, config,
+steps and warm-up; it loads none of this repository's compiled libraries.
+--workload NAME runs one secondary workload alone (decode0, prefill, dequant, mla_dequant, kstore,
+mla_kv, cp_prefill).
 """
 from __future__ import annotations
 
 import argparse
+import importlib.util
 import json
 import os
 import statistics
@@ -32,6 +41,17 @@ for _p in (REPO, PKG_ROOT):
         sys.path.insert(0, _p)
 
 L2_BYTES = 126 * 1024 * 1024
+METRIC = "indexer G-scores/s (rows x visible KV tokens / s), decode logits + top-2048"
+DTYPE = "fp8e4m3 x fp8e4m3 -> fp32"
+
+
+def _workloads():
+    """The seeded input generators, loaded by path so that no compiled library is imported."""
+    spec = importlib.util.spec_from_file_location("hcu_workloads",
+                                                  os.path.join(PKG_ROOT, "hcu_ops", "workloads.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
 
 
 def _peaks():
@@ -66,6 +86,7 @@ class ClockSampler:
     def __init__(self, index):
         self.index = index
         self.proc = None
+        self.out = ""
 
     def __enter__(self):
         try:
@@ -77,7 +98,6 @@ class ClockSampler:
         return self
 
     def __exit__(self, *a):
-        self.out = ""
         if self.proc is not None:
             time.sleep(0.25)
             self.proc.terminate()
@@ -108,21 +128,60 @@ def _dist():
     return world, rank, local
 
 
+def _events():
+    import torch
+
+    return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+
+def _timed(fn, steps, local):
+    """steps calls of fn on the current stream between CUDA events (synchronised on both sides),
+    clocks sampled meanwhile; returns (ms per call, clocks)."""
+    import torch
+
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        a, b = _events()
+        a.record()
+        for _ in range(steps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+    return a.elapsed_time(b) / steps, clk.summary()
+
+
+def _read_flush(dev):
+    """An L2 flush that leaves no dirty lines behind: a reduction reading 256 MB."""
+    import torch
+
+    buf = torch.ones(256 << 20, dtype=torch.uint8, device=dev)
+    return lambda: buf.sum(dtype=torch.int32)
+
+
+def _per_launch(fn, iters, flush, local):
+    """Mean time of single launches, each after an L2 flush (events around the launch only)."""
+    import torch
+
+    evs = []
+    with ClockSampler(local) as clk:
+        for _ in range(iters):
+            flush()
+            a, b = _events()
+            a.record()
+            fn()
+            b.record()
+            evs.append((a, b))
+        torch.cuda.synchronize()
+    return sum(a.elapsed_time(b) for a, b in evs) / iters, clk.summary()
+
+
 # ------------------------------------------------------------------------------------------------
-# decode (config 1) -- the headline
+# headline: decode (config 1)
 # ------------------------------------------------------------------------------------------------
-def decode_inputs(device, seed):
-    from hcu_ops.workloads import config1
-
-    return config1(device=device, seed=seed)
-
-
 def decode_alg_bytes(w):
     """Algorithmic HBM bytes of one logits launch: each group's K pages read once (128 fp8 + 4 B
     scale per token), q + weights, block-table entries, logits written at every visible token,
     and the mask words of the full width (each processed tile's words, the rest zeroed by the kernel)."""
-    import torch
-
     lens = w["context_lens"].long().cpu()
     G, H = w["group_size"], w["heads"]
     B = lens.numel()
@@ -132,45 +191,92 @@ def decode_alg_bytes(w):
     q_bytes = B * H * 128 + B * H * 4
     logits_bytes = int(lens.sum() * 4)
     mask_bytes = B * (w["max_context_len"] // 16) * 2 + int(((glen + 127) // 128).sum() * G * 16)
-    del torch
     return k_bytes + bt_bytes + q_bytes + logits_bytes + mask_bytes
+
+
+def decode_config(world, seed=0):
+    """The headline's `config` (identical in both arms); computed from the generator's lengths."""
+    wl = _workloads()
+    lens = wl.config1_lens(seed)
+    pages = sum((L + 63) // 64 for L in lens)
+    return {"workload": "config1: decode 64 req x next_n 2 (128 rows), ctx U[4096,65536], 64 heads x 128, "
+                        "64-token pages, shuffled pool; CUDA-graph replay",
+            "rows": 2 * len(lens), "heads": 64, "width": 65536, "pairs_per_gpu": sum(2 * L - 1 for L in lens),
+            "kv_pool_bytes": pages * 64 * 132, "l2": "no flush: K pool > 126 MB L2",
+            "parallelism": f"replicas x{world}"}
+
+
+def decode_oracle_check(w, lg, mk, out, n_req=8):
+    """The oracle on the first n_req requests of the step's inputs, against the device's logits, mask
+    and selection: (check dict, CPU seconds of the oracle's logits + top-k)."""
+    import numpy as np
+    import torch
+
+    from oracle import indexer as O
+
+    G = w["group_size"]
+    rows = n_req * G
+    W = w["max_context_len"]
+    q = w["q"][:rows].cpu().view(torch.uint8).numpy().reshape(rows, w["heads"], 128)
+    kv = w["kv_cache"].cpu().numpy().reshape(w["kv_cache"].shape[0], -1)
+    lens = w["context_lens"][:rows].cpu().numpy()
+    pt = w["page_table_size_1"][:rows].cpu().numpy()
+    t0 = time.perf_counter()
+    rl, rm, fl = O.mqa_logits_paged(q, kv, w["weights"][:rows].cpu().numpy(), lens, w["block_table"][:rows].cpu().numpy(),
+                                    W, G, want_floor=True)
+    ref = O.topk_transform(rl, rm, lens, pt)
+    dt = time.perf_counter() - t0
+    dl, dm, do = lg[:rows].cpu().numpy(), mk[:rows].cpu().numpy(), out[:rows].cpu().numpy()
+    md, mr = O.mask_bits(dm, W), O.mask_bits(rm, W)
+    both = md & mr
+    rel = np.abs(dl[both] - rl[both]) / np.maximum(np.abs(rl[both]), fl[both])
+    same = O.topk_transform(dl, dm, lens, pt)
+    ov = np.mean([len(set(a[a >= 0].tolist()) & set(b[b >= 0].tolist())) / max(int((b >= 0).sum()), 1)
+                  for a, b in zip(do, ref)])
+    chk = {"rows": rows, "logits_max_rel_err": float(rel.max(initial=0.0)), "logits_tol": 1e-2,
+           "mask_bits_differing": int((md ^ mr).sum()), "topk_exact_on_device_logits": bool(np.array_equal(do, same)),
+           "e2e_overlap": float(ov)}
+    chk["ok"] = bool(chk["logits_max_rel_err"] <= 1e-2 and chk["topk_exact_on_device_logits"] and ov >= 0.999)
+    return chk, dt, float(np.asarray(lens, np.int64).sum())
 
 
 def run_decode(args, world, rank, local):
     import torch
 
     import hcu_ops
+    from hcu_ops.workloads import config1
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    w = decode_inputs(dev, seed=rank)
+    w = config1(device=dev, seed=rank)
     pairs = int(w["context_lens"].long().sum())
     lens, pt, cu = w["context_lens"], w["page_table_size_1"], w["cu_seqlens_q"]
 
     def step():
         lg, mk = hcu_ops.mqa_logits(w["q"], w["kv_cache"], w["weights"], lens, w["block_table"],
                                     w["max_context_len"], w["group_size"], hist_lens=lens)
-        return hcu_ops.sparse_mask_topk_transform(lg, mk, lens, pt, cu, 2048)
+        return lg, mk, hcu_ops.sparse_mask_topk_transform(lg, mk, lens, pt, cu, 2048)
 
     def logits_only():
         return hcu_ops._C.mqa_logits_hist(w["q"], w["kv_cache"], w["weights"], lens, w["block_table"],
                                           w["max_context_len"], w["group_size"], 0, 0, None)
 
+    warm = max(args.warmup, 3)
     s = torch.cuda.Stream(device=dev)
     s.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(s):
-        for _ in range(max(args.warmup, 3)):
+        for _ in range(warm):
             step()
             logits_only()
     torch.cuda.current_stream().wait_stream(s)
     torch.cuda.synchronize()
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g):
-        out = step()
+        lg_g, mk_g, out = step()
     g_lg = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g_lg):
         logits_only()
-    for _ in range(max(args.warmup, 3)):
+    for _ in range(warm):
         g.replay()
         g_lg.replay()
     torch.cuda.synchronize()
@@ -180,77 +286,36 @@ def run_decode(args, world, rank, local):
             torch.distributed.barrier()
         torch.cuda.synchronize()
 
-    stream = torch.cuda.current_stream()
-    # ---- headline: K graph replays of the pipeline (inputs resident in HBM; K pool > L2)
-    with ClockSampler(local) as clk:
-        barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(args.steps):
-            g.replay()
-        e1.record(stream)
-        barrier()
-    ms = e0.elapsed_time(e1) / args.steps
-    # ---- dominant kernel alone (the logits op) for the roofline
+    # ---- headline: K graph replays of the pipeline (inputs resident in HBM; the K pool exceeds L2)
     barrier()
-    l0, l1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    l0.record(stream)
-    for _ in range(args.steps):
-        g_lg.replay()
-    l1.record(stream)
+    ms, clocks = _timed(g.replay, args.steps, local)
     barrier()
-    ms_logits = l0.elapsed_time(l1) / args.steps
-    # ---- e2e through the public API with host buffers: every step copies that step's inputs (query rows,
-    # head weights, context lengths, block table) from pinned host memory and reads the result back.  The KV
-    # cache and the per-token page table (page_table_size_1, built on the device from the request-to-token
-    # pool by the serving engine's metadata step) are device state, like the cache itself.
-    host = {k: w[k].cpu().pin_memory() for k in ("q", "weights", "context_lens", "block_table")}
-    dev_in = {k: torch.empty_like(w[k]) for k in host}
-    res_host = torch.empty((lens.numel(), 2048), dtype=torch.int32).pin_memory()
-    h2d = sum(t.numel() * t.element_size() for t in host.values())
-    d2h = res_host.numel() * 4
-
-    def e2e_step():
-        for k, t in host.items():
-            dev_in[k].copy_(t, non_blocking=True)
-        lg, mk = hcu_ops.mqa_logits(dev_in["q"], w["kv_cache"], dev_in["weights"], dev_in["context_lens"],
-                                    dev_in["block_table"], w["max_context_len"], w["group_size"],
-                                    hist_lens=dev_in["context_lens"])
-        o = hcu_ops.sparse_mask_topk_transform(lg, mk, dev_in["context_lens"], w["page_table_size_1"], cu, 2048)
-        res_host.copy_(o, non_blocking=True)
-
-    for _ in range(3):
-        e2e_step()
+    # ---- the dominant kernel alone (the logits op) for the roofline
+    ms_logits, _ = _timed(g_lg.replay, args.steps, local)
     barrier()
-    e2e_steps = min(args.steps, 200)
-    x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    x0.record(stream)
-    for _ in range(e2e_steps):
-        e2e_step()
-    x1.record(stream)
-    barrier()
-    ms_e2e = x0.elapsed_time(x1) / e2e_steps
+    ms_e2e, e2e_steps, h2d, d2h, e2e_ok = _decode_e2e(w, out, args.steps)
     st = hcu_ops.read_device_status(clear=True)
-    ok = torch.equal(res_host, out.cpu())
 
     t = torch.tensor([ms, ms_logits, ms_e2e, float(pairs)], dtype=torch.float64, device=dev)
+    per_rank_ms = [ms]
     if world > 1:
-        mx = t.clone()
-        torch.distributed.all_reduce(mx, op=torch.distributed.ReduceOp.MAX)
-        sm_ = t.clone()
-        torch.distributed.all_reduce(sm_, op=torch.distributed.ReduceOp.SUM)
-        ms, ms_logits, ms_e2e = mx[0].item(), mx[1].item(), mx[2].item()
-        total_pairs = sm_[3].item()
+        allt = [torch.zeros_like(t) for _ in range(world)]
+        torch.distributed.all_gather(allt, t)
+        per_rank_ms = [float(x[0]) for x in allt]
+        ms = max(float(x[0]) for x in allt)
+        ms_logits = max(float(x[1]) for x in allt)
+        ms_e2e = max(float(x[2]) for x in allt)
+        total_pairs = sum(float(x[3]) for x in allt)
     else:
         total_pairs = float(pairs)
     if rank != 0:
         return None
+    check, cpu_s, cpu_pairs = decode_oracle_check(w, lg_g, mk_g, out)
     hbm, _, src = _peaks()
     alg = decode_alg_bytes(w)
     achieved = alg / (ms_logits * 1e-3) / 1e9
-    traffic = _profile_traffic("mqa_logits_paged_config1")
     rec = {
-        "metric": "indexer G-scores/s (rows x visible KV tokens / s), decode logits + top-2048",
+        "metric": METRIC,
         "value": total_pairs / (ms * 1e-3) / 1e9,
         "unit": "G-scores/s",
         "n_gpus": world,
@@ -260,142 +325,342 @@ def run_decode(args, world, rank, local):
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "fp8e4m3 x fp8e4m3 -> fp32",
+        "dtype": DTYPE,
         "data": "synthetic (seeded; q,K ~ N(0,1) per-row/per-token amax/448 fp8; w ~ N(0,1)/8)",
-        "config": {"workload": "config1: decode 64 req x next_n 2 (128 rows), ctx U[4096,65536], "
-                               "64 heads x 128, 64-token pages, shuffled pool; CUDA-graph replay",
-                   "rows": int(lens.numel()), "heads": w["heads"], "width": w["max_context_len"],
-                   "pairs_per_gpu": pairs, "kv_pool_bytes": int(w["kv_cache"].numel()),
-                   "l2": "no flush: K pool > 126 MB L2", "parallelism": f"replicas x{world}"},
+        "config": decode_config(world),
+        "per_rank_ms": {"min": min(per_rank_ms), "median": statistics.median(per_rank_ms), "max": max(per_rank_ms)},
         "top_k_rows_per_s": lens.numel() * world / (ms * 1e-3),
         "logits_op_ms": ms_logits,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                     "traffic": traffic, "kernel": "mqa_logits_paged_kernel<64, false> (mask tails zeroed in-kernel)",
+                     "traffic": _profile_traffic("mqa_logits_paged_config1"),
+                     "kernel": "mqa_logits_paged_kernel<64, false> (mask tails zeroed in-kernel)",
                      "alg_bytes_per_launch": alg, "peak_source": src},
+        "step_roofline": {"alg_bytes": alg + lens.numel() * 2048 * 8, "frac_of_hbm": (alg + lens.numel() * 2048 * 8)
+                          / (ms * 1e-3) / 1e9 / hbm, "note": "logits launch bytes + the top-k's page-table gather "
+                                                             "and output"},
         "e2e": {"value": total_pairs / (ms_e2e * 1e-3) / 1e9, "unit": "G-scores/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e, "steps": e2e_steps,
-                "result_matches_graph": bool(ok)},
+                "result_matches_graph": bool(e2e_ok),
+                "how": "public API, eager; every step copies its inputs from pinned host memory and its "
+                       "[128, 2048] result back, on two copy streams double-buffered against the compute"},
         "gpu_launches": args.steps * 2,
-        "clocks": clk.summary(),
+        "clocks": clocks,
         "device_status": st,
+        "oracle_check": check,
     }
     if world == 1 and not args.no_cpu_baseline:
-        rec["cpu_baseline"] = cpu_decode_sample(w)
+        rec["cpu_baseline"] = {"value": cpu_pairs / cpu_s / 1e9, "unit": "G-scores/s", "cores": _threads(),
+                               "kind": "port",
+                               "sample": f"first 8 requests ({check['rows']} rows, {int(cpu_pairs)} scores) of the "
+                                         f"same workload, oracle logits + top-k, {cpu_s:.2f} s"}
     return rec
 
 
-def cpu_decode_sample(w, n_req=8):
-    """Oracle (CPU restatement) on the first n_req requests of the same workload."""
-    import numpy as np
+def _threads():
     import torch
 
-    from oracle import indexer as O
+    return torch.get_num_threads()
 
-    G = w["group_size"]
-    rows = n_req * G
-    q = w["q"][:rows].cpu().view(torch.uint8).numpy().reshape(rows, w["heads"], 128)
-    kv = w["kv_cache"].cpu().numpy().reshape(w["kv_cache"].shape[0], -1)
-    wt = w["weights"][:rows].cpu().numpy()
-    lens = w["context_lens"][:rows].cpu().numpy()
-    bt = w["block_table"][:rows].cpu().numpy()
-    pt = w["page_table_size_1"][:rows].cpu().numpy()
-    t0 = time.perf_counter()
-    lg, m, _ = O.mqa_logits_paged(q, kv, wt, lens, bt, w["max_context_len"], G)
-    O.topk_transform(lg, m, lens, pt)
-    dt = time.perf_counter() - t0
-    pairs = float(np.asarray(lens, np.int64).sum())
-    return {"value": pairs / dt / 1e9, "unit": "G-scores/s", "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"first {n_req} requests ({rows} rows, {int(pairs)} scores) of the same workload, "
-                      f"oracle logits + top-k, {dt:.2f} s"}
+
+def _decode_e2e(w, out_graph, steps):
+    """The headline metric through the public API with host buffers: every step copies its inputs
+    (query rows, head weights, context lengths, block table) from pinned host memory and reads its
+    [rows, 2048] result back; the KV cache and the per-token page table (built on the device by the
+    serving engine's metadata step) are device state.  Copies run on two copy streams, double-buffered,
+    so step i + 1's inputs and step i - 1's result move while step i computes."""
+    import torch
+
+    import hcu_ops
+
+    keys = ("q", "weights", "context_lens", "block_table")
+    host = {k: w[k].cpu().pin_memory() for k in keys}
+    sets = [{k: torch.empty_like(w[k]) for k in keys} for _ in range(2)]
+    rows = w["context_lens"].numel()
+    res_host = [torch.empty((rows, 2048), dtype=torch.int32).pin_memory() for _ in range(2)]
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = rows * 2048 * 4
+    comp = torch.cuda.current_stream()
+    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_done = [torch.cuda.Event() for _ in range(2)]
+    pt, cu, kv, width, G = (w["page_table_size_1"], w["cu_seqlens_q"], w["kv_cache"], w["max_context_len"],
+                            w["group_size"])
+
+    def load(i):
+        b = i % 2
+        with torch.cuda.stream(s_in):
+            if i >= 2:
+                s_in.wait_event(ev_done[b])  # step i - 2 is done with this input set
+            for k in keys:
+                sets[b][k].copy_(host[k], non_blocking=True)
+            ev_in[b].record(s_in)
+
+    def run(n):
+        load(0)
+        for i in range(n):
+            b = i % 2
+            if i + 1 < n:
+                load(i + 1)
+            comp.wait_event(ev_in[b])
+            d = sets[b]
+            lg, mk = hcu_ops.mqa_logits(d["q"], kv, d["weights"], d["context_lens"], d["block_table"], width, G,
+                                        hist_lens=d["context_lens"])
+            o = hcu_ops.sparse_mask_topk_transform(lg, mk, d["context_lens"], pt, cu, 2048)
+            ev_done[b].record(comp)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(ev_done[b])
+                res_host[b].copy_(o, non_blocking=True)
+                o.record_stream(s_out)
+        comp.wait_stream(s_out)
+        comp.wait_stream(s_in)
+
+    run(3)
+    torch.cuda.synchronize()
+    n = max(2, min(steps, 200))
+    a, b = _events()
+    a.record()
+    run(n)
+    b.record()
+    torch.cuda.synchronize()
+    ok = torch.equal(res_host[(n - 1) % 2], out_graph.cpu())
+    return a.elapsed_time(b) / n, n, h2d, d2h, ok
+
+
+def _decode_ref_sample_reqs(steps, warmup, budget_s=120.0, per_step_s=1.3):
+    """Requests per reference step: the whole config when (steps + warm-up) fit the CPU budget,
+    else a proportional subset (each step is then a bounded sample of the workload)."""
+    n = int(64 * budget_s / max((steps + warmup) * per_step_s, 1e-9))
+    return max(1, min(64, n))
 
 
 def run_reference(args):
-    """CPU restatement of the reference pipeline on the same config, all host threads."""
+    """CPU restatement of the reference pipeline on the headline config, all host threads: logits of
+    every visible (row, token) pair and the exact top-2048 of every row, per step."""
     import numpy as np
     import torch
 
-    from hcu_ops.workloads import config1
     from oracle import indexer as O
 
+    wl = _workloads()
+    world, _, _ = _dist()
     torch.set_num_threads(os.cpu_count() or 1)
-    w = config1(device="cpu", seed=0)
+    w = wl.config1(device="cpu", seed=0)
     G = w["group_size"]
-    q = w["q"].view(torch.uint8).numpy().reshape(w["q"].shape[0], w["heads"], 128)
+    n_req = _decode_ref_sample_reqs(args.steps, args.warmup)
+    rows = n_req * G
+    q = w["q"][:rows].view(torch.uint8).numpy().reshape(rows, w["heads"], 128)
     kv = w["kv_cache"].numpy().reshape(w["kv_cache"].shape[0], -1)
-    lens = w["context_lens"].numpy()
+    lens = w["context_lens"][:rows].numpy()
+    bt = w["block_table"][:rows].numpy()
+    pt = w["page_table_size_1"][:rows].numpy()
+    wt = w["weights"][:rows].numpy()
     pairs = float(lens.astype(np.int64).sum())
 
     def step():
-        lg, m, _ = O.mqa_logits_paged(q, kv, w["weights"].numpy(), lens, w["block_table"].numpy(),
-                                      w["max_context_len"], G)
-        O.topk_transform(lg, m, lens, w["page_table_size_1"].numpy())
+        lg, m, _ = O.mqa_logits_paged(q, kv, wt, lens, bt, w["max_context_len"], G)
+        O.topk_transform(lg, m, lens, pt)
 
-    steps = min(args.steps, 20)  # each step is the whole config on the CPU (~1-2 s)
-    for _ in range(min(args.warmup, 1)):
+    for _ in range(args.warmup):
         step()
     t0 = time.perf_counter()
-    for _ in range(steps):
+    for _ in range(args.steps):
         step()
-    dt = (time.perf_counter() - t0) / steps
+    dt = (time.perf_counter() - t0) / args.steps
     v = pairs / dt / 1e9
+    sample = ("whole config 1 per step" if n_req == 64 else
+              f"first {n_req} of 64 requests ({rows} rows, {int(pairs)} scores) per step")
     return {
         "impl": "reference",
-        "metric": "indexer G-scores/s (rows x visible KV tokens / s), decode logits + top-2048",
-        "value": v, "unit": "G-scores/s", "n_gpus": 0, "steps": steps, "warmup": min(args.warmup, 1),
-        "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "fp8e4m3 x fp8e4m3 -> fp32", "data": "synthetic (seeded, same generator as the GPU arm)",
-        "config": {"workload": "config1: decode 64 req x next_n 2 (128 rows), ctx U[4096,65536], 64 heads x 128",
-                   "pairs": int(pairs)},
+        "metric": METRIC, "value": v, "unit": "G-scores/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": DTYPE, "data": "synthetic (seeded, same generator as the GPU arm)",
+        "config": decode_config(world),
         "cpu_baseline": {"value": v, "unit": "G-scores/s", "cores": torch.get_num_threads(), "kind": "port",
-                         "sample": "whole config 1 per step (oracle restatement: the reference's kernels are "
-                                   "HIP for gfx938 and lightop is closed)"},
+                         "sample": sample + " (CPU restatement of the reference's algorithm: its kernels are HIP "
+                                            "for gfx938 and its bit-exact oracle library is closed)"},
         "e2e": {"value": v, "unit": "G-scores/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
 
 # ------------------------------------------------------------------------------------------------
-# secondary workloads: bench.py --workload decode0 | prefill | dequant | mla_dequant | kstore | mla_kv | cp_prefill
-# (BASELINE configs 0, 2, 3, the 656-byte MLA dequant, and 4).  Inputs that fit in L2 are timed one
-# launch at a time with a 256 MB L2 flush between launches (events around the launch only).
+# config 4: context-parallel prefill (every N)
 # ------------------------------------------------------------------------------------------------
-def _timed_iters(fn, iters, flush):
+CP_ROWS, CP_N = 16384, 131072
+
+
+def _stratified(rows, n=64):
+    import numpy as np
+
+    return np.unique(np.linspace(0, rows - 1, n).astype(np.int64))
+
+
+def _ragged_cpu_sample(rows, prefix, topk_too=True):
+    """CPU oracle (logits + top-k) on 64 stratified rows of a ragged workload: (G-scores/s, sample text)."""
+    import numpy as np
     import torch
 
-    evs = []
-    for _ in range(iters):
-        if flush is not None:
-            flush()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        fn()
-        b.record()
-        evs.append((a, b))
-    torch.cuda.synchronize()
-    return sum(a.elapsed_time(b) for a, b in evs) / iters  # ms
+    from oracle import indexer as O
+
+    w = _workloads().make_ragged(rows, prefix, heads=64)
+    sel = _stratified(rows)
+    t0 = time.perf_counter()
+    lg, m, _ = O.mqa_logits_ragged(w["q"].view(torch.uint8).numpy(), w["k_fp8"].view(torch.uint8).numpy(),
+                                   w["k_scale"].numpy(), w["weights"].numpy(), w["row_start"].numpy(),
+                                   w["row_end"].numpy(), rows=list(sel))
+    if topk_too:
+        N = lg.shape[1]
+        O.topk_transform(lg, m, w["row_end"].numpy()[sel], np.broadcast_to(np.arange(N, dtype=np.int32), (len(sel), N)))
+    dt = time.perf_counter() - t0
+    pairs = float(w["row_end"].numpy()[sel].astype(np.int64).sum())
+    return pairs / dt / 1e9, (f"{len(sel)} stratified rows of {rows} ({int(pairs)} scores, {dt:.2f} s), oracle "
+                              f"logits + top-k; rate extrapolated to the whole workload by pair count")
 
 
-def _flusher(dev):
-    import torch
-
-    buf = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    return lambda: buf.zero_()
-
-
-def _base_record(args, world, metric, value, unit, ms, workload, **cfg):
-    return {"metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "fp8e4m3 x fp8e4m3 -> fp32", "data": "synthetic (seeded)",
-            "config": dict(workload=workload, **cfg)}
-
-
-def run_decode0(args, world, rank, local):
+def run_cp_prefill(args, world, rank, local, steps=None, warmup=None):
     import torch
 
     import hcu_ops
-    from hcu_ops.workloads import config0
+    from hcu_ops.cp import cp_prefill_topk, kv_range, list_len
 
     dev = torch.device("cuda", local)
-    w = config0(device=dev, seed=rank)
+    torch.cuda.set_device(dev)
+    rows, N = CP_ROWS, CP_N
+    w = _workloads().make_ragged(rows, N - rows, heads=64, seed=0, device=dev)  # identical on every rank
+    lo, hi = kv_range(rank, world, N, causal_rows=rows)
+    kf, ks = w["k_fp8"][lo:hi].contiguous(), w["k_scale"][lo:hi].contiguous()
+    steps = steps or min(args.steps, 20)
+    warmup = warmup or max(3, min(args.warmup, 5))
+    stats = {}
+
+    def step():
+        return cp_prefill_topk(w["q"], kf, ks, w["weights"], w["row_end"], N, causal_rows=rows, stats=stats)
+
+    for _ in range(warmup):
+        out = step()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    stats.clear()
+    with ClockSampler(local) as clk:
+        a, b = _events()
+        a.record()
+        for _ in range(steps):
+            out = step()
+        b.record()
+        torch.cuda.synchronize()
+    ms_mine = a.elapsed_time(b) / steps
+    t = torch.tensor([ms_mine], dtype=torch.float64, device=dev)
+    per_rank = [ms_mine]
+    if world > 1:
+        allt = [torch.zeros_like(t) for _ in range(world)]
+        torch.distributed.all_gather(allt, t)
+        per_rank = [float(x.item()) for x in allt]
+    ms = max(per_rank)
+    reruns = stats.get("reruns", 0)
+    if world > 1:
+        r = torch.tensor([reruns], dtype=torch.int64, device=dev)
+        torch.distributed.all_reduce(r, op=torch.distributed.ReduceOp.MAX)
+        reruns = int(r.item())
+    if rank != 0:
+        return None
+    # the one-range result on this GPU (untimed equality check), then its time on the same box
+    ident = torch.arange(N, dtype=torch.int32, device=dev).expand(rows, N)
+    cu = torch.arange(rows + 1, dtype=torch.int32, device=dev)
+    zeros = torch.zeros(rows, dtype=torch.int32, device=dev)
+
+    def one_gpu():
+        lg, mk = hcu_ops.mqa_logits_ragged(w["q"], w["k_fp8"], w["k_scale"], w["weights"], zeros, w["row_end"])
+        return hcu_ops.sparse_mask_topk_transform(lg, mk, w["row_end"], ident, cu, 2048)
+
+    ref = one_gpu()
+    matches = bool(torch.equal(out, ref))
+    del ref
+    ms_one = None
+    if world > 1:
+        one_gpu()
+        ms_one, _ = _timed(one_gpu, 3, local)
+    pairs = int(w["row_end"].long().sum())
+    flops = 2.0 * 64 * 128 * pairs
+    _, bf16, src = _peaks()
+    achieved = flops / (ms * 1e-3) / 1e12
+    rec = {"metric": "CP prefill indexer G-scores/s (rows x visible KV tokens / s): logits + bounds + filter + "
+                     "exchange + merge", "value": pairs / (ms * 1e-3) / 1e9, "unit": "G-scores/s", "n_gpus": world,
+           "steps": steps, "warmup": warmup, "ms_per_step": ms, "scaling": "strong",
+           "per_rank_ms": {"min": min(per_rank), "median": statistics.median(per_rank), "max": max(per_rank)},
+           "config": {"workload": f"config4: {rows} rows x ({N - rows} + i + 1) tokens over a {N}-token context in "
+                                  f"{world} KV ranges balanced by visible pairs, 64 heads", "pairs": pairs,
+                      "parallelism": f"cp{world}", "l2": "no flush: logits and inputs exceed L2"},
+           "list_len": list_len(world) if world > 1 else None, "reruns": reruns,
+           "exchange": stats.get("exchange", "none (one range)"),
+           "matches_1gpu": matches,
+           "roofline": {"bound": "tensor", "achieved": achieved, "peak": 2.0 * bf16 * world, "unit": "TFLOP/s",
+                        "frac": achieved / (2.0 * bf16 * world), "traffic": None,
+                        "peak_source": src + " (fp8 dense = 2 x measured bf16 burst, x n_gpus)"},
+           "gpu_launches_per_step": stats.get("launches"),
+           "clocks": clk.summary()}
+    if ms_one is not None:
+        rec["one_gpu_ms_same_box"] = ms_one
+        rec["speedup_vs_one_gpu"] = ms_one / ms
+    if world == 1 and not args.no_cpu_baseline:
+        v, sample = _ragged_cpu_sample(rows, N - rows)
+        rec["cpu_baseline"] = {"value": v, "unit": "G-scores/s", "cores": _threads(), "kind": "port",
+                               "sample": sample}
+    return rec
+
+
+# ------------------------------------------------------------------------------------------------
+# secondary workloads (N = 1): configs 0, 2, 3, the 656-byte MLA dequant, the K writer, the MLA front end
+# ------------------------------------------------------------------------------------------------
+def _rec(metric, value, unit, ms, steps, workload, higher=True, **cfg):
+    return {"metric": metric, "value": value, "unit": unit, "ms_per_step": ms, "steps": steps,
+            "higher_is_better": higher, "config": dict(workload=workload, **cfg)}
+
+
+def _rotating_graph(fns, launches, dev):
+    """A CUDA graph of `launches` calls cycling through the instances' callables (their inputs
+    together exceed L2); every launch's output stays allocated, so each writes its own buffer and
+    every launch streams from and to HBM.  Returns (graph, the outputs it writes)."""
+    import torch
+
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for f in fns:
+            f()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    keep = []
+    with torch.cuda.graph(g):
+        for i in range(launches):
+            keep.append(fns[i % len(fns)]())
+    return g, keep
+
+
+def _hbm_loop(fns, per_launch_bytes, steps, local, dev):
+    """Graph-replayed back-to-back launches over rotating instances: (ms per launch, clocks, launches)."""
+    per_graph = 4 * len(fns)
+    g, keep = _rotating_graph(fns, per_graph, dev)
+    for _ in range(3):
+        g.replay()
+    reps = max(1, min(steps, 50))
+    ms, clocks = _timed(g.replay, reps, local)
+    del keep
+    return ms / per_graph, clocks, reps * per_graph
+
+
+def _instances(bytes_per_instance):
+    return max(2, -(-3 * L2_BYTES // max(bytes_per_instance, 1)))
+
+
+def sec_decode0(args, local):
+    import torch
+
+    import hcu_ops
+
+    dev = torch.device("cuda", local)
+    wl = _workloads()
+    w = wl.config0(device=dev, seed=0)
     lens, pt, cu = w["context_lens"], w["page_table_size_1"], w["cu_seqlens_q"]
 
     def step():
@@ -403,62 +668,161 @@ def run_decode0(args, world, rank, local):
                                     w["max_context_len"], 1, hist_lens=lens)
         return hcu_ops.sparse_mask_topk_transform(lg, mk, lens, pt, cu, 2048)
 
-    for _ in range(max(args.warmup, 3)):
+    for _ in range(5):
         step()
-    flush = _flusher(dev)
-    iters = min(args.steps, 500)
-    ms = _timed_iters(step, iters, flush)
+    iters = max(10, min(args.steps, 200))
+    ms, clocks = _per_launch(step, iters, _read_flush(dev), local)
     pairs = int(lens.long().sum())
     hbm, _, src = _peaks()
     alg = decode_alg_bytes(w)
-    rec = _base_record(args, world, "decode indexer latency, config 0 (1 row x 8192 tokens, 64 heads)",
-                       ms * 1e3, "us", ms, "config0: decode 1 x 8192, 64 heads, permuted pages; L2 flushed",
-                       pairs=pairs)
-    rec["higher_is_better"] = False
-    rec["g_scores_per_s"] = pairs / (ms * 1e-3) / 1e9
+    rec = _rec("decode indexer latency, config 0 (1 row x 8192 tokens, 64 heads), logits + top-2048", ms * 1e3,
+               "us", ms, iters, "config0: decode 1 x 8192, 64 heads, permuted pages; L2 flushed (read) before "
+               "every call", higher=False, pairs=pairs)
     rec["roofline"] = {"bound": "latency", "achieved": alg / (ms * 1e-3) / 1e9, "peak": hbm, "unit": "GB/s",
                        "frac": alg / (ms * 1e-3) / 1e9 / hbm, "traffic": None, "peak_source": src,
                        "note": "1.1 MB of work: latency-bound, roofline not claimed"}
-    rec["gpu_launches"] = iters * 2
+    rec["gpu_launches"] = iters * 3
+    rec["clocks"] = clocks
+    if not args.no_cpu_baseline:
+        import numpy as np
+
+        from oracle import indexer as O
+
+        wc = wl.config0()
+        t0 = time.perf_counter()
+        lg, m, _ = O.mqa_logits_paged(wc["q"].view(torch.uint8).numpy().reshape(1, 64, 128),
+                                      wc["kv_cache"].numpy().reshape(wc["kv_cache"].shape[0], -1),
+                                      wc["weights"].numpy(), wc["context_lens"].numpy(), wc["block_table"].numpy(),
+                                      wc["max_context_len"], 1)
+        O.topk_transform(lg, m, wc["context_lens"].numpy(), wc["page_table_size_1"].numpy())
+        dt = time.perf_counter() - t0
+        rec["cpu_baseline"] = {"value": dt * 1e6, "unit": "us", "cores": _threads(), "kind": "port",
+                               "sample": "whole config 0 (oracle logits + top-k)"}
+        del np
     return rec
 
 
-def run_dequant(args, world, rank, local, mla=False):
+def sec_prefill(args, local):
+    """Config 2: logits + top-k of a 8192-row prefill chunk over a 65536-token prefix."""
     import torch
 
     import hcu_ops
-    from hcu_ops.workloads import make_index_k_dequant, make_mla_dequant
 
     dev = torch.device("cuda", local)
-    if mla:
-        n = int(os.environ.get("HCU_BENCH_MLA_TOKENS", "392832"))
-        w = make_mla_dequant(n, 1 << 19, seed=rank, device=dev)
-        fn = lambda: hcu_ops.dequantize_k_cache_paged(w["quant_k_cache"], w["page_table_1_flattened"])  # noqa: E731
-        per_tok = 656 + 1152 + 4
-        name = f"MLA 656-byte paged dequant, {n} tokens (pool 2^19 slots)"
-    else:
-        n = 131072
-        w = make_index_k_dequant(n, 4096, seed=rank, device=dev)
-        fn = lambda: hcu_ops.dequant_index_k_paged(w["kv_cache"], w["token_loc"])  # noqa: E731
-        per_tok = 132 + 256 + 4
-        name = "config3: indexer-K paged dequant, 131072 tokens over permuted 64-token pages"
-    for _ in range(max(args.warmup, 3)):
-        fn()
-    iters = min(args.steps, 500)
-    ms = _timed_iters(fn, iters, _flusher(dev))
-    alg = per_tok * n
-    gbs = alg / (ms * 1e-3) / 1e9
-    hbm, _, src = _peaks()
-    rec = _base_record(args, world, "paged K-cache dequant throughput (algorithmic bytes / s)", gbs * world,
-                       "GB/s", ms, name + "; L2 flushed between launches", tokens=n, bytes_per_token=per_tok)
-    rec["dtype"] = "fp8e4m3 -> fp32 -> bf16"
-    rec["roofline"] = {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
-                       "traffic": None, "alg_bytes_per_launch": alg, "peak_source": src}
-    rec["gpu_launches"] = iters
+    p_rows, p_prefix = (8192, 65536) if not args.prefill_shape else args.prefill_shape
+    w = _workloads().make_ragged(p_rows, p_prefix, heads=64, seed=0, device=dev)
+    N = w["k_fp8"].shape[0]
+    rows = w["q"].shape[0]
+    lens = w["row_end"]
+    ident = torch.arange(N, dtype=torch.int32, device=dev).expand(rows, N)
+    cu = torch.arange(rows + 1, dtype=torch.int32, device=dev)
+    state = {}
+
+    def logits():
+        state["lg"] = hcu_ops.mqa_logits_ragged(w["q"], w["k_fp8"], w["k_scale"], w["weights"], w["row_start"], lens)
+
+    def topk():
+        lg, mk = state["lg"]
+        return hcu_ops.sparse_mask_topk_transform(lg, mk, lens, ident, cu, 2048)
+
+    def step():
+        logits()
+        return topk()
+
+    for _ in range(3):
+        step()
+    iters = max(3, min(args.steps, 10))
+    ms, clocks = _timed(step, iters, local)
+    ms_lg, _ = _timed(logits, iters, local)
+    ms_tk, _ = _timed(topk, iters, local)
+    pairs = int((lens.long() - w["row_start"].long()).sum())
+    flops = 2.0 * 64 * 128 * pairs
+    hbm, bf16, src = _peaks()
+    fp8_peak = 2.0 * bf16
+    tflops = flops / (ms_lg * 1e-3) / 1e12
+    shape = "config2" if not args.prefill_shape else "reduced shape (profiling)"
+    rec = _rec("prefill indexer G-scores/s (rows x visible KV tokens / s), logits + top-2048",
+               pairs / (ms * 1e-3) / 1e9, "G-scores/s", ms, iters,
+               f"{shape}: prefill chunk {rows} rows x ({p_prefix} + i + 1) tokens, 64 heads; logits "
+               f"{rows * N * 4 / 1e9:.1f} GB > L2, no flush", pairs=pairs)
+    rec["logits_op_ms"] = ms_lg
+    rec["topk_op_ms"] = ms_tk
+    rec["top_k_rows_per_s"] = rows / (ms_tk * 1e-3)
+    topk_bytes = rows * N * 4 + rows * (N // 16) * 2 + rows * 2048 * 8
+    rec["topk_roofline"] = {"bound": "hbm", "achieved": topk_bytes / (ms_tk * 1e-3) / 1e9, "peak": hbm,
+                            "unit": "GB/s", "frac": topk_bytes / (ms_tk * 1e-3) / 1e9 / hbm}
+    rec["roofline"] = {"bound": "tensor", "achieved": tflops, "peak": fp8_peak, "unit": "TFLOP/s",
+                       "frac": tflops / fp8_peak, "traffic": None, "kernel": "mqa_logits_ragged_kernel<64>",
+                       "flops_per_launch": flops, "peak_source": src + " (fp8 dense = 2 x measured bf16 burst)"}
+    rec["gpu_launches"] = iters * 3
+    rec["clocks"] = clocks
+    if not args.no_cpu_baseline and not args.prefill_shape:
+        v, sample = _ragged_cpu_sample(p_rows, p_prefix)
+        rec["cpu_baseline"] = {"value": v, "unit": "G-scores/s", "cores": _threads(), "kind": "port",
+                               "sample": sample}
     return rec
 
 
-def run_kstore(args, world, rank, local):
+def sec_dequant(args, local, mla=False):
+    """Config 3 (indexer-K pages -> bf16) or the 656-byte MLA slots -> bf16, HBM-bound: back-to-back
+    graph-replayed launches over enough rotating instances that every launch streams from HBM."""
+    import numpy as np
+    import torch
+
+    import hcu_ops
+
+    dev = torch.device("cuda", local)
+    wl = _workloads()
+    if mla:
+        n = int(os.environ.get("HCU_BENCH_MLA_TOKENS", "392832"))
+        per_tok = 656 + 1152 + 4
+        inst = [wl.make_mla_dequant(n, 1 << 19, seed=i, device=dev) for i in range(2)]
+        fns = [lambda m=m: hcu_ops.dequantize_k_cache_paged(m["quant_k_cache"], m["page_table_1_flattened"])
+               for m in inst]
+        name = f"MLA 656-byte paged dequant, {n} tokens over a 2^19-slot pool"
+        kernel = "dequant_mla_kernel"
+    else:
+        n = 131072
+        per_tok = 132 + 256 + 4
+        k = _instances(n * per_tok)
+        inst = [wl.make_index_k_dequant(n, 4096, seed=i, device=dev) for i in range(k)]
+        fns = [lambda m=m: hcu_ops.dequant_index_k_paged(m["kv_cache"], m["token_loc"]) for m in inst]
+        name = f"config3: indexer-K paged dequant, {n} tokens over permuted 64-token pages"
+        kernel = "dequant_index_k_kernel"
+    alg = per_tok * n
+    ms, clocks, launches = _hbm_loop(fns, alg, args.steps, local, dev)
+    gbs = alg / (ms * 1e-3) / 1e9
+    hbm, _, src = _peaks()
+    rec = _rec("paged K-cache dequant throughput (algorithmic bytes / s)", gbs, "GB/s", ms, launches,
+               f"{name}; graph-replayed launches cycling {len(fns)} input/output sets "
+               f"({len(fns) * alg / 1e6:.0f} MB > L2)", tokens=n, bytes_per_token=per_tok)
+    rec["dtype"] = "fp8e4m3 -> fp32 -> bf16"
+    rec["roofline"] = {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                       "traffic": _profile_traffic(kernel + ("_mla" if mla else "_config3")),
+                       "kernel": kernel, "alg_bytes_per_launch": alg, "peak_source": src}
+    rec["gpu_launches"] = launches
+    rec["clocks"] = clocks
+    if not args.no_cpu_baseline:
+        from oracle import indexer as O
+
+        if mla:
+            m = wl.make_mla_dequant(32768, 1 << 19)
+            t0 = time.perf_counter()
+            O.dequant_mla_656(m["quant_k_cache"].view(torch.uint8).numpy().reshape(-1, 656),
+                              m["page_table_1_flattened"].numpy())
+            dt, nn = time.perf_counter() - t0, 32768
+        else:
+            m = wl.make_index_k_dequant(n, 4096)
+            t0 = time.perf_counter()
+            O.dequant_index_k(m["kv_cache"].numpy().reshape(4096, -1), m["token_loc"].numpy())
+            dt, nn = time.perf_counter() - t0, n
+        rec["cpu_baseline"] = {"value": nn * per_tok / dt / 1e9, "unit": "GB/s", "cores": _threads(), "kind": "port",
+                               "sample": f"{nn} tokens, oracle dequant ({dt:.2f} s)"}
+    del np
+    return rec
+
+
+def sec_kstore(args, local):
     """Indexer-K cache writer: 131072 bf16 K rows quantised into permuted slots of a 4096-page pool."""
     import torch
 
@@ -466,27 +830,42 @@ def run_kstore(args, world, rank, local):
 
     dev = torch.device("cuda", local)
     n, pool_pages = 131072, 4096
-    g = torch.Generator(device=dev)
-    g.manual_seed(rank)
-    k = torch.randn(n, 128, generator=g, device=dev).to(torch.bfloat16)
-    loc = torch.randperm(pool_pages * 64, generator=g, device=dev)[:n].to(torch.int32)
-    pool = torch.zeros(pool_pages, 64, 1, 132, dtype=torch.uint8, device=dev)
-    fn = lambda: hcu_ops.quant_store_index_k(k, loc, pool)  # noqa: E731
-    for _ in range(max(args.warmup, 3)):
-        fn()
-    iters = min(args.steps, 500)
-    ms = _timed_iters(fn, iters, _flusher(dev))
     per_tok = 256 + 4 + 132
+    inst = []
+    for i in range(_instances(n * per_tok + pool_pages * 64 * 132)):
+        g = torch.Generator(device=dev)
+        g.manual_seed(i)
+        k = torch.randn(n, 128, generator=g, device=dev).to(torch.bfloat16)
+        loc = torch.randperm(pool_pages * 64, generator=g, device=dev)[:n].to(torch.int32)
+        inst.append((k, loc, torch.zeros(pool_pages, 64, 1, 132, dtype=torch.uint8, device=dev)))
+    fns = [lambda m=m: hcu_ops.quant_store_index_k(*m) for m in inst]
     alg = per_tok * n
+    ms, clocks, launches = _hbm_loop(fns, alg, args.steps, local, dev)
     gbs = alg / (ms * 1e-3) / 1e9
     hbm, _, src = _peaks()
-    rec = _base_record(args, world, "indexer-K cache writer throughput (algorithmic bytes / s)", gbs * world, "GB/s",
-                       ms, "indexer-K writer: 131072 bf16 rows -> fp8 + scale into permuted slots of 4096 pages; "
-                       "L2 flushed between launches", tokens=n, bytes_per_token=per_tok)
+    rec = _rec("indexer-K cache writer throughput (algorithmic bytes / s)", gbs, "GB/s", ms, launches,
+               f"indexer-K writer: {n} bf16 rows -> fp8 + scale into permuted slots of {pool_pages} pages; "
+               f"graph-replayed launches cycling {len(fns)} sets", tokens=n, bytes_per_token=per_tok)
     rec["dtype"] = "bf16 -> fp32 -> fp8e4m3"
     rec["roofline"] = {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
-                       "traffic": None, "alg_bytes_per_launch": alg, "peak_source": src}
-    rec["gpu_launches"] = iters
+                       "traffic": _profile_traffic("quant_store_index_k_kernel"), "kernel": "quant_store_index_k_kernel",
+                       "alg_bytes_per_launch": alg, "peak_source": src}
+    rec["gpu_launches"] = launches
+    rec["clocks"] = clocks
+    if not args.no_cpu_baseline:
+        import numpy as np
+
+        from oracle import indexer as O
+
+        g = torch.Generator().manual_seed(0)
+        kc = torch.randn(n, 128, generator=g).to(torch.bfloat16).float().numpy()
+        locc = torch.randperm(pool_pages * 64, generator=g)[:n].to(torch.int32).numpy()
+        pool = np.zeros((pool_pages, 64 * 132), np.uint8)
+        t0 = time.perf_counter()
+        O.quant_store_index_k(kc, locc, pool)
+        dt = time.perf_counter() - t0
+        rec["cpu_baseline"] = {"value": n * per_tok / dt / 1e9, "unit": "GB/s", "cores": _threads(), "kind": "port",
+                               "sample": f"{n} tokens (whole workload), oracle writer ({dt:.2f} s)"}
     return rec
 
 
@@ -512,178 +891,35 @@ def _mla_inputs(dev, T, seed):
     return packed, q, pos, cache, w, loc, buf
 
 
-def run_mla_kv(args, world, rank, local):
+def sec_mla_kv(args, local):
     """MLA decode front end (rope_qout_kv_store): 128 tokens x 64 q heads per call, q rotated in place."""
-    import torch
-
-    import hcu_ops
-
-    dev = torch.device("cuda", local)
-    packed, q, pos, cache, w, loc, buf = _mla_inputs(dev, MLA_T, rank)
-    kv_c, k_pe, q_pe = packed[:, 2048:2560], packed[:, 2560:].unsqueeze(1), q[..., 192:]
-    fn = lambda: hcu_ops.rope_qout_kv_store(pos, q_pe, q_pe, kv_c, w, 1e-6, k_pe, cache, False, buf, loc)  # noqa
-    for _ in range(max(args.warmup, 3)):
-        fn()
-    iters = min(args.steps, 500)
-    ms = _timed_iters(fn, iters, _flusher(dev))
-    alg = MLA_BYTES_PER_TOKEN * MLA_T + 1024
-    gbs = alg / (ms * 1e-3) / 1e9
-    hbm, _, src = _peaks()
-    rec = _base_record(args, world, "MLA decode front end latency (us per call, 128 tokens x 64 q heads)",
-                       ms * 1e3, "us", ms, "MLA front end: q rope (64 heads), latent RMS norm in place, k rope, fp8 "
-                       "656-byte slot store, 128 decode tokens; L2 flushed between launches", tokens=MLA_T,
-                       bytes_per_token=MLA_BYTES_PER_TOKEN)
-    rec["higher_is_better"] = False
-    rec["dtype"] = "bf16 -> fp32 -> bf16 / fp8e4m3"
-    rec["roofline"] = {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
-                       "traffic": None, "alg_bytes_per_launch": alg, "peak_source": src}
-    rec["gpu_launches"] = iters
-    return rec
-
-
-def _prefill_inputs(dev, rows, prefix, seed):
-    from hcu_ops.workloads import make_ragged
-
-    return make_ragged(rows, prefix, heads=64, seed=seed, device=dev)
-
-
-def run_prefill(args, world, rank, local):
-    import torch
-
-    import hcu_ops
-
-    dev = torch.device("cuda", local)
-    p_rows, p_prefix = (8192, 65536) if not args.prefill_shape else args.prefill_shape
-    w = _prefill_inputs(dev, p_rows, p_prefix, seed=rank)
-    N = w["k_fp8"].shape[0]
-    rows = w["q"].shape[0]
-    lens = w["row_end"]
-    ident = torch.arange(N, dtype=torch.int32, device=dev).expand(rows, N)
-    cu = torch.arange(rows + 1, dtype=torch.int32, device=dev)
-
-    def logits():
-        return hcu_ops.mqa_logits_ragged(w["q"], w["k_fp8"], w["k_scale"], w["weights"], w["row_start"], lens)
-
-    def step():
-        lg, mk = logits()
-        return hcu_ops._C.sparse_mask_topk_transform(lg, mk, lens, ident, cu, 2048)
-
-    for _ in range(max(min(args.warmup, 3), 1)):
-        step()
-    iters = min(args.steps, 10)
-    ms = _timed_iters(step, iters, None)
-    ms_lg = _timed_iters(logits, iters, None)
-    pairs = int((lens.long() - w["row_start"].long()).sum())
-    flops = 2.0 * 64 * 128 * pairs
-    _, bf16, src = _peaks()
-    fp8_peak = 2.0 * bf16
-    tflops = flops / (ms_lg * 1e-3) / 1e12
-    rec = _base_record(args, world, "prefill indexer G-scores/s (rows x visible KV tokens / s), logits + top-2048",
-                       pairs / (ms * 1e-3) / 1e9 * world, "G-scores/s", ms,
-                       (f"config2: prefill chunk {rows} rows x ({p_prefix} + i + 1) tokens, 64 heads; "
-                        + ("inputs 77 MB, logits 2.4 GB > L2" if not args.prefill_shape else "reduced shape (profiling)")),
-                       pairs=pairs)
-    rec["logits_op_ms"] = ms_lg
-    rec["top_k_rows_per_s"] = rows / ((ms - ms_lg) * 1e-3)
-    rec["roofline"] = {"bound": "tensor", "achieved": tflops, "peak": fp8_peak, "unit": "TFLOP/s",
-                       "frac": tflops / fp8_peak, "traffic": None, "kernel": "mqa_logits_ragged_kernel<64>",
-                       "flops_per_launch": flops, "peak_source": src + " (fp8 dense = 2 x measured bf16 burst)"}
-    rec["gpu_launches"] = iters * 2
-    return rec
-
-
-def run_cp_prefill(args, world, rank, local):
-    import torch
-
-    from hcu_ops.cp import cp_prefill_topk, kv_range
-
-    dev = torch.device("cuda", local)
-    rows, prefix = 16384, 131072 - 16384
-    w = _prefill_inputs(dev, rows, prefix, seed=0)  # identical on every rank (replicated q, full K generated)
-    N = w["k_fp8"].shape[0]
-    lo, hi = kv_range(rank, world, N, causal_rows=rows)  # ranges balanced by visible pairs
-    kf = w["k_fp8"][lo:hi].contiguous()
-    ks = w["k_scale"][lo:hi].contiguous()
-    del w["k_fp8"], w["k_scale"]
-    torch.cuda.empty_cache()
-
-    def step():
-        return cp_prefill_topk(w["q"], kf, ks, w["weights"], w["row_end"], N, causal_rows=rows)
-
-    for _ in range(max(min(args.warmup, 2), 1)):
-        out = step()
-    torch.cuda.synchronize()
-    if world > 1:
-        torch.distributed.barrier()
-    iters = min(args.steps, 5)
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
-    for _ in range(iters):
-        out = step()
-    b.record()
-    torch.cuda.synchronize()
-    ms = a.elapsed_time(b) / iters
-    t = torch.tensor([ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    ms = t.item()
-    pairs = int(w["row_end"].long().sum())
-    del out
-    if rank != 0:
-        return None
-    flops = 2.0 * 64 * 128 * pairs
-    _, bf16, src = _peaks()
-    rec = _base_record(args, world, "CP prefill indexer G-scores/s (rows x visible KV tokens / s), logits + local "
-                       "top-2048 + exchange + merge", pairs / (ms * 1e-3) / 1e9, "G-scores/s", ms,
-                       "config4: 16384 rows x (114688 + i + 1) tokens over a 131072-token context split into "
-                       f"{world} contiguous KV ranges, 64 heads; row-sharded NCCL exchange", pairs=pairs,
-                       parallelism=f"cp{world}")
-    rec["scaling"] = "strong"
-    achieved = flops / (ms * 1e-3) / 1e12
-    rec["roofline"] = {"bound": "tensor", "achieved": achieved, "peak": 2.0 * bf16 * world, "unit": "TFLOP/s",
-                       "frac": achieved / (2.0 * bf16 * world), "traffic": None,
-                       "peak_source": src + " (fp8 dense = 2 x measured bf16 burst, x n_gpus)"}
-    rec["gpu_launches"] = iters * 3
-    return rec
-
-
-WORKLOADS = {"decode0": run_decode0, "dequant": run_dequant, "kstore": run_kstore, "mla_kv": run_mla_kv,
-             "mla_dequant": lambda a, w, r, l: run_dequant(a, w, r, l, mla=True),
-             "prefill": run_prefill, "cp_prefill": run_cp_prefill}
-
-
-def run_reference_sample(args):
-    """CPU oracle on a bounded sample of a secondary workload (--impl reference)."""
     import numpy as np
     import torch
 
-    from oracle import indexer as O
+    import hcu_ops
 
-    torch.set_num_threads(os.cpu_count() or 1)
-    wl = args.workload
-    t0 = time.perf_counter()
-    if wl == "decode0":
-        from hcu_ops.workloads import config0
-
-        w = config0()
-        lg, m, _ = O.mqa_logits_paged(w["q"].view(torch.uint8).numpy().reshape(1, 64, 128),
-                                      w["kv_cache"].numpy().reshape(w["kv_cache"].shape[0], -1),
-                                      w["weights"].numpy(), w["context_lens"].numpy(), w["block_table"].numpy(),
-                                      w["max_context_len"], 1)
-        O.topk_transform(lg, m, w["context_lens"].numpy(), w["page_table_size_1"].numpy())
-        dt = time.perf_counter() - t0
-        value, unit, sample = dt * 1e6, "us", "whole config 0"
-    elif wl == "kstore":
-        n, pool_pages = 131072, 4096
-        g = torch.Generator().manual_seed(0)
-        k = torch.randn(n, 128, generator=g).to(torch.bfloat16).float().numpy()
-        loc = torch.randperm(pool_pages * 64, generator=g)[:n].to(torch.int32).numpy()
-        pool = np.zeros((pool_pages, 64 * 132), np.uint8)
-        t0 = time.perf_counter()
-        O.quant_store_index_k(k, loc, pool)
-        dt = time.perf_counter() - t0
-        value, unit, sample = n * (256 + 4 + 132) / dt / 1e9, "GB/s", f"{n} tokens (whole workload)"
-    elif wl == "mla_kv":
+    dev = torch.device("cuda", local)
+    packed, q, pos, cache, w, loc, buf = _mla_inputs(dev, MLA_T, 0)
+    kv_c, k_pe, q_pe = packed[:, 2048:2560], packed[:, 2560:].unsqueeze(1), q[..., 192:]
+    fn = lambda: hcu_ops.rope_qout_kv_store(pos, q_pe, q_pe, kv_c, w, 1e-6, k_pe, cache, False, buf, loc)  # noqa
+    for _ in range(5):
+        fn()
+    iters = max(10, min(args.steps, 200))
+    ms, clocks = _per_launch(fn, iters, _read_flush(dev), local)
+    alg = MLA_BYTES_PER_TOKEN * MLA_T + 1024
+    gbs = alg / (ms * 1e-3) / 1e9
+    hbm, _, src = _peaks()
+    rec = _rec("MLA decode front end latency (us per call, 128 tokens x 64 q heads)", ms * 1e3, "us", ms, iters,
+               "MLA front end: q rope (64 heads), latent RMS norm in place, k rope, fp8 656-byte slot store, 128 "
+               "decode tokens; L2 flushed (read) before every call", higher=False, tokens=MLA_T,
+               bytes_per_token=MLA_BYTES_PER_TOKEN)
+    rec["dtype"] = "bf16 -> fp32 -> bf16 / fp8e4m3"
+    rec["roofline"] = {"bound": "latency", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                       "traffic": None, "alg_bytes_per_launch": alg, "peak_source": src,
+                       "note": "2.5 MB per call: latency-bound, roofline not claimed"}
+    rec["gpu_launches"] = iters
+    rec["clocks"] = clocks
+    if not args.no_cpu_baseline:
         from oracle import mla as M
 
         packed, q, pos, cache, w, loc, buf = _mla_inputs(torch.device("cpu"), MLA_T, 0)
@@ -692,55 +928,66 @@ def run_reference_sample(args):
         M.rope_qout_kv_store(pos.numpy(), u(q[..., 192:]), u(packed[:, 2048:2560]), u(w), 1e-6, u(packed[:, 2560:]),
                              u(cache), False, buf.numpy(), loc.numpy())
         dt = time.perf_counter() - t0
-        value, unit, sample = dt * 1e6, "us", f"one call, {MLA_T} tokens x {MLA_H} q heads (whole workload)"
-    elif wl in ("dequant", "mla_dequant"):
-        from hcu_ops.workloads import make_index_k_dequant, make_mla_dequant
+        rec["cpu_baseline"] = {"value": dt * 1e6, "unit": "us", "cores": _threads(), "kind": "port",
+                               "sample": f"one call, {MLA_T} tokens x {MLA_H} q heads (whole workload)"}
+    return rec
 
-        if wl == "dequant":
-            w = make_index_k_dequant(131072, 4096)
-            t0 = time.perf_counter()
-            O.dequant_index_k(w["kv_cache"].numpy().reshape(4096, -1), w["token_loc"].numpy())
-            n, per = 131072, 392
-        else:
-            w = make_mla_dequant(32768, 1 << 19)
-            t0 = time.perf_counter()
-            O.dequant_mla_656(w["quant_k_cache"].view(torch.uint8).numpy().reshape(-1, 656),
-                              w["page_table_1_flattened"].numpy())
-            n, per = 32768, 1812
-        dt = time.perf_counter() - t0
-        value, unit, sample = n * per / dt / 1e9, "GB/s", f"{n} tokens"
+
+SECONDARY = {"decode0": sec_decode0, "prefill": sec_prefill, "dequant": sec_dequant,
+             "mla_dequant": lambda a, l: sec_dequant(a, l, mla=True), "kstore": sec_kstore, "mla_kv": sec_mla_kv}
+
+
+def _standalone(args, world, rank, local):
+    """--workload NAME: one secondary workload (or config 4) as its own JSON line."""
+    if args.workload == "cp_prefill":
+        rec = run_cp_prefill(args, world, rank, local)
+    elif rank == 0:
+        rec = SECONDARY[args.workload](args, local)
     else:
-        rows, prefix = (8192, 65536) if wl == "prefill" else (16384, 131072 - 16384)
-        from hcu_ops.workloads import make_ragged
+        rec = None
+    if rec is not None:
+        rec.update({"n_gpus": world, "warmup": args.warmup, "vs_baseline": None,
+                    "data": "synthetic (seeded)", "dtype": rec.get("dtype", DTYPE)})
+        rec.setdefault("scaling", "weak")
+    return rec
 
-        w = make_ragged(rows, prefix, heads=64)
-        sel = np.linspace(0, rows - 1, 64).astype(int)  # stratified subset of rows
-        t0 = time.perf_counter()
-        lg, m, _ = O.mqa_logits_ragged(w["q"].view(torch.uint8).numpy(), w["k_fp8"].view(torch.uint8).numpy(),
-                                       w["k_scale"].numpy(), w["weights"].numpy(), w["row_start"].numpy(),
-                                       w["row_end"].numpy(), rows=list(sel))
-        N = lg.shape[1]
-        O.topk_transform(lg, m, w["row_end"].numpy()[sel], np.tile(np.arange(N, dtype=np.int32), (64, 1)))
-        dt = time.perf_counter() - t0
-        pairs_s = float(w["row_end"].numpy()[sel].astype(np.int64).sum())
-        value, unit = pairs_s / dt / 1e9, "G-scores/s"
-        sample = f"64 stratified rows of {rows} ({int(pairs_s)} scores), rate extrapolated by pair count"
-    return {"impl": "reference", "metric": f"{wl} (CPU oracle)", "value": value, "unit": unit, "n_gpus": 0,
-            "steps": 1, "warmup": 0, "ms_per_step": dt * 1e3, "higher_is_better": unit != "us",
-            "config": {"workload": wl},
-            "cpu_baseline": {"value": value, "unit": unit, "cores": torch.get_num_threads(), "kind": "port",
+
+def run_reference_sample(args):
+    """--impl reference --workload NAME: the CPU oracle on a bounded sample of that workload."""
+    import torch
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    wl = args.workload
+    if wl in ("prefill", "cp_prefill"):
+        rows, prefix = (8192, 65536) if wl == "prefill" else (CP_ROWS, CP_N - CP_ROWS)
+        v, sample = _ragged_cpu_sample(rows, prefix)
+        unit = "G-scores/s"
+    else:
+        a = argparse.Namespace(**vars(args))
+        a.no_cpu_baseline = False
+        rec = None
+        import torch as _t
+
+        if not _t.cuda.is_available():
+            raise SystemExit("--impl reference --workload " + wl + ": that sample reuses the GPU workload's setup")
+        rec = SECONDARY[wl](a, 0)
+        v, unit, sample = rec["cpu_baseline"]["value"], rec["cpu_baseline"]["unit"], rec["cpu_baseline"]["sample"]
+    return {"impl": "reference", "metric": f"{wl} (CPU oracle)", "value": v, "unit": unit, "n_gpus": 0,
+            "steps": 1, "warmup": 0, "higher_is_better": unit != "us", "config": {"workload": wl},
+            "cpu_baseline": {"value": v, "unit": unit, "cores": torch.get_num_threads(), "kind": "port",
                              "sample": sample},
-            "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=3000)
-    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="decode")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true", help="headline and cp_prefill only")
     ap.add_argument("--prefill-shape", type=int, nargs=2, metavar=("ROWS", "PREFIX"), default=None,
                     help="prefill workload at a reduced shape (for profiler captures); default config 2")
     args = ap.parse_args()
@@ -761,10 +1008,17 @@ def main():
     try:
         if args.workload == "decode":
             rec = run_decode(args, world, rank, local)
-        elif args.workload in WORKLOADS:
-            rec = WORKLOADS[args.workload](args, world, rank, local)
-            if rec is not None and world > 1 and args.workload != "cp_prefill":
-                rec = rec if rank == 0 else None
+            cp = run_cp_prefill(args, world, rank, local)
+            if rank == 0:
+                rec["cp_prefill"] = cp
+                if world == 1 and not args.no_secondary:
+                    sec = {}
+                    for name, fn in SECONDARY.items():
+                        sec[name] = fn(args, local)
+                        torch.cuda.empty_cache()
+                    rec["secondary"] = sec
+        elif args.workload in SECONDARY or args.workload == "cp_prefill":
+            rec = _standalone(args, world, rank, local)
         else:
             raise SystemExit(f"unknown workload {args.workload}")
         if rec is not None:

@@ -150,14 +150,17 @@ def list_len(world: int) -> int:
 
 
 def cp_prefill_topk(q, k_fp8_local, k_scale_local, weights, row_end, n_tokens, group=None, mode="rowshard",
-                    ops=None, bounded=True, causal_rows=0):
+                    ops=None, bounded=True, causal_rows=0, stats=None):
     """Global top-2048 token indices of every query row, computed over P KV ranges.
 
     q: fp8 ``[rows, H, 128]`` (replicated); ``k_fp8_local``/``k_scale_local``: this rank's
     KV range ``kv_range(rank, P, n_tokens, causal_rows)``; ``row_end``: int32 ``[rows]`` global visible end
     (row r sees tokens ``[0, row_end[r])``).  Returns int32 ``[rows, 2048]`` (-1 pads) on
-    every rank.  Every rank takes the same collective steps in the same order.
+    every rank.  Every rank takes the same collective steps in the same order.  ``stats`` (optional
+    dict): "reruns" is incremented when the bounded exchange had to be redone exactly, "exchange"
+    names the exchange used.
     """
+    stats = {} if stats is None else stats
     ops = ops or CudaOps()
     world = dist.get_world_size(group) if dist.is_initialized() else 1
     rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -171,13 +174,17 @@ def cp_prefill_topk(q, k_fp8_local, k_scale_local, weights, row_end, n_tokens, g
     width = hi - lo
     gtab = (torch.arange(width, dtype=torch.int32, device=dev) + lo).expand(rows, width)
     if world == 1:  # one range: the canonical top-k is the answer (no exchange, no merge)
+        stats["exchange"] = "none (one range)"
         return ops.topk(lg, mk, lens, gtab)
     vis = row_end.clamp(max=n_tokens).to(torch.int32)
     rps = (rows + world - 1) // world  # row-sharded exchange: rank d merges rows [d*rps, (d+1)*rps)
     if mode == "rowshard" and bounded:
         out = _bounded_rowshard(ops, lg, mk, lens, gtab, vis, rows, rps, world, rank, group)
         if out is not None:
+            stats["exchange"] = "nccl: bounded row-sharded lists (all_to_all) + all_gather of merged rows"
             return out[:rows]
+        stats["reruns"] = stats.get("reruns", 0) + 1
+    stats["exchange"] = f"nccl: exact local top-2048 lists ({mode})"
     idx, keys = ops.local_topk(lg, mk, lens, gtab)
     if mode == "allgather":
         all_k = torch.empty((world * rows, TOPK), dtype=keys.dtype, device=dev)
