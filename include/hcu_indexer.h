@@ -51,6 +51,13 @@ enum {
   HCU_STATUS_BAD_INPUT = 1u << 1,    /* a kernel saw an out-of-range index and skipped it */
 };
 
+/* Sets the limit of every bounded wait of the library's kernels on the current
+ * device (0 restores the default of 2 s).  A wait that reaches it records
+ * HCU_STATUS_WAIT_TIMEOUT and the kernel returns without finishing its work, so
+ * the context stays usable.  Synchronous; call it outside stream capture.  (No
+ * counterpart in the reference, whose kernels wait without a bound.) */
+int hcu_set_wait_limit_ns(uint64_t ns);
+
 /* Library version string and the compile target ("sm_100a"). */
 const char* hcu_version(void);
 
@@ -292,6 +299,85 @@ int hcu_cp_filter(const float* score, int64_t rows, int64_t width, int64_t score
 int hcu_cp_topk_merge_lists(const uint32_t* keys, const int32_t* gidx, int64_t n_parts, int64_t list_len,
                             int64_t part_stride, int64_t rows, const int32_t* lengths, int32_t* flag,
                             int32_t short_identity, int32_t* dst, hcu_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Context-parallel exchange over peer memory (no counterpart in the reference).
+ *
+ * The same bounded exchange as above, with each exchange fused into the kernel
+ * that produces its data: every rank's buffers below are mapped into every
+ * other rank's address space (CUDA IPC / symmetric memory over NVLink), the
+ * kernels store straight into the destination rank's buffer and publish their
+ * completion with a per-step flag (system-scope release store); the consumer
+ * kernels wait for the flags of all ranks (bounded waits, acquire loads).  A
+ * step is, per rank, in stream order:
+ *   hcu_cp_peer_bound   bounds of this range -> slot `rank` of every rank's bounds
+ *   hcu_cp_peer_filter  waits for all bounds, takes their minimum per row, stores
+ *                       each row's list into slot `rank` of the row owner's lists
+ *   hcu_cp_peer_merge   waits for all lists of this rank's rows, merges them and
+ *                       stores each result row into every rank's out
+ *   hcu_cp_peer_finish  waits for every rank's rows; ws[HCU_CP_WS_FLAG] = 1 when
+ *                       any rank flagged a row (the bounded exchange was not exact)
+ * and then, predicated on that flag on the device (identical on every rank, so
+ * all ranks take the same branch and no host read is needed), the exact redo:
+ *   hcu_topk_keys_if          local top-2048 with keys of every row
+ *   hcu_cp_peer_scatter_exact lists -> slot `rank` of the row owner's lists_exact
+ *   hcu_cp_peer_merge         (exact = 1) merge of the 2048-entry lists
+ *   hcu_cp_peer_finish        (exact = 1) ws[HCU_CP_WS_RERUNS] += 1
+ * Rank d owns rows [d * rps, (d + 1) * rps).  Every buffer is written by one rank
+ * per slot, so no two ranks write the same word.  `epoch` starts at 1 and grows
+ * by 1 per step; flags hold (epoch << 1 | flag bit).  The result in out is valid
+ * until the next step's merge of any rank.
+ * ------------------------------------------------------------------------ */
+#define HCU_CP_MAX_PARTS 16
+enum {
+  HCU_CP_WS_FLAG = 8,    /* ws word: this step's bounded exchange was flagged (the exact redo ran) */
+  HCU_CP_WS_RERUNS = 9,  /* ws word: number of exact redos so far */
+  HCU_CP_WS_WORDS = 16,  /* int32 words of ws (zeroed before the first step) */
+  HCU_CP_SIG_WORDS = 5   /* signal words per source rank (x parts) */
+};
+typedef struct {
+  int32_t parts;         /* P <= HCU_CP_MAX_PARTS */
+  int32_t rank;          /* this rank */
+  int32_t rows;          /* query rows R (the same on every rank) */
+  int32_t rows_per_rank; /* rps = ceil(R / P) */
+  int32_t list_len;      /* C: slots per (rank, row) list of the bounded exchange (power of two, 256..2048) */
+  uint32_t epoch;        /* step number, from 1 */
+  int32_t* ws;           /* this rank's local workspace, HCU_CP_WS_WORDS int32 */
+  int32_t* bounds[HCU_CP_MAX_PARTS];      /* rank p's int32 [P, R] */
+  int32_t* lists[HCU_CP_MAX_PARTS];       /* rank p's int32 [P, 2, rps, C]: keys then entries */
+  int32_t* lists_exact[HCU_CP_MAX_PARTS]; /* rank p's int32 [P, 2, rps, 2048] */
+  int32_t* out[HCU_CP_MAX_PARTS];         /* rank p's int32 [P * rps, 2048] result */
+  uint32_t* sig[HCU_CP_MAX_PARTS];        /* rank p's uint32 [HCU_CP_SIG_WORDS, P] flags */
+} hcu_cp_peers_t;
+
+/* lengths: this range's visible tokens per row; totals: each row's visible
+ * tokens over all ranges.  Score / mask as hcu_cp_local_bound. */
+int hcu_cp_peer_bound(const float* score, int64_t width, int64_t score_stride, const int16_t* mask,
+                      int64_t mask_stride, const int32_t* lengths, const int32_t* totals,
+                      const hcu_cp_peers_t* peers, hcu_stream_t stream);
+
+/* page_table: [R, >= width] global token index of each local token (as hcu_cp_filter). */
+int hcu_cp_peer_filter(const float* score, int64_t width, int64_t score_stride, const int16_t* mask,
+                       int64_t mask_stride, const int32_t* lengths, const int32_t* page_table,
+                       int64_t pt_stride, const hcu_cp_peers_t* peers, hcu_stream_t stream);
+
+/* totals: visible tokens of this rank's rows (rps entries; rows past R: 0).
+ * exact = 0: the bounded lists; exact = 1: the 2048-entry lists of the redo
+ * (does nothing unless ws[HCU_CP_WS_FLAG] is set). */
+int hcu_cp_peer_merge(const int32_t* totals, int32_t exact, const hcu_cp_peers_t* peers, hcu_stream_t stream);
+
+/* keys / entries: this rank's hcu_topk_keys output for all R rows ([R, 2048]).
+ * Does nothing unless ws[HCU_CP_WS_FLAG] is set. */
+int hcu_cp_peer_scatter_exact(const uint32_t* keys, const int32_t* entries, const hcu_cp_peers_t* peers,
+                              hcu_stream_t stream);
+
+int hcu_cp_peer_finish(int32_t exact, const hcu_cp_peers_t* peers, hcu_stream_t stream);
+
+/* hcu_topk_keys that does nothing unless *run_if != 0 (a device word). */
+int hcu_topk_keys_if(const float* score, int64_t rows, int64_t width, int64_t score_stride,
+                     const int16_t* mask, int64_t mask_stride, const int32_t* lengths,
+                     const int32_t* page_table, int64_t pt_stride, int32_t* dst, uint32_t* dst_keys,
+                     const int32_t* run_if, hcu_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -391,6 +391,115 @@ torch::Tensor cp_topk_merge_lists(const torch::Tensor& recv, const torch::Tensor
   return dst;
 }
 
+// ---- context-parallel exchange over peer memory
+// peers: int64 CPU tensor [7 + 5 * HCU_CP_MAX_PARTS] = parts, rank, rows, rows_per_rank, list_len, epoch,
+// ws pointer, then the per-rank pointers of bounds, lists, lists_exact, out and sig (HCU_CP_MAX_PARTS each).
+hcu_cp_peers_t unpack_peers(const torch::Tensor& t) {
+  TORCH_CHECK(t.device().is_cpu() && t.scalar_type() == at::kLong && t.dim() == 1 && t.is_contiguous() &&
+                  t.numel() == 7 + 5 * HCU_CP_MAX_PARTS,
+              "peers must be a contiguous int64 CPU tensor of 7 + 5 x ", HCU_CP_MAX_PARTS, " entries");
+  const int64_t* v = t.data_ptr<int64_t>();
+  hcu_cp_peers_t p{};
+  p.parts = static_cast<int32_t>(v[0]);
+  p.rank = static_cast<int32_t>(v[1]);
+  p.rows = static_cast<int32_t>(v[2]);
+  p.rows_per_rank = static_cast<int32_t>(v[3]);
+  p.list_len = static_cast<int32_t>(v[4]);
+  p.epoch = static_cast<uint32_t>(v[5]);
+  p.ws = reinterpret_cast<int32_t*>(v[6]);
+  for (int i = 0; i < HCU_CP_MAX_PARTS; ++i) {
+    p.bounds[i] = reinterpret_cast<int32_t*>(v[7 + i]);
+    p.lists[i] = reinterpret_cast<int32_t*>(v[7 + HCU_CP_MAX_PARTS + i]);
+    p.lists_exact[i] = reinterpret_cast<int32_t*>(v[7 + 2 * HCU_CP_MAX_PARTS + i]);
+    p.out[i] = reinterpret_cast<int32_t*>(v[7 + 3 * HCU_CP_MAX_PARTS + i]);
+    p.sig[i] = reinterpret_cast<uint32_t*>(v[7 + 4 * HCU_CP_MAX_PARTS + i]);
+  }
+  return p;
+}
+
+void cp_peer_bound(const torch::Tensor& score, const torch::Tensor& nonzero_mask, const torch::Tensor& lengths,
+                   const torch::Tensor& totals, const torch::Tensor& peers) {
+  const hcu_cp_peers_t p = unpack_peers(peers);
+  TORCH_CHECK(score.is_cuda() && score.scalar_type() == at::kFloat && score.dim() == 2 && score.stride(1) == 1 &&
+                  score.size(0) == p.rows,
+              "score must be row-contiguous float32 [rows, width]");
+  TORCH_CHECK(nonzero_mask.scalar_type() == at::kShort && nonzero_mask.dim() == 2 && nonzero_mask.stride(1) == 1 &&
+                  nonzero_mask.size(0) == p.rows,
+              "nonzero_mask must be row-contiguous int16 [rows, ceil(width/16)]");
+  TORCH_CHECK(lengths.scalar_type() == at::kInt && lengths.is_contiguous() && lengths.numel() == p.rows &&
+                  totals.scalar_type() == at::kInt && totals.is_contiguous() && totals.numel() == p.rows,
+              "lengths and totals must be contiguous int32 [rows]");
+  const c10::cuda::CUDAGuard guard(score.device());
+  check_status(hcu_cp_peer_bound(ptr<const float>(score), score.size(1), score.stride(0),
+                                 ptr<const int16_t>(nonzero_mask), nonzero_mask.stride(0), ptr<const int32_t>(lengths),
+                                 ptr<const int32_t>(totals), &p, cur_stream()),
+               "cp_peer_bound");
+}
+
+void cp_peer_filter(const torch::Tensor& score, const torch::Tensor& nonzero_mask, const torch::Tensor& lengths,
+                    const torch::Tensor& page_table, const torch::Tensor& peers) {
+  const hcu_cp_peers_t p = unpack_peers(peers);
+  check_topk_inputs(score, nonzero_mask, lengths, page_table, torch::empty({score.size(0) + 1}, lengths.options()),
+                    kTopK);
+  TORCH_CHECK(score.size(0) == p.rows, "score rows must equal the exchange's rows");
+  const c10::cuda::CUDAGuard guard(score.device());
+  check_status(hcu_cp_peer_filter(ptr<const float>(score), score.size(1), score.stride(0),
+                                  ptr<const int16_t>(nonzero_mask), nonzero_mask.stride(0),
+                                  ptr<const int32_t>(lengths), ptr<const int32_t>(page_table), page_table.stride(0),
+                                  &p, cur_stream()),
+               "cp_peer_filter");
+}
+
+void cp_peer_merge(const torch::Tensor& totals, bool exact, const torch::Tensor& peers) {
+  const hcu_cp_peers_t p = unpack_peers(peers);
+  TORCH_CHECK(totals.is_cuda() && totals.scalar_type() == at::kInt && totals.is_contiguous() &&
+                  totals.numel() == p.rows_per_rank,
+              "totals must be contiguous int32 [rows_per_rank] (this rank's rows)");
+  const c10::cuda::CUDAGuard guard(totals.device());
+  check_status(hcu_cp_peer_merge(ptr<const int32_t>(totals), exact ? 1 : 0, &p, cur_stream()), "cp_peer_merge");
+}
+
+void cp_peer_scatter_exact(const torch::Tensor& keys, const torch::Tensor& entries, const torch::Tensor& peers) {
+  const hcu_cp_peers_t p = unpack_peers(peers);
+  TORCH_CHECK(keys.is_cuda() && keys.scalar_type() == at::kInt && keys.is_contiguous() && keys.dim() == 2 &&
+                  keys.size(0) == p.rows && keys.size(1) == kTopK && entries.sizes() == keys.sizes() &&
+                  entries.scalar_type() == at::kInt && entries.is_contiguous(),
+              "keys and entries must be contiguous int32 [rows, 2048]");
+  const c10::cuda::CUDAGuard guard(keys.device());
+  check_status(hcu_cp_peer_scatter_exact(ptr<const uint32_t>(keys), ptr<const int32_t>(entries), &p, cur_stream()),
+               "cp_peer_scatter_exact");
+}
+
+void cp_peer_finish(bool exact, const torch::Tensor& peers) {
+  const hcu_cp_peers_t p = unpack_peers(peers);
+  check_status(hcu_cp_peer_finish(exact ? 1 : 0, &p, cur_stream()), "cp_peer_finish");
+}
+
+std::vector<torch::Tensor> topk_keys_if(const torch::Tensor& score, const torch::Tensor& nonzero_mask,
+                                        const torch::Tensor& lengths, const torch::Tensor& page_table,
+                                        const torch::Tensor& run_if) {
+  check_topk_inputs(score, nonzero_mask, lengths, page_table,
+                    torch::empty({score.size(0) + 1}, lengths.options()), kTopK);
+  TORCH_CHECK(run_if.is_cuda() && run_if.scalar_type() == at::kInt && run_if.numel() >= 1,
+              "run_if must be an int32 device word");
+  const c10::cuda::CUDAGuard guard(score.device());
+  const int64_t rows = score.size(0);
+  auto dst = torch::empty({rows, kTopK}, score.options().dtype(at::kInt));
+  auto keys = torch::empty({rows, kTopK}, score.options().dtype(at::kInt));
+  if (rows == 0) return {dst, keys};
+  check_status(hcu_topk_keys_if(ptr<const float>(score), rows, score.size(1), score.stride(0),
+                                ptr<const int16_t>(nonzero_mask), nonzero_mask.stride(0), ptr<const int32_t>(lengths),
+                                ptr<const int32_t>(page_table), page_table.stride(0), ptr<int32_t>(dst),
+                                ptr<uint32_t>(keys), ptr<const int32_t>(run_if), cur_stream()),
+               "topk_keys_if");
+  return {dst, keys};
+}
+
+void set_wait_limit_ns(int64_t ns) {
+  TORCH_CHECK(ns >= 0, "the wait limit must be >= 0 (0: the default)");
+  check_status(hcu_set_wait_limit_ns(static_cast<uint64_t>(ns)), "set_wait_limit_ns");
+}
+
 int64_t read_device_status(bool clear) {
   uint32_t s = 0;
   check_status(hcu_read_device_status(&s, clear ? 1 : 0), "read_device_status");
@@ -423,5 +532,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "quantise K rows per token to fp8 e4m3 + fp32 scale into indexer-K pages (in place)");
   m.def("cp_topk_merge", &cp_topk_merge, "merge per-range (key, global index) top-2048 lists");
   m.def("read_device_status", &read_device_status, "sticky device status bits of the library (synchronises)");
+  m.def("cp_peer_bound", &cp_peer_bound, "context-parallel over peer memory: bounds to every rank");
+  m.def("cp_peer_filter", &cp_peer_filter, "context-parallel over peer memory: lists to the rows' owners");
+  m.def("cp_peer_merge", &cp_peer_merge, "context-parallel over peer memory: merge, rows to every rank");
+  m.def("cp_peer_scatter_exact", &cp_peer_scatter_exact, "context-parallel over peer memory: the redo's lists");
+  m.def("cp_peer_finish", &cp_peer_finish, "context-parallel over peer memory: wait for every rank's rows");
+  m.def("topk_keys_if", &topk_keys_if, "topk_keys predicated on a device word (does nothing when it is 0)");
+  m.def("set_wait_limit_ns", &set_wait_limit_ns, "limit of the library's bounded waits (0: default 2 s)");
   m.def("version", []() { return std::string(hcu_version()); });
 }

@@ -63,3 +63,16 @@ extern "C" int hcu_read_device_status(uint32_t* status, int clear) {
   }
   return HCU_OK;
 }
+
+extern "C" int hcu_set_wait_limit_ns(uint64_t ns) {
+  if (ns == 0) ns = hcu::kWaitLimitNs;
+  cudaError_t e = hcu::status_dequant_set_wait_limit(ns);
+  if (e == cudaSuccess) e = hcu::status_topk_set_wait_limit(ns);
+  if (e == cudaSuccess) e = hcu::status_logits_set_wait_limit(ns);
+  if (e == cudaSuccess) e = hcu::status_mla_set_wait_limit(ns);
+  if (e != cudaSuccess) {
+    hcu::set_last_error(e);
+    return HCU_ERR_LAUNCH;
+  }
+  return HCU_OK;
+}

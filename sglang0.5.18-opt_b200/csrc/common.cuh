@@ -18,8 +18,9 @@ constexpr uint32_t kZeroKey = 0x80000000u;
 constexpr int kBins = 4096;
 constexpr int kZeroBin = 0x800;
 
-// A bounded wait gives up after this many nanoseconds of %globaltimer.  Every
-// legitimate wait in these kernels is microseconds long.
+// A bounded wait gives up after g_hcu_wait_limit_ns nanoseconds of %globaltimer
+// (default kWaitLimitNs; hcu_set_wait_limit_ns changes it).  Every legitimate
+// wait in these kernels is microseconds to milliseconds long.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
 // Monotone float -> uint32 key: larger float <=> larger key; -0 < +0.
@@ -27,6 +28,18 @@ constexpr uint64_t kWaitLimitNs = 2000000000ull;
 __device__ __forceinline__ uint32_t to_key(float x) {
   const uint32_t b = __float_as_uint(x);
   return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+}  // namespace hcu
+
+// Per-translation-unit wait limit (no relocatable device code: each unit that
+// waits keeps its own copy, set through its hcu::set_wait_limit_* accessor).
+static __device__ uint64_t g_hcu_wait_limit_ns = hcu::kWaitLimitNs;
+
+namespace hcu {
+
+__device__ __forceinline__ uint64_t wait_limit_ns() {
+  return *reinterpret_cast<volatile uint64_t*>(&g_hcu_wait_limit_ns);
 }
 
 __device__ __forceinline__ uint64_t globaltimer() {
@@ -86,17 +99,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Waits for the phase with the given parity to complete.  Gives up after
-// kWaitLimitNs (or at once when *abort is set by another warp), records
+// Waits for the phase with the given parity to complete.  Gives up after the
+// wait limit (or at once when *abort is set by another warp), records
 // HCU_STATUS_WAIT_TIMEOUT in `status`, sets *abort and returns false.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
                                           unsigned int* status) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
+  const uint64_t lim = wait_limit_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort) return false;
-    if (globaltimer() - t0 > kWaitLimitNs) {
+    if (globaltimer() - t0 > lim) {
       atomicOr(status, HCU_STATUS_WAIT_TIMEOUT);
       *abort = 1;
       return false;
@@ -107,13 +121,26 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 // Same wait without the abort short-cut: used to drain copies already issued.
 __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, unsigned int* status) {
   const uint64_t t0 = globaltimer();
+  const uint64_t lim = wait_limit_ns();
   while (!mbar_try_wait(bar, parity)) {
-    if (globaltimer() - t0 > kWaitLimitNs) {
+    if (globaltimer() - t0 > lim) {
       atomicOr(status, HCU_STATUS_WAIT_TIMEOUT);
       return false;
     }
   }
   return true;
+}
+
+// ---------------------------------------------------------------- cross-GPU flags
+// System-scope release store / acquire load of a 32-bit flag (another GPU
+// writes or reads it over NVLink).
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 
 // ---------------------------------------------------------------- TMA
@@ -198,6 +225,27 @@ __device__ __forceinline__ void relu_fma2(float2& acc, uint32_t x0, uint32_t x1,
       ".reg .b64 p, q, r;\n\t"
       "fma.rn.sat.f32 a, %2, 0f33000000, 0f00000000;\n\t"
       "fma.rn.sat.f32 b, %3, 0f33000000, 0f00000000;\n\t"
+      "mov.b64 p, {a, b};\n\t"
+      "mov.b64 q, {%4, %5};\n\t"
+      "mov.b64 r, {%0, %1};\n\t"
+      "fma.rn.f32x2 r, p, q, r;\n\t"
+      "mov.b64 {%0, %1}, r;\n\t"
+      "}"
+      : "+f"(acc.x), "+f"(acc.y)
+      : "f"(__uint_as_float(x0)), "f"(__uint_as_float(x1)), "f"(w0), "f"(w1));
+}
+
+// The same sum with the ReLU split over two pipes: lane x0 through the
+// saturating FMA (its weight w0 pre-scaled by 2^25), lane x1 through max.f32 on
+// the ALU pipe (w1 unscaled; max returns 0 for a NaN x1, like fmaxf).  Both
+// products are exact scalings of relu(x) * w, so the result equals
+// relu_fma2's bit for bit while the FMA pipe issues one instruction fewer per pair.
+__device__ __forceinline__ void relu_fma2_mixed(float2& acc, uint32_t x0, uint32_t x1, float w0, float w1) {
+  asm("{\n\t"
+      ".reg .f32 a, b;\n\t"
+      ".reg .b64 p, q, r;\n\t"
+      "fma.rn.sat.f32 a, %2, 0f33000000, 0f00000000;\n\t"
+      "max.f32 b, %3, 0f00000000;\n\t"
       "mov.b64 p, {a, b};\n\t"
       "mov.b64 q, {%4, %5};\n\t"
       "mov.b64 r, {%0, %1};\n\t"
@@ -339,10 +387,14 @@ __host__ __device__ constexpr uint32_t idesc_e4m3_f32(int M, int N) {
 
 }  // namespace hcu
 
-// Per-translation-unit sticky status word (no relocatable device code).
+// Per-translation-unit sticky status word (no relocatable device code), its
+// reader and the setter of the unit's wait limit.
 #define HCU_DEFINE_STATUS(accessor)                                                        \
   static __device__ unsigned int g_hcu_status;                                             \
   namespace hcu {                                                                          \
+  cudaError_t accessor##_set_wait_limit(uint64_t ns) {                                     \
+    return cudaMemcpyToSymbol(g_hcu_wait_limit_ns, &ns, sizeof(ns));                       \
+  }                                                                                        \
   cudaError_t accessor(uint32_t* out, int clear) {                                         \
     unsigned int v = 0;                                                                    \
     cudaError_t e = cudaMemcpyFromSymbol(&v, g_hcu_status, sizeof(v));                     \
@@ -366,4 +418,8 @@ cudaError_t status_dequant(uint32_t* out, int clear);
 cudaError_t status_topk(uint32_t* out, int clear);
 cudaError_t status_logits(uint32_t* out, int clear);
 cudaError_t status_mla(uint32_t* out, int clear);
+cudaError_t status_dequant_set_wait_limit(uint64_t ns);
+cudaError_t status_topk_set_wait_limit(uint64_t ns);
+cudaError_t status_logits_set_wait_limit(uint64_t ns);
+cudaError_t status_mla_set_wait_limit(uint64_t ns);
 }  // namespace hcu

@@ -31,6 +31,7 @@
 // and frees its TMEM before returning.
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -648,7 +649,7 @@ struct RCursor {
   }
 };
 
-template <int H>
+template <int H, bool kMixed>
 __global__ __launch_bounds__(kPfThreads, 1) void mqa_logits_ragged_kernel(const __grid_constant__ CUtensorMap tm_k,
                                                                          const __grid_constant__ CUtensorMap tm_q,
                                                                          const RaggedArgs p) {
@@ -825,8 +826,10 @@ __global__ __launch_bounds__(kPfThreads, 1) void mqa_logits_ragged_kernel(const 
         for (int lr = 0; lr < kQB * RPW; ++lr) {
           const int row = row0 + (lr / RPW) * RB + (lr % RPW) * kPfTeams + rsel;
           const bool in = row < p.rows;
-          for (int h = lane; h < H; h += 32)
-            wsm[lr * H + h] = in ? __ldg(p.weights + static_cast<int64_t>(row) * H + h) * kReluScale : 0.f;
+          for (int h = lane; h < H; h += 32)  // pre-scaled by 2^25 where the ReLU is the saturating FMA
+            wsm[lr * H + h] = in ? __ldg(p.weights + static_cast<int64_t>(row) * H + h) *
+                                       ((kMixed && (h & 1)) ? 1.f : kReluScale)
+                                 : 0.f;
           if (lane == 0) {
             const int a0 = in ? max(__ldg(p.rs + row), 0) : 0;
             const int e0 = in ? min(__ldg(p.re + row), p.n_tokens) : 0;
@@ -868,10 +871,17 @@ __global__ __launch_bounds__(kPfThreads, 1) void mqa_logits_ragged_kernel(const 
               const float4 wa = w4[jj];
               const float4 wb = w4[jj + 1];
               const uint32_t* x = &v[4 * jj];
-              relu_fma2(acc0, x[0], x[1], wa.x, wa.y);
-              relu_fma2(acc1, x[2], x[3], wa.z, wa.w);
-              relu_fma2(acc2, x[4], x[5], wb.x, wb.y);
-              relu_fma2(acc3, x[6], x[7], wb.z, wb.w);
+              if constexpr (kMixed) {
+                relu_fma2_mixed(acc0, x[0], x[1], wa.x, wa.y);
+                relu_fma2_mixed(acc1, x[2], x[3], wa.z, wa.w);
+                relu_fma2_mixed(acc2, x[4], x[5], wb.x, wb.y);
+                relu_fma2_mixed(acc3, x[6], x[7], wb.z, wb.w);
+              } else {
+                relu_fma2(acc0, x[0], x[1], wa.x, wa.y);
+                relu_fma2(acc1, x[2], x[3], wa.z, wa.w);
+                relu_fma2(acc2, x[4], x[5], wb.x, wb.y);
+                relu_fma2(acc3, x[6], x[7], wb.z, wb.w);
+              }
             }
           }
           float s0 = ((acc0.x + acc0.y) + (acc1.x + acc1.y)) + ((acc2.x + acc2.y) + (acc3.x + acc3.y));
@@ -961,6 +971,14 @@ int launch_paged_t(const CUtensorMap& tkv, const CUtensorMap& tsc, const CUtenso
                        static_cast<int>(smem));
   mqa_logits_paged_kernel<H, kHist><<<sm_count(), kLgThreads, smem, stream>>>(tkv, tsc, tq, a);
   return launch_status();
+}
+
+template <int H, bool kMixed>
+void launch_ragged(const CUtensorMap& tk, const CUtensorMap& tq, const RaggedArgs& a, cudaStream_t st) {
+  const size_t smem = sizeof(PfSmem) + 1024;
+  cudaFuncSetAttribute(mqa_logits_ragged_kernel<H, kMixed>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       static_cast<int>(smem));
+  mqa_logits_ragged_kernel<H, kMixed><<<sm_count(), kPfThreads, smem, st>>>(tk, tq, a);
 }
 
 template <int H>
@@ -1059,15 +1077,13 @@ extern "C" int hcu_mqa_logits_ragged(const uint8_t* q, int64_t rows, int64_t hea
   a.stride = logits_stride;
   a.rows = static_cast<int>(rows);
   a.n_tokens = static_cast<int>(n_tokens);
-  const size_t smem = sizeof(PfSmem) + 1024;
-  if (heads == 64) {
-    cudaFuncSetAttribute(mqa_logits_ragged_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         static_cast<int>(smem));
-    mqa_logits_ragged_kernel<64><<<sm_count(), kPfThreads, smem, st>>>(tk, tq, a);
-  } else {
-    cudaFuncSetAttribute(mqa_logits_ragged_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         static_cast<int>(smem));
-    mqa_logits_ragged_kernel<32><<<sm_count(), kPfThreads, smem, st>>>(tk, tq, a);
-  }
+  static const bool mixed = [] {
+    const char* e = std::getenv("HCU_PF_RELU");
+    return e != nullptr && e[0] == 'm';
+  }();
+  if (heads == 64)
+    mixed ? launch_ragged<64, true>(tk, tq, a, st) : launch_ragged<64, false>(tk, tq, a, st);
+  else
+    mixed ? launch_ragged<32, true>(tk, tq, a, st) : launch_ragged<32, false>(tk, tq, a, st);
   return launch_status();
 }

@@ -629,7 +629,7 @@ __global__ __launch_bounds__(kT, 1024 / kT) void topk_row_kernel(
     const float* __restrict__ score, int64_t score_stride, int width, const int16_t* __restrict__ mask,
     int64_t mask_stride, const int32_t* __restrict__ lengths, const int32_t* __restrict__ pt, int64_t pt_stride,
     int32_t* __restrict__ dst, uint32_t* __restrict__ dst_keys, const int32_t* __restrict__ pre_ws, int rows,
-    int splits) {
+    int splits, const int32_t* __restrict__ run_if) {
   constexpr int kTkThreads = kT;
   constexpr int kCandCap = Tk<kT>::kCandCap;
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -637,6 +637,7 @@ __global__ __launch_bounds__(kT, 1024 / kT) void topk_row_kernel(
   // launched with programmatic stream serialization: wait for the previous kernel (the logits that
   // this reads) to complete before the first global read; a no-op after an ordinary dependency
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (run_if != nullptr && __ldcg(run_if) == 0) return;  // predicated launch: nothing to do this time
   const int row = kSplit ? static_cast<int>(blockIdx.x) / splits : static_cast<int>(blockIdx.x);
   const int rank = kSplit ? static_cast<int>(blockIdx.x) % splits : 0;
   const int tid = threadIdx.x;
@@ -903,7 +904,8 @@ void launch_split(const float* score, int rows, int width, int64_t score_stride,
 template <int kT, bool kVec, bool kSorted>
 void launch_rows_t(const float* score, int rows, int width, int64_t score_stride, const int16_t* mask,
                    int64_t mask_stride, const int32_t* lengths, const int32_t* pt, int64_t pt_stride, int32_t* dst,
-                   uint32_t* dst_keys, const int32_t* pre_ws, cudaStream_t stream, int splits) {
+                   uint32_t* dst_keys, const int32_t* pre_ws, cudaStream_t stream, int splits,
+                   const int32_t* run_if = nullptr) {
   const size_t smem = sizeof(TopkSmem<kT>);
   if (kSorted || splits <= 1) {
     // programmatic stream serialization: the grid may be scheduled while the previous kernel drains
@@ -920,7 +922,7 @@ void launch_rows_t(const float* score, int rows, int width, int64_t score_stride
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     cudaLaunchKernelEx(&cfg, kern, score, score_stride, width, mask, mask_stride, lengths, pt, pt_stride, dst,
-                       dst_keys, pre_ws, rows, 1);
+                       dst_keys, pre_ws, rows, 1, run_if);
     return;
   }
   if constexpr (!kSorted) launch_split<kT, kVec>(score, rows, width, score_stride, mask, mask_stride, lengths, pt,
@@ -981,31 +983,32 @@ void launch_split(const float* score, int rows, int width, int64_t score_stride,
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cudaLaunchKernelEx(&cfg, kern, score, score_stride, width, mask, mask_stride, lengths, pt, pt_stride, dst, dst_keys,
-                     pre_ws, rows, splits);
+                     pre_ws, rows, splits, static_cast<const int32_t*>(nullptr));
 }
 
 template <int kT>
 void launch_rows_sized(const float* score, int r, int w, int64_t score_stride, const int16_t* mask,
                        int64_t mask_stride, const int32_t* lengths, const int32_t* pt, int64_t pt_stride, int32_t* dst,
                        uint32_t* dst_keys, const int32_t* pre_ws, cudaStream_t stream, bool vec, bool sorted,
-                       int splits) {
+                       int splits, const int32_t* run_if) {
   if (vec && !sorted)
     launch_rows_t<kT, true, false>(score, r, w, score_stride, mask, mask_stride, lengths, pt, pt_stride, dst, dst_keys,
-                                   pre_ws, stream, splits);
+                                   pre_ws, stream, splits, run_if);
   else if (vec)
     launch_rows_t<kT, true, true>(score, r, w, score_stride, mask, mask_stride, lengths, pt, pt_stride, dst, dst_keys,
-                                  pre_ws, stream, splits);
+                                  pre_ws, stream, splits, run_if);
   else if (!sorted)
     launch_rows_t<kT, false, false>(score, r, w, score_stride, mask, mask_stride, lengths, pt, pt_stride, dst,
-                                    dst_keys, pre_ws, stream, splits);
+                                    dst_keys, pre_ws, stream, splits, run_if);
   else
     launch_rows_t<kT, false, true>(score, r, w, score_stride, mask, mask_stride, lengths, pt, pt_stride, dst, dst_keys,
-                                   pre_ws, stream, splits);
+                                   pre_ws, stream, splits, run_if);
 }
 
 int launch_rows(const float* score, int64_t rows, int64_t width, int64_t score_stride, const int16_t* mask,
                 int64_t mask_stride, const int32_t* lengths, const int32_t* pt, int64_t pt_stride, int32_t* dst,
-                uint32_t* dst_keys, const int32_t* pre_ws, cudaStream_t stream, bool sorted = false, int splits = 1) {
+                uint32_t* dst_keys, const int32_t* pre_ws, cudaStream_t stream, bool sorted = false, int splits = 1,
+                const int32_t* run_if = nullptr) {
   const int w = static_cast<int>(width);
   const int r = static_cast<int>(rows);
   const bool vec = use_vec(score, width, score_stride);
@@ -1015,10 +1018,10 @@ int launch_rows(const float* score, int64_t rows, int64_t width, int64_t score_s
   const int64_t part = (width + splits - 1) / splits;
   if (part <= kNarrowWidth || (rows >= 2 * static_cast<int64_t>(sm_count()) && part <= kManyRowsWidth))
     launch_rows_sized<512>(score, r, w, score_stride, mask, mask_stride, lengths, pt, pt_stride, dst, dst_keys, pre_ws,
-                           stream, vec, sorted, splits);
+                           stream, vec, sorted, splits, run_if);
   else
     launch_rows_sized<1024>(score, r, w, score_stride, mask, mask_stride, lengths, pt, pt_stride, dst, dst_keys,
-                            pre_ws, stream, vec, sorted, splits);
+                            pre_ws, stream, vec, sorted, splits, run_if);
   return launch_status();
 }
 
@@ -1075,7 +1078,7 @@ struct ListKeys {
   __device__ __forceinline__ void operator()(F&& f) const {
     for (int i = 0; i < per; ++i) {
       const int64_t o = merge_off(c0 + i, lshift, pstride, row);
-      if (__ldg(gidx + o) >= 0) f(__ldg(keys + o));
+      if (__ldcg(gidx + o) >= 0) f(__ldcg(keys + o));
     }
   }
 };
@@ -1105,9 +1108,9 @@ __device__ void merge_exact(TopkSmem<kT>& sm, const uint32_t* __restrict__ keys,
   int pa = ex & 0xFFFF, pq = ex >> 16;
   for (int i = 0; i < per; ++i) {
     const int64_t o = merge_off(c0 + i, lshift, pstride, row);
-    const int g = __ldg(gidx + o);
+    const int g = __ldcg(gidx + o);
     if (g < 0) continue;
-    const uint32_t k = __ldg(keys + o);
+    const uint32_t k = __ldcg(keys + o);
     if (k > thr) {
       out[pa++] = g;
     } else if (k == thr) {
@@ -1124,20 +1127,15 @@ __device__ void merge_exact(TopkSmem<kT>& sm, const uint32_t* __restrict__ keys,
 // -2: the largest key its list may have dropped);
 // short_identity: rows of at most kTopK visible tokens [0, len) output
 // 0, 1, .., len - 1 without reading the lists (identity page table).
+// The merge of one row (every thread of the CTA calls it), result into out[0, kTopK).
 template <int kT>
-__global__ __launch_bounds__(kT, 1024 / kT) void cp_merge_kernel(const uint32_t* __restrict__ keys,
-                                                                const int32_t* __restrict__ gidx, int parts,
-                                                                int lshift, int64_t pstride,
-                                                                const int32_t* __restrict__ lengths,
-                                                                int32_t* __restrict__ dst, int32_t* __restrict__ flag,
-                                                                int short_identity) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  TopkSmem<kT>& sm = *reinterpret_cast<TopkSmem<kT>*>(smem_raw);
-  const int row = blockIdx.x;
+__device__ __noinline__ void merge_row(TopkSmem<kT>& sm, const uint32_t* __restrict__ keys,
+                                       const int32_t* __restrict__ gidx, int parts, int lshift, int64_t pstride,
+                                       const int32_t* __restrict__ lengths, int row, int32_t* __restrict__ out,
+                                       int32_t* __restrict__ flag, int short_identity) {
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int w = tid >> 5;
-  int32_t* out = dst + static_cast<int64_t>(row) * kTopK;
   if (short_identity) {
     const int vl = __ldg(lengths + row);
     if (vl <= kTopK) {
@@ -1161,7 +1159,7 @@ __global__ __launch_bounds__(kT, 1024 / kT) void cp_merge_kernel(const uint32_t*
   for (int j = 0; j < kMs / kT; ++j) {
     const int c = static_cast<int>(static_cast<int64_t>(tid + j * kT) * n_ent / kMs) + n_ent / (2 * kMs);
     const int64_t o = merge_off(min(c, n_ent - 1), lshift, pstride, row);
-    sk[j] = __ldg(gidx + o) >= 0 ? __ldg(keys + o) : 0u;  // a missing entry ranks below every key
+    sk[j] = __ldcg(gidx + o) >= 0 ? __ldcg(keys + o) : 0u;  // a missing entry ranks below every key
     atomicAdd(&sm.hist[sk[j] >> 20], 1);
   }
   __syncthreads();
@@ -1197,8 +1195,8 @@ __global__ __launch_bounds__(kT, 1024 / kT) void cp_merge_kernel(const uint32_t*
       kk[u] = 0u;
       if (i0 + u < per && c0 + i0 + u < n_ent) {
         const int64_t o = merge_off(c0 + i0 + u, lshift, pstride, row);
-        kk[u] = __ldg(keys + o);
-        gg[u] = __ldg(gidx + o);
+        kk[u] = __ldcg(keys + o);
+        gg[u] = __ldcg(gidx + o);
       }
     }
 #pragma unroll
@@ -1229,8 +1227,8 @@ __global__ __launch_bounds__(kT, 1024 / kT) void cp_merge_kernel(const uint32_t*
       for (int u = 0; u < 8; ++u) {
         if ((cbits >> (i0 + u)) & 1u) {
           const int64_t o = merge_off(c0 + i0 + u, lshift, pstride, row);
-          kk[u] = __ldg(keys + o);
-          gg[u] = __ldg(gidx + o);
+          kk[u] = __ldcg(keys + o);
+          gg[u] = __ldcg(gidx + o);
         }
       }
 #pragma unroll
@@ -1279,6 +1277,20 @@ __global__ __launch_bounds__(kT, 1024 / kT) void cp_merge_kernel(const uint32_t*
   if (tid == 0 && flag && sm.mark_any && sm.mark_max >= thr) atomicOr(flag, 1);  // a truncated list
   write_candidates<kT, false>(sm, n, thr, above, out, nullptr);
 }
+
+template <int kT>
+__global__ __launch_bounds__(kT, 1024 / kT) void cp_merge_kernel(const uint32_t* __restrict__ keys,
+                                                                const int32_t* __restrict__ gidx, int parts,
+                                                                int lshift, int64_t pstride,
+                                                                const int32_t* __restrict__ lengths,
+                                                                int32_t* __restrict__ dst, int32_t* __restrict__ flag,
+                                                                int short_identity) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  TopkSmem<kT>& sm = *reinterpret_cast<TopkSmem<kT>*>(smem_raw);
+  const int row = blockIdx.x;
+  merge_row(sm, keys, gidx, parts, lshift, pstride, lengths, row, dst + static_cast<int64_t>(row) * kTopK, flag,
+            short_identity);
+}
 // ---------------------------------------------------------------------------
 // Context-parallel candidate filter (the bounded exchange of hcu_ops/cp.py).
 //
@@ -1313,76 +1325,83 @@ struct __align__(16) BoundSmem {
 // every range's bound down.  Exactness never rests on the estimate: the merge
 // checks that the union holds kTopK entries.
 template <bool kVec>
-__global__ __launch_bounds__(kBoundWarps * 32) void cp_bound_kernel(
-    const float* __restrict__ score, int64_t score_stride, int width, const int16_t* __restrict__ mask,
-    int64_t mask_stride, const int32_t* __restrict__ lengths, const int32_t* __restrict__ totals, int rows,
-    int32_t* __restrict__ bounds) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  BoundSmem& sm = *reinterpret_cast<BoundSmem*>(smem_raw);
+__device__ __forceinline__ uint32_t row_bound(BoundSmem& sm, const float* __restrict__ score, int64_t score_stride,
+                                              int width, const int16_t* __restrict__ mask, int64_t mask_stride,
+                                              const int32_t* __restrict__ lengths,
+                                              const int32_t* __restrict__ totals, int row) {
   const int lane = threadIdx.x & 31;
   const int w = threadIdx.x >> 5;
-  const int row = blockIdx.x * kBoundWarps + w;
-  if (row >= rows) return;  // whole warps; the kernel has no block barrier
   int n = __ldg(lengths + row);
   n = n < 0 ? 0 : (n > width ? width : n);
   const int total = __ldg(totals + row);
   uint32_t v = 0xFFFFFFFFu;
   if (total > kTopK && static_cast<int64_t>(kTopK) * n >= total) {
     v = 0u;
-    {
-      const int m = n <= kBoundSamples ? n : kBoundSamples;
-      const float t = static_cast<float>(kTopK) * static_cast<float>(m) / static_cast<float>(total);
-      const int r_lo = static_cast<int>(ceilf(t + 3.f * sqrtf(t) + 2.f));
-      if (r_lo < m) {
-        const float* vals = score + static_cast<int64_t>(row) * score_stride;
-        const int16_t* mrow = mask + static_cast<int64_t>(row) * mask_stride;
-        uint32_t* ks = sm.k[w];
-        if (n <= kBoundSamples) {  // every token
-          for (int i = lane; i < n; i += 32) {
-            const bool set = (static_cast<uint16_t>(__ldg(mrow + (i >> 4))) >> (i & 15)) & 1u;
-            ks[i] = set ? to_key(__ldg(vals + i)) : kZeroKey;
-          }
-        } else {  // group g: tokens i .. i + 3 < n, i = ((2g + 1) n / (2 m / 4)) rounded down to a multiple of 4
-          constexpr int kGroups = kBoundSamples / 4;
-          for (int g = lane; g < kGroups; g += 32) {
-            const int i = min(static_cast<int>((2 * static_cast<int64_t>(g) + 1) * n / (2 * kGroups)), n - 4) & ~3;
-            const uint32_t mb = static_cast<uint16_t>(__ldg(mrow + (i >> 4))) >> (i & 15);
-            float f[4];
-            if constexpr (kVec) {
-              const float4 q = __ldg(reinterpret_cast<const float4*>(vals + i));
-              f[0] = q.x; f[1] = q.y; f[2] = q.z; f[3] = q.w;
-            } else {
-#pragma unroll
-              for (int e = 0; e < 4; ++e) f[e] = __ldg(vals + i + e);
-            }
-#pragma unroll
-            for (int e = 0; e < 4; ++e) ks[4 * g + e] = ((mb >> e) & 1u) ? to_key(f[e]) : kZeroKey;
-          }
+    const int m = n <= kBoundSamples ? n : kBoundSamples;
+    const float t = static_cast<float>(kTopK) * static_cast<float>(m) / static_cast<float>(total);
+    const int r_lo = static_cast<int>(ceilf(t + 3.f * sqrtf(t) + 2.f));
+    if (r_lo < m) {
+      const float* vals = score + static_cast<int64_t>(row) * score_stride;
+      const int16_t* mrow = mask + static_cast<int64_t>(row) * mask_stride;
+      uint32_t* ks = sm.k[w];
+      if (n <= kBoundSamples) {  // every token
+        for (int i = lane; i < n; i += 32) {
+          const bool set = (static_cast<uint16_t>(__ldg(mrow + (i >> 4))) >> (i & 15)) & 1u;
+          ks[i] = set ? to_key(__ldg(vals + i)) : kZeroKey;
         }
-        // r_lo-th largest sample key: four 8-bit radix passes over the warp's samples
-        uint32_t pre = 0u;
-        int need = r_lo;
-        int* h = sm.h[w];
-        for (int pass = 0; pass < 4; ++pass) {
-          const int sh = 24 - 8 * pass;
-          for (int i = lane; i < 256; i += 32) h[i] = 0;
-          __syncwarp();
-          for (int j = lane; j < m; j += 32) {
-            const uint32_t k = ks[j];
-            if (pass == 0 || (k >> (sh + 8)) == pre) atomicAdd(&h[(k >> sh) & 0xFFu], 1);
+      } else {  // group g: tokens i .. i + 3 < n, i = ((2g + 1) n / (2 m / 4)) rounded down to a multiple of 4
+        constexpr int kGroups = kBoundSamples / 4;
+        for (int g = lane; g < kGroups; g += 32) {
+          const int i = min(static_cast<int>((2 * static_cast<int64_t>(g) + 1) * n / (2 * kGroups)), n - 4) & ~3;
+          const uint32_t mb = static_cast<uint16_t>(__ldg(mrow + (i >> 4))) >> (i & 15);
+          float f[4];
+          if constexpr (kVec) {
+            const float4 q = __ldg(reinterpret_cast<const float4*>(vals + i));
+            f[0] = q.x; f[1] = q.y; f[2] = q.z; f[3] = q.w;
+          } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) f[e] = __ldg(vals + i + e);
           }
-          __syncwarp();
-          warp_find<256>(h, need, sm.res[w]);
-          __syncwarp();
-          pre = (pre << 8) | static_cast<uint32_t>(sm.res[w][0]);
-          need -= sm.res[w][1];
-          __syncwarp();
+#pragma unroll
+          for (int e = 0; e < 4; ++e) ks[4 * g + e] = ((mb >> e) & 1u) ? to_key(f[e]) : kZeroKey;
         }
-        v = pre;
       }
+      // r_lo-th largest sample key: four 8-bit radix passes over the warp's samples
+      uint32_t pre = 0u;
+      int need = r_lo;
+      int* h = sm.h[w];
+      for (int pass = 0; pass < 4; ++pass) {
+        const int sh = 24 - 8 * pass;
+        for (int i = lane; i < 256; i += 32) h[i] = 0;
+        __syncwarp();
+        for (int j = lane; j < m; j += 32) {
+          const uint32_t k = ks[j];
+          if (pass == 0 || (k >> (sh + 8)) == pre) atomicAdd(&h[(k >> sh) & 0xFFu], 1);
+        }
+        __syncwarp();
+        warp_find<256>(h, need, sm.res[w]);
+        __syncwarp();
+        pre = (pre << 8) | static_cast<uint32_t>(sm.res[w][0]);
+        need -= sm.res[w][1];
+        __syncwarp();
+      }
+      v = pre;
     }
   }
-  if (lane == 0) bounds[row] = static_cast<int32_t>(v ^ kZeroKey);
+  return v;
+}
+
+template <bool kVec>
+__global__ __launch_bounds__(kBoundWarps * 32) void cp_bound_kernel(
+    const float* __restrict__ score, int64_t score_stride, int width, const int16_t* __restrict__ mask,
+    int64_t mask_stride, const int32_t* __restrict__ lengths, const int32_t* __restrict__ totals, int rows,
+    int32_t* __restrict__ bounds) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  BoundSmem& sm = *reinterpret_cast<BoundSmem*>(smem_raw);
+  const int row = blockIdx.x * kBoundWarps + (threadIdx.x >> 5);
+  if (row >= rows) return;  // whole warps; the kernel has no block barrier
+  const uint32_t v = row_bound<kVec>(sm, score, score_stride, width, mask, mask_stride, lengths, totals, row);
+  if ((threadIdx.x & 31) == 0) bounds[row] = static_cast<int32_t>(v ^ kZeroKey);
 }
 
 // One CTA per row: every token of [0, len) with key >= the row's bound, in
@@ -1395,23 +1414,13 @@ __global__ __launch_bounds__(kBoundWarps * 32) void cp_bound_kernel(
 // (entry -2, key = the largest key it may have dropped) that the merge checks;
 // past the candidate capacity *flag |= 1.
 template <int kT, bool kVec>
-__global__ __launch_bounds__(kT, 1024 / kT) void cp_filter_kernel(
-    const float* __restrict__ score, int64_t score_stride, int width, const int16_t* __restrict__ mask,
-    int64_t mask_stride, const int32_t* __restrict__ lengths, const int32_t* __restrict__ pt, int64_t pt_stride,
-    const int32_t* __restrict__ bounds, int cap, uint32_t* __restrict__ out_keys, int32_t* __restrict__ out_gidx,
-    int rows_per_block, int64_t block_stride, int32_t* __restrict__ counts, int32_t* __restrict__ flag) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  TopkSmem<kT>& sm = *reinterpret_cast<TopkSmem<kT>*>(smem_raw);
-  const int row = blockIdx.x;
+__device__ __noinline__ int filter_row(TopkSmem<kT>& sm, const float* __restrict__ vals,
+                                       const int16_t* __restrict__ mrow, const int32_t* __restrict__ src, int len,
+                                       uint32_t lo, int cap, uint32_t* __restrict__ ok, int32_t* __restrict__ og,
+                                       int32_t* __restrict__ flag) {
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int w = tid >> 5;
-  int len = __ldg(lengths + row);
-  len = len < 0 ? 0 : (len > width ? width : len);
-  const uint32_t lo = static_cast<uint32_t>(__ldg(bounds + row)) ^ kZeroKey;
-  const float* vals = score + static_cast<int64_t>(row) * score_stride;
-  const int16_t* mrow = mask + static_cast<int64_t>(row) * mask_stride;
-  const int32_t* src = pt + static_cast<int64_t>(row) * pt_stride;
   uint32_t b0[16], valid0 = 0u;
   const uint32_t mw0 = load16_raw<kVec>(vals, mrow, w * (32 * kLaneTok) + lane * kLaneTok, len, b0, valid0);
   for (int i = tid; i < 2 * 512; i += kT) (&sm.hb[0][0])[i] = 0;  // the select's digit histograms
@@ -1419,9 +1428,6 @@ __global__ __launch_bounds__(kT, 1024 / kT) void cp_filter_kernel(
                               : collect_candidates<kT, kVec, false>(vals, mrow, src, 0, len, lo, sm, b0, mw0, valid0);
   cp_async_wait_all();
   __syncthreads();
-  const int64_t lo_off = (row / rows_per_block) * block_stride + static_cast<int64_t>(row % rows_per_block) * cap;
-  uint32_t* ok = out_keys + lo_off;
-  int32_t* og = out_gidx + lo_off;
   if (n > cap && n <= Tk<kT>::kCandCap) {
     // More candidates than slots.  cap = kTopK: the range's exact top-kTopK among them, in token
     // order, holds every token of the row's global top-kTopK that lies in this range.  cap < kTopK:
@@ -1444,8 +1450,29 @@ __global__ __launch_bounds__(kT, 1024 / kT) void cp_filter_kernel(
     }
     if (tid == 0 && n > cap) atomicOr(flag, 1);  // past the candidate capacity
   }
-  if (tid == 0 && counts) counts[row] = n;
+  return n;
 }
+
+template <int kT, bool kVec>
+__global__ __launch_bounds__(kT, 1024 / kT) void cp_filter_kernel(
+    const float* __restrict__ score, int64_t score_stride, int width, const int16_t* __restrict__ mask,
+    int64_t mask_stride, const int32_t* __restrict__ lengths, const int32_t* __restrict__ pt, int64_t pt_stride,
+    const int32_t* __restrict__ bounds, int cap, uint32_t* __restrict__ out_keys, int32_t* __restrict__ out_gidx,
+    int rows_per_block, int64_t block_stride, int32_t* __restrict__ counts, int32_t* __restrict__ flag) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  TopkSmem<kT>& sm = *reinterpret_cast<TopkSmem<kT>*>(smem_raw);
+  const int row = blockIdx.x;
+  int len = __ldg(lengths + row);
+  len = len < 0 ? 0 : (len > width ? width : len);
+  const uint32_t lo = static_cast<uint32_t>(__ldg(bounds + row)) ^ kZeroKey;
+  const int64_t lo_off = (row / rows_per_block) * block_stride + static_cast<int64_t>(row % rows_per_block) * cap;
+  const int n = filter_row<kT, kVec>(sm, score + static_cast<int64_t>(row) * score_stride,
+                                     mask + static_cast<int64_t>(row) * mask_stride,
+                                     pt + static_cast<int64_t>(row) * pt_stride, len, lo, cap, out_keys + lo_off,
+                                     out_gidx + lo_off, flag);
+  if (threadIdx.x == 0 && counts) counts[row] = n;
+}
+
 }  // namespace
 
 // Used by the logits translation unit for the hist_lens path: zeroes the
@@ -1528,6 +1555,19 @@ extern "C" int hcu_topk_keys(const float* score, int64_t rows, int64_t width, in
   if (!dst_keys) return HCU_ERR_ARG;
   return launch_rows(score, rows, width, score_stride, mask, mask_stride, lengths, page_table, pt_stride, dst,
                      dst_keys, nullptr, reinterpret_cast<cudaStream_t>(stream), /*sorted=*/true);
+}
+
+extern "C" int hcu_topk_keys_if(const float* score, int64_t rows, int64_t width, int64_t score_stride,
+                                const int16_t* mask, int64_t mask_stride, const int32_t* lengths,
+                                const int32_t* page_table, int64_t pt_stride, int32_t* dst, uint32_t* dst_keys,
+                                const int32_t* run_if, hcu_stream_t stream) {
+  using namespace hcu;
+  int st = check_common(score, rows, width, score_stride, mask, mask_stride, lengths, page_table, pt_stride, kTopK,
+                        dst);
+  if (st != HCU_OK || rows == 0) return st;
+  if (!dst_keys || !run_if) return HCU_ERR_ARG;
+  return launch_rows(score, rows, width, score_stride, mask, mask_stride, lengths, page_table, pt_stride, dst,
+                     dst_keys, nullptr, reinterpret_cast<cudaStream_t>(stream), /*sorted=*/true, 1, run_if);
 }
 
 extern "C" int hcu_cp_topk_merge_lists(const uint32_t* keys, const int32_t* gidx, int64_t n_parts,
@@ -1631,6 +1671,313 @@ extern "C" int hcu_cp_filter(const float* score, int64_t rows, int64_t width, in
       launch_filter<1024, false>(score, r, w, score_stride, mask, mask_stride, lengths, page_table, pt_stride, bounds,
                                  c, keys, gidx, rpb, block_stride, counts, flag, s);
   }
+  return launch_status();
+}
+
+// ---------------------------------------------------------------------------
+// Context-parallel exchange over peer memory (hcu_cp_peer_*): the bound, filter
+// and merge kernels store their results straight into the consuming ranks'
+// buffers (mapped over NVLink) and publish completion with one flag per (step,
+// phase, source rank); the consumers wait for every rank's flag.
+//
+// Publication: every thread fences its stores at system scope, the CTA
+// synchronises, and thread 0 counts the CTA into a local counter; the launch's
+// last CTA (it sees the count reach the grid size) resets the counter, takes
+// the launch's local flag word and stores (epoch << 1 | flag) into every
+// rank's signal word for (phase, this rank) with a system-scope release.
+// Waiting: thread 0 spins with acquire loads on the P words of the phase until
+// each holds this epoch, bounded by the wait limit (on expiry the status bit is
+// set and the CTA skips its work, flagging the step); the CTA then synchronises.
+// ---------------------------------------------------------------------------
+namespace hcu {
+namespace {
+
+enum : int {
+  kWsBoundCnt = 0, kWsFilterCnt = 1, kWsMergeCnt = 2, kWsScatterCnt = 3, kWsXMergeCnt = 4,
+  kWsFilterFlag = 5, kWsMergeFlag = 6, kWsXMergeFlag = 7,
+};
+enum : int { kPhBounds = 0, kPhLists = 1, kPhRows = 2, kPhXLists = 3, kPhXRows = 4 };
+static_assert(HCU_CP_SIG_WORDS == 5 && HCU_CP_WS_FLAG == 8 && HCU_CP_WS_RERUNS == 9, "signal and workspace layout");
+
+__device__ __forceinline__ void peer_publish(const hcu_cp_peers_t& pp, int phase, int* counter, int* flagw) {
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned int grid = gridDim.x * gridDim.y * gridDim.z;
+    if (atomicAdd(reinterpret_cast<unsigned int*>(counter), 1u) + 1u == grid) {
+      __threadfence_system();
+      const int f = flagw ? atomicExch(flagw, 0) : 0;
+      atomicExch(counter, 0);
+      const uint32_t v = (pp.epoch << 1) | (f != 0 ? 1u : 0u);
+      for (int p = 0; p < pp.parts; ++p) st_release_sys(pp.sig[p] + phase * pp.parts + pp.rank, v);
+    }
+  }
+}
+
+// Thread 0 only.  True when every rank published `phase` for this epoch; *flag
+// = the OR of their flag bits.  False (status set) when the wait limit passed.
+__device__ __noinline__ bool peer_wait(const hcu_cp_peers_t& pp, int phase, int* flag) {
+  const uint32_t* sig = pp.sig[pp.rank] + phase * pp.parts;
+  const uint64_t lim = wait_limit_ns();
+  const uint64_t t0 = globaltimer();
+  int f = 0;
+  for (int p = 0; p < pp.parts; ++p) {
+    uint32_t v = ld_acquire_sys(sig + p);
+    while ((v >> 1) < pp.epoch) {
+      if (globaltimer() - t0 > lim) {
+        atomicOr(&g_hcu_status, HCU_STATUS_WAIT_TIMEOUT);
+        *flag = 1;
+        return false;
+      }
+      __nanosleep(128);
+      v = ld_acquire_sys(sig + p);
+    }
+    f |= static_cast<int>(v & 1u);
+  }
+  *flag = f;
+  return true;
+}
+
+// Waits in thread 0 and shares the outcome with the CTA; the flag bits of the
+// sources are ORed into *flagw (when given).
+__device__ __forceinline__ bool cta_wait(const hcu_cp_peers_t& pp, int phase, int* flagw, int* s_ok) {
+  if (threadIdx.x == 0) {
+    int f = 0;
+    *s_ok = peer_wait(pp, phase, &f) ? 1 : 0;
+    if (f && flagw) atomicOr(flagw, 1);
+  }
+  __syncthreads();
+  return *s_ok != 0;
+}
+
+template <bool kVec>
+__global__ __launch_bounds__(kBoundWarps * 32) void cp_peer_bound_kernel(
+    const float* __restrict__ score, int64_t score_stride, int width, const int16_t* __restrict__ mask,
+    int64_t mask_stride, const int32_t* __restrict__ lengths, const int32_t* __restrict__ totals,
+    const hcu_cp_peers_t pp) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  BoundSmem& sm = *reinterpret_cast<BoundSmem*>(smem_raw);
+  __shared__ __align__(16) int32_t vals[kBoundWarps];
+  const int w = threadIdx.x >> 5;
+  const int row0 = blockIdx.x * kBoundWarps;
+  const int row = row0 + w;
+  if (row < pp.rows) {
+    const uint32_t v = row_bound<kVec>(sm, score, score_stride, width, mask, mask_stride, lengths, totals, row);
+    if ((threadIdx.x & 31) == 0) vals[w] = static_cast<int32_t>(v ^ kZeroKey);
+  }
+  __syncthreads();
+  // the CTA's (up to) 8 consecutive bounds into slot `rank` of every rank's [P, R] bounds
+  const int nv = min(kBoundWarps, pp.rows - row0);
+  for (int i = threadIdx.x; i < pp.parts * nv; i += blockDim.x) {
+    const int p = i / nv, j = i - (i / nv) * nv;
+    pp.bounds[p][static_cast<int64_t>(pp.rank) * pp.rows + row0 + j] = vals[j];
+  }
+  peer_publish(pp, kPhBounds, pp.ws + kWsBoundCnt, nullptr);
+}
+
+template <int kT, bool kVec>
+__global__ __launch_bounds__(kT, 1024 / kT) void cp_peer_filter_kernel(
+    const float* __restrict__ score, int64_t score_stride, int width, const int16_t* __restrict__ mask,
+    int64_t mask_stride, const int32_t* __restrict__ lengths, const int32_t* __restrict__ pt, int64_t pt_stride,
+    const hcu_cp_peers_t pp) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  TopkSmem<kT>& sm = *reinterpret_cast<TopkSmem<kT>*>(smem_raw);
+  __shared__ int s_ok;
+  const int row = blockIdx.x;
+  int* flagw = pp.ws + kWsFilterFlag;
+  if (cta_wait(pp, kPhBounds, nullptr, &s_ok)) {
+    // the row's bound: the minimum over ranks of their published estimates (order-preserving int32)
+    int32_t b = INT32_MAX;
+    const int32_t* bl = pp.bounds[pp.rank];
+    for (int p = 0; p < pp.parts; ++p) b = min(b, __ldcg(bl + static_cast<int64_t>(p) * pp.rows + row));
+    int len = __ldg(lengths + row);
+    len = len < 0 ? 0 : (len > width ? width : len);
+    const int d = row / pp.rows_per_rank;  // the row's owner
+    const int64_t C = pp.list_len;
+    int32_t* keys = pp.lists[d] + (static_cast<int64_t>(2 * pp.rank) * pp.rows_per_rank + row % pp.rows_per_rank) * C;
+    filter_row<kT, kVec>(sm, score + static_cast<int64_t>(row) * score_stride,
+                         mask + static_cast<int64_t>(row) * mask_stride, pt + static_cast<int64_t>(row) * pt_stride,
+                         len, static_cast<uint32_t>(b) ^ kZeroKey, pp.list_len, reinterpret_cast<uint32_t*>(keys),
+                         keys + static_cast<int64_t>(pp.rows_per_rank) * C, flagw);
+  } else if (threadIdx.x == 0) {
+    atomicOr(flagw, 1);
+  }
+  peer_publish(pp, kPhLists, pp.ws + kWsFilterCnt, flagw);
+}
+
+// One CTA per row of this rank (rps rows): waits for every rank's lists of its
+// rows, merges them into its own out row, then copies that row to every other
+// rank's out.  exact: the 2048-entry lists of the redo (predicated on the flag).
+template <int kT>
+__global__ __launch_bounds__(kT, 1024 / kT) void cp_peer_merge_kernel(const int32_t* __restrict__ totals, int exact,
+                                                                     const hcu_cp_peers_t pp) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  TopkSmem<kT>& sm = *reinterpret_cast<TopkSmem<kT>*>(smem_raw);
+  __shared__ int s_ok;
+  if (exact && __ldcg(pp.ws + HCU_CP_WS_FLAG) == 0) return;  // grid-uniform: no redo this step
+  const int row = blockIdx.x;
+  const int rps = pp.rows_per_rank;
+  int* flagw = pp.ws + (exact ? kWsXMergeFlag : kWsMergeFlag);
+  const int64_t off = (static_cast<int64_t>(pp.rank) * rps + row) * kTopK;
+  int32_t* mine = pp.out[pp.rank] + off;
+  if (cta_wait(pp, exact ? kPhXLists : kPhLists, flagw, &s_ok)) {
+    const int C = exact ? kTopK : pp.list_len;
+    const int lshift = 31 - __clz(C);
+    const int32_t* lists = exact ? pp.lists_exact[pp.rank] : pp.lists[pp.rank];
+    merge_row(sm, reinterpret_cast<const uint32_t*>(lists), lists + static_cast<int64_t>(rps) * C, pp.parts, lshift,
+              2 * static_cast<int64_t>(rps) * C, totals, row, mine, flagw, 1);
+  } else if (threadIdx.x == 0) {
+    atomicOr(flagw, 1);
+  }
+  __syncthreads();  // the row is complete in this rank's out
+  const int4* src = reinterpret_cast<const int4*>(mine);
+  for (int i = threadIdx.x; i < kTopK / 4; i += kT) {
+    const int4 v = __ldcg(src + i);
+    for (int p = 0; p < pp.parts; ++p)
+      if (p != pp.rank) reinterpret_cast<int4*>(pp.out[p] + off)[i] = v;
+  }
+  peer_publish(pp, exact ? kPhXRows : kPhRows, pp.ws + (exact ? kWsXMergeCnt : kWsMergeCnt), flagw);
+}
+
+// The redo's lists: row r's local top-2048 (keys, entries) into slot `rank` of its owner's lists_exact.
+__global__ __launch_bounds__(256) void cp_peer_scatter_kernel(const uint32_t* __restrict__ keys,
+                                                              const int32_t* __restrict__ entries,
+                                                              const hcu_cp_peers_t pp) {
+  if (__ldcg(pp.ws + HCU_CP_WS_FLAG) == 0) return;  // grid-uniform
+  const int row = blockIdx.x;
+  const int rps = pp.rows_per_rank;
+  int32_t* dk = pp.lists_exact[row / rps] + (static_cast<int64_t>(2 * pp.rank) * rps + row % rps) * kTopK;
+  int32_t* dg = dk + static_cast<int64_t>(rps) * kTopK;
+  const int4* sk = reinterpret_cast<const int4*>(keys + static_cast<int64_t>(row) * kTopK);
+  const int4* sg = reinterpret_cast<const int4*>(entries + static_cast<int64_t>(row) * kTopK);
+  for (int i = threadIdx.x; i < kTopK / 4; i += blockDim.x) {
+    reinterpret_cast<int4*>(dk)[i] = __ldcg(sk + i);
+    reinterpret_cast<int4*>(dg)[i] = __ldcg(sg + i);
+  }
+  peer_publish(pp, kPhXLists, pp.ws + kWsScatterCnt, nullptr);
+}
+
+// Waits for every rank's rows of the step; the bounded pass records the step's
+// flag (the OR over ranks, identical on every rank), the redo counts itself.
+__global__ __launch_bounds__(32) void cp_peer_finish_kernel(int exact, const hcu_cp_peers_t pp) {
+  if (threadIdx.x != 0) return;
+  if (exact && __ldcg(pp.ws + HCU_CP_WS_FLAG) == 0) return;
+  int f = 0;
+  const bool ok = peer_wait(pp, exact ? kPhXRows : kPhRows, &f);
+  if (!exact)
+    atomicExch(pp.ws + HCU_CP_WS_FLAG, (f || !ok) ? 1 : 0);
+  else
+    atomicAdd(pp.ws + HCU_CP_WS_RERUNS, 1);
+}
+
+int check_peers(const hcu_cp_peers_t* pp) {
+  if (!pp) return HCU_ERR_ARG;
+  const hcu_cp_peers_t& p = *pp;
+  if (p.parts < 1 || p.parts > HCU_CP_MAX_PARTS || p.rank < 0 || p.rank >= p.parts || p.rows < 0) return HCU_ERR_ARG;
+  if (p.rows_per_rank < 0 || static_cast<int64_t>(p.rows_per_rank) * p.parts < p.rows) return HCU_ERR_ARG;
+  if (p.list_len < 256 || p.list_len > kTopK || (p.list_len & (p.list_len - 1)) ||
+      static_cast<int64_t>(p.list_len) * p.parts < kTopK)
+    return HCU_ERR_ARG;
+  if (p.epoch < 1 || p.epoch > 0x7FFFFFFFu || !p.ws) return HCU_ERR_ARG;
+  for (int i = 0; i < p.parts; ++i)
+    if (!p.bounds[i] || !p.lists[i] || !p.lists_exact[i] || !p.out[i] || !p.sig[i]) return HCU_ERR_ARG;
+  return HCU_OK;
+}
+
+template <int kT, bool kVec>
+void launch_peer_filter(const float* score, int width, int64_t score_stride, const int16_t* mask, int64_t mask_stride,
+                        const int32_t* lengths, const int32_t* pt, int64_t pt_stride, const hcu_cp_peers_t& pp,
+                        cudaStream_t st) {
+  const size_t smem = sizeof(TopkSmem<kT>);
+  cudaFuncSetAttribute(cp_peer_filter_kernel<kT, kVec>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       static_cast<int>(smem));
+  cp_peer_filter_kernel<kT, kVec><<<static_cast<unsigned>(pp.rows), kT, smem, st>>>(
+      score, score_stride, width, mask, mask_stride, lengths, pt, pt_stride, pp);
+}
+
+}  // namespace
+}  // namespace hcu
+
+extern "C" int hcu_cp_peer_bound(const float* score, int64_t width, int64_t score_stride, const int16_t* mask,
+                                 int64_t mask_stride, const int32_t* lengths, const int32_t* totals,
+                                 const hcu_cp_peers_t* peers, hcu_stream_t stream) {
+  using namespace hcu;
+  if (check_peers(peers) != HCU_OK) return HCU_ERR_ARG;
+  const hcu_cp_peers_t& pp = *peers;
+  if (width < 0 || width > INT32_MAX / 2 || score_stride < width || mask_stride < (width + 15) / 16) return HCU_ERR_ARG;
+  if (pp.rows == 0) return HCU_OK;
+  if (!score || !mask || !lengths || !totals) return HCU_ERR_ARG;
+  const size_t smem = sizeof(BoundSmem);
+  const unsigned grid = static_cast<unsigned>((pp.rows + kBoundWarps - 1) / kBoundWarps);
+  const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (use_vec(score, width, score_stride)) {
+    cudaFuncSetAttribute(cp_peer_bound_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(smem));
+    cp_peer_bound_kernel<true><<<grid, kBoundWarps * 32, smem, st>>>(score, score_stride, static_cast<int>(width),
+                                                                     mask, mask_stride, lengths, totals, pp);
+  } else {
+    cudaFuncSetAttribute(cp_peer_bound_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(smem));
+    cp_peer_bound_kernel<false><<<grid, kBoundWarps * 32, smem, st>>>(score, score_stride, static_cast<int>(width),
+                                                                      mask, mask_stride, lengths, totals, pp);
+  }
+  return launch_status();
+}
+
+extern "C" int hcu_cp_peer_filter(const float* score, int64_t width, int64_t score_stride, const int16_t* mask,
+                                  int64_t mask_stride, const int32_t* lengths, const int32_t* page_table,
+                                  int64_t pt_stride, const hcu_cp_peers_t* peers, hcu_stream_t stream) {
+  using namespace hcu;
+  if (check_peers(peers) != HCU_OK) return HCU_ERR_ARG;
+  const hcu_cp_peers_t& pp = *peers;
+  const int st0 = check_common(score, pp.rows, width, score_stride, mask, mask_stride, lengths, page_table, pt_stride,
+                               kTopK, page_table);
+  if (st0 != HCU_OK || pp.rows == 0) return st0;
+  const int w = static_cast<int>(width);
+  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const bool vec = use_vec(score, width, score_stride);
+  if (width <= kNarrowWidth || (pp.rows >= 2 * static_cast<int64_t>(sm_count()) && width <= kManyRowsWidth)) {
+    vec ? launch_peer_filter<512, true>(score, w, score_stride, mask, mask_stride, lengths, page_table, pt_stride, pp, s)
+        : launch_peer_filter<512, false>(score, w, score_stride, mask, mask_stride, lengths, page_table, pt_stride, pp,
+                                         s);
+  } else {
+    vec ? launch_peer_filter<1024, true>(score, w, score_stride, mask, mask_stride, lengths, page_table, pt_stride, pp,
+                                         s)
+        : launch_peer_filter<1024, false>(score, w, score_stride, mask, mask_stride, lengths, page_table, pt_stride,
+                                          pp, s);
+  }
+  return launch_status();
+}
+
+extern "C" int hcu_cp_peer_merge(const int32_t* totals, int32_t exact, const hcu_cp_peers_t* peers,
+                                 hcu_stream_t stream) {
+  using namespace hcu;
+  if (check_peers(peers) != HCU_OK || !totals) return HCU_ERR_ARG;
+  const hcu_cp_peers_t& pp = *peers;
+  if (pp.rows_per_rank == 0) return HCU_OK;
+  const size_t smem = sizeof(TopkSmem<1024>);
+  cudaFuncSetAttribute(cp_peer_merge_kernel<1024>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       static_cast<int>(smem));
+  cp_peer_merge_kernel<1024><<<static_cast<unsigned>(pp.rows_per_rank), 1024, smem,
+                               reinterpret_cast<cudaStream_t>(stream)>>>(totals, exact ? 1 : 0, pp);
+  return launch_status();
+}
+
+extern "C" int hcu_cp_peer_scatter_exact(const uint32_t* keys, const int32_t* entries, const hcu_cp_peers_t* peers,
+                                         hcu_stream_t stream) {
+  using namespace hcu;
+  if (check_peers(peers) != HCU_OK || !keys || !entries) return HCU_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(keys) | reinterpret_cast<uintptr_t>(entries)) % 16 != 0) return HCU_ERR_ARG;
+  if (peers->rows == 0) return HCU_OK;
+  cp_peer_scatter_kernel<<<static_cast<unsigned>(peers->rows), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      keys, entries, *peers);
+  return launch_status();
+}
+
+extern "C" int hcu_cp_peer_finish(int32_t exact, const hcu_cp_peers_t* peers, hcu_stream_t stream) {
+  using namespace hcu;
+  if (check_peers(peers) != HCU_OK) return HCU_ERR_ARG;
+  cp_peer_finish_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(exact ? 1 : 0, *peers);
   return launch_status();
 }
 

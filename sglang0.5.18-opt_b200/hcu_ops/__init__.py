@@ -29,7 +29,8 @@ SGLANG_DSA_FAST_DEQUANT_PAGED = os.environ.get("SGLANG_DSA_FAST_DEQUANT_PAGED", 
 SGLANG_DSA_FAST_DEQUANT_TOKENS = int(os.environ.get("SGLANG_DSA_FAST_DEQUANT_TOKENS", "8"))
 SGLANG_DSA_FAST_DEQUANT_WARPS = int(os.environ.get("SGLANG_DSA_FAST_DEQUANT_WARPS", "4"))
 
-# split: few rows are spread over up to HCU_TOPK_SPLITS CTAs each; single: 1 CTA per row
+# HCU_TOPK_IMPL: "split" lets a long row be shared by a thread-block cluster of up to HCU_TOPK_SPLITS
+# CTAs when the batch leaves SMs idle; "single" keeps every row on one CTA.
 _TOPK_IMPL = os.environ.get("HCU_TOPK_IMPL", "split")
 _TOPK_SPLITS = int(os.environ.get("HCU_TOPK_SPLITS", "8"))
 

@@ -5,7 +5,7 @@ query row it scores only that range (ragged logits kernel), selects a local
 top-2048 of (uint32 key, global token index) in ascending token order, and the
 ranks exchange and merge those lists:
 
-* ``mode="rowshard"`` (default): an all-to-all hands rank r the P lists of its
+* ``mode="rowshard"`` (NCCL; the default with stand-in ops): an all-to-all hands rank r the P lists of its
   1/P share of the rows, rank r merges them, and an all-gather of the final
   int32 indices gives every rank the whole ``[rows, 2048]`` result.  Each rank
   receives ``(P-1)/P`` of one rank's lists instead of ``P-1`` whole lists.
@@ -23,6 +23,13 @@ ranks exchange and merge those lists:
   of the flag tells every rank, and the step then reruns with local top-2048
   lists (the exact path).
 * ``mode="allgather"``: every rank all-gathers all lists and merges all rows.
+* ``mode="peer"`` (default for the CUDA ops): the bounded exchange without NCCL.  Every rank's
+  exchange buffers are mapped into every other rank (symmetric memory over NVLink); the bound,
+  filter and merge kernels store their results straight into the consuming ranks' buffers and
+  publish per-step flags that the consumers wait for (``PeerExchange``; C ABI ``hcu_cp_peer_*``).
+  The exact redo is predicated on a device word that every rank computes identically, so a step
+  has no host synchronisation.  When symmetric memory cannot be set up the NCCL row-shard exchange
+  is used instead.
 
 The global top-2048 under (key desc, global index asc) is a subset of the union
 of the local ones, and the merge writes the single-GPU canonical order, so the
@@ -149,7 +156,156 @@ def list_len(world: int) -> int:
     return n
 
 
-def cp_prefill_topk(q, k_fp8_local, k_scale_local, weights, row_end, n_tokens, group=None, mode="rowshard",
+# --------------------------------------------------------------------------- peer-memory exchange
+_MAX_PARTS = 16  # HCU_CP_MAX_PARTS
+_WS_FLAG, _WS_RERUNS, _WS_WORDS = 8, 9, 16
+
+
+def _peer_layout(parts, rows, rps):
+    """int32 offsets of one rank's regions in its exchange allocation (256-byte aligned):
+    bounds [P, R] | lists [P, 2, rps, 2048] (also the redo's lists) | out [P * rps, 2048] | sig [5, P]."""
+    offs, n = {}, 0
+    for name, size in (("bounds", parts * rows), ("lists", parts * 2 * rps * TOPK), ("out", parts * rps * TOPK),
+                       ("sig", 5 * parts)):
+        offs[name] = n
+        n += (size + 63) // 64 * 64
+    return offs, n
+
+
+class PeerExchange:
+    """The exchange buffers of one rank and the kernels of one step (``hcu_cp_peer_*``).
+
+    ``bases``: the device address of every rank's exchange allocation as mapped in this process;
+    ``local``: this rank's allocation (int32 tensor); ``ws``: this rank's 16-word workspace.  Use
+    ``over_group`` (one rank per process, symmetric memory) or ``emulated`` (all ranks in one process
+    on one device, for tests: each phase must then be issued for every rank before the next phase).
+    The returned rows are a view of the exchange buffer, valid until the next step's merge."""
+
+    def __init__(self, parts, rank, rows, cap, bases, local, ws):
+        from . import _C
+
+        self._C = _C
+        self.parts, self.rank, self.rows, self.cap = parts, rank, rows, cap
+        self.rps = (rows + parts - 1) // parts
+        offs, _ = _peer_layout(parts, rows, self.rps)
+        self.local, self.ws = local, ws
+        self.epoch = 0
+        t = torch.zeros(7 + 5 * _MAX_PARTS, dtype=torch.int64)
+        t[0], t[1], t[2], t[3], t[4] = parts, rank, rows, self.rps, cap
+        t[6] = ws.data_ptr()
+        for i, name in enumerate(("bounds", "lists", "lists", "out", "sig")):
+            for p in range(parts):
+                t[7 + i * _MAX_PARTS + p] = bases[p] + 4 * offs[name]
+        self.peers = t
+        o = offs["out"]
+        self.out = local[o:o + parts * self.rps * TOPK].view(parts * self.rps, TOPK)
+
+    @staticmethod
+    def _zeroed(n, dev, alloc):
+        t = alloc(n)
+        t.zero_()
+        return t
+
+    @classmethod
+    def over_group(cls, group, rows, dev, cap):
+        import torch.distributed._symmetric_memory as symm
+
+        world = dist.get_world_size(group)
+        rank = dist.get_rank(group)
+        rps = (rows + world - 1) // world
+        _, n = _peer_layout(world, rows, rps)
+        local = symm.empty(n, dtype=torch.int32, device=dev)
+        local.zero_()
+        pg = group if group is not None else dist.group.WORLD
+        hdl = symm.rendezvous(local, pg)
+        bases = [hdl.get_remote_tensor(p, (n,), torch.int32).data_ptr() for p in range(world)]
+        bases[rank] = local.data_ptr()
+        ws = torch.zeros(_WS_WORDS, dtype=torch.int32, device=dev)
+        torch.cuda.synchronize(dev)
+        dist.barrier(group)  # every rank's buffers are zero before any rank's first flag
+        ex = cls(world, rank, rows, cap, bases, local, ws)
+        ex._hdl = hdl
+        return ex
+
+    @classmethod
+    def emulated(cls, parts, rows, dev, cap):
+        rps = (rows + parts - 1) // parts
+        _, n = _peer_layout(parts, rows, rps)
+        locals_ = [torch.zeros(n, dtype=torch.int32, device=dev) for _ in range(parts)]
+        bases = [t.data_ptr() for t in locals_]
+        return [cls(parts, r, rows, cap, bases, locals_[r], torch.zeros(_WS_WORDS, dtype=torch.int32, device=dev))
+                for r in range(parts)]
+
+    # ---- the phases of a step, in order
+    def begin(self):
+        self.epoch += 1
+        self.peers[5] = self.epoch
+
+    def bound(self, lg, mk, lens, vis):
+        self._C.cp_peer_bound(lg, mk, lens, vis, self.peers)
+
+    def filter(self, lg, mk, lens, gtab):
+        self._C.cp_peer_filter(lg, mk, lens, gtab, self.peers)
+
+    def mine(self, vis):
+        """This rank's rows' visible totals (rps entries, 0 past the batch)."""
+        m = vis[self.rank * self.rps:(self.rank + 1) * self.rps]
+        if m.numel() < self.rps:
+            m = torch.cat([m, torch.zeros(self.rps - m.numel(), dtype=vis.dtype, device=vis.device)])
+        return m.contiguous()
+
+    def merge(self, vis, exact=False):
+        self._C.cp_peer_merge(self.mine(vis), exact, self.peers)
+
+    def finish(self, exact=False):
+        self._C.cp_peer_finish(exact, self.peers)
+
+    def redo_lists(self, lg, mk, lens, gtab):
+        idx, keys = self._C.topk_keys_if(lg, mk, lens, gtab, self.ws[_WS_FLAG:_WS_FLAG + 1])
+        self._C.cp_peer_scatter_exact(keys, idx, self.peers)
+
+    def step(self, lg, mk, lens, gtab, vis):
+        """One whole step for this rank (one rank per process)."""
+        self.begin()
+        self.bound(lg, mk, lens, vis)
+        self.filter(lg, mk, lens, gtab)
+        self.merge(vis)
+        self.finish()
+        self.redo_lists(lg, mk, lens, gtab)  # the exact redo: does nothing unless the step was flagged
+        self.merge(vis, exact=True)
+        self.finish(exact=True)
+        return self.out[:self.rows]
+
+    def reruns(self):
+        """Exact redos so far (reads a device word: synchronises)."""
+        return int(self.ws[_WS_RERUNS].item())
+
+
+_PEER_CACHE = {}
+
+
+def _peer_exchange(group, rows, dev, world):
+    """The cached PeerExchange of (group, rows, device), or None when symmetric memory is unavailable
+    (decided identically on every rank: a MIN all-reduce of each rank's setup outcome)."""
+    key = (id(group), rows, str(dev), world, list_len(world))
+    if key in _PEER_CACHE:
+        return _PEER_CACHE[key]
+    ex, err = None, ""
+    try:
+        ex = PeerExchange.over_group(group, rows, dev, list_len(world))
+    except Exception as e:  # noqa: BLE001  (no symmetric memory on this system: the NCCL exchange is used)
+        err = f"{type(e).__name__}: {e}"
+    ok = torch.tensor([1 if ex is not None else 0], dtype=torch.int32, device=dev)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+    if int(ok.item()) == 0:
+        ex = None
+    _PEER_CACHE[key] = ex
+    if ex is None:
+        _PEER_CACHE[("error",) + key] = err
+    return ex
+
+
+def cp_prefill_topk(q, k_fp8_local, k_scale_local, weights, row_end, n_tokens, group=None, mode=None,
                     ops=None, bounded=True, causal_rows=0, stats=None):
     """Global top-2048 token indices of every query row, computed over P KV ranges.
 
@@ -161,6 +317,8 @@ def cp_prefill_topk(q, k_fp8_local, k_scale_local, weights, row_end, n_tokens, g
     names the exchange used.
     """
     stats = {} if stats is None else stats
+    if mode is None:
+        mode = "peer" if ops is None else "rowshard"
     ops = ops or CudaOps()
     world = dist.get_world_size(group) if dist.is_initialized() else 1
     rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -178,6 +336,15 @@ def cp_prefill_topk(q, k_fp8_local, k_scale_local, weights, row_end, n_tokens, g
         return ops.topk(lg, mk, lens, gtab)
     vis = row_end.clamp(max=n_tokens).to(torch.int32)
     rps = (rows + world - 1) // world  # row-sharded exchange: rank d merges rows [d*rps, (d+1)*rps)
+    if mode == "peer":
+        ex = _peer_exchange(group, rows, dev, world)
+        if ex is not None:
+            stats["exchange"] = ("peer memory: bounds, bounded lists and merged rows stored by the kernels into "
+                                 "the consuming ranks' buffers over NVLink; exact redo predicated on the device")
+            stats["peer_exchange"] = ex
+            return ex.step(lg, mk, lens, gtab, vis)
+        stats["peer_unavailable"] = _PEER_CACHE.get(("error", id(group), rows, str(dev), world, list_len(world)), "")
+        mode = "rowshard"
     if mode == "rowshard" and bounded:
         out = _bounded_rowshard(ops, lg, mk, lens, gtab, vis, rows, rps, world, rank, group)
         if out is not None:

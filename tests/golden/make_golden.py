@@ -167,7 +167,9 @@ def dequant_case(ref):
 
 
 if __name__ == "__main__":
-    ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    if len(sys.argv) != 2:
+        sys.exit("usage: python make_golden.py <path of the reference checkout>")
+    ref = sys.argv[1]
     print("topk cases", topk_cases(ref))
     print("hist cases", hist_cases(ref))
     print("dequant tokens", dequant_case(ref))

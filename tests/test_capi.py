@@ -134,3 +134,44 @@ def test_rope_qout_kv_store_argument_checks(lib):
     assert call(n_loc=5) == HCU_ERR_ARG          # more slots than tokens
     assert call(slot_stride=648) == HCU_ERR_ARG  # slots shorter than 656 bytes
     assert call(T=0, n_loc=0) == HCU_OK          # nothing to do
+
+
+class CpPeers(ctypes.Structure):
+    """hcu_cp_peers_t (HCU_CP_MAX_PARTS = 16)."""
+    _fields_ = [("parts", ctypes.c_int32), ("rank", ctypes.c_int32), ("rows", ctypes.c_int32),
+                ("rows_per_rank", ctypes.c_int32), ("list_len", ctypes.c_int32), ("epoch", ctypes.c_uint32),
+                ("ws", ctypes.c_void_p), ("bounds", ctypes.c_void_p * 16), ("lists", ctypes.c_void_p * 16),
+                ("lists_exact", ctypes.c_void_p * 16), ("out", ctypes.c_void_p * 16), ("sig", ctypes.c_void_p * 16)]
+
+
+def test_cp_peer_exchange_argument_checks(lib):
+    """The peer-memory exchange refuses a missing or inconsistent description before any launch."""
+    fn = lib.hcu_cp_peer_finish
+    fn.argtypes = [ctypes.c_int32, ctypes.POINTER(CpPeers), ctypes.c_void_p]
+    assert fn(0, None, None) == HCU_ERR_ARG
+    fake = 1 << 20  # never dereferenced: every call below is refused by its checks
+
+    def peers(**kw):
+        p = CpPeers(parts=2, rank=0, rows=10, rows_per_rank=5, list_len=1024, epoch=1, ws=fake)
+        for i in range(2):
+            p.bounds[i] = p.lists[i] = p.lists_exact[i] = p.out[i] = p.sig[i] = fake
+        for k, v in kw.items():
+            setattr(p, k, v)
+        return p
+
+    bad = [dict(parts=0), dict(parts=17), dict(rank=2), dict(rows_per_rank=4), dict(list_len=1000),
+           dict(list_len=512), dict(epoch=0), dict(ws=None)]
+    for b in bad:
+        p = peers(**b)
+        assert fn(0, ctypes.byref(p), None) == HCU_ERR_ARG, b
+    p = peers()
+    p.sig[1] = None
+    assert fn(0, ctypes.byref(p), None) == HCU_ERR_ARG
+    merge = lib.hcu_cp_peer_merge
+    merge.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.POINTER(CpPeers), ctypes.c_void_p]
+    assert merge(None, 0, ctypes.byref(peers()), None) == HCU_ERR_ARG  # no totals
+
+
+def test_wait_limit_entry_point_is_exported(lib):
+    lib.hcu_set_wait_limit_ns.argtypes = [ctypes.c_uint64]
+    assert hasattr(lib, "hcu_set_wait_limit_ns")

@@ -228,3 +228,40 @@ def test_config4_cp_prefill_one_gpu(hcu, dev):
     assert torch.equal(got, one)
     got, _ = _cp_emulated(hcu, d, rows, N, 8, bounded=False)
     assert torch.equal(got, one)
+    # P = 8 through the peer-memory exchange (emulated ranks on one device): every rank holds every row
+    outs, reruns = _cp_peer_emulated(hcu, d, rows, N, 8)
+    assert reruns == 0
+    for o in outs:
+        assert torch.equal(o, one)
+
+
+def _cp_peer_emulated(hcu, d, rows, N, parts):
+    from hcu_ops.cp import PeerExchange, kv_range, list_len, local_rows
+
+    vis = d["row_end"]
+    locs = []
+    for p in range(parts):
+        lo, hi = kv_range(p, parts, N, causal_rows=rows)
+        lens = local_rows(vis, lo, hi)
+        lg, mk = hcu.mqa_logits_ragged(d["q"], d["k_fp8"][lo:hi].contiguous(), d["k_scale"][lo:hi].contiguous(),
+                                       d["weights"], torch.zeros_like(lens), lens)
+        gtab = (torch.arange(hi - lo, dtype=torch.int32, device=vis.device) + lo).expand(rows, hi - lo)
+        locs.append((lg, mk, lens, gtab))
+    exs = PeerExchange.emulated(parts, rows, vis.device, list_len(parts))
+    for ex in exs:
+        ex.begin()
+    for ex, (lg, mk, lens, _) in zip(exs, locs):
+        ex.bound(lg, mk, lens, vis)
+    for ex, (lg, mk, lens, gt) in zip(exs, locs):
+        ex.filter(lg, mk, lens, gt)
+    for ex in exs:
+        ex.merge(vis)
+    for ex in exs:
+        ex.finish()
+    for ex, loc in zip(exs, locs):
+        ex.redo_lists(*loc)
+    for ex in exs:
+        ex.merge(vis, exact=True)
+    for ex in exs:
+        ex.finish(exact=True)
+    return [ex.out[:rows] for ex in exs], exs[0].reruns()

@@ -160,3 +160,103 @@ def test_cp_merge_lists_flags_a_missed_bound(hcu, dev):
     assert hcu.read_device_status(clear=False) == 0
     assert np.array_equal(out[1], np.where(np.arange(2048) < 100, np.arange(2048), -1))
     assert np.array_equal(out[2], np.arange(2048))
+
+
+def _peer_on_one_gpu(hcu, dev, x, mask, vis, parts, cap, steps=2):
+    """The peer-memory exchange with `parts` emulated ranks on one device: every phase is issued for
+    all ranks before the next phase (so every wait is already satisfied when its kernel starts).
+    Returns (every rank's rows after the last step, redo count of rank 0)."""
+    from hcu_ops.cp import PeerExchange
+
+    rows, N = x.shape
+    xd, md, visd = x.to(dev), mask.to(dev), vis.to(dev)
+    locs = [_local(xd, md, vis, a, b, dev) for a, b in _ranges(N, parts)]
+    exs = PeerExchange.emulated(parts, rows, dev, cap)
+    for _ in range(steps):
+        for ex in exs:
+            ex.begin()
+        for ex, (sx, sm, lens, _) in zip(exs, locs):
+            ex.bound(sx, sm, lens, visd)
+        for ex, (sx, sm, lens, pt) in zip(exs, locs):
+            ex.filter(sx, sm, lens, pt)
+        for ex in exs:
+            ex.merge(visd)
+        for ex in exs:
+            ex.finish()
+        for ex, loc in zip(exs, locs):
+            ex.redo_lists(*loc)
+        for ex in exs:
+            ex.merge(visd, exact=True)
+        for ex in exs:
+            ex.finish(exact=True)
+    return [ex.out[:rows].cpu().numpy() for ex in exs], exs[0].reruns()
+
+
+@pytest.mark.parametrize("parts,cap", [(2, 2048), (4, 2048), (8, 1024)])
+@pytest.mark.parametrize("dist", ["relu_sum", "ties"])
+def test_cp_peer_exchange_on_one_gpu(hcu, dev, parts, cap, dist):
+    """Bounds, lists and merged rows stored into the emulated ranks' buffers with per-step flags:
+    every rank ends with the single-range top-k of every row, over two steps (the flags of the second
+    step carry the next step number).  With 2048-slot lists no redo is needed; with 1024-slot lists
+    (P = 8) row 4 (6001 tokens, ~1400 of its top-2048 in range 0) overflows its list and the step is
+    redone exactly on the device."""
+    rows, N = 13, 32768
+    x, mask, _, _ = make_scores(rows, N, dist, W=N, seed=parts + 200)
+    vis = torch.tensor([N, 30000, 2048, 100, 6001, 2049, 1, 12000, 20000, 4097, 8191, 0, 25000], dtype=torch.int32)
+    full = O.topk_transform(x.numpy(), mask.numpy(), vis.numpy(), torch.arange(N, dtype=torch.int32).repeat(rows, 1)
+                            .numpy())
+    outs, reruns = _peer_on_one_gpu(hcu, dev, x, mask, vis, parts, cap)
+    assert reruns == (0 if cap == 2048 else 2)
+    for r, o in enumerate(outs):
+        assert np.array_equal(o, full), r
+
+
+def test_cp_peer_exchange_exact_redo(hcu, dev):
+    """A row that one range holds almost entirely overflows that range's 1024-slot list; its marker
+    is not below the row's threshold, the merge flags the step and every rank redoes it with local
+    top-2048 lists on the device (no host read): the result is still exact, and the redo counted."""
+    rows, N, parts = 12, 65536, 8
+    x, mask, _, _ = make_scores(rows, N, "relu_sum", W=N, seed=7)
+    vis = torch.tensor([N, 60000, 50000, 7000, 65000, 33000, 64000, 58000, 45000, 38000, 62000, 36000],
+                       dtype=torch.int32)
+    full = O.topk_transform(x.numpy(), mask.numpy(), vis.numpy(), torch.arange(N, dtype=torch.int32).repeat(rows, 1)
+                            .numpy())
+    outs, reruns = _peer_on_one_gpu(hcu, dev, x, mask, vis, parts, 1024, steps=2)
+    assert reruns == 2
+    for r, o in enumerate(outs):
+        assert np.array_equal(o, full), r
+
+
+def test_cp_peer_wait_expires_and_device_stays_usable(hcu, dev, request):
+    """Failure detection without a fault: with the wait limit set to 1 ms, a finish kernel waits for
+    flags that no rank ever sets.  It gives up, records HCU_STATUS_WAIT_TIMEOUT and flags the step,
+    the launch returns, and the next exchange on the same device is exact with a clean status."""
+    import time
+
+    from hcu_ops.cp import PeerExchange
+
+    request.node.allowed_status = 1
+    exs = PeerExchange.emulated(2, 64, dev, 2048)
+    hcu._C.set_wait_limit_ns(1_000_000)
+    try:
+        exs[0].begin()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        exs[0].finish()  # rank 1 never merges: its flag for this step never arrives
+        torch.cuda.synchronize()
+        dt = time.perf_counter() - t0
+        st = hcu.read_device_status(clear=True)
+    finally:
+        hcu._C.set_wait_limit_ns(0)
+    assert st == 1, st
+    assert int(exs[0].ws[8].item()) == 1
+    assert dt < 0.5, dt
+    rows, N = 9, 20000
+    x, mask, _, _ = make_scores(rows, N, "mixed", W=N, seed=3)
+    vis = torch.tensor([N, 15000, 2048, 100, 6001, 2049, 1, 12000, 20000], dtype=torch.int32)
+    full = O.topk_transform(x.numpy(), mask.numpy(), vis.numpy(), torch.arange(N, dtype=torch.int32).repeat(rows, 1)
+                            .numpy())
+    outs, _ = _peer_on_one_gpu(hcu, dev, x, mask, vis, 2, 2048, steps=1)
+    for o in outs:
+        assert np.array_equal(o, full)
+    assert hcu.read_device_status(clear=True) == 0
