@@ -208,6 +208,11 @@ class PeerExchange:
 
     @classmethod
     def over_group(cls, group, rows, dev, cap):
+        import os
+
+        # The kernels use plain peer loads and stores only: keep the allocation off NVLink multicast
+        # objects (no multimem here, and a rank leaving while bound to one disturbs the others).
+        os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
         import torch.distributed._symmetric_memory as symm
 
         world = dist.get_world_size(group)
