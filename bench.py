@@ -767,12 +767,25 @@ def sec_prefill(args, local):
         logits()
         return topk()
 
+    flag = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def fused():
+        return hcu_ops.mqa_topk_ragged(w["q"], w["k_fp8"], w["k_scale"], w["weights"], lens, ident, fallback_flag=flag)
+
     for _ in range(3):
-        step()
+        ref = step()
+        got = fused()
+    fused_equal = bool(torch.equal(got, ref))
+    del ref, got
     iters = max(3, min(args.steps, 10))
-    ms, clocks = _timed(step, iters, local)
+    ms_pair, _ = _timed(step, iters, local)
     ms_lg, _ = _timed(logits, iters, local)
     ms_tk, _ = _timed(topk, iters, local)
+    state.clear()
+    torch.cuda.empty_cache()
+    ms_fused, clocks = _timed(fused, iters, local)
+    fell_back = int(flag.item())
+    ms = min(ms_pair, ms_fused)  # the record's value: the faster of the two public paths
     pairs = int((lens.long() - w["row_start"].long()).sum())
     flops = 2.0 * 64 * 128 * pairs
     hbm, bf16, src = _peaks()
@@ -781,8 +794,16 @@ def sec_prefill(args, local):
     shape = "config2" if not args.prefill_shape else "reduced shape (profiling)"
     rec = _rec("prefill indexer G-scores/s (rows x visible KV tokens / s), logits + top-2048",
                pairs / (ms * 1e-3) / 1e9, "G-scores/s", ms, iters,
-               f"{shape}: prefill chunk {rows} rows x ({p_prefix} + i + 1) tokens, 64 heads; logits "
-               f"{rows * N * 4 / 1e9:.1f} GB > L2, no flush", pairs=pairs)
+               f"{shape}: prefill chunk {rows} rows x ({p_prefix} + i + 1) tokens, 64 heads; the faster of "
+               f"the materialised pair and the fused hcu_ops.mqa_topk_ragged; inputs > L2, no flush", pairs=pairs)
+    rec["path"] = "fused" if ms_fused <= ms_pair else "materialised_pair"
+    rec["fused"] = {"ms": ms_fused, "value": pairs / (ms_fused * 1e-3) / 1e9,
+                    "equals_materialised_pair": fused_equal, "exact_path_ran": fell_back,
+                    "how": "sampled bound (1/64 of K) -> logits appending tokens at or above it to per-row "
+                           "lists -> select; exact materialising path predicated on a device flag"}
+    rec["materialised_pair"] = {"ms": ms_pair, "value": pairs / (ms_pair * 1e-3) / 1e9,
+                                "logits_bytes": rows * N * 4,
+                                "how": "mqa_logits_ragged (logits + mask in HBM) -> sparse_mask_topk_transform"}
     rec["logits_op_ms"] = ms_lg
     rec["topk_op_ms"] = ms_tk
     rec["top_k_rows_per_s"] = rows / (ms_tk * 1e-3)
@@ -792,7 +813,7 @@ def sec_prefill(args, local):
     rec["roofline"] = {"bound": "tensor", "achieved": tflops, "peak": fp8_peak, "unit": "TFLOP/s",
                        "frac": tflops / fp8_peak, "traffic": None, "kernel": "mqa_logits_ragged_kernel<64>",
                        "flops_per_launch": flops, "peak_source": src + " (fp8 dense = 2 x measured bf16 burst)"}
-    rec["gpu_launches"] = iters * 3
+    rec["gpu_launches"] = iters * 7  # fused: prep, sampled logits, bound, logits, select, two predicated
     rec["clocks"] = clocks
     if not args.no_cpu_baseline and not args.prefill_shape:
         v, sample = _ragged_cpu_sample(p_rows, p_prefix)

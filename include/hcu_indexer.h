@@ -177,6 +177,29 @@ int hcu_mqa_logits_ragged(const uint8_t* q, int64_t rows, int64_t heads, const u
                           const int32_t* row_start, const int32_t* row_end, float* logits,
                           int64_t logits_stride, int16_t* mask, hcu_stream_t stream);
 
+/* Fused prefill indexer (new; no counterpart in the reference, whose prefill
+ * indexer is the closed lightop _mqa_logits followed by the materialised
+ * top-k): the result of hcu_mqa_logits_ragged (row_start = 0) followed by
+ * hcu_sparse_mask_topk_transform (lengths = row_end), without writing the
+ * logits.  A sampled pass estimates each row's top-2048 threshold, the full
+ * pass appends the tokens at or above it to per-row lists, and a select writes
+ * their top-2048 in the canonical order; rows whose list cannot prove
+ * exactness raise a device flag and are recomputed by the materialising pair,
+ * predicated on that flag (no host synchronisation).
+ *   q       fp8 [rows, heads, 128]; weights fp32 [rows, heads]
+ *   k_fp8   fp8 [n_tokens, 128]; k_scale fp32 [n_tokens]; n_tokens <= 131072
+ *   row_end int32 [rows]: row r sees tokens [0, row_end[r])
+ *   page_table int32 [rows, >= n_tokens] row stride pt_stride (0: one row for all)
+ *   dst     int32 [rows, 2048]
+ *   workspace >= hcu_mqa_topk_ragged_workspace_bytes(rows, n_tokens), 16-byte aligned
+ *   fallback_flag (nullable) int32 [1]: 1 when the exact path ran. */
+int64_t hcu_mqa_topk_ragged_workspace_bytes(int64_t rows, int64_t n_tokens);
+int hcu_mqa_topk_ragged(const uint8_t* q, int64_t rows, int64_t heads, const uint8_t* k_fp8,
+                        const float* k_scale, int64_t n_tokens, const float* weights,
+                        const int32_t* row_end, const int32_t* page_table, int64_t pt_stride,
+                        int32_t* dst, void* workspace, int64_t workspace_bytes, int32_t* fallback_flag,
+                        hcu_stream_t stream);
+
 /* ------------------------------------------------------------------------
  * Stage 3: exact top-2048 + page-table transform
  * ------------------------------------------------------------------------ */

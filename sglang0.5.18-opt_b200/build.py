@@ -24,7 +24,7 @@ INCLUDE = os.path.join(REPO, "include")
 CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 NVCC = os.path.join(CUDA_HOME, "bin", "nvcc")
 
-CU_SOURCES = ["capi.cu", "dequant.cu", "topk.cu", "logits.cu", "mla_kv.cu"]
+CU_SOURCES = ["capi.cu", "dequant.cu", "topk.cu", "logits.cu", "mla_kv.cu", "fused.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
               "-Xptxas", "-v"] + ARCH

@@ -213,6 +213,49 @@ std::vector<torch::Tensor> mqa_logits_ragged(const torch::Tensor& q, const torch
   return {logits.narrow(1, 0, N), mask.narrow(1, 0, (N + 15) / 16)};
 }
 
+// Fused prefill logits -> top-2048 (hcu_mqa_topk_ragged); fallback_flag (optional int32 [1]) is set
+// to 1 when the exact path ran.
+torch::Tensor mqa_topk_ragged(const torch::Tensor& q, const torch::Tensor& k_fp8, const torch::Tensor& k_scale,
+                              const torch::Tensor& weights, const torch::Tensor& row_end,
+                              const torch::Tensor& page_table, const c10::optional<torch::Tensor>& fallback_flag) {
+  TORCH_CHECK(q.is_cuda() && q.scalar_type() == at::kFloat8_e4m3fn && q.dim() == 3 &&
+                  (q.size(1) == 32 || q.size(1) == 64) && q.size(2) == 128 && q.is_contiguous(),
+              "q must be contiguous fp8 e4m3fn [rows, 32|64, 128]");
+  const int64_t R = q.size(0);
+  const int64_t H = q.size(1);
+  TORCH_CHECK(k_fp8.scalar_type() == at::kFloat8_e4m3fn && k_fp8.dim() == 2 && k_fp8.size(1) == 128 &&
+                  k_fp8.is_contiguous(),
+              "k_fp8 must be contiguous fp8 e4m3fn [tokens, 128]");
+  const int64_t N = k_fp8.size(0);
+  TORCH_CHECK(N <= 131072, "mqa_topk_ragged supports at most 131072 tokens");
+  TORCH_CHECK(k_scale.scalar_type() == at::kFloat && k_scale.numel() == N && k_scale.is_contiguous(),
+              "k_scale must be contiguous float32 [tokens]");
+  TORCH_CHECK(weights.scalar_type() == at::kFloat && weights.dim() == 2 && weights.size(0) == R &&
+                  weights.size(1) == H && weights.is_contiguous(),
+              "weights must be contiguous float32 [rows, heads]");
+  TORCH_CHECK(row_end.scalar_type() == at::kInt && row_end.numel() == R && row_end.is_contiguous(),
+              "row_end must be contiguous int32 [rows]");
+  TORCH_CHECK(page_table.scalar_type() == at::kInt && page_table.dim() == 2 && page_table.size(0) == R &&
+                  page_table.size(1) >= N && page_table.stride(1) == 1,
+              "page_table must be int32 [rows, >= tokens] with unit last stride");
+  if (fallback_flag.has_value())
+    TORCH_CHECK(fallback_flag->scalar_type() == at::kInt && fallback_flag->numel() >= 1 && fallback_flag->is_cuda(),
+                "fallback_flag must be a CUDA int32 tensor of at least one element");
+  const c10::cuda::CUDAGuard guard(q.device());
+  auto out = torch::empty({R, kTopK}, q.options().dtype(at::kInt));
+  if (R == 0) return out;
+  const int64_t wsb = hcu_mqa_topk_ragged_workspace_bytes(R, N);
+  auto ws = torch::empty({wsb}, q.options().dtype(at::kByte));
+  check_status(hcu_mqa_topk_ragged(ptr<const uint8_t>(q), R, H, ptr<const uint8_t>(k_fp8), ptr<const float>(k_scale), N,
+                                   ptr<const float>(weights), ptr<const int32_t>(row_end),
+                                   ptr<const int32_t>(page_table), page_table.stride(0), ptr<int32_t>(out),
+                                   ws.data_ptr(), wsb,
+                                   fallback_flag.has_value() ? fallback_flag->data_ptr<int32_t>() : nullptr,
+                                   cur_stream()),
+               "mqa_topk_ragged");
+  return out;
+}
+
 torch::Tensor dequantize_k_cache_paged(const torch::Tensor& quant_k_cache, const torch::Tensor& page_table_1) {
   TORCH_CHECK(quant_k_cache.is_cuda() && quant_k_cache.element_size() == 1 && quant_k_cache.size(-1) == 656 &&
                   quant_k_cache.stride(-1) == 1,
@@ -524,6 +567,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("cp_topk_merge_lists", &cp_topk_merge_lists, "context-parallel: merge of the exchanged bounded lists");
   m.def("mqa_logits_ragged", &mqa_logits_ragged,
         "prefill fp8 indexer logits over a contiguous K with per-row [start, end) -> {logits, mask}");
+  m.def("mqa_topk_ragged", &mqa_topk_ragged,
+        "fused prefill indexer: ragged logits (rows from token 0) -> exact top-2048 through the page table, "
+        "without materialising the logits",
+        py::arg("q"), py::arg("k_fp8"), py::arg("k_scale"), py::arg("weights"), py::arg("row_end"),
+        py::arg("page_table"), py::arg("fallback_flag") = py::none());
   m.def("topk_keys", &topk_keys, "top-2048 indices through a page table plus the selected uint32 keys");
   m.def("dequantize_k_cache_paged", &dequantize_k_cache_paged,
         "MLA 656-byte slot paged dequant -> bf16 [n, 1, 576] (sglang dequantize_k_cache_paged drop-in)");

@@ -235,6 +235,16 @@ __device__ __forceinline__ void relu_fma2(float2& acc, uint32_t x0, uint32_t x1,
       : "f"(__uint_as_float(x0)), "f"(__uint_as_float(x1)), "f"(w0), "f"(w1));
 }
 
+// The same step with the compiler's packed-FMA intrinsic: relu(x) * 2^-25 as a
+// saturating multiply (exact scaling; the saturation clamps negatives, -0 and
+// NaN to +0 and never reaches 1 since |x| < 2^25), then one fma.rn.f32x2 with
+// the pre-scaled weight pair.  Bit-identical to relu_fma2; the register pairs are
+// left to the compiler.
+__device__ __forceinline__ void relu_fma2_pk(float2& acc, uint32_t x0, uint32_t x1, float2 w) {
+  const float2 r = make_float2(__saturatef(__uint_as_float(x0) * 0x1p-25f), __saturatef(__uint_as_float(x1) * 0x1p-25f));
+  acc = __ffma2_rn(r, w, acc);
+}
+
 // The same sum with the ReLU split over two pipes: lane x0 through the
 // saturating FMA (its weight w0 pre-scaled by 2^25), lane x1 through max.f32 on
 // the ALU pipe (w1 unscaled; max returns 0 for a NaN x1, like fmaxf).  Both

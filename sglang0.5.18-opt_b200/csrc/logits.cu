@@ -573,6 +573,7 @@ constexpr int kQB = 4;
 constexpr int kPfEpiWarps = 16;  // warps 2..17: kPfTeams per TMEM lane quadrant
 constexpr int kPfTeams = kPfEpiWarps / 4;  // warp t of a quadrant takes rows r % kPfTeams == t of every row block
 constexpr int kPfThreads = (2 + kPfEpiWarps) * 32;
+constexpr int kCandFifo = 64;  // kCand: staged candidates per epilogue warp
 
 struct __align__(1024) PfSmem {
   uint8_t q[kQB][kQTile];
@@ -580,8 +581,10 @@ struct __align__(1024) PfSmem {
   float w[kPfEpiWarps][kQB * kMaxN / kPfTeams];  // weights of the rows this epilogue warp owns
   int rs[kPfEpiWarps][16];          // first visible token of each owned row
   int re[kPfEpiWarps][16];          // visible length of each owned row
-  float* lrow[kPfEpiWarps][16];     // logits row of each owned row (super-block)
-  uint32_t* mrow[kPfEpiWarps][16];  // mask row (as 32-bit words) of each owned row
+  float* lrow[kPfEpiWarps][16];     // logits row of each owned row (super-block); kCand: its list
+  uint32_t* mrow[kPfEpiWarps][16];  // mask row (as 32-bit words) of each owned row; kCand: its count
+  uint32_t lo[kPfEpiWarps][16];     // kCand: the owned rows' bounds as keys
+  int2 cfifo[kPfEpiWarps][kCandFifo];  // kCand: each warp's staged candidates
   uint64_t full[kPfStages];
   uint64_t empty[kPfStages];
   uint64_t qfull;
@@ -606,7 +609,65 @@ struct RaggedArgs {
   int64_t stride;  // logits row stride (elements), multiple of 64
   int rows;
   int n_tokens;
+  // kCand (the fused prefill top-k): instead of logits and mask, every visible token whose key is
+  // at or above the row's bound is appended as (key, token) to the row's list cand[row * cand_cap ..]
+  // (cand_cnt[row] counts all of them, also past cand_cap); rows of at most cand_all_len visible
+  // tokens take every visible token.
+  const int32_t* bounds;  // order-preserving int32 (key ^ 0x80000000)
+  int32_t* cand_cnt;
+  int2* cand;
+  int cand_cap;
+  int cand_all_len;
+  const int32_t* run_if;  // non-null: the launch does nothing while *run_if == 0
 };
+
+// kCand staging: each epilogue warp collects its candidates (key, token | owned-row slot << 24) in a
+// private shared-memory FIFO of kCandFifo entries and moves them to the rows' global lists when a
+// warp-row's entries would not fit (and before its owned rows change): one reservation atomic per
+// owned row with entries, issued together, per flush, instead of one per warp-row.
+
+// Flush of one warp's FIFO (every lane calls it).  Entries e with owned-row slot s (< NS) go to
+// list(s)[base_s + rank of e among the slot's entries], base_s reserved from count(s).
+template <int NS>
+__device__ __forceinline__ void cand_flush(int2* fifo, int fill, float* const* lrow, uint32_t* const* mrow, int cap,
+                                           int lane) {
+  if (fill == 0) return;
+  int2 e[2];
+  int sl[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int i = lane + 32 * h;
+    e[h] = i < fill ? fifo[i] : make_int2(0, -1);
+    sl[h] = i < fill ? (e[h].y >> 24) : -1;
+  }
+  uint32_t m[2][NS];
+  int n_s = 0;  // lane s < NS: entries of slot s
+#pragma unroll
+  for (int s = 0; s < NS; ++s) {
+    m[0][s] = __ballot_sync(0xffffffffu, sl[0] == s);
+    m[1][s] = __ballot_sync(0xffffffffu, sl[1] == s);
+    if (lane == s) n_s = __popc(m[0][s]) + __popc(m[1][s]);
+  }
+  int base = 0;
+  if (lane < NS && n_s > 0) base = atomicAdd(reinterpret_cast<int*>(mrow[lane]), n_s);
+  const uint32_t lt = (1u << lane) - 1u;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    int pre0 = 0, pre1 = 0;  // entries of this entry's slot in half 0, and below this lane in its half
+#pragma unroll
+    for (int q = 0; q < NS; ++q)
+      if (q == sl[h]) {
+        pre0 = __popc(m[0][q] & (h ? 0xffffffffu : lt));
+        pre1 = h ? __popc(m[1][q] & lt) : 0;
+      }
+    const int b = __shfl_sync(0xffffffffu, base, sl[h] < 0 ? 0 : sl[h]);
+    if (sl[h] >= 0) {
+      const int pos = b + pre0 + pre1;
+      if (pos < cap) reinterpret_cast<int2*>(lrow[sl[h]])[pos] = make_int2(e[h].x, e[h].y & 0xFFFFFF);
+    }
+  }
+  __syncwarp();
+}
 
 template <int H>
 __device__ __forceinline__ void sb_tiles(const RaggedArgs& p, int sb, int& t0, int& tiles) {
@@ -649,12 +710,13 @@ struct RCursor {
   }
 };
 
-template <int H, bool kMixed>
+template <int H, bool kMixed, bool kCand>
 __global__ __launch_bounds__(kPfThreads, 1) void mqa_logits_ragged_kernel(const __grid_constant__ CUtensorMap tm_k,
                                                                          const __grid_constant__ CUtensorMap tm_q,
                                                                          const RaggedArgs p) {
   constexpr int RB = kMaxN / H;  // rows per row block (N = 256)
   constexpr int SBR = kQB * RB;  // rows per super-block
+  if (p.run_if != nullptr && __ldcg(p.run_if) == 0) return;  // grid-uniform, before any barrier or TMEM use
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   PfSmem& sm = smem_aligned_1024<PfSmem>(smem_raw);
   const int warp = threadIdx.x >> 5;
@@ -816,12 +878,17 @@ __global__ __launch_bounds__(kPfThreads, 1) void mqa_logits_ragged_kernel(const 
     cur.init(p, sm.start_sb, sm.start_local);
     int qsb = -1, nrb = 0, u = 0;
     bool ok = true;
+    int cfill = 0;  // kCand: entries in this warp's FIFO
     for (int it = 0; it < count && ok; ++it) {
       const int tile = cur.next(p);
       const int row0 = cur.sb * SBR;
       if (cur.sb != qsb) {
         qsb = cur.sb;
         nrb = min(kQB, (p.rows - row0 + RB - 1) / RB);
+        if constexpr (kCand) {  // before the owned rows change
+          cand_flush<kQB * RPW>(sm.cfifo[ew], cfill, sm.lrow[ew], sm.mrow[ew], p.cand_cap, lane);
+          cfill = 0;
+        }
         __syncwarp();
         for (int lr = 0; lr < kQB * RPW; ++lr) {
           const int row = row0 + (lr / RPW) * RB + (lr % RPW) * kPfTeams + rsel;
@@ -835,8 +902,17 @@ __global__ __launch_bounds__(kPfThreads, 1) void mqa_logits_ragged_kernel(const 
             const int e0 = in ? min(__ldg(p.re + row), p.n_tokens) : 0;
             rs[lr] = a0;
             re[lr] = e0 > a0 ? e0 - a0 : 0;  // visible length: token is visible iff (unsigned)(token - rs) < len
-            sm.lrow[ew][lr] = p.logits + static_cast<int64_t>(in ? row : 0) * p.stride;
-            sm.mrow[ew][lr] = reinterpret_cast<uint32_t*>(p.mask) + static_cast<int64_t>(in ? row : 0) * (p.stride / 32);
+            if constexpr (kCand) {
+              // the row's list and count in place of its logits and mask rows; its bound as a key
+              const int64_t r = in ? row : 0;
+              sm.lrow[ew][lr] = reinterpret_cast<float*>(p.cand + r * p.cand_cap);
+              sm.mrow[ew][lr] = reinterpret_cast<uint32_t*>(p.cand_cnt + r);
+              sm.lo[ew][lr] = !in ? 0xFFFFFFFFu
+                                  : (re[lr] <= p.cand_all_len ? 0u : static_cast<uint32_t>(__ldg(p.bounds + row)) ^ kZeroKey);
+            } else {
+              sm.lrow[ew][lr] = p.logits + static_cast<int64_t>(in ? row : 0) * p.stride;
+              sm.mrow[ew][lr] = reinterpret_cast<uint32_t*>(p.mask) + static_cast<int64_t>(in ? row : 0) * (p.stride / 32);
+            }
           }
         }
         __syncwarp();
@@ -877,26 +953,45 @@ __global__ __launch_bounds__(kPfThreads, 1) void mqa_logits_ragged_kernel(const 
                 relu_fma2_mixed(acc2, x[4], x[5], wb.x, wb.y);
                 relu_fma2_mixed(acc3, x[6], x[7], wb.z, wb.w);
               } else {
-                relu_fma2(acc0, x[0], x[1], wa.x, wa.y);
-                relu_fma2(acc1, x[2], x[3], wa.z, wa.w);
-                relu_fma2(acc2, x[4], x[5], wb.x, wb.y);
-                relu_fma2(acc3, x[6], x[7], wb.z, wb.w);
+                relu_fma2_pk(acc0, x[0], x[1], make_float2(wa.x, wa.y));
+                relu_fma2_pk(acc1, x[2], x[3], make_float2(wa.z, wa.w));
+                relu_fma2_pk(acc2, x[4], x[5], make_float2(wb.x, wb.y));
+                relu_fma2_pk(acc3, x[6], x[7], make_float2(wb.z, wb.w));
               }
             }
           }
           float s0 = ((acc0.x + acc0.y) + (acc1.x + acc1.y)) + ((acc2.x + acc2.y) + (acc3.x + acc3.y));
           s0 *= ksc;
-          const bool keep = static_cast<uint32_t>(token - rs[lr]) < static_cast<uint32_t>(re[lr]) &&
-                            __float_as_uint(s0) != 0u;
-          const uint32_t bits = __ballot_sync(0xffffffffu, keep);
-          st_u32_if(sm.mrow[ew][lr] + mword, bits, mstore);
-          st_f32_if(sm.lrow[ew][lr] + token, s0, keep);
+          if constexpr (kCand) {
+            // key of a visible token: to_key(+0) is the +0 key an unset mask bit stands for, so the
+            // keys equal those the top-k derives from the logits and mask
+            const uint32_t key = to_key(s0);
+            const bool c = static_cast<uint32_t>(token - rs[lr]) < static_cast<uint32_t>(re[lr]) && key >= sm.lo[ew][lr];
+            const uint32_t bal = __ballot_sync(0xffffffffu, c);
+            if (bal) {  // into this warp's FIFO (flushed first when the row's entries might not fit)
+              const int k = __popc(bal);
+              if (cfill + k > kCandFifo) {
+                cand_flush<kQB * RPW>(sm.cfifo[ew], cfill, sm.lrow[ew], sm.mrow[ew], p.cand_cap, lane);
+                cfill = 0;
+              }
+              if (c) sm.cfifo[ew][cfill + __popc(bal & ((1u << lane) - 1u))] = make_int2(static_cast<int>(key), token | (lr << 24));
+              cfill += k;
+              __syncwarp();
+            }
+          } else {
+            const bool keep = static_cast<uint32_t>(token - rs[lr]) < static_cast<uint32_t>(re[lr]) &&
+                              __float_as_uint(s0) != 0u;
+            const uint32_t bits = __ballot_sync(0xffffffffu, keep);
+            st_u32_if(sm.mrow[ew][lr] + mword, bits, mstore);
+            st_f32_if(sm.lrow[ew][lr] + token, s0, keep);
+          }
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.tempty[a]);
       }
     }
+    if constexpr (kCand) cand_flush<kQB * RPW>(sm.cfifo[ew], cfill, sm.lrow[ew], sm.mrow[ew], p.cand_cap, lane);
   }
 
   __syncthreads();
@@ -973,12 +1068,12 @@ int launch_paged_t(const CUtensorMap& tkv, const CUtensorMap& tsc, const CUtenso
   return launch_status();
 }
 
-template <int H, bool kMixed>
+template <int H, bool kMixed, bool kCand = false>
 void launch_ragged(const CUtensorMap& tk, const CUtensorMap& tq, const RaggedArgs& a, cudaStream_t st) {
   const size_t smem = sizeof(PfSmem) + 1024;
-  cudaFuncSetAttribute(mqa_logits_ragged_kernel<H, kMixed>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  cudaFuncSetAttribute(mqa_logits_ragged_kernel<H, kMixed, kCand>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        static_cast<int>(smem));
-  mqa_logits_ragged_kernel<H, kMixed><<<sm_count(), kPfThreads, smem, st>>>(tk, tq, a);
+  mqa_logits_ragged_kernel<H, kMixed, kCand><<<sm_count(), kPfThreads, smem, st>>>(tk, tq, a);
 }
 
 template <int H>
@@ -1042,6 +1137,58 @@ extern "C" int hcu_mqa_logits_hist(const uint8_t* q, int64_t batch, int64_t head
   return heads == 64 ? launch_paged<64>(tkv, tsc, tq, a, st) : launch_paged<32>(tkv, tsc, tq, a, st);
 }
 
+namespace hcu {
+// Ragged logits launch without the mask memset (internal: the fused prefill top-k).  Rows see
+// [row_start, row_end); with bounds set, the candidate-list epilogue replaces the logits and mask
+// stores (logits and mask may then be null); run_if predicates the launch on a device word.
+int launch_ragged_logits(const uint8_t* q, int64_t rows, int64_t heads, const uint8_t* k_fp8, const float* k_scale,
+                         int64_t n_tokens, const float* weights, const int32_t* row_start, const int32_t* row_end,
+                         float* logits, int64_t logits_stride, int16_t* mask, const int32_t* bounds,
+                         int32_t* cand_cnt, int2* cand, int cand_cap, int cand_all_len, const int32_t* run_if,
+                         cudaStream_t st) {
+  if (rows == 0 || n_tokens == 0) return HCU_OK;
+  CUtensorMap tk, tq;
+  const int RB = static_cast<int>(kMaxN / heads);
+  if (!make_map_2d(&tk, k_fp8, kHeadDim, static_cast<uint64_t>(n_tokens), kHeadDim, kHeadDim, kTileTok,
+                   CU_TENSOR_MAP_SWIZZLE_128B))
+    return map_error("k_fp8");
+  if (!make_map_2d(&tq, q, kHeadDim, static_cast<uint64_t>(rows * heads), kHeadDim, kHeadDim,
+                   static_cast<uint32_t>(RB * heads), CU_TENSOR_MAP_SWIZZLE_128B))
+    return map_error("q");
+  RaggedArgs a{};
+  a.k_scale = k_scale;
+  a.weights = weights;
+  a.rs = row_start;
+  a.re = row_end;
+  a.logits = logits;
+  a.mask = mask;
+  a.stride = logits_stride;
+  a.rows = static_cast<int>(rows);
+  a.n_tokens = static_cast<int>(n_tokens);
+  a.bounds = bounds;
+  a.cand_cnt = cand_cnt;
+  a.cand = cand;
+  a.cand_cap = cand_cap;
+  a.cand_all_len = cand_all_len;
+  a.run_if = run_if;
+  static const bool mixed = [] {
+    const char* e = std::getenv("HCU_PF_RELU");
+    return e != nullptr && e[0] == 'm';
+  }();
+  if (bounds != nullptr) {
+    if (heads == 64)
+      launch_ragged<64, false, true>(tk, tq, a, st);
+    else
+      launch_ragged<32, false, true>(tk, tq, a, st);
+  } else if (heads == 64) {
+    mixed ? launch_ragged<64, true>(tk, tq, a, st) : launch_ragged<64, false>(tk, tq, a, st);
+  } else {
+    mixed ? launch_ragged<32, true>(tk, tq, a, st) : launch_ragged<32, false>(tk, tq, a, st);
+  }
+  return launch_status();
+}
+}  // namespace hcu
+
 extern "C" int hcu_mqa_logits_ragged(const uint8_t* q, int64_t rows, int64_t heads, const uint8_t* k_fp8,
                                      const float* k_scale, int64_t n_tokens, const float* weights,
                                      const int32_t* row_start, const int32_t* row_end, float* logits,
@@ -1058,32 +1205,6 @@ extern "C" int hcu_mqa_logits_ragged(const uint8_t* q, int64_t rows, int64_t hea
   const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(mask, 0, static_cast<size_t>(rows * (logits_stride / 16)) * sizeof(int16_t), st) != cudaSuccess)
     return launch_status();
-  if (n_tokens == 0) return HCU_OK;
-  CUtensorMap tk, tq;
-  const int RB = static_cast<int>(kMaxN / heads);
-  if (!make_map_2d(&tk, k_fp8, kHeadDim, static_cast<uint64_t>(n_tokens), kHeadDim, kHeadDim, kTileTok,
-                   CU_TENSOR_MAP_SWIZZLE_128B))
-    return map_error("k_fp8");
-  if (!make_map_2d(&tq, q, kHeadDim, static_cast<uint64_t>(rows * heads), kHeadDim, kHeadDim,
-                   static_cast<uint32_t>(RB * heads), CU_TENSOR_MAP_SWIZZLE_128B))
-    return map_error("q");
-  RaggedArgs a;
-  a.k_scale = k_scale;
-  a.weights = weights;
-  a.rs = row_start;
-  a.re = row_end;
-  a.logits = logits;
-  a.mask = mask;
-  a.stride = logits_stride;
-  a.rows = static_cast<int>(rows);
-  a.n_tokens = static_cast<int>(n_tokens);
-  static const bool mixed = [] {
-    const char* e = std::getenv("HCU_PF_RELU");
-    return e != nullptr && e[0] == 'm';
-  }();
-  if (heads == 64)
-    mixed ? launch_ragged<64, true>(tk, tq, a, st) : launch_ragged<64, false>(tk, tq, a, st);
-  else
-    mixed ? launch_ragged<32, true>(tk, tq, a, st) : launch_ragged<32, false>(tk, tq, a, st);
-  return launch_status();
+  return launch_ragged_logits(q, rows, heads, k_fp8, k_scale, n_tokens, weights, row_start, row_end, logits,
+                              logits_stride, mask, nullptr, nullptr, nullptr, 0, 0, nullptr, st);
 }

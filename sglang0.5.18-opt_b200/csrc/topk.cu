@@ -373,9 +373,18 @@ __device__ __forceinline__ int collect_candidates(const float* __restrict__ vals
 // all keys >= lo): a radix select of u = key - lo with 9-bit digits from the
 // top bit of (largest candidate - lo) down.  *above = candidates with a
 // larger key.  sm.hb[0] and sm.hb[1] must be zero on entry.
+template <int kT, class Sm>
+__device__ __forceinline__ uint32_t select_candidates_in(Sm& sm, int n, uint32_t lo, int* above, int k = kTopK);
+
 template <int kT>
 __device__ __forceinline__ uint32_t select_candidates(TopkSmem<kT>& sm, int n, uint32_t lo, int* above,
                                                      int k = kTopK) {
+  return select_candidates_in<kT>(sm, n, lo, above, k);
+}
+
+// The select over any shared-memory layout holding cand_key[], wmax[], hb[2][512] and res[].
+template <int kT, class Sm>
+__device__ __forceinline__ uint32_t select_candidates_in(Sm& sm, int n, uint32_t lo, int* above, int k) {
   constexpr int kDigit = 9;
   const int tid = threadIdx.x;
   const int lane = tid & 31;
@@ -1473,11 +1482,230 @@ __global__ __launch_bounds__(kT, 1024 / kT) void cp_filter_kernel(
   if (threadIdx.x == 0 && counts) counts[row] = n;
 }
 
+// ---------------------------------------------------------------------------
+// Fused prefill top-k, last step: the ragged logits kernel appended every
+// visible token at or above the row's bound to the row's list (unordered
+// (key, token) pairs, cnt[row] of them).  One CTA per row selects the top
+// kTopK of the list (the radix select over u = key - lo) and writes them in
+// the canonical order -- tokens above the threshold in ascending token order,
+// then threshold ties in ascending token order -- through token bitmaps in
+// shared memory.  The result equals the top-k of the materialised logits iff
+// the list is complete (cnt <= cap) and holds at least kTopK tokens; other
+// rows raise *flag (the caller's exact path then rewrites every row).  Rows of
+// at most kTopK visible tokens are written as the identity.
+// ---------------------------------------------------------------------------
+constexpr int kFusedMaxWidth = 131072;  // two token bitmaps of the row in shared memory
+constexpr int kFusedCap = 8192;         // candidate list capacity of the select
+
+// Fused prefill bound: one warp per row over every sampled score of the row
+// (its n = e_s[row] sampled tokens, at most kFusedSamples), the sample key of
+// rank t + 5 sqrt(t) + 5 with t = kTopK * n / len the expected sample rank of
+// the row's threshold (the wide margin keeps the chance that a row's list
+// misses the threshold, which sends the whole call down the exact path, far
+// below one in the thousands of rows of a prefill chunk).  Rows of at most
+// kTopK tokens and rows whose sample cannot bound anything give the largest
+// key.  Output: order-preserving int32 (key ^ 0x80000000).
+constexpr int kFusedSamples = 4096;  // 131072 tokens / 32
+constexpr int kFusedBoundWarps = 4;
+
+struct __align__(16) FusedBoundSmem {
+  uint32_t k[kFusedBoundWarps][kFusedSamples];
+  alignas(16) int h[kFusedBoundWarps][256];
+  int res[kFusedBoundWarps][4];
+};
+
+__global__ __launch_bounds__(kFusedBoundWarps * 32) void fused_bound_kernel(
+    const float* __restrict__ score, int64_t score_stride, const int16_t* __restrict__ mask, int64_t mask_stride,
+    const int32_t* __restrict__ e_s, const int32_t* __restrict__ row_end, int width, int rows,
+    int32_t* __restrict__ bounds) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  FusedBoundSmem& sm = *reinterpret_cast<FusedBoundSmem*>(smem_raw);
+  const int lane = threadIdx.x & 31;
+  const int w = threadIdx.x >> 5;
+  const int row = blockIdx.x * kFusedBoundWarps + w;
+  if (row >= rows) return;  // whole warps; no block barrier below
+  int len = __ldg(row_end + row);
+  len = len < 0 ? 0 : (len > width ? width : len);
+  const int n = min(__ldg(e_s + row), kFusedSamples);
+  uint32_t v = 0xFFFFFFFFu;
+  if (len > kTopK && n > 0) {
+    const float t = static_cast<float>(kTopK) * static_cast<float>(n) / static_cast<float>(len);
+    const int r_lo = static_cast<int>(ceilf(t + 5.f * sqrtf(t) + 5.f));
+    if (r_lo <= n) {
+      const float* vals = score + static_cast<int64_t>(row) * score_stride;
+      const int16_t* mrow = mask + static_cast<int64_t>(row) * mask_stride;
+      uint32_t* ks = sm.k[w];
+      for (int i = lane; i < n; i += 32) {
+        const bool set = (static_cast<uint16_t>(__ldg(mrow + (i >> 4))) >> (i & 15)) & 1u;
+        ks[i] = set ? to_key(__ldg(vals + i)) : kZeroKey;
+      }
+      uint32_t pre = 0u;
+      int need = r_lo;
+      int* h = sm.h[w];
+      for (int pass = 0; pass < 4; ++pass) {  // the r_lo-th largest key, 8 bits at a time
+        const int sh = 24 - 8 * pass;
+        for (int i = lane; i < 256; i += 32) h[i] = 0;
+        __syncwarp();
+        for (int j = lane; j < n; j += 32) {
+          const uint32_t k = ks[j];
+          if (pass == 0 || (k >> (sh + 8)) == pre) atomicAdd(&h[(k >> sh) & 0xFFu], 1);
+        }
+        __syncwarp();
+        warp_find<256>(h, need, sm.res[w]);
+        __syncwarp();
+        pre = (pre << 8) | static_cast<uint32_t>(sm.res[w][0]);
+        need -= sm.res[w][1];
+        __syncwarp();
+      }
+      v = pre;
+    }
+  }
+  if (lane == 0) bounds[row] = static_cast<int32_t>(v ^ kZeroKey);
+}
+
+template <int kT>
+struct __align__(16) FusedSelSmem {
+  uint32_t cand_key[kFusedCap];
+  int32_t cand_idx[kFusedCap];
+  uint32_t bm[2 * (kFusedMaxWidth / 32)];  // tokens above the threshold, then threshold ties
+  alignas(16) int hb[2][512];
+  uint32_t wmax[kT / 32];
+  int wtot[32];
+  int res[4];
+};
+
+template <int kT>
+__global__ __launch_bounds__(kT, 2) void fused_select_kernel(
+    const int2* __restrict__ cand, const int32_t* __restrict__ cnt, int cap, const int32_t* __restrict__ row_end,
+    int width, const int32_t* __restrict__ bounds, int all_len, const int32_t* __restrict__ pt, int64_t pt_stride,
+    int32_t* __restrict__ dst, int32_t* __restrict__ flag) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  FusedSelSmem<kT>& sm = *reinterpret_cast<FusedSelSmem<kT>*>(smem_raw);
+  const int row = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int w = tid >> 5;
+  int len = __ldg(row_end + row);
+  len = len < 0 ? 0 : (len > width ? width : len);
+  const int32_t* src = pt + static_cast<int64_t>(row) * pt_stride;
+  int32_t* out = dst + static_cast<int64_t>(row) * kTopK;
+  if (len <= kTopK) {
+    for (int i = tid; i < kTopK; i += kT) out[i] = i < len ? src[i] : -1;
+    return;
+  }
+  const int n = __ldg(cnt + row);
+  if (n > cap || n < kTopK || n > kFusedCap) {  // incomplete list or a bound above the threshold
+    if (tid == 0) atomicOr(flag, 1);
+    return;
+  }
+  const uint32_t lo = len <= all_len ? 0u : static_cast<uint32_t>(__ldg(bounds + row)) ^ kZeroKey;
+  const int nw = (len + 31) >> 5;
+  uint32_t* abm = sm.bm;       // tokens above the threshold
+  uint32_t* tbm = sm.bm + nw;  // threshold ties
+  for (int i = tid; i < 2 * nw; i += kT) abm[i] = 0u;
+  for (int i = tid; i < 2 * 512; i += kT) (&sm.hb[0][0])[i] = 0;
+  const int2* lst = cand + static_cast<int64_t>(row) * cap;
+  uint32_t m = 0u;
+  for (int i = tid; i < n; i += kT) {
+    const int2 e = __ldcg(lst + i);
+    const uint32_t k = static_cast<uint32_t>(e.x);
+    sm.cand_key[i] = k;
+    sm.cand_idx[i] = e.y;
+    m = k > m ? k : m;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const uint32_t y = __shfl_xor_sync(0xffffffffu, m, o);
+    m = y > m ? y : m;
+  }
+  if (lane == 0) sm.wmax[w] = m;
+  __syncthreads();
+  int above = 0;
+  const uint32_t thr = select_candidates_in<kT>(sm, n, lo, &above);
+  for (int i = tid; i < n; i += kT) {
+    const uint32_t k = sm.cand_key[i];
+    const int t = sm.cand_idx[i];
+    if (k > thr)
+      atomicOr(abm + (t >> 5), 1u << (t & 31));
+    else if (k == thr)
+      atomicOr(tbm + (t >> 5), 1u << (t & 31));
+  }
+  __syncthreads();
+  // thread tid takes words [i0, i1) of both bitmaps: its above tokens go after the above tokens of
+  // lower words, its ties after the lower words' ties (the first kTopK - above ties are kept)
+  const int per = (nw + kT - 1) / kT;
+  const int i0 = min(nw, tid * per);
+  const int i1 = min(nw, i0 + per);
+  int na = 0, nt = 0;
+  for (int i = i0; i < i1; ++i) {
+    na += __popc(abm[i]);
+    nt += __popc(tbm[i]);
+  }
+  int total;
+  const int ex = block_excl_scan<kT>(na | (nt << 16), sm.wtot, &total);
+  int ea = ex & 0xFFFF;
+  int et = ex >> 16;
+  const int remaining = kTopK - above;
+  for (int i = i0; i < i1; ++i) {
+    uint32_t a = abm[i];
+    while (a) {
+      const int b = __ffs(a) - 1;
+      a &= a - 1u;
+      out[ea++] = __ldg(src + (i << 5) + b);
+    }
+    uint32_t t = tbm[i];
+    while (t && et < remaining) {
+      const int b = __ffs(t) - 1;
+      t &= t - 1u;
+      out[above + et++] = __ldg(src + (i << 5) + b);
+    }
+  }
+}
+
 }  // namespace
 
 // Used by the logits translation unit for the hist_lens path: zeroes the
 // pass-1 workspace and preloads each row's +0 bin and zero count with its
 // histogram length; the logits kernel's epilogue then does pass 1.
+// Launchers of the fused prefill top-k (fused.cu): the list select, the exact
+// top-k predicated on the select's flag, and the sampled per-row bound.
+int launch_fused_select(const int2* cand, const int32_t* cnt, int cap, const int32_t* row_end, int64_t rows,
+                        int64_t width, const int32_t* bounds, int all_len, const int32_t* pt, int64_t pt_stride,
+                        int32_t* dst, int32_t* flag, cudaStream_t stream) {
+  if (rows <= 0) return HCU_OK;
+  if (width > kFusedMaxWidth || cap > kFusedCap) return HCU_ERR_ARG;
+  const size_t smem = sizeof(FusedSelSmem<512>);
+  cudaFuncSetAttribute(fused_select_kernel<512>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       static_cast<int>(smem));
+  fused_select_kernel<512><<<static_cast<unsigned>(rows), 512, smem, stream>>>(
+      cand, cnt, cap, row_end, static_cast<int>(width), bounds, all_len, pt, pt_stride, dst, flag);
+  return launch_status();
+}
+
+int launch_topk_if(const float* score, int64_t rows, int64_t width, int64_t score_stride, const int16_t* mask,
+                   int64_t mask_stride, const int32_t* lengths, const int32_t* pt, int64_t pt_stride, int32_t* dst,
+                   const int32_t* run_if, cudaStream_t stream) {
+  if (rows <= 0) return HCU_OK;
+  return launch_rows(score, rows, width, score_stride, mask, mask_stride, lengths, pt, pt_stride, dst, nullptr,
+                     nullptr, stream, false, 1, run_if);
+}
+
+int launch_fused_bound(const float* score, int64_t score_stride, const int16_t* mask, int64_t mask_stride,
+                       const int32_t* e_s, const int32_t* row_end, int64_t width, int64_t rows, int32_t* bounds,
+                       cudaStream_t stream) {
+  if (rows <= 0) return HCU_OK;
+  const size_t smem = sizeof(FusedBoundSmem);
+  cudaFuncSetAttribute(fused_bound_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  const unsigned grid = static_cast<unsigned>((rows + kFusedBoundWarps - 1) / kFusedBoundWarps);
+  fused_bound_kernel<<<grid, kFusedBoundWarps * 32, smem, stream>>>(score, score_stride, mask, mask_stride, e_s,
+                                                                     row_end, static_cast<int>(width),
+                                                                     static_cast<int>(rows), bounds);
+  return launch_status();
+}
+
+int fused_max_width() { return kFusedMaxWidth; }
+int fused_max_cap() { return kFusedCap; }
+
 int launch_hist_init(int32_t* zws, const int32_t* hist_lens, int64_t rows, int64_t width, cudaStream_t stream) {
   if (rows == 0) return HCU_OK;
   hist_init_kernel<<<static_cast<int>(rows), 256, 0, stream>>>(zws, hist_lens, static_cast<int>(width),

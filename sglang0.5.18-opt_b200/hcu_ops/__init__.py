@@ -169,6 +169,20 @@ def mqa_logits_ragged(q, k_fp8, k_scale, weights, row_start, row_end):
     return _C.mqa_logits_ragged(q, k_fp8, k_scale, weights, row_start, row_end)
 
 
+def mqa_topk_ragged(q, k_fp8, k_scale, weights, row_end, page_table=None, fallback_flag=None):
+    """Fused prefill indexer: the top-2048 of ``mqa_logits_ragged(q, k_fp8, k_scale, weights, 0, row_end)``
+    through ``page_table`` -- equal to ``sparse_mask_topk_transform`` on those logits with
+    ``lengths = row_end`` -- without writing the logits.
+
+    Row r sees tokens ``[0, row_end[r])`` of at most 131072.  ``page_table``: int32 ``[rows, >= tokens]``
+    (default: the token index).  ``fallback_flag`` (optional int32 CUDA tensor): set to 1 when some
+    row's candidate list could not prove exactness and the materialising path ran instead."""
+    if page_table is None:
+        n = k_fp8.shape[0]
+        page_table = torch.arange(n, dtype=torch.int32, device=q.device).expand(q.shape[0], n)
+    return _C.mqa_topk_ragged(q, k_fp8, k_scale, weights, row_end, page_table, fallback_flag)
+
+
 def quant_store_index_k(k, token_loc, kv_cache):
     """Indexer-K cache writer: quantise each K row (fp32 or bf16 ``[n, 128]``) per token to fp8 e4m3 with an
     fp32 scale ``max(amax, 1e-12) / 448`` and store it into slot ``token_loc[i] = page * 64 + offset`` of
