@@ -1908,8 +1908,8 @@ extern "C" int hcu_cp_filter(const float* score, int64_t rows, int64_t width, in
 // buffers (mapped over NVLink) and publish completion with one flag per (step,
 // phase, source rank); the consumers wait for every rank's flag.
 //
-// Publication: every thread fences its stores at system scope, the CTA
-// synchronises, and thread 0 counts the CTA into a local counter; the launch's
+// Publication: the CTA synchronises, thread 0 fences the CTA's stores at
+// system scope and counts the CTA into a local counter; the launch's
 // last CTA (it sees the count reach the grid size) resets the counter, takes
 // the launch's local flag word and stores (epoch << 1 | flag) into every
 // rank's signal word for (phase, this rank) with a system-scope release.
@@ -1928,9 +1928,12 @@ enum : int { kPhBounds = 0, kPhLists = 1, kPhRows = 2, kPhXLists = 3, kPhXRows =
 static_assert(HCU_CP_SIG_WORDS == 5 && HCU_CP_WS_FLAG == 8 && HCU_CP_WS_RERUNS == 9, "signal and workspace layout");
 
 __device__ __forceinline__ void peer_publish(const hcu_cp_peers_t& pp, int phase, int* counter, int* flagw) {
-  __threadfence_system();
+  // The CTA barrier orders every thread's stores before thread 0's system-scope fence, whose
+  // release is cumulative over them (the pattern of a grid-wide barrier): one fence per CTA
+  // instead of one per thread.
   __syncthreads();
   if (threadIdx.x == 0) {
+    __threadfence_system();
     const unsigned int grid = gridDim.x * gridDim.y * gridDim.z;
     if (atomicAdd(reinterpret_cast<unsigned int*>(counter), 1u) + 1u == grid) {
       __threadfence_system();
@@ -2011,31 +2014,37 @@ __global__ __launch_bounds__(kT, 1024 / kT) void cp_peer_filter_kernel(
   extern __shared__ __align__(16) unsigned char smem_raw[];
   TopkSmem<kT>& sm = *reinterpret_cast<TopkSmem<kT>*>(smem_raw);
   __shared__ int s_ok;
-  const int row = blockIdx.x;
   int* flagw = pp.ws + kWsFilterFlag;
+  // persistent CTAs (rows strided over the grid): one wait and one publication per CTA
   if (cta_wait(pp, kPhBounds, nullptr, &s_ok)) {
-    // the row's bound: the minimum over ranks of their published estimates (order-preserving int32)
-    int32_t b = INT32_MAX;
-    const int32_t* bl = pp.bounds[pp.rank];
-    for (int p = 0; p < pp.parts; ++p) b = min(b, __ldcg(bl + static_cast<int64_t>(p) * pp.rows + row));
-    int len = __ldg(lengths + row);
-    len = len < 0 ? 0 : (len > width ? width : len);
-    const int d = row / pp.rows_per_rank;  // the row's owner
-    const int64_t C = pp.list_len;
-    int32_t* keys = pp.lists[d] + (static_cast<int64_t>(2 * pp.rank) * pp.rows_per_rank + row % pp.rows_per_rank) * C;
-    filter_row<kT, kVec>(sm, score + static_cast<int64_t>(row) * score_stride,
-                         mask + static_cast<int64_t>(row) * mask_stride, pt + static_cast<int64_t>(row) * pt_stride,
-                         len, static_cast<uint32_t>(b) ^ kZeroKey, pp.list_len, reinterpret_cast<uint32_t*>(keys),
-                         keys + static_cast<int64_t>(pp.rows_per_rank) * C, flagw);
+    for (int row = blockIdx.x; row < pp.rows; row += gridDim.x) {
+      // the row's bound: the minimum over ranks of their published estimates (order-preserving int32)
+      int32_t b = INT32_MAX;
+      const int32_t* bl = pp.bounds[pp.rank];
+      for (int p = 0; p < pp.parts; ++p) b = min(b, __ldcg(bl + static_cast<int64_t>(p) * pp.rows + row));
+      int len = __ldg(lengths + row);
+      len = len < 0 ? 0 : (len > width ? width : len);
+      const int d = row / pp.rows_per_rank;  // the row's owner
+      const int64_t C = pp.list_len;
+      int32_t* keys =
+          pp.lists[d] + (static_cast<int64_t>(2 * pp.rank) * pp.rows_per_rank + row % pp.rows_per_rank) * C;
+      filter_row<kT, kVec>(sm, score + static_cast<int64_t>(row) * score_stride,
+                           mask + static_cast<int64_t>(row) * mask_stride, pt + static_cast<int64_t>(row) * pt_stride,
+                           len, static_cast<uint32_t>(b) ^ kZeroKey, pp.list_len, reinterpret_cast<uint32_t*>(keys),
+                           keys + static_cast<int64_t>(pp.rows_per_rank) * C, flagw);
+      __syncthreads();  // the row's shared state is read out before the next row reuses it
+    }
   } else if (threadIdx.x == 0) {
     atomicOr(flagw, 1);
   }
   peer_publish(pp, kPhLists, pp.ws + kWsFilterCnt, flagw);
 }
 
-// One CTA per row of this rank (rps rows): waits for every rank's lists of its
-// rows, merges them into its own out row, then copies that row to every other
-// rank's out.  exact: the 2048-entry lists of the redo (predicated on the flag).
+// Persistent CTAs over the rps rows of this rank: each waits once for every
+// rank's lists of the step, then per row merges the lists into this rank's out
+// row and copies that row to every other rank's out.  exact: the 2048-entry
+// lists of the redo (predicated on the flag: with it clear the small grid
+// returns at once).
 template <int kT>
 __global__ __launch_bounds__(kT, 1024 / kT) void cp_peer_merge_kernel(const int32_t* __restrict__ totals, int exact,
                                                                      const hcu_cp_peers_t pp) {
@@ -2043,26 +2052,29 @@ __global__ __launch_bounds__(kT, 1024 / kT) void cp_peer_merge_kernel(const int3
   TopkSmem<kT>& sm = *reinterpret_cast<TopkSmem<kT>*>(smem_raw);
   __shared__ int s_ok;
   if (exact && __ldcg(pp.ws + HCU_CP_WS_FLAG) == 0) return;  // grid-uniform: no redo this step
-  const int row = blockIdx.x;
   const int rps = pp.rows_per_rank;
   int* flagw = pp.ws + (exact ? kWsXMergeFlag : kWsMergeFlag);
-  const int64_t off = (static_cast<int64_t>(pp.rank) * rps + row) * kTopK;
-  int32_t* mine = pp.out[pp.rank] + off;
-  if (cta_wait(pp, exact ? kPhXLists : kPhLists, flagw, &s_ok)) {
-    const int C = exact ? kTopK : pp.list_len;
-    const int lshift = 31 - __clz(C);
-    const int32_t* lists = exact ? pp.lists_exact[pp.rank] : pp.lists[pp.rank];
-    merge_row(sm, reinterpret_cast<const uint32_t*>(lists), lists + static_cast<int64_t>(rps) * C, pp.parts, lshift,
-              2 * static_cast<int64_t>(rps) * C, totals, row, mine, flagw, 1);
-  } else if (threadIdx.x == 0) {
-    atomicOr(flagw, 1);
-  }
-  __syncthreads();  // the row is complete in this rank's out
-  const int4* src = reinterpret_cast<const int4*>(mine);
-  for (int i = threadIdx.x; i < kTopK / 4; i += kT) {
-    const int4 v = __ldcg(src + i);
-    for (int p = 0; p < pp.parts; ++p)
-      if (p != pp.rank) reinterpret_cast<int4*>(pp.out[p] + off)[i] = v;
+  // persistent CTAs (rows strided over the grid): one wait and one publication per CTA
+  const bool ok = cta_wait(pp, exact ? kPhXLists : kPhLists, flagw, &s_ok);
+  if (!ok && threadIdx.x == 0) atomicOr(flagw, 1);
+  for (int row = blockIdx.x; row < rps; row += gridDim.x) {
+    const int64_t off = (static_cast<int64_t>(pp.rank) * rps + row) * kTopK;
+    int32_t* mine = pp.out[pp.rank] + off;
+    if (ok) {
+      const int C = exact ? kTopK : pp.list_len;
+      const int lshift = 31 - __clz(C);
+      const int32_t* lists = exact ? pp.lists_exact[pp.rank] : pp.lists[pp.rank];
+      merge_row(sm, reinterpret_cast<const uint32_t*>(lists), lists + static_cast<int64_t>(rps) * C, pp.parts,
+                lshift, 2 * static_cast<int64_t>(rps) * C, totals, row, mine, flagw, 1);
+    }
+    __syncthreads();  // the row is complete in this rank's out
+    const int4* src = reinterpret_cast<const int4*>(mine);
+    for (int i = threadIdx.x; i < kTopK / 4; i += kT) {
+      const int4 v = __ldcg(src + i);
+      for (int p = 0; p < pp.parts; ++p)
+        if (p != pp.rank) reinterpret_cast<int4*>(pp.out[p] + off)[i] = v;
+    }
+    __syncthreads();  // shared state free for the next row
   }
   peer_publish(pp, exact ? kPhXRows : kPhRows, pp.ws + (exact ? kWsXMergeCnt : kWsMergeCnt), flagw);
 }
@@ -2119,7 +2131,8 @@ void launch_peer_filter(const float* score, int width, int64_t score_stride, con
   const size_t smem = sizeof(TopkSmem<kT>);
   cudaFuncSetAttribute(cp_peer_filter_kernel<kT, kVec>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        static_cast<int>(smem));
-  cp_peer_filter_kernel<kT, kVec><<<static_cast<unsigned>(pp.rows), kT, smem, st>>>(
+  const int grid = static_cast<int>(std::min<int64_t>(pp.rows, static_cast<int64_t>(sm_count()) * (1024 / kT)));
+  cp_peer_filter_kernel<kT, kVec><<<static_cast<unsigned>(grid), kT, smem, st>>>(
       score, score_stride, width, mask, mask_stride, lengths, pt, pt_stride, pp);
 }
 
@@ -2186,8 +2199,9 @@ extern "C" int hcu_cp_peer_merge(const int32_t* totals, int32_t exact, const hcu
   const size_t smem = sizeof(TopkSmem<1024>);
   cudaFuncSetAttribute(cp_peer_merge_kernel<1024>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        static_cast<int>(smem));
-  cp_peer_merge_kernel<1024><<<static_cast<unsigned>(pp.rows_per_rank), 1024, smem,
-                               reinterpret_cast<cudaStream_t>(stream)>>>(totals, exact ? 1 : 0, pp);
+  const int grid = static_cast<int>(std::min<int64_t>(pp.rows_per_rank, sm_count()));
+  cp_peer_merge_kernel<1024><<<static_cast<unsigned>(grid), 1024, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
+      totals, exact ? 1 : 0, pp);
   return launch_status();
 }
 
