@@ -573,7 +573,6 @@ constexpr int kQB = 4;
 constexpr int kPfEpiWarps = 16;  // warps 2..17: kPfTeams per TMEM lane quadrant
 constexpr int kPfTeams = kPfEpiWarps / 4;  // warp t of a quadrant takes rows r % kPfTeams == t of every row block
 constexpr int kPfThreads = (2 + kPfEpiWarps) * 32;
-constexpr int kCandFifo = 64;  // kCand: staged candidates per epilogue warp
 
 struct __align__(1024) PfSmem {
   uint8_t q[kQB][kQTile];
@@ -584,7 +583,7 @@ struct __align__(1024) PfSmem {
   float* lrow[kPfEpiWarps][16];     // logits row of each owned row (super-block); kCand: its list
   uint32_t* mrow[kPfEpiWarps][16];  // mask row (as 32-bit words) of each owned row; kCand: its count
   uint32_t lo[kPfEpiWarps][16];     // kCand: the owned rows' bounds as keys
-  int2 cfifo[kPfEpiWarps][kCandFifo];  // kCand: each warp's staged candidates
+  int2 cfifo[kPfEpiWarps][2][32];  // kCand: each warp's two staging halves
   uint64_t full[kPfStages];
   uint64_t empty[kPfStages];
   uint64_t qfull;
@@ -621,51 +620,85 @@ struct RaggedArgs {
   const int32_t* run_if;  // non-null: the launch does nothing while *run_if == 0
 };
 
-// kCand staging: each epilogue warp collects its candidates (key, token | owned-row slot << 24) in a
-// private shared-memory FIFO of kCandFifo entries and moves them to the rows' global lists when a
-// warp-row's entries would not fit (and before its owned rows change): one reservation atomic per
-// owned row with entries, issued together, per flush, instead of one per warp-row.
+// kCand staging: each epilogue warp collects its candidates (key, token | owned-row slot << 24) in
+// one of two 32-entry shared-memory halves.  When a warp-row's entries do not fit the current half,
+// the warp seals it -- one slot-reservation atomic per owned row with entries, issued together and
+// not waited for -- and switches halves; the sealed half's entries are written to the rows' global
+// lists at the next seal (or before the owned rows change), when the reservations have long
+// arrived.  So no epilogue warp waits on a global atomic in the steady state.
+struct CandStage {
+  int fill = 0;      // entries in the current half
+  int half = 0;      // the current half
+  int pend = 0;      // entries of the sealed half (0: none pending)
+  int base = 0;      // lane s < NS: the sealed half's first slot in owned row s
+};
 
-// Flush of one warp's FIFO (every lane calls it).  Entries e with owned-row slot s (< NS) go to
-// list(s)[base_s + rank of e among the slot's entries], base_s reserved from count(s).
+// Per-slot ballots of a half's entries: lane i holds entry i (slot sl, -1 past `fill`).
 template <int NS>
-__device__ __forceinline__ void cand_flush(int2* fifo, int fill, float* const* lrow, uint32_t* const* mrow, int cap,
-                                           int lane) {
-  if (fill == 0) return;
-  int2 e[2];
-  int sl[2];
+__device__ __forceinline__ void cand_slots(const int2* half, int fill, int lane, int2& e, int& sl, int& pre, int& n_s) {
+  e = lane < fill ? half[lane] : make_int2(0, 0);
+  sl = lane < fill ? (e.y >> 24) : -1;
+  pre = 0;
+  n_s = 0;
 #pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const int i = lane + 32 * h;
-    e[h] = i < fill ? fifo[i] : make_int2(0, -1);
-    sl[h] = i < fill ? (e[h].y >> 24) : -1;
+  for (int q = 0; q < NS; ++q) {
+    const uint32_t m = __ballot_sync(0xffffffffu, sl == q);
+    if (sl == q) pre = __popc(m & ((1u << lane) - 1u));
+    if (lane == q) n_s = __popc(m);
   }
-  uint32_t m[2][NS];
-  int n_s = 0;  // lane s < NS: entries of slot s
-#pragma unroll
-  for (int s = 0; s < NS; ++s) {
-    m[0][s] = __ballot_sync(0xffffffffu, sl[0] == s);
-    m[1][s] = __ballot_sync(0xffffffffu, sl[1] == s);
-    if (lane == s) n_s = __popc(m[0][s]) + __popc(m[1][s]);
+}
+
+// Seal: reserve list slots for the current half (the returned base is consumed by cand_complete).
+template <int NS>
+__device__ __forceinline__ int cand_seal(const int2* half, int fill, uint32_t* const* mrow, int lane) {
+  int2 e;
+  int sl, pre, n_s;
+  cand_slots<NS>(half, fill, lane, e, sl, pre, n_s);
+  return (lane < NS && n_s > 0) ? atomicAdd(reinterpret_cast<int*>(mrow[lane]), n_s) : 0;
+}
+
+// Complete: write a sealed half's entries at their reserved slots.
+template <int NS>
+__device__ __forceinline__ void cand_complete(const int2* half, int fill, int base, float* const* lrow, int cap,
+                                              int lane) {
+  int2 e;
+  int sl, pre, n_s;
+  cand_slots<NS>(half, fill, lane, e, sl, pre, n_s);
+  const int b = __shfl_sync(0xffffffffu, base, sl < 0 ? 0 : sl);
+  if (sl >= 0 && b + pre < cap) reinterpret_cast<int2*>(lrow[sl])[b + pre] = make_int2(e.x, e.y & 0xFFFFFF);
+}
+
+// Appends this warp-row's candidates (lanes with c; bal = their ballot), sealing first when they
+// do not fit the current half.
+template <int NS>
+__device__ __forceinline__ void cand_append(CandStage& st, int2 (*halves)[32], float* const* lrow,
+                                            uint32_t* const* mrow, int cap, int lane, bool c, uint32_t bal, int2 ent) {
+  const int k = __popc(bal);
+  if (st.fill + k > 32) {
+    __syncwarp();  // the current half's entries are visible to every lane
+    if (st.pend) cand_complete<NS>(halves[st.half ^ 1], st.pend, st.base, lrow, cap, lane);
+    st.base = cand_seal<NS>(halves[st.half], st.fill, mrow, lane);
+    st.pend = st.fill;
+    st.half ^= 1;
+    st.fill = 0;
+    __syncwarp();  // the completed half is free
   }
-  int base = 0;
-  if (lane < NS && n_s > 0) base = atomicAdd(reinterpret_cast<int*>(mrow[lane]), n_s);
-  const uint32_t lt = (1u << lane) - 1u;
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    int pre0 = 0, pre1 = 0;  // entries of this entry's slot in half 0, and below this lane in its half
-#pragma unroll
-    for (int q = 0; q < NS; ++q)
-      if (q == sl[h]) {
-        pre0 = __popc(m[0][q] & (h ? 0xffffffffu : lt));
-        pre1 = h ? __popc(m[1][q] & lt) : 0;
-      }
-    const int b = __shfl_sync(0xffffffffu, base, sl[h] < 0 ? 0 : sl[h]);
-    if (sl[h] >= 0) {
-      const int pos = b + pre0 + pre1;
-      if (pos < cap) reinterpret_cast<int2*>(lrow[sl[h]])[pos] = make_int2(e[h].x, e[h].y & 0xFFFFFF);
-    }
+  if (c) halves[st.half][st.fill + __popc(bal & ((1u << lane) - 1u))] = ent;
+  st.fill += k;
+}
+
+// Writes out everything staged (before the owned rows change, and at the end).
+template <int NS>
+__device__ __forceinline__ void cand_drain(CandStage& st, int2 (*halves)[32], float* const* lrow,
+                                           uint32_t* const* mrow, int cap, int lane) {
+  __syncwarp();
+  if (st.pend) cand_complete<NS>(halves[st.half ^ 1], st.pend, st.base, lrow, cap, lane);
+  if (st.fill) {
+    const int base = cand_seal<NS>(halves[st.half], st.fill, mrow, lane);
+    cand_complete<NS>(halves[st.half], st.fill, base, lrow, cap, lane);
   }
+  st.pend = 0;
+  st.fill = 0;
   __syncwarp();
 }
 
@@ -878,7 +911,7 @@ __global__ __launch_bounds__(kPfThreads, 1) void mqa_logits_ragged_kernel(const 
     cur.init(p, sm.start_sb, sm.start_local);
     int qsb = -1, nrb = 0, u = 0;
     bool ok = true;
-    int cfill = 0;  // kCand: entries in this warp's FIFO
+    CandStage cst;  // kCand: this warp's staged candidates
     for (int it = 0; it < count && ok; ++it) {
       const int tile = cur.next(p);
       const int row0 = cur.sb * SBR;
@@ -886,8 +919,7 @@ __global__ __launch_bounds__(kPfThreads, 1) void mqa_logits_ragged_kernel(const 
         qsb = cur.sb;
         nrb = min(kQB, (p.rows - row0 + RB - 1) / RB);
         if constexpr (kCand) {  // before the owned rows change
-          cand_flush<kQB * RPW>(sm.cfifo[ew], cfill, sm.lrow[ew], sm.mrow[ew], p.cand_cap, lane);
-          cfill = 0;
+          cand_drain<kQB * RPW>(cst, sm.cfifo[ew], sm.lrow[ew], sm.mrow[ew], p.cand_cap, lane);
         }
         __syncwarp();
         for (int lr = 0; lr < kQB * RPW; ++lr) {
@@ -968,16 +1000,8 @@ __global__ __launch_bounds__(kPfThreads, 1) void mqa_logits_ragged_kernel(const 
             const uint32_t key = to_key(s0);
             const bool c = static_cast<uint32_t>(token - rs[lr]) < static_cast<uint32_t>(re[lr]) && key >= sm.lo[ew][lr];
             const uint32_t bal = __ballot_sync(0xffffffffu, c);
-            if (bal) {  // into this warp's FIFO (flushed first when the row's entries might not fit)
-              const int k = __popc(bal);
-              if (cfill + k > kCandFifo) {
-                cand_flush<kQB * RPW>(sm.cfifo[ew], cfill, sm.lrow[ew], sm.mrow[ew], p.cand_cap, lane);
-                cfill = 0;
-              }
-              if (c) sm.cfifo[ew][cfill + __popc(bal & ((1u << lane) - 1u))] = make_int2(static_cast<int>(key), token | (lr << 24));
-              cfill += k;
-              __syncwarp();
-            }
+            cand_append<kQB * RPW>(cst, sm.cfifo[ew], sm.lrow[ew], sm.mrow[ew], p.cand_cap, lane, c, bal,
+                                   make_int2(static_cast<int>(key), token | (lr << 24)));
           } else {
             const bool keep = static_cast<uint32_t>(token - rs[lr]) < static_cast<uint32_t>(re[lr]) &&
                               __float_as_uint(s0) != 0u;
@@ -991,7 +1015,7 @@ __global__ __launch_bounds__(kPfThreads, 1) void mqa_logits_ragged_kernel(const 
         if (lane == 0) mbar_arrive(&sm.tempty[a]);
       }
     }
-    if constexpr (kCand) cand_flush<kQB * RPW>(sm.cfifo[ew], cfill, sm.lrow[ew], sm.mrow[ew], p.cand_cap, lane);
+    if constexpr (kCand) cand_drain<kQB * RPW>(cst, sm.cfifo[ew], sm.lrow[ew], sm.mrow[ew], p.cand_cap, lane);
   }
 
   __syncthreads();
