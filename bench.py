@@ -21,7 +21,7 @@ Sub-records of the same JSON line:
 for gfx938 and its oracle library is closed) on the host cores, rank 0 only, same metric, config,
 steps and warm-up; it loads none of this repository's compiled libraries.
 --workload NAME runs one secondary workload alone (decode0, prefill, dequant, mla_dequant, kstore,
-mla_kv, cp_prefill).
+mla_kv, cp_filter, cp_prefill).
 """
 from __future__ import annotations
 
@@ -992,8 +992,76 @@ def sec_mla_kv(args, local):
     return rec
 
 
+def sec_cp_filter(args, local):
+    """One rank's share of config 4's bounded exchange at P = 8 (rank 3 of 8, balanced ranges): the sampled
+    per-row bound and the filter over that rank's materialised local logits (16384 rows x its range),
+    timed over the rank's real logits; HBM-bound reads of the logits and mask."""
+    import torch
+
+    import hcu_ops
+    from hcu_ops.cp import kv_range, list_len, local_rows
+
+    dev = torch.device("cuda", local)
+    rows, N, P, r = CP_ROWS, CP_N, 8, 3
+    w = _workloads().make_ragged(rows, N - rows, heads=64, seed=0, device=dev)
+    lo, hi = kv_range(r, P, N, causal_rows=rows)
+    lens = local_rows(w["row_end"], lo, hi)
+    lg, mk = hcu_ops.mqa_logits_ragged(w["q"], w["k_fp8"][lo:hi].contiguous(), w["k_scale"][lo:hi].contiguous(),
+                                       w["weights"], torch.zeros_like(lens), lens)
+    del w["k_fp8"]
+    vis = (w["row_end"].clamp(max=N)).to(torch.int32)
+    gtab = (torch.arange(hi - lo, dtype=torch.int32, device=dev) + lo).expand(rows, hi - lo)
+    cap = list_len(P)
+    send = torch.empty((P, 2, rows // P, cap), dtype=torch.int32, device=dev)
+    flag = torch.zeros(1, dtype=torch.int32, device=dev)
+    state = {}
+
+    def bound():
+        state["b"] = hcu_ops.cp_local_bound(lg, mk, lens, vis)
+
+    def filt():
+        hcu_ops.cp_filter(lg, mk, lens, gtab, state["b"], send, flag)
+
+    for _ in range(3):
+        bound()
+        filt()
+    iters = max(3, min(args.steps, 20))
+    ms_b, _ = _timed(bound, iters, local)
+    ms, clocks = _timed(filt, iters, local)
+    width = hi - lo
+    nbytes = rows * width * 4 + rows * (width // 16) * 2 + send.numel() * 4
+    hbm, _, src = _peaks()
+    rec = _rec("CP bounded-exchange filter throughput, one rank at P = 8 (algorithmic bytes / s)",
+               nbytes / (ms * 1e-3) / 1e9, "GB/s", ms, iters,
+               f"config4 rank {r} of {P}: {rows} rows x {width} local tokens (materialised logits "
+               f"{rows * width * 4 / 1e9:.2f} GB > L2), {cap}-slot lists; bound timed separately", rows=rows,
+               width=width)
+    rec["bound_ms"] = ms_b
+    rec["flag"] = int(flag.item())
+    rec["roofline"] = {"bound": "hbm", "achieved": nbytes / (ms * 1e-3) / 1e9, "peak": hbm, "unit": "GB/s",
+                       "frac": nbytes / (ms * 1e-3) / 1e9 / hbm, "traffic": None, "kernel": "cp_filter_kernel<512>",
+                       "alg_bytes_per_launch": nbytes, "peak_source": src}
+    rec["gpu_launches"] = iters * 2
+    rec["clocks"] = clocks
+    if not args.no_cpu_baseline:
+        from oracle import indexer as O
+
+        sel = _stratified(rows, 2048)
+        sl = torch.as_tensor(sel, device=dev)
+        x, m = lg[sl].cpu().numpy(), mk[sl].cpu().numpy()
+        ln, bb, gt = lens[sl].cpu().numpy(), state["b"][sl].cpu().numpy(), gtab[sl].cpu().numpy()
+        t0 = time.perf_counter()
+        O.cp_filter(x, m, ln, gt, bb, cap)
+        dt = time.perf_counter() - t0
+        cb = len(sel) * (width * 4 + (width // 16) * 2 + 2 * cap * 4)
+        rec["cpu_baseline"] = {"value": cb / dt / 1e9, "unit": "GB/s", "cores": _threads(), "kind": "port",
+                               "sample": f"{len(sel)} stratified rows of {rows} through the oracle's filter ({dt:.2f} s)"}
+    return rec
+
+
 SECONDARY = {"decode0": sec_decode0, "prefill": sec_prefill, "dequant": sec_dequant,
-             "mla_dequant": lambda a, l: sec_dequant(a, l, mla=True), "kstore": sec_kstore, "mla_kv": sec_mla_kv}
+             "mla_dequant": lambda a, l: sec_dequant(a, l, mla=True), "kstore": sec_kstore, "mla_kv": sec_mla_kv,
+             "cp_filter": sec_cp_filter}
 
 
 def _standalone(args, world, rank, local):
