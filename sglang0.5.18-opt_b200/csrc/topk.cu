@@ -32,6 +32,7 @@
 // than the threshold in token order, then the first threshold ties in token
 // order (ties broken toward the lower index).
 #include <cooperative_groups.h>
+#include <cstddef>
 
 #include <mutex>
 #include <vector>
@@ -1492,7 +1493,9 @@ __global__ __launch_bounds__(kT, 1024 / kT) void cp_filter_kernel(
 // shared memory.  The result equals the top-k of the materialised logits iff
 // the list is complete (cnt <= cap) and holds at least kTopK tokens; other
 // rows raise *flag (the caller's exact path then rewrites every row).  Rows of
-// at most kTopK visible tokens are written as the identity.
+// at most kTopK visible tokens are written as the identity.  256-thread CTAs
+// with the list's keys in shared memory: several rows per SM hide the per-row
+// latency of the load, the radix rounds and the ordered write.
 // ---------------------------------------------------------------------------
 constexpr int kFusedMaxWidth = 131072;  // two token bitmaps of the row in shared memory
 constexpr int kFusedCap = 8192;         // candidate list capacity of the select
@@ -1563,19 +1566,21 @@ __global__ __launch_bounds__(kFusedBoundWarps * 32) void fused_bound_kernel(
   if (lane == 0) bounds[row] = static_cast<int32_t>(v ^ kZeroKey);
 }
 
+// Keys only (the tokens are re-read from the list, L2-resident, once the threshold is known), and
+// the two token bitmaps sized to the row width after the struct, so that four 256-thread CTAs fit
+// an SM at the benchmark widths.
 template <int kT>
 struct __align__(16) FusedSelSmem {
   uint32_t cand_key[kFusedCap];
-  int32_t cand_idx[kFusedCap];
-  uint32_t bm[2 * (kFusedMaxWidth / 32)];  // tokens above the threshold, then threshold ties
   alignas(16) int hb[2][512];
   uint32_t wmax[kT / 32];
   int wtot[32];
   int res[4];
+  alignas(16) uint32_t bm[1];  // 2 x ceil(width / 32) words: tokens above the threshold, then threshold ties
 };
 
 template <int kT>
-__global__ __launch_bounds__(kT, 2) void fused_select_kernel(
+__global__ __launch_bounds__(kT, 1024 / kT) void fused_select_kernel(
     const int2* __restrict__ cand, const int32_t* __restrict__ cnt, int cap, const int32_t* __restrict__ row_end,
     int width, const int32_t* __restrict__ bounds, int all_len, const int32_t* __restrict__ pt, int64_t pt_stride,
     int32_t* __restrict__ dst, int32_t* __restrict__ flag) {
@@ -1607,10 +1612,8 @@ __global__ __launch_bounds__(kT, 2) void fused_select_kernel(
   const int2* lst = cand + static_cast<int64_t>(row) * cap;
   uint32_t m = 0u;
   for (int i = tid; i < n; i += kT) {
-    const int2 e = __ldcg(lst + i);
-    const uint32_t k = static_cast<uint32_t>(e.x);
+    const uint32_t k = static_cast<uint32_t>(__ldcg(&lst[i].x));
     sm.cand_key[i] = k;
-    sm.cand_idx[i] = e.y;
     m = k > m ? k : m;
   }
 #pragma unroll
@@ -1624,7 +1627,8 @@ __global__ __launch_bounds__(kT, 2) void fused_select_kernel(
   const uint32_t thr = select_candidates_in<kT>(sm, n, lo, &above);
   for (int i = tid; i < n; i += kT) {
     const uint32_t k = sm.cand_key[i];
-    const int t = sm.cand_idx[i];
+    if (k < thr) continue;
+    const int t = __ldcg(&lst[i].y);
     if (k > thr)
       atomicOr(abm + (t >> 5), 1u << (t & 31));
     else if (k == thr)
@@ -1674,10 +1678,11 @@ int launch_fused_select(const int2* cand, const int32_t* cnt, int cap, const int
                         int32_t* dst, int32_t* flag, cudaStream_t stream) {
   if (rows <= 0) return HCU_OK;
   if (width > kFusedMaxWidth || cap > kFusedCap) return HCU_ERR_ARG;
-  const size_t smem = sizeof(FusedSelSmem<512>);
-  cudaFuncSetAttribute(fused_select_kernel<512>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       static_cast<int>(smem));
-  fused_select_kernel<512><<<static_cast<unsigned>(rows), 512, smem, stream>>>(
+  constexpr int kT = 256;
+  const size_t smem = offsetof(FusedSelSmem<kT>, bm) + 2 * static_cast<size_t>((width + 31) / 32) * 4;
+  cudaFuncSetAttribute(fused_select_kernel<kT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       static_cast<int>(sizeof(FusedSelSmem<kT>) + 2 * (kFusedMaxWidth / 32) * 4));
+  fused_select_kernel<kT><<<static_cast<unsigned>(rows), kT, smem, stream>>>(
       cand, cnt, cap, row_end, static_cast<int>(width), bounds, all_len, pt, pt_stride, dst, flag);
   return launch_status();
 }
