@@ -298,10 +298,12 @@ def run_decode(args, world, rank, local):
 
     t = torch.tensor([ms, ms_logits, ms_e2e, float(pairs)], dtype=torch.float64, device=dev)
     per_rank_ms = [ms]
+    per_rank_logits = [ms_logits]
     if world > 1:
         allt = [torch.zeros_like(t) for _ in range(world)]
         torch.distributed.all_gather(allt, t)
         per_rank_ms = [float(x[0]) for x in allt]
+        per_rank_logits = [float(x[1]) for x in allt]
         ms = max(float(x[0]) for x in allt)
         ms_logits = max(float(x[1]) for x in allt)
         ms_e2e = max(float(x[2]) for x in allt)
@@ -328,7 +330,10 @@ def run_decode(args, world, rank, local):
         "dtype": DTYPE,
         "data": "synthetic (seeded; q,K ~ N(0,1) per-row/per-token amax/448 fp8; w ~ N(0,1)/8)",
         "config": decode_config(world),
-        "per_rank_ms": {"min": min(per_rank_ms), "median": statistics.median(per_rank_ms), "max": max(per_rank_ms)},
+        "per_rank_ms": {"min": min(per_rank_ms), "median": statistics.median(per_rank_ms), "max": max(per_rank_ms),
+                        "all": per_rank_ms},
+        "per_rank_logits_op_ms": {"min": min(per_rank_logits), "median": statistics.median(per_rank_logits),
+                                  "max": max(per_rank_logits), "all": per_rank_logits},
         "top_k_rows_per_s": lens.numel() * world / (ms * 1e-3),
         "logits_op_ms": ms_logits,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
