@@ -175,3 +175,30 @@ def test_cp_peer_exchange_argument_checks(lib):
 def test_wait_limit_entry_point_is_exported(lib):
     lib.hcu_set_wait_limit_ns.argtypes = [ctypes.c_uint64]
     assert hasattr(lib, "hcu_set_wait_limit_ns")
+
+
+def test_fused_prefill_workspace_and_argument_checks(lib):
+    """The fused prefill indexer's workspace query grows with rows and tokens (the exact path's
+    logits dominate it), and the entry point refuses bad arguments before launching anything."""
+    ws = lib.hcu_mqa_topk_ragged_workspace_bytes
+    ws.restype = ctypes.c_int64
+    ws.argtypes = [ctypes.c_int64, ctypes.c_int64]
+    assert ws(-1, 10) == -1
+    small, big = ws(16, 20000), ws(8192, 73728)
+    assert 0 < small < big
+    assert big >= 8192 * 73728 * 4  # at least the materialised logits of the exact path
+    assert ws(8192, 73728) % 256 == 0
+    f = lib.hcu_mqa_topk_ragged
+    f.restype = ctypes.c_int
+    p, i64 = ctypes.c_void_p(16), ctypes.c_int64
+
+    def call(rows=4, heads=64, n=4096, pt_stride=4096, wsb=None, workspace=p):
+        b = ws(rows, n) if wsb is None else wsb
+        return f(p, i64(rows), i64(heads), p, p, i64(n), p, p, p, i64(pt_stride), p, workspace, i64(b), None, None)
+
+    assert call(heads=48) == HCU_ERR_UNSUPPORTED
+    assert call(n=131073) == HCU_ERR_ARG        # past the width the select's bitmaps cover
+    assert call(wsb=1024) == HCU_ERR_ARG        # workspace too small
+    assert call(workspace=None) == HCU_ERR_ARG
+    assert call(pt_stride=-1) == HCU_ERR_ARG
+    assert call(rows=0) == HCU_OK
