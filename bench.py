@@ -563,20 +563,26 @@ def run_cp_prefill(args, world, rank, local, steps=None, warmup=None):
     import torch
 
     import hcu_ops
-    from hcu_ops.cp import cp_prefill_topk, kv_range, list_len
+    from hcu_ops.cp import calibrate_shares, cp_prefill_topk, kv_range, list_len
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     rows, N = CP_ROWS, CP_N
+    # KV ranges balanced by visible pairs, weighted by each GPU's measured prefill-logits rate (GPUs of
+    # one box differ; the step waits for the slowest rank).  HCU_CP_SHARES=equal: unweighted.
+    shares = None
+    if world > 1 and os.environ.get("HCU_CP_SHARES", "calibrated") != "equal":
+        shares = calibrate_shares(device=dev)
     w = _workloads().make_ragged(rows, N - rows, heads=64, seed=0, device=dev)  # identical on every rank
-    lo, hi = kv_range(rank, world, N, causal_rows=rows)
+    lo, hi = kv_range(rank, world, N, causal_rows=rows, shares=shares)
     kf, ks = w["k_fp8"][lo:hi].contiguous(), w["k_scale"][lo:hi].contiguous()
     steps = steps or min(args.steps, 20)
     warmup = warmup or max(3, min(args.warmup, 5))
     stats = {}
 
     def step():
-        return cp_prefill_topk(w["q"], kf, ks, w["weights"], w["row_end"], N, causal_rows=rows, stats=stats)
+        return cp_prefill_topk(w["q"], kf, ks, w["weights"], w["row_end"], N, causal_rows=rows, stats=stats,
+                               shares=shares)
 
     for _ in range(warmup):
         out = step()
@@ -631,7 +637,9 @@ def run_cp_prefill(args, world, rank, local, steps=None, warmup=None):
            "steps": steps, "warmup": warmup, "ms_per_step": ms, "scaling": "strong",
            "per_rank_ms": {"min": min(per_rank), "median": statistics.median(per_rank), "max": max(per_rank)},
            "config": {"workload": f"config4: {rows} rows x ({N - rows} + i + 1) tokens over a {N}-token context in "
-                                  f"{world} KV ranges balanced by visible pairs, 64 heads", "pairs": pairs,
+                                  f"{world} KV ranges balanced by visible pairs" +
+                                  (", weighted by each GPU's measured logits rate" if shares else "") + ", 64 heads",
+                      "pairs": pairs, "shares": [round(x / max(shares), 4) for x in shares] if shares else None,
                       "parallelism": f"cp{world}", "l2": "no flush: logits and inputs exceed L2"},
            "list_len": list_len(world) if world > 1 else None, "reruns": reruns,
            "exchange": stats.get("exchange", "none (one range)"),

@@ -88,18 +88,31 @@ class CudaOps:
         return cp_topk_merge(keys, gidx, lengths)
 
 
-def kv_range(rank: int, world: int, n_tokens: int, causal_rows: int = 0):
+def kv_range(rank: int, world: int, n_tokens: int, causal_rows: int = 0, shares=None):
     """Contiguous KV range of a rank; boundaries are multiples of 16 (mask words stay aligned).
 
     ``causal_rows = 0``: equal token counts.  ``causal_rows = R``: the query rows are the last R
     positions of the context (row i sees tokens [0, n_tokens - R + i + 1)), and the boundaries
     give every rank about the same number of visible (row, token) pairs, so the rank that holds
-    the causal triangle takes a longer range instead of idling."""
+    the causal triangle takes a longer range instead of idling.  ``shares`` (one positive weight
+    per rank, e.g. from ``calibrate_shares``): rank r takes a fraction shares[r] / sum(shares) of
+    the tokens (of the visible pairs with ``causal_rows``) instead of an equal one.  Every rank
+    must pass the same arguments."""
     if rank >= world:
         return n_tokens, n_tokens
+    if shares is not None:
+        w = [float(x) for x in shares]
+        if len(w) != world or min(w) <= 0:
+            raise ValueError("shares: one positive weight per rank")
+        cum = [0.0]
+        for x in w:
+            cum.append(cum[-1] + x)
+        frac = [c / cum[-1] for c in cum]
+    else:
+        frac = [r / world for r in range(world + 1)]
     if causal_rows <= 0:
         def b(r):
-            return (n_tokens * r // world) // 16 * 16 if r < world else n_tokens
+            return int(n_tokens * frac[r]) // 16 * 16 if r < world else n_tokens
         return b(rank), b(rank + 1)
     R = min(int(causal_rows), n_tokens)
     p = n_tokens - R
@@ -117,7 +130,7 @@ def kv_range(rank: int, world: int, n_tokens: int, causal_rows: int = 0):
             return 0
         if r >= world:
             return n_tokens
-        target = total * r // world
+        target = total * r // world if shares is None else int(total * frac[r])
         lo, hi = 0, n_tokens  # smallest x with pairs(x) >= target, then down to a multiple of 16
         while lo < hi:
             mid = (lo + hi) // 2
@@ -128,6 +141,41 @@ def kv_range(rank: int, world: int, n_tokens: int, causal_rows: int = 0):
         return lo // 16 * 16
 
     return b(rank), b(rank + 1)
+
+
+def calibrate_shares(group=None, device=None, rows=2048, tokens=32768, reps=5):
+    """Relative prefill-logits rates of the ranks' GPUs, for ``kv_range(..., shares=...)``.
+
+    GPUs of one box can differ by tens of percent on the same kernel, and a context-parallel step
+    waits for its slowest rank; weighting each rank's range by its measured rate evens out the
+    ranks' step times.  Every rank times the ragged logits kernel on the same seeded block (median
+    of ``reps`` runs), the times are all-gathered, and each rank gets weight 1 / time (identical
+    list on every rank).  A collective step: call it on every rank, once, outside any timed region."""
+    from . import mqa_logits_ragged
+    from .workloads import make_ragged
+
+    dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+    w = make_ragged(rows, tokens - rows, heads=64, seed=123, device=dev)
+    zeros = torch.zeros_like(w["row_end"])
+    for _ in range(2):
+        mqa_logits_ragged(w["q"], w["k_fp8"], w["k_scale"], w["weights"], zeros, w["row_end"])
+    times = []
+    for _ in range(reps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        mqa_logits_ragged(w["q"], w["k_fp8"], w["k_scale"], w["weights"], zeros, w["row_end"])
+        b.record()
+        torch.cuda.synchronize(dev)
+        times.append(a.elapsed_time(b))
+    t = torch.tensor([sorted(times)[len(times) // 2]], dtype=torch.float64, device=dev)
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    if world > 1:
+        allt = [torch.zeros_like(t) for _ in range(world)]
+        dist.all_gather(allt, t, group=group)
+        ts = [float(x.item()) for x in allt]
+    else:
+        ts = [float(t.item())]
+    return [1.0 / x for x in ts]
 
 
 def local_rows(row_end: torch.Tensor, lo: int, hi: int) -> torch.Tensor:
@@ -311,11 +359,11 @@ def _peer_exchange(group, rows, dev, world):
 
 
 def cp_prefill_topk(q, k_fp8_local, k_scale_local, weights, row_end, n_tokens, group=None, mode=None,
-                    ops=None, bounded=True, causal_rows=0, stats=None):
+                    ops=None, bounded=True, causal_rows=0, stats=None, shares=None):
     """Global top-2048 token indices of every query row, computed over P KV ranges.
 
     q: fp8 ``[rows, H, 128]`` (replicated); ``k_fp8_local``/``k_scale_local``: this rank's
-    KV range ``kv_range(rank, P, n_tokens, causal_rows)``; ``row_end``: int32 ``[rows]`` global visible end
+    KV range ``kv_range(rank, P, n_tokens, causal_rows, shares)``; ``row_end``: int32 ``[rows]`` global visible end
     (row r sees tokens ``[0, row_end[r])``).  Returns int32 ``[rows, 2048]`` (-1 pads) on
     every rank.  Every rank takes the same collective steps in the same order.  ``stats`` (optional
     dict): "reruns" is incremented when the bounded exchange had to be redone exactly, "exchange"
@@ -329,7 +377,7 @@ def cp_prefill_topk(q, k_fp8_local, k_scale_local, weights, row_end, n_tokens, g
     rank = dist.get_rank(group) if dist.is_initialized() else 0
     rows = q.shape[0]
     dev = q.device
-    lo, hi = kv_range(rank, world, n_tokens, causal_rows)
+    lo, hi = kv_range(rank, world, n_tokens, causal_rows, shares)
     assert k_fp8_local.shape[0] == hi - lo, "local K does not match this rank's range"
     lens = local_rows(row_end, lo, hi)
     zeros = torch.zeros_like(lens)

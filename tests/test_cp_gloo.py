@@ -109,12 +109,13 @@ def _worker(rank, world, port, mode, variant, q):
 
         w = make_ragged(23, 2600, heads=32, seed=11)  # same seed on every rank: replicated q
         N = w["k_fp8"].shape[0]
-        cr = 23 if variant == "balanced" else 0
-        lo, hi = kv_range(rank, world, N, causal_rows=cr)
+        cr = 23 if variant in ("balanced", "weighted") else 0
+        shares = [1.0 + 0.5 * r for r in range(world)] if variant == "weighted" else None  # unequal GPU rates
+        lo, hi = kv_range(rank, world, N, causal_rows=cr, shares=shares)
         ops = {"miss": MissOps, "overflow": OverflowOps}.get(variant, OracleOps)()
         out = cp_prefill_topk(w["q"], w["k_fp8"][lo:hi].contiguous(), w["k_scale"][lo:hi].contiguous(),
                               w["weights"], w["row_end"], N, mode=mode, ops=ops, bounded=variant != "exact",
-                              causal_rows=cr)
+                              causal_rows=cr, shares=shares)
         q.put((rank, out.numpy()))
     finally:
         dist.destroy_process_group()
@@ -124,7 +125,7 @@ def _worker(rank, world, port, mode, variant, q):
                                                 (2, "rowshard", "exact"), (2, "allgather", "exact"),
                                                 (3, "rowshard", "bounded"), (2, "rowshard", "miss"),
                                                 (3, "rowshard", "overflow"), (3, "rowshard", "balanced"),
-                                                (2, "rowshard", "short_lists")])
+                                                (2, "rowshard", "short_lists"), (3, "rowshard", "weighted")])
 def test_cp_driver_equals_single_range(world, mode, variant):
     """Every rank's result equals the single-range top-k: the bounded exchange, the exact one,
     and the bounded exchange whose bound misses (too high) or overflows the lists (too low),
@@ -171,3 +172,33 @@ def test_cp_list_len_override_is_checked(monkeypatch, value, world, ok):
     else:
         with pytest.raises(ValueError):
             list_len(world)
+
+
+def test_kv_range_shares():
+    """Weighted ranges tile [0, N) in order with 16-token boundaries; without causal rows the token
+    counts follow the weights, with causal rows the visible pairs do."""
+    from hcu_ops.cp import kv_range
+
+    N, R = 131072, 16384
+    shares = [1.0, 1.2, 0.9, 1.1, 1.0, 0.8, 1.3, 1.0]
+    for cr in (0, R):
+        rng = [kv_range(r, 8, N, causal_rows=cr, shares=shares) for r in range(8)]
+        assert rng[0][0] == 0 and rng[-1][1] == N
+        assert all(rng[i][1] == rng[i + 1][0] for i in range(7))
+        assert all(a % 16 == 0 for a, _ in rng)
+
+        def pairs(x):  # visible pairs in [0, x) for rows seeing [0, N - R + i + 1)
+            if not cr:
+                return x
+            p = N - R
+            if x <= p:
+                return R * x
+            d = x - p
+            return R * p + d * (d + 1) // 2 + (R - d) * d
+
+        tot = pairs(N)
+        for r, (a, b) in enumerate(rng):
+            assert abs((pairs(b) - pairs(a)) / tot - shares[r] / sum(shares)) < 2e-3
+    assert kv_range(3, 8, N, causal_rows=R) == kv_range(3, 8, N, causal_rows=R, shares=[2.0] * 8)
+    with pytest.raises(ValueError):
+        kv_range(0, 2, N, shares=[1.0, 0.0])
