@@ -10,8 +10,9 @@
 //   scales) -> bf16 [n, 128]; 8 lanes per token, 4 tokens per warp access.
 //
 // quant_store_index_k_kernel: the writer of that page layout: per token
-//   scale = max(amax, 1e-12) / 448 and fp8 e4m3 of x / scale (IEEE division,
-//   saturating round-to-nearest-even conversion), 8 lanes per token.
+//   scale = max(amax, 1e-12) / 448 and fp8 e4m3 of x / scale (the correctly
+//   rounded quotient, from one reciprocal per token and an FMA correction per
+//   value; saturating round-to-nearest-even conversion), 8 lanes per token.
 //
 // All issue every load of kUnroll tokens before the first store so that each
 // warp keeps several KB in flight (HBM latency x bandwidth per SM is ~40 KB).
@@ -103,7 +104,7 @@ __global__ __launch_bounds__(kDqThreads) void dequant_mla_kernel(const uint8_t* 
   }
 }
 
-__global__ __launch_bounds__(kDqThreads) void dequant_index_k_kernel(const uint8_t* __restrict__ kv,
+__global__ __launch_bounds__(kDqThreads, 1) void dequant_index_k_kernel(const uint8_t* __restrict__ kv,
                                                                      int64_t n_pages, int64_t page_stride,
                                                                      const int32_t* __restrict__ loc, int64_t n,
                                                                      uint16_t* __restrict__ out) {
@@ -142,28 +143,44 @@ __global__ __launch_bounds__(kDqThreads) void dequant_index_k_kernel(const uint8
 }
 
 
-// 16 values of one K row (fp32 or bf16) starting at p (16-byte aligned), as fp32.
+// The 16 values of one K row that a lane quantises, held as the raw words loaded (bf16: 8 words,
+// two values each; fp32: 16 words) and widened to fp32 on use (bf16 -> fp32 is exact: the bf16
+// bits are the high half of the fp32 word).
 template <bool kBf16>
-__device__ __forceinline__ void load16_k(const void* p, float (&v)[16]) {
-  if constexpr (kBf16) {
-    const uint4 a = ld_stream(p);
-    const uint4 b = ld_stream(static_cast<const uint8_t*>(p) + 16);
-    const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+struct Row16 {
+  static constexpr int kWords = kBf16 ? 8 : 16;
+  uint32_t w[kWords];
+  __device__ __forceinline__ void load(const void* p) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      v[2 * i] = __uint_as_float(w[i] << 16);  // bf16 -> fp32 is exact: the high half of the fp32 word
-      v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
-    }
-  } else {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < kWords / 4; ++i) {
       const uint4 a = ld_stream(static_cast<const uint8_t*>(p) + 16 * i);
-      v[4 * i] = __uint_as_float(a.x);
-      v[4 * i + 1] = __uint_as_float(a.y);
-      v[4 * i + 2] = __uint_as_float(a.z);
-      v[4 * i + 3] = __uint_as_float(a.w);
+      w[4 * i] = a.x;
+      w[4 * i + 1] = a.y;
+      w[4 * i + 2] = a.z;
+      w[4 * i + 3] = a.w;
     }
   }
+  __device__ __forceinline__ float operator[](int j) const {
+    if constexpr (kBf16) return __uint_as_float((j & 1) ? (w[j >> 1] & 0xFFFF0000u) : (w[j >> 1] << 16));
+    return __uint_as_float(w[j]);
+  }
+};
+
+// x / s rounded to nearest even, as the fp8 conversion needs it, from rc = RN(1/s) (one correctly
+// rounded reciprocal per token instead of 16 divisions per lane): q = RN(x * rc) is within one ulp
+// of x / s, the remainder x - q * s is exact in one FMA, and RN(q + rem * rc) is the correctly
+// rounded quotient (Markstein's correction theorem: P. Markstein, "Computation of elementary
+// functions on the IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990; also
+// Muller et al., Handbook of Floating-Point Arithmetic, ch. 4) while the quotient is a normal
+// number.  Below 2^-11 the fp8 e4m3 conversion gives a zero of the quotient's sign whatever the
+// low bits, and q already has that sign, so q is used there (this also covers s = inf: rc = 0).
+// Bit-identical to IEEE division followed by the fp8 conversion (tested against the oracle's
+// numpy division, fp8 rounding midpoints included).
+__device__ __forceinline__ float div_rn_by(float x, float s, float rc) {
+  const float q = x * rc;
+  const float rem = fmaf(-q, s, x);
+  const float q2 = fmaf(rem, rc, q);
+  return fabsf(q) < 0x1p-11f ? q : q2;
 }
 
 template <bool kBf16>
@@ -180,14 +197,14 @@ __global__ __launch_bounds__(kDqThreads) void quant_store_index_k_kernel(const v
   const int64_t n_warps = (static_cast<int64_t>(gridDim.x) * kDqThreads) >> 5;
   const int64_t n_slots = n_pages * kPage;
   for (int64_t t0 = warp * 4 * kIdxUnroll; t0 < n; t0 += n_warps * 4 * kIdxUnroll) {
-    float v[kIdxUnroll][16];
+    Row16<kBf16> v[kIdxUnroll];
     int64_t l[kIdxUnroll];
 #pragma unroll
     for (int u = 0; u < kIdxUnroll; ++u) {
       const int64_t t = t0 + 4 * u + sub;
       const int64_t tt = t < n ? t : n - 1;  // a full 4-token group of loads; the stores check t
       l[u] = t < n ? static_cast<int64_t>(__ldg(loc + t)) : -1;
-      load16_k<kBf16>(static_cast<const uint8_t*>(k) + tt * k_stride_bytes + 16 * kElem * part, v[u]);
+      v[u].load(static_cast<const uint8_t*>(k) + tt * k_stride_bytes + 16 * kElem * part);
     }
 #pragma unroll
     for (int u = 0; u < kIdxUnroll; ++u) {
@@ -200,14 +217,16 @@ __global__ __launch_bounds__(kDqThreads) void quant_store_index_k_kernel(const v
       amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
       amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
       const float scale = __fdiv_rn(fmaxf(amax, 1e-12f), 448.f);
+      const float rc = __frcp_rn(scale);
       uint32_t w[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const __nv_fp8x2_storage_t lo2 = __nv_cvt_float2_to_fp8x2(
-            make_float2(__fdiv_rn(v[u][4 * i], scale), __fdiv_rn(v[u][4 * i + 1], scale)), __NV_SATFINITE, __NV_E4M3);
-        const __nv_fp8x2_storage_t hi2 = __nv_cvt_float2_to_fp8x2(
-            make_float2(__fdiv_rn(v[u][4 * i + 2], scale), __fdiv_rn(v[u][4 * i + 3], scale)), __NV_SATFINITE,
+            make_float2(div_rn_by(v[u][4 * i], scale, rc), div_rn_by(v[u][4 * i + 1], scale, rc)), __NV_SATFINITE,
             __NV_E4M3);
+        const __nv_fp8x2_storage_t hi2 = __nv_cvt_float2_to_fp8x2(
+            make_float2(div_rn_by(v[u][4 * i + 2], scale, rc), div_rn_by(v[u][4 * i + 3], scale, rc)),
+            __NV_SATFINITE, __NV_E4M3);
         w[i] = static_cast<uint32_t>(lo2) | (static_cast<uint32_t>(hi2) << 16);
       }
       if (t >= n) continue;
@@ -223,10 +242,13 @@ __global__ __launch_bounds__(kDqThreads) void quant_store_index_k_kernel(const v
   }
 }
 
-int grid_for(int64_t warps_needed) {
+// Blocks for `warps_needed` warps of work, at most cap_per_sm per SM (the kernels loop over the
+// rest).  The indexer-K dequant runs best at 3 per SM over a grid-stride loop (measured on config 3:
+// 12.0 us against 13.1 with every block its own warp's work at 5 resident per SM).
+int grid_for(int64_t warps_needed, int cap_per_sm = 8) {
   const int64_t per_block = kDqThreads / 32;
   int64_t blocks = (warps_needed + per_block - 1) / per_block;
-  const int64_t cap = static_cast<int64_t>(sm_count()) * 8;  // 8 x 256 threads resident per SM
+  const int64_t cap = static_cast<int64_t>(sm_count()) * cap_per_sm;
   if (blocks > cap) blocks = cap;
   return static_cast<int>(blocks < 1 ? 1 : blocks);
 }
@@ -258,7 +280,7 @@ extern "C" int hcu_dequant_index_k_paged(const uint8_t* kv_cache, int64_t n_page
   if (n_tokens == 0) return HCU_OK;
   if (!kv_cache || !token_loc || !out) return HCU_ERR_ARG;
   if ((reinterpret_cast<uintptr_t>(kv_cache) | reinterpret_cast<uintptr_t>(out)) % 16 != 0) return HCU_ERR_ARG;
-  const int grid = grid_for((n_tokens + 4 * kIdxUnroll - 1) / (4 * kIdxUnroll));
+  const int grid = grid_for((n_tokens + 4 * kIdxUnroll - 1) / (4 * kIdxUnroll), 3);
   dequant_index_k_kernel<<<grid, kDqThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       kv_cache, n_pages, page_stride, token_loc, n_tokens, out);
   return launch_status();

@@ -37,6 +37,46 @@ def test_kstore_bit_exact(hcu, dev, dtype, n):
     assert np.array_equal(pool.view(n_pages, -1).cpu().numpy(), ref)
 
 
+def _midpoint_rows(n_rows, seed):
+    """fp32 rows whose quotients x / scale sit on and beside the rounding midpoints of fp8 e4m3:
+    per row an awkward amax (so an inexact scale), then x = fl(m * scale) and its two fp32
+    neighbours for midpoints m between consecutive e4m3 values, both signs."""
+    rng = np.random.default_rng(seed)
+    e4 = torch.arange(0, 127, dtype=torch.uint8).view(torch.float8_e4m3fn).float().numpy()
+    mids = ((e4[:-1] + e4[1:]) / 2)
+    mids = mids[mids < 440.0].astype(np.float32)
+    rows = np.zeros((n_rows, 128), np.float32)
+    for r in range(n_rows):
+        amax = np.float32(rng.uniform(0.5, 2.0) * 2.0 ** rng.integers(-30, 40))
+        scale = np.float32(np.maximum(amax, np.float32(1e-12)) / np.float32(448.0))
+        m = rng.choice(mids, 42) * rng.choice(np.array([-1.0, 1.0], np.float32), 42)
+        x = (m.astype(np.float32) * scale).astype(np.float32)
+        v = np.concatenate([x, np.nextafter(x, np.float32(np.inf)), np.nextafter(x, np.float32(-np.inf))])
+        rows[r, 0] = amax
+        rows[r, 1:127] = v[:126]
+        rows[r, 127] = -amax
+    return torch.from_numpy(rows)
+
+
+@pytest.mark.parametrize("kind", ["midpoints", "wide_exponents"])
+def test_kstore_division_edges(hcu, dev, kind):
+    """The quotient x / scale is formed from one reciprocal per token and an FMA correction: bit
+    equal to the oracle's IEEE division on values at and beside every e4m3 rounding midpoint, and on
+    values spread over 2^-60 .. 2^60 within a row."""
+    n = 2048
+    if kind == "midpoints":
+        k = _midpoint_rows(n, seed=5)
+    else:
+        g = torch.Generator().manual_seed(6)
+        k = torch.randn(n, 128, generator=g) * torch.exp2(torch.randint(-60, 61, (n, 128), generator=g).float())
+    n_pages = n // 64
+    loc = torch.arange(n, dtype=torch.int32)
+    ref = O.quant_store_index_k(k.numpy(), loc.numpy(), np.zeros((n_pages, 64 * 132), np.uint8))
+    pool = torch.zeros(n_pages, 64, 1, 132, dtype=torch.uint8, device=dev)
+    hcu.quant_store_index_k(k.to(dev), loc.to(dev), pool)
+    assert np.array_equal(pool.view(n_pages, -1).cpu().numpy(), ref)
+
+
 def test_kstore_strided_rows(hcu, dev):
     n, n_pages = 200, 8
     big = _rows(n, seed=9, dtype=torch.float32)
