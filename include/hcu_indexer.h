@@ -236,6 +236,23 @@ int hcu_sparse_mask_topk_transform_split(const float* score, int64_t rows, int64
                                          void* workspace, int64_t workspace_bytes, int32_t* dst,
                                          hcu_stream_t stream);
 
+/* List strategy for many rows (new; serves the same call as
+ * hcu_sparse_mask_topk_transform, sparse_mask_topk.cu:896-908, with a caller
+ * workspace like the split variants').  One warp per row derives a bound from
+ * 2048 samples of the row; one warp per row streams the row into a list of the
+ * tokens at or above it; the top 2048 of each list are written in the canonical
+ * order; a row whose list cannot prove exactness is rewritten by the plain
+ * kernel, launched last and predicated per row.  Same arguments and result as
+ * hcu_sparse_mask_topk_transform; width <= 131072; workspace 256-byte aligned,
+ * at least hcu_sparse_mask_topk_transform_lists_workspace_bytes(rows, width)
+ * (about 64 KiB per row), no initial contents needed. */
+int64_t hcu_sparse_mask_topk_transform_lists_workspace_bytes(int64_t rows, int64_t width);
+int hcu_sparse_mask_topk_transform_lists(const float* score, int64_t rows, int64_t width,
+                                         int64_t score_stride, const int16_t* mask, int64_t mask_stride,
+                                         const int32_t* lengths, const int32_t* page_table,
+                                         int64_t pt_stride, int64_t topk, void* workspace,
+                                         int64_t workspace_bytes, int32_t* dst, hcu_stream_t stream);
+
 /* Split variant whose pass 1 was built by hcu_mqa_logits_hist(hist_lens=lengths)
  * into zws (replaces _C.sparse_mask_topk_transform_split_pre, sparse_mask_topk.cu:986-1051). */
 int hcu_sparse_mask_topk_transform_split_pre(const float* score, int64_t rows, int64_t width,

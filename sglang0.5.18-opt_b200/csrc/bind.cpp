@@ -73,6 +73,29 @@ torch::Tensor sparse_mask_topk_transform(const torch::Tensor& score, const torch
   return dst;
 }
 
+// List strategy for many rows (a warp streams each row into a short candidate list; same result).
+torch::Tensor sparse_mask_topk_transform_lists(const torch::Tensor& score, const torch::Tensor& nonzero_mask,
+                                               const torch::Tensor& lengths, const torch::Tensor& page_table_size_1,
+                                               const torch::Tensor& cu_seqlens_q, int64_t topk) {
+  check_topk_inputs(score, nonzero_mask, lengths, page_table_size_1, cu_seqlens_q, topk);
+  TORCH_CHECK(score.size(1) <= 131072, "sparse_mask_topk_transform_lists: width above 131072");
+  const c10::cuda::CUDAGuard guard(score.device());
+  const int64_t rows = score.size(0);
+  auto dst = torch::empty({rows, kTopK}, score.options().dtype(at::kInt));
+  if (rows == 0) return dst;
+  const int64_t wsb = hcu_sparse_mask_topk_transform_lists_workspace_bytes(rows, score.size(1));
+  TORCH_CHECK(wsb > 0, "sparse_mask_topk_transform_lists: bad shape");
+  auto ws = torch::empty({wsb}, score.options().dtype(at::kByte));
+  check_status(hcu_sparse_mask_topk_transform_lists(ptr<const float>(score), rows, score.size(1), score.stride(0),
+                                                    ptr<const int16_t>(nonzero_mask), nonzero_mask.stride(0),
+                                                    ptr<const int32_t>(lengths),
+                                                    ptr<const int32_t>(page_table_size_1),
+                                                    page_table_size_1.stride(0), topk, ws.data_ptr(), wsb,
+                                                    ptr<int32_t>(dst), cur_stream()),
+               "sparse_mask_topk_transform_lists");
+  return dst;
+}
+
 torch::Tensor sparse_mask_topk_transform_split(const torch::Tensor& score, const torch::Tensor& nonzero_mask,
                                                const torch::Tensor& lengths, const torch::Tensor& page_table_size_1,
                                                const torch::Tensor& cu_seqlens_q, int64_t topk, int64_t max_splits) {
@@ -554,6 +577,8 @@ int64_t read_device_status(bool clear) {
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sparse_mask_topk_transform", &sparse_mask_topk_transform,
         "Exact top-2048 + page-table transform over sparse-mask MQA logits");
+  m.def("sparse_mask_topk_transform_lists", &sparse_mask_topk_transform_lists,
+        "top-2048 + page-table transform through per-row candidate lists (many rows)");
   m.def("sparse_mask_topk_transform_split", &sparse_mask_topk_transform_split,
         "Same as sparse_mask_topk_transform; few rows may be split over several CTAs");
   m.def("sparse_mask_topk_transform_split_pre", &sparse_mask_topk_transform_split_pre,

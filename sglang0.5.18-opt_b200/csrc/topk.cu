@@ -639,7 +639,7 @@ __global__ __launch_bounds__(kT, 1024 / kT) void topk_row_kernel(
     const float* __restrict__ score, int64_t score_stride, int width, const int16_t* __restrict__ mask,
     int64_t mask_stride, const int32_t* __restrict__ lengths, const int32_t* __restrict__ pt, int64_t pt_stride,
     int32_t* __restrict__ dst, uint32_t* __restrict__ dst_keys, const int32_t* __restrict__ pre_ws, int rows,
-    int splits, const int32_t* __restrict__ run_if) {
+    int splits, const int32_t* __restrict__ run_if, int run_if_stride) {
   constexpr int kTkThreads = kT;
   constexpr int kCandCap = Tk<kT>::kCandCap;
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -647,7 +647,11 @@ __global__ __launch_bounds__(kT, 1024 / kT) void topk_row_kernel(
   // launched with programmatic stream serialization: wait for the previous kernel (the logits that
   // this reads) to complete before the first global read; a no-op after an ordinary dependency
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  if (run_if != nullptr && __ldcg(run_if) == 0) return;  // predicated launch: nothing to do this time
+  // predicated launch (one word for every row, or a word per row): nothing to do this time
+  if (run_if != nullptr &&
+      __ldcg(run_if + static_cast<int64_t>(kSplit ? static_cast<int>(blockIdx.x) / splits : blockIdx.x) *
+                          run_if_stride) == 0)
+    return;
   const int row = kSplit ? static_cast<int>(blockIdx.x) / splits : static_cast<int>(blockIdx.x);
   const int rank = kSplit ? static_cast<int>(blockIdx.x) % splits : 0;
   const int tid = threadIdx.x;
@@ -915,7 +919,7 @@ template <int kT, bool kVec, bool kSorted>
 void launch_rows_t(const float* score, int rows, int width, int64_t score_stride, const int16_t* mask,
                    int64_t mask_stride, const int32_t* lengths, const int32_t* pt, int64_t pt_stride, int32_t* dst,
                    uint32_t* dst_keys, const int32_t* pre_ws, cudaStream_t stream, int splits,
-                   const int32_t* run_if = nullptr) {
+                   const int32_t* run_if = nullptr, int run_if_stride = 0) {
   const size_t smem = sizeof(TopkSmem<kT>);
   if (kSorted || splits <= 1) {
     // programmatic stream serialization: the grid may be scheduled while the previous kernel drains
@@ -932,7 +936,7 @@ void launch_rows_t(const float* score, int rows, int width, int64_t score_stride
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     cudaLaunchKernelEx(&cfg, kern, score, score_stride, width, mask, mask_stride, lengths, pt, pt_stride, dst,
-                       dst_keys, pre_ws, rows, 1, run_if);
+                       dst_keys, pre_ws, rows, 1, run_if, run_if_stride);
     return;
   }
   if constexpr (!kSorted) launch_split<kT, kVec>(score, rows, width, score_stride, mask, mask_stride, lengths, pt,
@@ -993,32 +997,32 @@ void launch_split(const float* score, int rows, int width, int64_t score_stride,
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cudaLaunchKernelEx(&cfg, kern, score, score_stride, width, mask, mask_stride, lengths, pt, pt_stride, dst, dst_keys,
-                     pre_ws, rows, splits, static_cast<const int32_t*>(nullptr));
+                     pre_ws, rows, splits, static_cast<const int32_t*>(nullptr), 0);
 }
 
 template <int kT>
 void launch_rows_sized(const float* score, int r, int w, int64_t score_stride, const int16_t* mask,
                        int64_t mask_stride, const int32_t* lengths, const int32_t* pt, int64_t pt_stride, int32_t* dst,
                        uint32_t* dst_keys, const int32_t* pre_ws, cudaStream_t stream, bool vec, bool sorted,
-                       int splits, const int32_t* run_if) {
+                       int splits, const int32_t* run_if, int run_if_stride) {
   if (vec && !sorted)
     launch_rows_t<kT, true, false>(score, r, w, score_stride, mask, mask_stride, lengths, pt, pt_stride, dst, dst_keys,
-                                   pre_ws, stream, splits, run_if);
+                                   pre_ws, stream, splits, run_if, run_if_stride);
   else if (vec)
     launch_rows_t<kT, true, true>(score, r, w, score_stride, mask, mask_stride, lengths, pt, pt_stride, dst, dst_keys,
-                                  pre_ws, stream, splits, run_if);
+                                  pre_ws, stream, splits, run_if, run_if_stride);
   else if (!sorted)
     launch_rows_t<kT, false, false>(score, r, w, score_stride, mask, mask_stride, lengths, pt, pt_stride, dst,
-                                    dst_keys, pre_ws, stream, splits, run_if);
+                                    dst_keys, pre_ws, stream, splits, run_if, run_if_stride);
   else
     launch_rows_t<kT, false, true>(score, r, w, score_stride, mask, mask_stride, lengths, pt, pt_stride, dst, dst_keys,
-                                   pre_ws, stream, splits, run_if);
+                                   pre_ws, stream, splits, run_if, run_if_stride);
 }
 
 int launch_rows(const float* score, int64_t rows, int64_t width, int64_t score_stride, const int16_t* mask,
                 int64_t mask_stride, const int32_t* lengths, const int32_t* pt, int64_t pt_stride, int32_t* dst,
                 uint32_t* dst_keys, const int32_t* pre_ws, cudaStream_t stream, bool sorted = false, int splits = 1,
-                const int32_t* run_if = nullptr) {
+                const int32_t* run_if = nullptr, int run_if_stride = 0) {
   const int w = static_cast<int>(width);
   const int r = static_cast<int>(rows);
   const bool vec = use_vec(score, width, score_stride);
@@ -1028,10 +1032,10 @@ int launch_rows(const float* score, int64_t rows, int64_t width, int64_t score_s
   const int64_t part = (width + splits - 1) / splits;
   if (part <= kNarrowWidth || (rows >= 2 * static_cast<int64_t>(sm_count()) && part <= kManyRowsWidth))
     launch_rows_sized<512>(score, r, w, score_stride, mask, mask_stride, lengths, pt, pt_stride, dst, dst_keys, pre_ws,
-                           stream, vec, sorted, splits, run_if);
+                           stream, vec, sorted, splits, run_if, run_if_stride);
   else
     launch_rows_sized<1024>(score, r, w, score_stride, mask, mask_stride, lengths, pt, pt_stride, dst, dst_keys,
-                            pre_ws, stream, vec, sorted, splits, run_if);
+                            pre_ws, stream, vec, sorted, splits, run_if, run_if_stride);
   return launch_status();
 }
 
@@ -1583,7 +1587,7 @@ template <int kT>
 __global__ __launch_bounds__(kT, 1024 / kT) void fused_select_kernel(
     const int2* __restrict__ cand, const int32_t* __restrict__ cnt, int cap, const int32_t* __restrict__ row_end,
     int width, const int32_t* __restrict__ bounds, int all_len, const int32_t* __restrict__ pt, int64_t pt_stride,
-    int32_t* __restrict__ dst, int32_t* __restrict__ flag) {
+    int32_t* __restrict__ dst, int32_t* __restrict__ flag, int flag_per_row) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   FusedSelSmem<kT>& sm = *reinterpret_cast<FusedSelSmem<kT>*>(smem_raw);
   const int row = blockIdx.x;
@@ -1594,15 +1598,24 @@ __global__ __launch_bounds__(kT, 1024 / kT) void fused_select_kernel(
   len = len < 0 ? 0 : (len > width ? width : len);
   const int32_t* src = pt + static_cast<int64_t>(row) * pt_stride;
   int32_t* out = dst + static_cast<int64_t>(row) * kTopK;
+  // flag_per_row: every row's word of flag is written (1: the row is left to the exact path), else
+  // one word for the call, raised by any failing row
   if (len <= kTopK) {
     for (int i = tid; i < kTopK; i += kT) out[i] = i < len ? src[i] : -1;
+    if (flag_per_row && tid == 0) flag[row] = 0;
     return;
   }
-  const int n = __ldg(cnt + row);
+  const int n = __ldcg(cnt + row);
   if (n > cap || n < kTopK || n > kFusedCap) {  // incomplete list or a bound above the threshold
-    if (tid == 0) atomicOr(flag, 1);
+    if (tid == 0) {
+      if (flag_per_row)
+        flag[row] = 1;
+      else
+        atomicOr(flag, 1);
+    }
     return;
   }
+  if (flag_per_row && tid == 0) flag[row] = 0;
   const uint32_t lo = len <= all_len ? 0u : static_cast<uint32_t>(__ldg(bounds + row)) ^ kZeroKey;
   const int nw = (len + 31) >> 5;
   uint32_t* abm = sm.bm;       // tokens above the threshold
@@ -1666,6 +1679,200 @@ __global__ __launch_bounds__(kT, 1024 / kT) void fused_select_kernel(
   }
 }
 
+// ---------------------------------------------------------------------------
+// List top-k for many rows (at least two rows per SM: prefill chunks, the
+// one-GPU context-parallel case).  The block-per-row kernel keeps two rows in
+// flight per SM and its per-row latency bounds it; here the row stream is
+// split from the select:
+//   1. list_bound_kernel, one warp per row: kListSamples samples of the row
+//      (evenly spaced groups of 4 consecutive tokens) and the sample key of
+//      rank t + 5 sqrt(t) + 5, t = kTopK * kListSamples / len the expected
+//      sample rank of the row's threshold, as the row's bound lo;
+//   2. list_collect_kernel, one warp per row: streams the row and appends
+//      every visible token with key >= lo, as (key, token), to the row's list
+//      (rows of at most all_len tokens list every token);
+//   3. fused_select_kernel: the top kTopK of each list in the canonical order,
+//      with a word per row telling whether the list proved exactness;
+//   4. the block-per-row kernel, predicated per row on those words, rewrites
+//      the rows whose list missed or overflowed.
+// The stream runs with tens of rows in flight per SM, so the pass reads the
+// scores at close to the HBM rate; the select reads only the short lists.
+// ---------------------------------------------------------------------------
+constexpr int kListSamples = 2048;
+constexpr int kListBoundWarps = 8;
+constexpr int kListAllLen = 4096;  // rows of at most this many tokens list every token
+
+struct __align__(16) ListBoundSmem {
+  uint32_t k[kListBoundWarps][kListSamples];
+  alignas(16) int h[kListBoundWarps][256];
+  int res[kListBoundWarps][4];
+};
+
+template <bool kVec>
+__global__ __launch_bounds__(kListBoundWarps * 32) void list_bound_kernel(
+    const float* __restrict__ score, int64_t score_stride, int width, const int16_t* __restrict__ mask,
+    int64_t mask_stride, const int32_t* __restrict__ lengths, int rows, int32_t* __restrict__ bounds) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  ListBoundSmem& sm = *reinterpret_cast<ListBoundSmem*>(smem_raw);
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int lane = threadIdx.x & 31;
+  const int w = threadIdx.x >> 5;
+  const int row = blockIdx.x * kListBoundWarps + w;
+  if (row >= rows) return;  // whole warps; no block barrier below
+  int len = __ldg(lengths + row);
+  len = len < 0 ? 0 : (len > width ? width : len);
+  uint32_t v = 0u;  // rows listed whole ignore it
+  if (len > kListAllLen) {
+    const float t = static_cast<float>(kTopK) * static_cast<float>(kListSamples) / static_cast<float>(len);
+    const int r_lo = static_cast<int>(ceilf(t + 5.f * sqrtf(t) + 5.f));  // < kListSamples for len > kListAllLen
+    const float* vals = score + static_cast<int64_t>(row) * score_stride;
+    const int16_t* mrow = mask + static_cast<int64_t>(row) * mask_stride;
+    uint32_t* ks = sm.k[w];
+    // kListSamples / 32 evenly spaced blocks of 32 consecutive tokens (one 128-byte line each, so
+    // the sample reads stay a small share of the row's bytes); 8 lanes per block, 4 tokens a lane
+    constexpr int kGroups = kListSamples / 4;
+    constexpr int kBlocks = kListSamples / 32;
+    const float stride_b = static_cast<float>(len) / static_cast<float>(kBlocks);
+    const int blast = (len - 32) & ~31;
+    uint32_t kmax = 0u, kmin = 0xFFFFFFFFu;
+#pragma unroll 4
+    for (int g = lane; g < kGroups; g += 32) {
+      const int blk = g >> 3;
+      const int i = min(blast, static_cast<int>((static_cast<float>(blk) + 0.5f) * stride_b) & ~31) + 4 * (g & 7);
+      const uint32_t mb = static_cast<uint32_t>(static_cast<uint16_t>(__ldg(mrow + (i >> 4)))) >> (i & 15);
+      float f[4];
+      if constexpr (kVec) {
+        const float4 q = __ldg(reinterpret_cast<const float4*>(vals + i));
+        f[0] = q.x; f[1] = q.y; f[2] = q.z; f[3] = q.w;
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) f[e] = __ldg(vals + i + e);
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const uint32_t k = ((mb >> e) & 1u) ? key_of(f[e]) : kZeroKey;
+        ks[4 * g + e] = k;
+        kmax = k > kmax ? k : kmax;
+        kmin = k < kmin ? k : kmin;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      kmax = max(kmax, __shfl_xor_sync(0xffffffffu, kmax, o));
+      kmin = min(kmin, __shfl_xor_sync(0xffffffffu, kmin, o));
+    }
+    // the r_lo-th largest key: a radix select over u = key - kmin, 8-bit digits from the top bit
+    // of kmax - kmin (digits of the raw key put nearly every sample of a row in one or two bins)
+    const uint32_t span = kmax - kmin;
+    const int d = span ? 31 - __clz(span) : 0;
+    uint32_t pre = 0u;
+    int need = r_lo;
+    int* h = sm.h[w];
+    for (int s = d - 7;; s -= 8) {
+      const int sh = s > 0 ? s : 0;
+      const int nb = s + 8 - sh;
+      const uint32_t dm = (1u << nb) - 1u;
+      for (int i = lane; i < 256; i += 32) h[i] = 0;
+      __syncwarp();
+      for (int j = lane; j < kListSamples; j += 32) {
+        const uint32_t u = ks[j] - kmin;
+        if ((static_cast<uint64_t>(u) >> (sh + nb)) == pre) atomicAdd(&h[(u >> sh) & dm], 1);
+      }
+      __syncwarp();
+      warp_find<256>(h, need, sm.res[w]);
+      __syncwarp();
+      pre = (pre << nb) | static_cast<uint32_t>(sm.res[w][0]);
+      need -= sm.res[w][1];
+      __syncwarp();
+      if (sh == 0) break;
+    }
+    v = kmin + pre;
+  }
+  if (lane == 0) bounds[row] = static_cast<int32_t>(v ^ kZeroKey);
+}
+
+template <bool kVec>
+__global__ __launch_bounds__(256) void list_collect_kernel(
+    const float* __restrict__ score, int64_t score_stride, int width, const int16_t* __restrict__ mask,
+    int64_t mask_stride, const int32_t* __restrict__ lengths, const int32_t* __restrict__ bounds, int rows,
+    int2* __restrict__ lists, int cap, int32_t* __restrict__ cnt) {
+  __shared__ __align__(16) uint32_t stage[256 * kLaneTok];  // each lane's 16 words of the current chunk
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int lane = threadIdx.x & 31;
+  const int warp_in_cta = threadIdx.x >> 5;
+  const int n_warps = static_cast<int>((gridDim.x * blockDim.x) >> 5);
+  for (int row = static_cast<int>((blockIdx.x * blockDim.x + threadIdx.x) >> 5); row < rows; row += n_warps) {
+    int len = __ldg(lengths + row);
+    len = len < 0 ? 0 : (len > width ? width : len);
+    if (len <= kTopK) {  // the select writes these rows as the identity
+      if (lane == 0) cnt[row] = 0;
+      continue;
+    }
+    const uint32_t lo = len <= kListAllLen ? 0u : static_cast<uint32_t>(__ldg(bounds + row)) ^ kZeroKey;
+    // a positive bound: a token passes iff its mask bit is set and its raw bits, as a signed int,
+    // reach the bound's (the key order of positive floats), and its key is bits | sign bit
+    const bool pos = lo > kZeroKey;
+    const int lo_bits = static_cast<int>(lo & 0x7FFFFFFFu);
+    const float* vals = score + static_cast<int64_t>(row) * score_stride;
+    const int16_t* mrow = mask + static_cast<int64_t>(row) * mask_stride;
+    int2* lst = lists + static_cast<int64_t>(row) * cap;
+    int base = 0;  // uniform over the warp
+    constexpr int kStep = 2 * 32 * kLaneTok;  // tokens per warp iteration (4 KB of scores)
+    // the first two iterations' lines into L2, then each iteration prefetches the one two ahead:
+    // the loads that follow find their lines in L2 (no registers held for the prefetch)
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const int p = q * kStep + lane * 2 * kLaneTok;
+      if (p < len) asm volatile("prefetch.global.L2 [%0];" ::"l"(vals + p));
+    }
+    for (int c0 = 0; c0 < len; c0 += kStep) {
+      {
+        const int p = c0 + 2 * kStep + lane * 2 * kLaneTok;  // 128 bytes per lane
+        if (p < len) asm volatile("prefetch.global.L2 [%0];" ::"l"(vals + p));
+      }
+      uint32_t b[2][16], valid[2], mw[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u)
+        mw[u] = load16_raw<kVec>(vals, mrow, c0 + (u * 32 + lane) * kLaneTok, len, b[u], valid[u]);
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int i0 = c0 + (u * 32 + lane) * kLaneTok;
+        uint32_t hit = 0u;
+        if (pos) {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) hit |= (static_cast<int>(b[u][e]) >= lo_bits ? 1u : 0u) << e;
+          hit &= mw[u] & valid[u];
+        } else {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const uint32_t k = ((mw[u] >> e) & 1u) ? key_of(__uint_as_float(b[u][e])) : kZeroKey;
+            b[u][e] = k;
+            hit |= (((valid[u] >> e) & 1u) && k >= lo) ? (1u << e) : 0u;
+          }
+        }
+        const int c = __popc(hit);
+        const int inc = warp_incl_scan(c);
+        int at = base + inc - c;
+        base += __shfl_sync(0xffffffffu, inc, 31);
+        if (hit) {  // the lane's words through shared memory, read back at the set bits only
+          uint4* st4 = reinterpret_cast<uint4*>(stage + (warp_in_cta * 32 + lane) * kLaneTok);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) st4[q] = make_uint4(b[u][4 * q], b[u][4 * q + 1], b[u][4 * q + 2], b[u][4 * q + 3]);
+          const uint32_t* sw = stage + (warp_in_cta * 32 + lane) * kLaneTok;
+          const uint32_t kbit = pos ? kZeroKey : 0u;
+          do {
+            const int e = __ffs(hit) - 1;
+            hit &= hit - 1u;
+            if (at < cap) lst[at] = make_int2(static_cast<int>(sw[e] | kbit), i0 + e);
+            ++at;
+          } while (hit);
+        }
+      }
+    }
+    if (lane == 0) cnt[row] = base;
+  }
+}
+
 }  // namespace
 
 // Used by the logits translation unit for the hist_lens path: zeroes the
@@ -1673,9 +1880,20 @@ __global__ __launch_bounds__(kT, 1024 / kT) void fused_select_kernel(
 // histogram length; the logits kernel's epilogue then does pass 1.
 // Launchers of the fused prefill top-k (fused.cu): the list select, the exact
 // top-k predicated on the select's flag, and the sampled per-row bound.
+int launch_list_select(const int2* cand, const int32_t* cnt, int cap, const int32_t* row_end, int64_t rows,
+                       int64_t width, const int32_t* bounds, int all_len, const int32_t* pt, int64_t pt_stride,
+                       int32_t* dst, int32_t* flag, cudaStream_t stream, bool flag_per_row);
+
 int launch_fused_select(const int2* cand, const int32_t* cnt, int cap, const int32_t* row_end, int64_t rows,
                         int64_t width, const int32_t* bounds, int all_len, const int32_t* pt, int64_t pt_stride,
                         int32_t* dst, int32_t* flag, cudaStream_t stream) {
+  return launch_list_select(cand, cnt, cap, row_end, rows, width, bounds, all_len, pt, pt_stride, dst, flag, stream,
+                            false);
+}
+
+int launch_list_select(const int2* cand, const int32_t* cnt, int cap, const int32_t* row_end, int64_t rows,
+                       int64_t width, const int32_t* bounds, int all_len, const int32_t* pt, int64_t pt_stride,
+                       int32_t* dst, int32_t* flag, cudaStream_t stream, bool flag_per_row) {
   if (rows <= 0) return HCU_OK;
   if (width > kFusedMaxWidth || cap > kFusedCap) return HCU_ERR_ARG;
   constexpr int kT = 256;
@@ -1683,7 +1901,8 @@ int launch_fused_select(const int2* cand, const int32_t* cnt, int cap, const int
   cudaFuncSetAttribute(fused_select_kernel<kT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        static_cast<int>(sizeof(FusedSelSmem<kT>) + 2 * (kFusedMaxWidth / 32) * 4));
   fused_select_kernel<kT><<<static_cast<unsigned>(rows), kT, smem, stream>>>(
-      cand, cnt, cap, row_end, static_cast<int>(width), bounds, all_len, pt, pt_stride, dst, flag);
+      cand, cnt, cap, row_end, static_cast<int>(width), bounds, all_len, pt, pt_stride, dst, flag,
+      flag_per_row ? 1 : 0);
   return launch_status();
 }
 
@@ -1739,6 +1958,99 @@ extern "C" int hcu_sparse_mask_topk_transform(const float* score, int64_t rows, 
   if (st != HCU_OK || rows == 0) return st;
   return launch_rows(score, rows, width, score_stride, mask, mask_stride, lengths, page_table, pt_stride, dst,
                      nullptr, nullptr, reinterpret_cast<cudaStream_t>(stream));
+}
+
+namespace hcu {
+namespace {
+
+struct ListLayout {
+  int64_t bounds, cnt, fail, lists, total;
+};
+
+ListLayout list_layout(int64_t rows) {
+  auto al = [](int64_t x) { return (x + 255) / 256 * 256; };
+  ListLayout L{};
+  int64_t o = 0;
+  L.bounds = o;
+  o += al(rows * 4);
+  L.cnt = o;
+  o += al(rows * 4);
+  L.fail = o;
+  o += al(rows * 4);
+  L.lists = o;
+  o += al(rows * static_cast<int64_t>(kFusedCap) * 8);
+  L.total = o;
+  return L;
+}
+
+}  // namespace
+}  // namespace hcu
+
+extern "C" int64_t hcu_sparse_mask_topk_transform_lists_workspace_bytes(int64_t rows, int64_t width) {
+  if (rows < 0 || width < 0) return -1;
+  return hcu::list_layout(rows).total;
+}
+
+extern "C" int hcu_sparse_mask_topk_transform_lists(const float* score, int64_t rows, int64_t width,
+                                                    int64_t score_stride, const int16_t* mask, int64_t mask_stride,
+                                                    const int32_t* lengths, const int32_t* page_table,
+                                                    int64_t pt_stride, int64_t topk, void* workspace,
+                                                    int64_t workspace_bytes, int32_t* dst, hcu_stream_t stream) {
+  using namespace hcu;
+  int st = check_common(score, rows, width, score_stride, mask, mask_stride, lengths, page_table, pt_stride, topk,
+                        dst);
+  if (st != HCU_OK || rows == 0) return st;
+  if (width > kFusedMaxWidth) return HCU_ERR_ARG;
+  const ListLayout L = list_layout(rows);
+  if (!workspace || workspace_bytes < L.total || reinterpret_cast<uintptr_t>(workspace) % 256 != 0)
+    return HCU_ERR_ARG;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int32_t* bounds = reinterpret_cast<int32_t*>(ws + L.bounds);
+  int32_t* cnt = reinterpret_cast<int32_t*>(ws + L.cnt);
+  int32_t* fail = reinterpret_cast<int32_t*>(ws + L.fail);
+  int2* lists = reinterpret_cast<int2*>(ws + L.lists);
+  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int w = static_cast<int>(width);
+  const int r = static_cast<int>(rows);
+  const bool vec = use_vec(score, width, score_stride);
+  // the bound and the stream with programmatic stream serialization (each waits for the previous
+  // kernel before its first read)
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const size_t bsmem = sizeof(ListBoundSmem);
+  cfg.gridDim = dim3(static_cast<unsigned>((rows + kListBoundWarps - 1) / kListBoundWarps));
+  cfg.blockDim = dim3(kListBoundWarps * 32);
+  cfg.dynamicSmemBytes = bsmem;
+  if (vec) {
+    cudaFuncSetAttribute(list_bound_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bsmem));
+    cudaLaunchKernelEx(&cfg, list_bound_kernel<true>, score, score_stride, w, mask, mask_stride, lengths, r, bounds);
+  } else {
+    cudaFuncSetAttribute(list_bound_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(bsmem));
+    cudaLaunchKernelEx(&cfg, list_bound_kernel<false>, score, score_stride, w, mask, mask_stride, lengths, r, bounds);
+  }
+  if ((st = launch_status()) != HCU_OK) return st;
+  cfg.gridDim = dim3(static_cast<unsigned>((rows + 7) / 8));  // one warp per row
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = 0;
+  if (vec)
+    cudaLaunchKernelEx(&cfg, list_collect_kernel<true>, score, score_stride, w, mask, mask_stride, lengths,
+                       static_cast<const int32_t*>(bounds), r, lists, kFusedCap, cnt);
+  else
+    cudaLaunchKernelEx(&cfg, list_collect_kernel<false>, score, score_stride, w, mask, mask_stride, lengths,
+                       static_cast<const int32_t*>(bounds), r, lists, kFusedCap, cnt);
+  if ((st = launch_status()) != HCU_OK) return st;
+  if ((st = launch_list_select(lists, cnt, kFusedCap, lengths, rows, width, bounds, kListAllLen, page_table,
+                               pt_stride, dst, fail, s, true)) != HCU_OK)
+    return st;
+  // rows whose list could not prove exactness: the block-per-row kernel, predicated per row
+  return launch_rows(score, rows, width, score_stride, mask, mask_stride, lengths, page_table, pt_stride, dst, nullptr,
+                     nullptr, s, false, 1, fail, 1);
 }
 
 extern "C" int hcu_sparse_mask_topk_transform_split(const float* score, int64_t rows, int64_t width,

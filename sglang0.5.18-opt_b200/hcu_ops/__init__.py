@@ -33,6 +33,10 @@ SGLANG_DSA_FAST_DEQUANT_WARPS = int(os.environ.get("SGLANG_DSA_FAST_DEQUANT_WARP
 # CTAs when the batch leaves SMs idle; "single" keeps every row on one CTA.
 _TOPK_IMPL = os.environ.get("HCU_TOPK_IMPL", "split")
 _TOPK_SPLITS = int(os.environ.get("HCU_TOPK_SPLITS", "8"))
+# HCU_TOPK_LISTS: with at least two rows per SM (prefill chunks, one-GPU context parallelism) and
+# widths in (8192, 131072], a warp per row streams the row into a short candidate list above a
+# sampled bound and the lists are selected (same result); "0" keeps one CTA per row.
+_TOPK_LISTS = os.environ.get("HCU_TOPK_LISTS", "1") == "1"
 
 # Logits tuning knobs of the reference API.  The B200 kernel schedules its
 # persistent CTAs from the SM count and the lengths on the device, so
@@ -48,13 +52,17 @@ _N_CU = None
 SUPPORTED_HEADS = (32, 64)
 
 
-def _topk_splits(rows, width):
-    """Splits sparse_mask_topk_transform_split uses for [rows, width] scores
-    (``hcu_ops/hcu_ops/__init__.py:52-57`` of the reference)."""
+def _n_sm():
     global _N_CU
     if _N_CU is None:
         _N_CU = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
-    return min(max((width + 8191) // 8192, 1), _N_CU // max(rows, 1), min(_TOPK_SPLITS, 64))
+    return _N_CU
+
+
+def _topk_splits(rows, width):
+    """Splits sparse_mask_topk_transform_split uses for [rows, width] scores
+    (``hcu_ops/hcu_ops/__init__.py:52-57`` of the reference)."""
+    return min(max((width + 8191) // 8192, 1), _n_sm() // max(rows, 1), min(_TOPK_SPLITS, 64))
 
 
 def sparse_mask_topk_transform(score, nonzero_mask, lengths, page_table_size_1, cu_seqlens_q, topk=2048):
@@ -70,6 +78,9 @@ def sparse_mask_topk_transform(score, nonzero_mask, lengths, page_table_size_1, 
         if st[0] is score and st[1].data_ptr() == lengths.data_ptr() and st[1].shape == lengths.shape:
             return _C.sparse_mask_topk_transform_split_pre(score, nonzero_mask, lengths, page_table_size_1,
                                                            cu_seqlens_q, topk, _TOPK_SPLITS, st[2])
+    if _TOPK_LISTS and 8192 < score.shape[1] <= 131072 and score.shape[0] >= 2 * _n_sm():
+        return _C.sparse_mask_topk_transform_lists(score, nonzero_mask, lengths, page_table_size_1, cu_seqlens_q,
+                                                   topk)
     if _TOPK_IMPL == "single":
         return _C.sparse_mask_topk_transform(score, nonzero_mask, lengths, page_table_size_1, cu_seqlens_q, topk)
     return _C.sparse_mask_topk_transform_split(score, nonzero_mask, lengths, page_table_size_1, cu_seqlens_q,
