@@ -1663,20 +1663,29 @@ __global__ __launch_bounds__(kT, 1024 / kT) void fused_select_kernel(
   int ea = ex & 0xFFFF;
   int et = ex >> 16;
   const int remaining = kTopK - above;
+  // the output's tokens in the canonical order into the key array (the keys are no longer read),
+  // then every page-table entry at once (kTopK / kT independent loads a thread, not a chain)
+  int* const otok = reinterpret_cast<int*>(sm.cand_key);
   for (int i = i0; i < i1; ++i) {
     uint32_t a = abm[i];
     while (a) {
       const int b = __ffs(a) - 1;
       a &= a - 1u;
-      out[ea++] = __ldg(src + (i << 5) + b);
+      otok[ea++] = (i << 5) + b;
     }
     uint32_t t = tbm[i];
     while (t && et < remaining) {
       const int b = __ffs(t) - 1;
       t &= t - 1u;
-      out[above + et++] = __ldg(src + (i << 5) + b);
+      otok[above + et++] = (i << 5) + b;
     }
   }
+  __syncthreads();
+  int32_t v[kTopK / kT];
+#pragma unroll
+  for (int q = 0; q < kTopK / kT; ++q) v[q] = __ldg(src + otok[tid + q * kT]);
+#pragma unroll
+  for (int q = 0; q < kTopK / kT; ++q) out[tid + q * kT] = v[q];
 }
 
 // ---------------------------------------------------------------------------
