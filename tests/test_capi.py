@@ -202,3 +202,29 @@ def test_fused_prefill_workspace_and_argument_checks(lib):
     assert call(workspace=None) == HCU_ERR_ARG
     assert call(pt_stride=-1) == HCU_ERR_ARG
     assert call(rows=0) == HCU_OK
+
+
+def test_list_topk_workspace_and_argument_checks(lib):
+    """The many-row list top-k: its workspace query (about 64 KiB a row, 256-byte multiples) and
+    the checks it makes before launching anything."""
+    ws = lib.hcu_sparse_mask_topk_transform_lists_workspace_bytes
+    ws.restype = ctypes.c_int64
+    ws.argtypes = [ctypes.c_int64, ctypes.c_int64]
+    assert ws(-1, 10) == -1
+    assert ws(8192, 73728) >= 8192 * 8192 * 8
+    assert ws(8192, 73728) % 256 == 0
+    f = lib.hcu_sparse_mask_topk_transform_lists
+    f.restype = ctypes.c_int
+    p, i64 = ctypes.c_void_p(256), ctypes.c_int64
+
+    def call(rows=400, width=65536, topk=2048, wsb=None, workspace=p):
+        b = ws(rows, width) if wsb is None else wsb
+        return f(p, i64(rows), i64(width), i64(width), p, i64((width + 15) // 16), p, p, i64(width), i64(topk),
+                 workspace, i64(b), p, None)
+
+    assert call(topk=100) == HCU_ERR_ARG
+    assert call(width=131072 + 16) == HCU_ERR_ARG  # past the width the select's bitmaps cover
+    assert call(wsb=4096) == HCU_ERR_ARG           # workspace too small
+    assert call(workspace=None) == HCU_ERR_ARG
+    assert call(workspace=ctypes.c_void_p(272)) == HCU_ERR_ARG  # not 256-byte aligned
+    assert call(rows=0) == HCU_OK
