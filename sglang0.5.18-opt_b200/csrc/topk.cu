@@ -1467,24 +1467,127 @@ __device__ __noinline__ int filter_row(TopkSmem<kT>& sm, const float* __restrict
   return n;
 }
 
+// One row of the filter on one warp: the tokens of [0, len) with key >= lo, in token order, as (key,
+// page-table entry) into slots [0, cap) with key 0 / entry -1 pads -- the list filter_row writes
+// when it holds at most cap entries.  Lanes take 16 consecutive tokens, two chunks in flight; for a
+// positive lo the test is one signed compare of the raw bits.  `stage`: this warp's 32 x 16 words of
+// shared memory.  Returns the count (uniform); above cap nothing is padded and the caller runs
+// filter_row on the row instead (the list then takes the range's top entries and a marker).
+template <bool kVec>
+__device__ __forceinline__ int filter_row_warp(const float* __restrict__ vals, const int16_t* __restrict__ mrow,
+                                               const int32_t* __restrict__ src, int len, uint32_t lo, int cap,
+                                               uint32_t* __restrict__ ok, int32_t* __restrict__ og,
+                                               uint32_t* stage) {
+  const int lane = threadIdx.x & 31;
+  const bool pos = lo > kZeroKey;
+  const int lo_bits = static_cast<int>(lo & 0x7FFFFFFFu);
+  int n = 0;  // uniform over the warp
+  for (int c0 = 0; c0 < len; c0 += 2 * 32 * kLaneTok) {
+    uint32_t b[2][16], valid[2], mw[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+      mw[u] = load16_raw<kVec>(vals, mrow, c0 + (u * 32 + lane) * kLaneTok, len, b[u], valid[u]);
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int i0 = c0 + (u * 32 + lane) * kLaneTok;
+      uint32_t hit = 0u;
+      if (pos) {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) hit |= (static_cast<int>(b[u][e]) >= lo_bits ? 1u : 0u) << e;
+        hit &= mw[u] & valid[u];
+      } else {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const uint32_t k = ((mw[u] >> e) & 1u) ? key_of(__uint_as_float(b[u][e])) : kZeroKey;
+          b[u][e] = k;
+          hit |= (((valid[u] >> e) & 1u) && k >= lo) ? (1u << e) : 0u;
+        }
+      }
+      const int c = __popc(hit);
+      const int inc = warp_incl_scan(c);
+      int at = n + inc - c;
+      n += __shfl_sync(0xffffffffu, inc, 31);
+      if (hit && at < cap) {  // the lane's words through shared memory, read back at the set bits
+        uint4* st4 = reinterpret_cast<uint4*>(stage + lane * kLaneTok);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) st4[q] = make_uint4(b[u][4 * q], b[u][4 * q + 1], b[u][4 * q + 2], b[u][4 * q + 3]);
+        const uint32_t* sw = stage + lane * kLaneTok;
+        const uint32_t kbit = pos ? kZeroKey : 0u;
+        do {
+          const int e = __ffs(hit) - 1;
+          hit &= hit - 1u;
+          if (at < cap) {
+            ok[at] = sw[e] | kbit;
+            og[at] = __ldg(src + i0 + e);
+          }
+          ++at;
+        } while (hit);
+      }
+    }
+  }
+  if (n <= cap)
+    for (int i = n + lane; i < cap; i += 32) {
+      ok[i] = 0u;
+      og[i] = -1;
+    }
+  return n;
+}
+
+// Rows of a CTA per warp pass: at most this many (a bitmap of the rows whose list overflowed).
+constexpr int kFilterRowsPerCta = 4096;
+
 template <int kT, bool kVec>
 __global__ __launch_bounds__(kT, 1024 / kT) void cp_filter_kernel(
     const float* __restrict__ score, int64_t score_stride, int width, const int16_t* __restrict__ mask,
     int64_t mask_stride, const int32_t* __restrict__ lengths, const int32_t* __restrict__ pt, int64_t pt_stride,
     const int32_t* __restrict__ bounds, int cap, uint32_t* __restrict__ out_keys, int32_t* __restrict__ out_gidx,
-    int rows_per_block, int64_t block_stride, int32_t* __restrict__ counts, int32_t* __restrict__ flag) {
+    int rows_per_block, int64_t block_stride, int32_t* __restrict__ counts, int32_t* __restrict__ flag, int rows,
+    int warp_pass) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   TopkSmem<kT>& sm = *reinterpret_cast<TopkSmem<kT>*>(smem_raw);
-  const int row = blockIdx.x;
-  int len = __ldg(lengths + row);
-  len = len < 0 ? 0 : (len > width ? width : len);
-  const uint32_t lo = static_cast<uint32_t>(__ldg(bounds + row)) ^ kZeroKey;
-  const int64_t lo_off = (row / rows_per_block) * block_stride + static_cast<int64_t>(row % rows_per_block) * cap;
-  const int n = filter_row<kT, kVec>(sm, score + static_cast<int64_t>(row) * score_stride,
-                                     mask + static_cast<int64_t>(row) * mask_stride,
-                                     pt + static_cast<int64_t>(row) * pt_stride, len, lo, cap, out_keys + lo_off,
-                                     out_gidx + lo_off, flag);
-  if (threadIdx.x == 0 && counts) counts[row] = n;
+  __shared__ uint32_t ovf[kFilterRowsPerCta / 32];  // rows (by their index in this CTA) left to filter_row
+  auto lo_of = [&](int row) { return static_cast<uint32_t>(__ldg(bounds + row)) ^ kZeroKey; };
+  auto off_of = [&](int row) {
+    return (row / rows_per_block) * block_stride + static_cast<int64_t>(row % rows_per_block) * cap;
+  };
+  auto len_of = [&](int row) {
+    const int len = __ldg(lengths + row);
+    return len < 0 ? 0 : (len > width ? width : len);
+  };
+  // persistent CTAs, rows strided over the grid; with warp_pass, first a warp per row
+  const int nk = (rows - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x);
+  if (warp_pass) {
+    for (int i = threadIdx.x; i < kFilterRowsPerCta / 32; i += kT) ovf[i] = 0u;
+    __syncthreads();
+    const int w = threadIdx.x >> 5;
+    uint32_t* stage = reinterpret_cast<uint32_t*>(&sm.scr[0][0]) + w * 32 * kLaneTok;
+    for (int k = w; k < nk; k += kT / 32) {
+      const int row = static_cast<int>(blockIdx.x) + k * static_cast<int>(gridDim.x);
+      const int64_t off = off_of(row);
+      const int n = filter_row_warp<kVec>(score + static_cast<int64_t>(row) * score_stride,
+                                          mask + static_cast<int64_t>(row) * mask_stride,
+                                          pt + static_cast<int64_t>(row) * pt_stride, len_of(row), lo_of(row), cap,
+                                          out_keys + off, out_gidx + off, stage);
+      if ((threadIdx.x & 31) == 0) {
+        if (n > cap)
+          atomicOr(&ovf[k >> 5], 1u << (k & 31));
+        else if (counts)
+          counts[row] = n;
+      }
+    }
+    __syncthreads();
+  }
+  for (int k = 0; k < nk; ++k) {
+    if (warp_pass && !((ovf[k >> 5] >> (k & 31)) & 1u)) continue;  // uniform: shared state
+    const int row = static_cast<int>(blockIdx.x) + k * static_cast<int>(gridDim.x);
+    const int64_t off = off_of(row);
+    const int n = filter_row<kT, kVec>(sm, score + static_cast<int64_t>(row) * score_stride,
+                                       mask + static_cast<int64_t>(row) * mask_stride,
+                                       pt + static_cast<int64_t>(row) * pt_stride, len_of(row), lo_of(row), cap,
+                                       out_keys + off, out_gidx + off, flag);
+    if (threadIdx.x == 0 && counts) counts[row] = n;
+    __syncthreads();  // the row's shared state is read out before the next row reuses it
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -2186,9 +2289,12 @@ void launch_filter(const float* score, int rows, int width, int64_t score_stride
                    int32_t* counts, int32_t* flag, cudaStream_t st) {
   const size_t smem = sizeof(TopkSmem<kT>);
   cudaFuncSetAttribute(cp_filter_kernel<kT, kVec>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-  cp_filter_kernel<kT, kVec><<<static_cast<unsigned>(rows), kT, smem, st>>>(
+  // persistent CTAs; the warp pass when this CTA's rows fit its overflow bitmap
+  const int grid = static_cast<int>(std::min<int64_t>(rows, static_cast<int64_t>(sm_count()) * (1024 / kT)));
+  const int warp_pass = (rows + grid - 1) / grid <= kFilterRowsPerCta ? 1 : 0;
+  cp_filter_kernel<kT, kVec><<<static_cast<unsigned>(grid), kT, smem, st>>>(
       score, score_stride, width, mask, mask_stride, lengths, pt, pt_stride, bounds, cap, keys, gidx, rpb, bstride,
-      counts, flag);
+      counts, flag, rows, warp_pass);
 }
 }  // namespace
 }  // namespace hcu
@@ -2336,28 +2442,58 @@ template <int kT, bool kVec>
 __global__ __launch_bounds__(kT, 1024 / kT) void cp_peer_filter_kernel(
     const float* __restrict__ score, int64_t score_stride, int width, const int16_t* __restrict__ mask,
     int64_t mask_stride, const int32_t* __restrict__ lengths, const int32_t* __restrict__ pt, int64_t pt_stride,
-    const hcu_cp_peers_t pp) {
+    const hcu_cp_peers_t pp, int warp_pass) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   TopkSmem<kT>& sm = *reinterpret_cast<TopkSmem<kT>*>(smem_raw);
   __shared__ int s_ok;
+  __shared__ uint32_t ovf[kFilterRowsPerCta / 32];  // rows (by their index in this CTA) left to filter_row
   int* flagw = pp.ws + kWsFilterFlag;
-  // persistent CTAs (rows strided over the grid): one wait and one publication per CTA
+  // the row's bound: the minimum over ranks of their published estimates (order-preserving int32)
+  auto lo_of = [&](int row) {
+    int32_t b = INT32_MAX;
+    const int32_t* bl = pp.bounds[pp.rank];
+    for (int p = 0; p < pp.parts; ++p) b = min(b, __ldcg(bl + static_cast<int64_t>(p) * pp.rows + row));
+    return static_cast<uint32_t>(b) ^ kZeroKey;
+  };
+  auto len_of = [&](int row) {
+    const int len = __ldg(lengths + row);
+    return len < 0 ? 0 : (len > width ? width : len);
+  };
+  // this rank's list of the row in its owner's buffer: keys, then (rows_per_rank * C later) entries
+  auto keys_of = [&](int row) {
+    return pp.lists[row / pp.rows_per_rank] +
+           (static_cast<int64_t>(2 * pp.rank) * pp.rows_per_rank + row % pp.rows_per_rank) * pp.list_len;
+  };
+  const int64_t ent = static_cast<int64_t>(pp.rows_per_rank) * pp.list_len;
+  // persistent CTAs (rows strided over the grid): one wait and one publication per CTA; with
+  // warp_pass, first a warp per row, then the CTA on the rows whose list overflowed
   if (cta_wait(pp, kPhBounds, nullptr, &s_ok)) {
-    for (int row = blockIdx.x; row < pp.rows; row += gridDim.x) {
-      // the row's bound: the minimum over ranks of their published estimates (order-preserving int32)
-      int32_t b = INT32_MAX;
-      const int32_t* bl = pp.bounds[pp.rank];
-      for (int p = 0; p < pp.parts; ++p) b = min(b, __ldcg(bl + static_cast<int64_t>(p) * pp.rows + row));
-      int len = __ldg(lengths + row);
-      len = len < 0 ? 0 : (len > width ? width : len);
-      const int d = row / pp.rows_per_rank;  // the row's owner
-      const int64_t C = pp.list_len;
-      int32_t* keys =
-          pp.lists[d] + (static_cast<int64_t>(2 * pp.rank) * pp.rows_per_rank + row % pp.rows_per_rank) * C;
+    const int nk =
+        (pp.rows - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x);
+    if (warp_pass) {
+      for (int i = threadIdx.x; i < kFilterRowsPerCta / 32; i += kT) ovf[i] = 0u;
+      __syncthreads();
+      const int w = threadIdx.x >> 5;
+      uint32_t* stage = reinterpret_cast<uint32_t*>(&sm.scr[0][0]) + w * 32 * kLaneTok;
+      for (int k = w; k < nk; k += kT / 32) {
+        const int row = static_cast<int>(blockIdx.x) + k * static_cast<int>(gridDim.x);
+        int32_t* keys = keys_of(row);
+        const int n = filter_row_warp<kVec>(score + static_cast<int64_t>(row) * score_stride,
+                                            mask + static_cast<int64_t>(row) * mask_stride,
+                                            pt + static_cast<int64_t>(row) * pt_stride, len_of(row), lo_of(row),
+                                            pp.list_len, reinterpret_cast<uint32_t*>(keys), keys + ent, stage);
+        if ((threadIdx.x & 31) == 0 && n > pp.list_len) atomicOr(&ovf[k >> 5], 1u << (k & 31));
+      }
+      __syncthreads();
+    }
+    for (int k = 0; k < nk; ++k) {
+      if (warp_pass && !((ovf[k >> 5] >> (k & 31)) & 1u)) continue;  // uniform: shared state
+      const int row = static_cast<int>(blockIdx.x) + k * static_cast<int>(gridDim.x);
+      int32_t* keys = keys_of(row);
       filter_row<kT, kVec>(sm, score + static_cast<int64_t>(row) * score_stride,
                            mask + static_cast<int64_t>(row) * mask_stride, pt + static_cast<int64_t>(row) * pt_stride,
-                           len, static_cast<uint32_t>(b) ^ kZeroKey, pp.list_len, reinterpret_cast<uint32_t*>(keys),
-                           keys + static_cast<int64_t>(pp.rows_per_rank) * C, flagw);
+                           len_of(row), lo_of(row), pp.list_len, reinterpret_cast<uint32_t*>(keys), keys + ent,
+                           flagw);
       __syncthreads();  // the row's shared state is read out before the next row reuses it
     }
   } else if (threadIdx.x == 0) {
@@ -2458,8 +2594,9 @@ void launch_peer_filter(const float* score, int width, int64_t score_stride, con
   cudaFuncSetAttribute(cp_peer_filter_kernel<kT, kVec>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        static_cast<int>(smem));
   const int grid = static_cast<int>(std::min<int64_t>(pp.rows, static_cast<int64_t>(sm_count()) * (1024 / kT)));
+  const int warp_pass = (pp.rows + grid - 1) / grid <= kFilterRowsPerCta ? 1 : 0;
   cp_peer_filter_kernel<kT, kVec><<<static_cast<unsigned>(grid), kT, smem, st>>>(
-      score, score_stride, width, mask, mask_stride, lengths, pt, pt_stride, pp);
+      score, score_stride, width, mask, mask_stride, lengths, pt, pt_stride, pp, warp_pass);
 }
 
 }  // namespace
