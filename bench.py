@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark of the DSA lightning-indexer path on B200.
 
-Headline (BASELINE config 1, the decode indexer the metric is quoted on): 64 requests x next_n=2
+Headline (config 1 of BASELINE.json, the decode indexer the metric is quoted on): 64 requests x next_n=2
 rows, contexts U[4096, 65536], 64 index heads x 128 dim fp8, shared shuffled pool of 64-token pages.
 One step = one CUDA-graph replay of the sglang decode call pair: hcu_ops.mqa_logits (tcgen05 fp8
 paged logits + mask) -> hcu_ops.sparse_mask_topk_transform (exact top-2048 + page-table transform).
@@ -11,7 +11,7 @@ the slowest rank's time.  A stratified row sample of the headline step is checke
 oracle in the same run ("oracle_check").
 
 Sub-records of the same JSON line:
-  cp_prefill  BASELINE config 4 at this N (every N, 1 included): 16384 rows over a 131072-token
+  cp_prefill  config 4 of BASELINE.json at this N (every N, 1 included): 16384 rows over a 131072-token
               context split into N KV ranges (hcu_ops.cp); per-rank time spread, clocks, list length,
               reruns, and equality with the one-range result computed on rank 0.
   secondary   (N = 1) configs 0, 2, 3, the 656-byte MLA dequant, the indexer-K writer and the MLA

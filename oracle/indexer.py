@@ -124,7 +124,7 @@ def quant_store_index_k(k: np.ndarray, token_loc: np.ndarray, kv_pages: np.ndarr
     ``fp8 = e4m3_rne(clamp(x / scale, -448, 448))``; the 128 fp8 bytes go to the slot's row of
     the page, the scale to byte 8192 + 4 * offset.  Returns a written copy of ``kv_pages``
     (uint8 ``[n_pages, page_stride]``); out-of-range slots are skipped.  The arithmetic is the
-    per-token amax/448 quantisation BASELINE's configs use for K (``hcu_ops/workloads.py``)."""
+    per-token amax/448 quantisation the benchmark configs use for K (``hcu_ops/workloads.py``)."""
     x = np.asarray(k, dtype=np.float32).reshape(-1, HEAD_DIM)
     loc = np.asarray(token_loc, dtype=np.int64)
     out = np.array(kv_pages, dtype=np.uint8, copy=True)
